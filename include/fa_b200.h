@@ -1,0 +1,167 @@
+/*
+ * fa_b200.h -- C ABI of libfa_b200.so, the sm_100a (B200) FlashAttention kernels
+ * behind the tilelang_fa_v100 Python API.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t (passed
+ * as void*), returns 0 on success or a negative fa_status_t, never allocates
+ * device memory (outputs and workspaces belong to the caller) and never
+ * synchronises the stream.  Layouts are those of the reference API:
+ *   dense  q [B, Sq, H, D], k/v [B, Skv, Hk, D]   (last dim contiguous)
+ *   lse    [B, H, Sq] fp32                          (dense)
+ *   cache  [num_pages, page_size, Hkv, D]          (vLLM paged KV cache)
+ *   paged  q/out [num_tokens, H, D], lse [H, num_tokens] fp32
+ *   decode q/out [B, H, D]
+ * Supported: fp16 and bf16 inputs, head_dim 64/128 (dense, decode) and
+ * 64/128/256 (paged prefill), H % Hk == 0.
+ */
+#ifndef FA_B200_H_
+#define FA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  FA_OK = 0,
+  FA_ERR_INVALID_ARG = -1,       /* null pointer, bad size, H % Hk != 0, ... */
+  FA_ERR_UNSUPPORTED = -2,       /* head_dim / dtype / page_size not supported  */
+  FA_ERR_ALIGNMENT = -3,         /* pointer or stride not 16-byte aligned       */
+  FA_ERR_WORKSPACE = -4,         /* workspace missing or too small              */
+  FA_ERR_CUDA = -5,              /* a CUDA runtime/driver call failed           */
+  FA_ERR_DEVICE_TIMEOUT = -6,    /* a kernel's bounded wait expired (device)    */
+  FA_ERR_NOT_SM100 = -7          /* current device is not compute capability 10.x */
+} fa_status_t;
+
+typedef enum { FA_DTYPE_F16 = 0, FA_DTYPE_BF16 = 1 } fa_dtype_t;
+
+/* Dense forward.  Replaces tilelang_forward_lse(...)(q_, k_, v_) at
+ * tilelang_fa_v100/interface.py:35-36 (kernel: _kernels_forward.py:94-172), minus
+ * the BSHD<->BHSD permute copies (interface.py:19-21, 38): the kernel reads BSHD. */
+typedef struct {
+  const void* q;          /* [B, Sq, H, D]  */
+  const void* k;          /* [B, Skv, Hk, D] */
+  const void* v;          /* [B, Skv, Hk, D] */
+  void* out;              /* [B, Sq, H, D]  */
+  float* lse;             /* [B, H, Sq] (required) */
+  int64_t q_stride[3];    /* batch, seq, head strides in elements */
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int64_t o_stride[3];
+  int32_t batch, seqlen_q, seqlen_k, num_heads, num_heads_k, head_dim;
+  int32_t dtype;          /* fa_dtype_t */
+  int32_t causal;         /* bottom-right aligned: key j visible to row i iff j <= i + Skv - Sq */
+  float softmax_scale;
+} fa_fwd_args_t;
+
+int fa_fwd(const fa_fwd_args_t* args, void* stream);
+
+/* Dense backward.  Replaces tilelang_backward (_kernels_backward.py:200-208): the
+ * row-dot (:203), the dQ kernel (:10-85) and the dK/dV kernel (:88-176).
+ * Gradients are written in the BSHD layout of q/k/v.  Workspace (caller-owned,
+ * fa_bwd_workspace_size bytes, 256-byte aligned): the fp32 row-dot [B,H,Sq] and,
+ * in atomic mode, the fp32 dQ accumulator [B,H,Sq,D]. */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* out;
+  const void* dout;       /* [B, Sq, H, D] */
+  const float* lse;       /* [B, H, Sq] from fa_fwd */
+  void* dq;               /* [B, Sq, H, D] */
+  void* dk;               /* [B, Skv, Hk, D] */
+  void* dv;               /* [B, Skv, Hk, D] */
+  int64_t q_stride[3];
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int64_t o_stride[3];
+  int64_t do_stride[3];
+  int64_t dq_stride[3];
+  int64_t dk_stride[3];
+  int64_t dv_stride[3];
+  int32_t batch, seqlen_q, seqlen_k, num_heads, num_heads_k, head_dim;
+  int32_t dtype;
+  int32_t causal;
+  int32_t deterministic;  /* 1: dQ by a separate per-Q-tile kernel (bit-reproducible);
+                             0: dQ by fp32 atomics from the dK/dV kernel */
+  float softmax_scale;
+} fa_bwd_args_t;
+
+size_t fa_bwd_workspace_size(const fa_bwd_args_t* args);
+int fa_bwd(const fa_bwd_args_t* args, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Paged (vLLM-layout) prefill / chunked prefill forward.  Replaces
+ * get_paged_kernel(...)(q, k_cache, v_cache, block_table, seq_lens,
+ * query_start_loc, prefix_kv_lens, num_tokens, sm_scale) at
+ * _paged_adapter.py:40-46 (kernel: _kernels_paged.py:193-344).  Query row i of
+ * sequence b attends key j iff j < seq_lens[b] and, when causal,
+ * j <= prefix_kv_lens[b] + i (plus the optional sliding window of
+ * _kernels_paged.py:275-294).  Writes the real LSE [H, num_tokens]. */
+typedef struct {
+  const void* q;                  /* [num_tokens, H, D] */
+  const void* k_cache;            /* [num_pages, page_size, Hkv, D] */
+  const void* v_cache;
+  const int32_t* block_table;     /* [num_seqs, max_blocks] */
+  const int32_t* seq_lens;        /* [num_seqs] total KV length */
+  const int32_t* query_start_loc; /* [num_seqs + 1] */
+  const int32_t* prefix_kv_lens;  /* [num_seqs] */
+  void* out;                      /* [num_tokens, H, D] */
+  float* lse;                     /* [H, num_tokens] (may be NULL) */
+  int32_t num_tokens, num_seqs, num_heads, num_kv_heads, head_dim;
+  int32_t page_size, num_pages, max_blocks;
+  int32_t dtype;
+  int32_t causal;
+  int32_t sliding_window_q, sliding_window_k; /* <= 0: off (only honoured when causal) */
+  float softmax_scale;
+} fa_paged_args_t;
+
+int fa_paged_prefill(const fa_paged_args_t* args, void* stream);
+
+/* Paged decode (one query token per sequence), split-KV + LSE combine.  Replaces
+ * get_decode_kernel(...)(q, k_cache, v_cache, block_table, seq_lens) at
+ * _decode_adapter.py:46 (kernel: _kernels_paged.py:393-489).  Workspace
+ * (caller-owned, fa_decode_workspace_size bytes) holds the per-split partial
+ * outputs and LSEs. */
+typedef struct {
+  const void* q;                  /* [B, H, D] */
+  const void* k_cache;            /* [num_pages, page_size, Hkv, D] */
+  const void* v_cache;
+  const int32_t* block_table;     /* [B, max_blocks] */
+  const int32_t* seq_lens;        /* [B] */
+  void* out;                      /* [B, H, D] */
+  float* lse;                     /* [B, H] (may be NULL) */
+  int32_t batch, num_heads, num_kv_heads, head_dim;
+  int32_t page_size, num_pages, max_blocks;
+  int32_t dtype;
+  int32_t num_splits;             /* 0: heuristic from max_blocks and the SM count */
+  float softmax_scale;
+} fa_decode_args_t;
+
+size_t fa_decode_workspace_size(const fa_decode_args_t* args);
+int fa_decode(const fa_decode_args_t* args, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Diagnostics. */
+const char* fa_status_string(int status);
+/* Reads (and optionally clears) the library's device error word on the current
+ * device: code (0 = none, 1 = bounded wait expired), site and block index.
+ * Synchronises the device. */
+int fa_read_device_error(int32_t* code, int32_t* site, int32_t* block, int32_t clear);
+/* Library version and the number of kernels launched by this process so far. */
+const char* fa_version(void);
+int64_t fa_launch_count(void);
+
+/* Self-test of the tcgen05 building blocks used by the attention kernels: one
+ * 128 x N x K UMMA with the given operand majorness (0 = K-major, 1 = MN-major for
+ * B) and A from shared memory (a_tmem = 0) or tensor memory (a_tmem = 1).
+ * a: [128, K] row-major, b: [N, K] row-major (b_mn = 0) or [K, N] row-major
+ * (b_mn = 1), c: [128, N] fp32.  K in {16..256, multiple of 64}, N in {64, 128, 256}. */
+int fa_selftest_umma(const void* a, const void* b, float* c, int32_t n, int32_t k,
+                     int32_t dtype, int32_t b_mn, int32_t a_tmem, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA_B200_H_ */

@@ -1,0 +1,196 @@
+"""CPU oracle for the attention hot path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference arm may
+import this module, and only as the checker or the timed CPU baseline.  The
+product path (tilelang_fa_v100 + libfa_b200.so) never calls it.
+
+It restates, in numpy (float64 arithmetic, float32 results), the reference
+repository's pure-PyTorch attention oracles and the semantics of its kernels:
+
+* ``attention_ref``  -- ``pytorch_gqa_ref`` (tests/test_gqa_paged.py:19-45) and
+  ``pytorch_ref`` (tests/test_compare_ref.py:15-25): GQA head expansion
+  (test_gqa_paged.py:37-38), scores = q k^T * scale (:40), bottom-right causal mask
+  ``tril(ones(M, N), diagonal=N-M)`` (:41-43), softmax (:44), P V (:45).  The LSE
+  is the natural-log ``m * scale + ln(l)`` the kernels write
+  (_kernels_forward.py:170).
+* ``attention_bwd_ref`` -- gradients of the same function, i.e. what the reference
+  backward computes (_kernels_backward.py): D = rowsum(dO * O) (:203),
+  dP = dO V^T (:55), dS = P * (dP - D) (:72-74), dQ = scale dS K (:80),
+  dV = P^T dO (:166), dK = scale dS^T Q (:170).
+* ``paged_prefill_ref`` -- the paged kernel's masking (_kernels_paged.py:296-303):
+  query i of sequence b sees key j iff j < seq_lens[b] and, when causal,
+  j <= prefix_kv_lens[b] + i, plus the sliding window of :275-294; K/V gathered
+  page by page through block_table (:265-272).
+* ``decode_ref`` -- the decode kernel (_kernels_paged.py:393-489): one query per
+  sequence, every key j < seq_lens[b] visible.
+
+Pinning: tests/test_oracle_golden.py checks every function here against golden
+vectors produced by running the reference's own ``pytorch_gqa_ref`` and
+``make_paged_gqa`` (tests/golden/make_golden.py).
+"""
+import numpy as np
+
+NEG_INF = -np.inf
+
+
+def _softmax_lse(scores):
+    """Row softmax and natural-log LSE; fully masked rows give P = 0, LSE = -inf."""
+    m = np.max(scores, axis=-1, keepdims=True)
+    m_safe = np.where(np.isfinite(m), m, 0.0)
+    e = np.exp(scores - m_safe)
+    l = np.sum(e, axis=-1, keepdims=True)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        p = np.where(l > 0, e / np.where(l > 0, l, 1.0), 0.0)
+        lse = np.where(l > 0, m_safe + np.log(np.where(l > 0, l, 1.0)), NEG_INF)
+    return p, lse[..., 0]
+
+
+def causal_mask(m, n):
+    """Bottom-right aligned causal mask: key j visible to query i iff j <= i + n - m."""
+    i = np.arange(m)[:, None]
+    j = np.arange(n)[None, :]
+    return j <= i + (n - m)
+
+
+def _expand_kv(x, hq):
+    hkv = x.shape[1]
+    return np.repeat(x, hq // hkv, axis=1)
+
+
+def attention_ref(q, k, v, causal, scale=None, return_p=False):
+    """q [B, Hq, M, D], k/v [B, Hkv, N, D] -> out [B, Hq, M, D] f32, lse [B, Hq, M] f32."""
+    q = np.asarray(q, dtype=np.float64)
+    k = _expand_kv(np.asarray(k, dtype=np.float64), q.shape[1])
+    v = _expand_kv(np.asarray(v, dtype=np.float64), q.shape[1])
+    d = q.shape[-1]
+    scale = 1.0 / np.sqrt(d) if scale is None else scale
+    s = np.einsum("bhqd,bhkd->bhqk", q, k) * scale
+    if causal:
+        s = np.where(causal_mask(q.shape[2], k.shape[2]), s, NEG_INF)
+    p, lse = _softmax_lse(s)
+    out = np.einsum("bhqk,bhkd->bhqd", p, v)
+    if return_p:
+        return out.astype(np.float32), lse.astype(np.float32), p
+    return out.astype(np.float32), lse.astype(np.float32)
+
+
+def attention_bwd_ref(q, k, v, do, causal, scale=None):
+    """Gradients (dq [B,Hq,M,D], dk/dv [B,Hkv,N,D]) of attention_ref w.r.t. q, k, v."""
+    q64 = np.asarray(q, dtype=np.float64)
+    k64 = np.asarray(k, dtype=np.float64)
+    v64 = np.asarray(v, dtype=np.float64)
+    do64 = np.asarray(do, dtype=np.float64)
+    hq, hkv = q64.shape[1], k64.shape[1]
+    d = q64.shape[-1]
+    scale = 1.0 / np.sqrt(d) if scale is None else scale
+    ke = _expand_kv(k64, hq)
+    ve = _expand_kv(v64, hq)
+    s = np.einsum("bhqd,bhkd->bhqk", q64, ke) * scale
+    if causal:
+        s = np.where(causal_mask(q64.shape[2], ke.shape[2]), s, NEG_INF)
+    p, _ = _softmax_lse(s)
+    o = np.einsum("bhqk,bhkd->bhqd", p, ve)
+    dsum = np.sum(do64 * o, axis=-1, keepdims=True)        # row-dot D
+    dp = np.einsum("bhqd,bhkd->bhqk", do64, ve)            # dO V^T
+    ds = p * (dp - dsum)
+    dq = np.einsum("bhqk,bhkd->bhqd", ds, ke) * scale
+    dke = np.einsum("bhqk,bhqd->bhkd", ds, q64) * scale
+    dve = np.einsum("bhqk,bhqd->bhkd", p, do64)
+    g = hq // hkv
+    b, _, n, _ = dke.shape
+    dk = dke.reshape(b, hkv, g, n, d).sum(axis=2)
+    dv = dve.reshape(b, hkv, g, n, d).sum(axis=2)
+    return dq.astype(np.float32), dk.astype(np.float32), dv.astype(np.float32)
+
+
+def gather_pages(cache, block_table_row, length):
+    """Tokens [0, length) of one sequence from a [P, page, Hkv, D] cache -> [Hkv, length, D]."""
+    page = cache.shape[1]
+    idx = np.arange(length)
+    pages = np.asarray(block_table_row)[idx // page]
+    return np.asarray(cache)[pages, idx % page].transpose(1, 0, 2)
+
+
+def paged_prefill_ref(q, k_cache, v_cache, block_table, seq_lens, query_start_loc,
+                      prefix_kv_lens, causal=True, scale=None, sliding_window_q=-1,
+                      sliding_window_k=-1):
+    """q [T, H, D] -> out [T, H, D] f32, lse [H, T] f32 (reference kernel semantics)."""
+    q = np.asarray(q, dtype=np.float64)
+    t, h, d = q.shape
+    hkv = k_cache.shape[2]
+    scale = 1.0 / np.sqrt(d) if scale is None else scale
+    out = np.zeros((t, h, d), np.float64)
+    lse = np.full((h, t), NEG_INF, np.float64)
+    for b in range(len(seq_lens)):
+        q0, q1 = int(query_start_loc[b]), int(query_start_loc[b + 1])
+        if q1 <= q0:
+            continue
+        length = int(seq_lens[b])
+        kb = gather_pages(k_cache, block_table[b], length).astype(np.float64)
+        vb = gather_pages(v_cache, block_table[b], length).astype(np.float64)
+        kb = np.repeat(kb, h // hkv, axis=0)
+        vb = np.repeat(vb, h // hkv, axis=0)
+        qb = q[q0:q1].transpose(1, 0, 2)                      # [H, ql, D]
+        s = np.einsum("hqd,hkd->hqk", qb, kb) * scale
+        i = np.arange(q1 - q0)[:, None]
+        j = np.arange(length)[None, :]
+        vis = np.ones((q1 - q0, length), bool)
+        if causal:
+            vis &= j <= int(prefix_kv_lens[b]) + i
+            if sliding_window_q > 0:
+                vis &= i < j + sliding_window_q
+            if sliding_window_k > 0:
+                vis &= j < i + sliding_window_k
+        s = np.where(vis[None], s, NEG_INF)
+        p, l_ = _softmax_lse(s)
+        out[q0:q1] = np.einsum("hqk,hkd->hqd", p, vb).transpose(1, 0, 2)
+        lse[:, q0:q1] = l_
+    return out.astype(np.float32), lse.astype(np.float32)
+
+
+def decode_ref(q, k_cache, v_cache, block_table, seq_lens, scale=None):
+    """q [B, H, D] -> out [B, H, D] f32, lse [B, H] f32; all keys < seq_lens[b] visible."""
+    q = np.asarray(q, dtype=np.float64)
+    bsz, h, d = q.shape
+    qsl = np.arange(bsz + 1)
+    out, lse = paged_prefill_ref(q, k_cache, v_cache, block_table, seq_lens, qsl,
+                                 np.zeros(bsz, np.int64), causal=False, scale=scale)
+    return out, np.ascontiguousarray(lse.T)
+
+
+def make_paged_cache(k, v, page_size=16, shuffle_seed=None, num_pages=None):
+    """Dense k/v [B, Hkv, N, D] -> (k_cache, v_cache, block_table) in the vLLM layout.
+
+    Sequence b's logical page p holds tokens [p*page, (p+1)*page); physical pages are
+    a seeded permutation when ``shuffle_seed`` is given (scattered allocation)."""
+    bsz, hkv, n, d = k.shape
+    pps = -(-n // page_size)
+    total = bsz * pps if num_pages is None else num_pages
+    perm = np.arange(total)
+    if shuffle_seed is not None:
+        perm = np.random.default_rng(shuffle_seed).permutation(total)
+    kc = np.zeros((total, page_size, hkv, d), k.dtype)
+    vc = np.zeros((total, page_size, hkv, d), v.dtype)
+    bt = np.zeros((bsz, pps), np.int32)
+    for b in range(bsz):
+        for p in range(pps):
+            phys = perm[b * pps + p]
+            bt[b, p] = phys
+            t0, t1 = p * page_size, min(n, (p + 1) * page_size)
+            kc[phys, : t1 - t0] = k[b, :, t0:t1].transpose(1, 0, 2)
+            vc[phys, : t1 - t0] = v[b, :, t0:t1].transpose(1, 0, 2)
+    return kc, vc, bt
+
+
+def flops_dense(b, h, sq, skv, d, causal):
+    """Algorithmic forward FLOPs on visible (query, key) pairs: 4 * D per pair."""
+    return 4.0 * d * visible_pairs(b, h, sq, skv, causal)
+
+
+def visible_pairs(b, h, sq, skv, causal):
+    if not causal:
+        return float(b) * h * sq * skv
+    off = skv - sq
+    i = np.arange(sq, dtype=np.int64)
+    per_row = np.clip(i + off + 1, 0, skv)
+    return float(b) * h * float(per_row.sum())

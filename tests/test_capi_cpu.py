@@ -1,0 +1,110 @@
+"""CPU checks of the C ABI boundary: the library loads, exports every entry point
+include/fa_b200.h declares, its argument structs match the ctypes mirrors byte for
+byte, and the host-side validation answers without a GPU."""
+import ctypes
+import os
+import re
+import subprocess
+import tempfile
+
+import pytest
+
+from tilelang_fa_v100 import _ext
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "fa_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*[A-Za-z_][\w\s\*]*?\b(fa_\w+)\s*\(", src, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for must in ("fa_fwd", "fa_bwd", "fa_paged_prefill", "fa_decode", "fa_bwd_workspace_size",
+                 "fa_decode_workspace_size", "fa_status_string"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _ext.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+        assert name in _ext.SIGNATURES, "ctypes signature missing for " + name
+
+
+def _c_layout(struct_name, fields):
+    body = "\n".join('  printf("%%s %%zu\\n", "%s", offsetof(%s, %s));' % (f, struct_name, f)
+                     for f in fields)
+    prog = """#include <stdio.h>
+#include <stddef.h>
+#include "fa_b200.h"
+int main(void) {
+  printf("sizeof %%zu\\n", sizeof(%s));
+%s
+  return 0;
+}
+""" % (struct_name, body)
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "l.c")
+        exe = os.path.join(d, "l")
+        open(c, "w").write(prog)
+        subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), c, "-o", exe], check=True)
+        out = subprocess.run([exe], capture_output=True, text=True, check=True).stdout
+    return dict((a, int(b)) for a, b in (ln.split() for ln in out.strip().splitlines()))
+
+
+@pytest.mark.parametrize("cname,cls", [("fa_fwd_args_t", _ext.FwdArgs),
+                                       ("fa_bwd_args_t", _ext.BwdArgs),
+                                       ("fa_paged_args_t", _ext.PagedArgs),
+                                       ("fa_decode_args_t", _ext.DecodeArgs)])
+def test_struct_layout_matches_c(cname, cls):
+    fields = [f for f, _ in cls._fields_]
+    lay = _c_layout(cname, fields)
+    assert lay["sizeof"] == ctypes.sizeof(cls)
+    for f in fields:
+        assert lay[f] == getattr(cls, f).offset, f
+
+
+def test_status_strings_and_version():
+    lib = _ext.load()
+    assert b"sm_100a" in lib.fa_version()
+    for s in range(-7, 1):
+        assert lib.fa_status_string(s)
+    assert lib.fa_launch_count() >= 0
+
+
+def test_null_arguments_rejected_on_host():
+    lib = _ext.load()
+    a = _ext.FwdArgs()
+    assert lib.fa_fwd(ctypes.byref(a), None) == _ext.FA_ERR_INVALID_ARG
+    assert lib.fa_fwd(None, None) == _ext.FA_ERR_INVALID_ARG
+    p = _ext.PagedArgs()
+    assert lib.fa_paged_prefill(ctypes.byref(p), None) == _ext.FA_ERR_INVALID_ARG
+    d = _ext.DecodeArgs()
+    assert lib.fa_decode(ctypes.byref(d), None, 0, None) == _ext.FA_ERR_INVALID_ARG
+    b = _ext.BwdArgs()
+    assert lib.fa_bwd(ctypes.byref(b), None, 0, None) == _ext.FA_ERR_INVALID_ARG
+
+
+def test_unsupported_head_dim_rejected_on_host():
+    lib = _ext.load()
+    a = _ext.FwdArgs(1, 1, 1, 1, 1)
+    a.batch, a.seqlen_q, a.seqlen_k, a.num_heads, a.num_heads_k = 1, 8, 8, 2, 2
+    a.head_dim, a.dtype = 96, 0
+    assert lib.fa_fwd(ctypes.byref(a), None) == _ext.FA_ERR_UNSUPPORTED
+    a.head_dim, a.num_heads_k = 64, 3  # H % Hk != 0
+    assert lib.fa_fwd(ctypes.byref(a), None) == _ext.FA_ERR_INVALID_ARG
+
+
+def test_decode_workspace_size_is_host_computed():
+    lib = _ext.load()
+    d = _ext.DecodeArgs()
+    d.batch, d.num_heads, d.num_kv_heads, d.head_dim = 256, 32, 8, 128
+    d.page_size, d.num_pages, d.max_blocks, d.dtype = 16, 70000, 512, 1
+    n = lib.fa_decode_workspace_size(ctypes.byref(d))
+    assert n > 256 * 32 * 128 * 4  # several splits of fp32 partial outputs
+    d.num_splits = 1
+    assert lib.fa_decode_workspace_size(ctypes.byref(d)) == 0

@@ -1,0 +1,179 @@
+"""Dense attention on the GPU against the CPU oracle (pinned to the reference) and
+against the reference's own golden vectors."""
+import numpy as np
+import pytest
+import torch
+
+import tilelang_fa_v100 as fa
+from helpers import ATOL, RTOL, GRAD_ATOL, assert_close, golden, golden_names, max_abs
+from oracle import attention_ref as R
+
+pytestmark = pytest.mark.gpu
+
+
+def _to_bhsd(x):
+    return x.float().permute(0, 2, 1, 3).cpu().numpy()
+
+
+def _rand(shape, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape, generator=g).to(dtype)
+
+
+def _fwd(q, k, v, causal, scale=None):
+    out, lse, _ = fa.tilelang_flash_attn_func(q, k, v, causal=causal, softmax_scale=scale,
+                                              return_attn_probs=True)
+    torch.cuda.synchronize()
+    return out, lse
+
+
+@pytest.mark.parametrize("name", golden_names("dense_"))
+def test_golden_forward(cuda_dev, name):
+    g = golden(name)
+    q, k, v = (torch.from_numpy(g[x]).permute(0, 2, 1, 3).contiguous().to(cuda_dev)
+               for x in ("q", "k", "v"))
+    out, lse = _fwd(q, k, v, bool(g["causal"]))
+    ref_out, ref_lse = R.attention_ref(g["q"], g["k"], g["v"], bool(g["causal"]))
+    assert_close(_to_bhsd(out), ref_out, what=name + " out")
+    assert_close(lse.cpu().numpy(), ref_lse, what=name + " lse")
+    # and the reference's own fp16 output within its bar (max-abs < 0.01)
+    assert max_abs(_to_bhsd(out), g["out"].astype(np.float32)) < 1e-2
+
+
+FWD_CASES = [
+    # B, Sq, Skv, H, Hk, D, causal, dtype
+    (1, 128, 128, 2, 2, 64, False, torch.float16),
+    (2, 200, 200, 3, 3, 128, True, torch.bfloat16),
+    (1, 64, 300, 2, 2, 128, True, torch.float16),    # non-square causal (bottom-right)
+    (1, 300, 64, 2, 2, 64, True, torch.bfloat16),    # Sq > Skv: leading rows fully masked
+    (1, 257, 257, 4, 1, 128, True, torch.bfloat16),  # MQA
+    (1, 190, 190, 8, 2, 64, True, torch.float16),    # GQA 4:1
+    (1, 100, 100, 2, 2, 256, False, torch.float16),  # D = 256
+    (1, 1, 77, 2, 2, 64, False, torch.bfloat16),     # single query row
+    (2, 512, 512, 2, 2, 64, True, torch.float16),
+    (1, 1000, 1000, 1, 1, 128, True, torch.bfloat16),
+    (1, 384, 1024, 2, 2, 128, False, torch.float16),
+]
+
+
+@pytest.mark.parametrize("case", FWD_CASES, ids=lambda c: "-".join(map(str, c[:7])))
+def test_forward_vs_oracle(cuda_dev, case):
+    b, sq, skv, h, hk, d, causal, dt = case
+    q = _rand((b, sq, h, d), dt, 1)
+    k = _rand((b, skv, hk, d), dt, 2)
+    v = _rand((b, skv, hk, d), dt, 3)
+    out, lse = _fwd(q.to(cuda_dev), k.to(cuda_dev), v.to(cuda_dev), causal)
+    ref_out, ref_lse = R.attention_ref(_to_bhsd(q), _to_bhsd(k), _to_bhsd(v), causal)
+    assert_close(_to_bhsd(out), ref_out, what="out")
+    assert_close(lse.cpu().numpy(), ref_lse, what="lse")
+
+
+def test_custom_softmax_scale(cuda_dev):
+    q, k, v = (_rand((1, 130, 2, 64), torch.float16, s) for s in (4, 5, 6))
+    out, lse = _fwd(q.to(cuda_dev), k.to(cuda_dev), v.to(cuda_dev), True, scale=0.3)
+    ref_out, ref_lse = R.attention_ref(_to_bhsd(q), _to_bhsd(k), _to_bhsd(v), True, scale=0.3)
+    assert_close(_to_bhsd(out), ref_out, what="out")
+    assert_close(lse.cpu().numpy(), ref_lse, what="lse")
+
+
+def test_noncontiguous_inputs(cuda_dev):
+    # BHSD storage viewed as BSHD (what a caller holding [B,H,S,D] tensors passes)
+    q, k, v = (_rand((1, 2, 96, 64), torch.bfloat16, s).to(cuda_dev).permute(0, 2, 1, 3)
+               for s in (7, 8, 9))
+    out, lse = _fwd(q, k, v, True)
+    ref_out, _ = R.attention_ref(_to_bhsd(q), _to_bhsd(k), _to_bhsd(v), True)
+    assert_close(_to_bhsd(out), ref_out, what="out")
+
+
+def test_repeated_calls_are_deterministic(cuda_dev):
+    q, k, v = (_rand((2, 333, 4, 128), torch.bfloat16, s).to(cuda_dev) for s in (10, 11, 12))
+    o1, _ = _fwd(q, k, v, True)
+    o2, _ = _fwd(q, k, v, True)
+    assert torch.equal(o1, o2)
+
+
+BWD_CASES = [
+    (1, 128, 128, 2, 2, 64, False, torch.float16),
+    (2, 200, 200, 3, 3, 128, True, torch.bfloat16),
+    (1, 96, 300, 2, 2, 128, True, torch.float16),
+    (1, 257, 257, 4, 1, 128, True, torch.bfloat16),
+    (1, 190, 190, 4, 2, 64, True, torch.float16),
+    (1, 512, 512, 2, 2, 64, True, torch.bfloat16),
+]
+
+
+@pytest.mark.parametrize("deterministic", [False, True])
+@pytest.mark.parametrize("case", BWD_CASES, ids=lambda c: "-".join(map(str, c[:7])))
+def test_backward_vs_oracle(cuda_dev, case, deterministic):
+    b, sq, skv, h, hk, d, causal, dt = case
+    q = _rand((b, sq, h, d), dt, 21)
+    k = _rand((b, skv, hk, d), dt, 22)
+    v = _rand((b, skv, hk, d), dt, 23)
+    do = _rand((b, sq, h, d), dt, 24)
+    qd, kd, vd = (x.to(cuda_dev).requires_grad_(True) for x in (q, k, v))
+    out = fa.tilelang_flash_attn_func(qd, kd, vd, causal=causal, deterministic=deterministic)
+    out.backward(do.to(cuda_dev))
+    torch.cuda.synchronize()
+    dq, dk, dv = R.attention_bwd_ref(_to_bhsd(q), _to_bhsd(k), _to_bhsd(v), _to_bhsd(do), causal)
+    for got, want, w in ((qd.grad, dq, "dq"), (kd.grad, dk, "dk"), (vd.grad, dv, "dv")):
+        err = max_abs(_to_bhsd(got), want)
+        assert err <= GRAD_ATOL, "%s max-abs %.4g" % (w, err)
+
+
+@pytest.mark.parametrize("name", golden_names("dense_"))
+def test_golden_backward(cuda_dev, name):
+    g = golden(name)
+    q, k, v = (torch.from_numpy(g[x]).permute(0, 2, 1, 3).contiguous().to(cuda_dev)
+               .requires_grad_(True) for x in ("q", "k", "v"))
+    do = torch.from_numpy(g["do"]).permute(0, 2, 1, 3).to(torch.float16).contiguous().to(cuda_dev)
+    out = fa.tilelang_flash_attn_func(q, k, v, causal=bool(g["causal"]))
+    out.backward(do)
+    torch.cuda.synchronize()
+    dq, dk, dv = R.attention_bwd_ref(g["q"], g["k"], g["v"],
+                                     _to_bhsd(do.cpu()), bool(g["causal"]))
+    for got, want, w in ((q.grad, dq, "dq"), (k.grad, dk, "dk"), (v.grad, dv, "dv")):
+        assert max_abs(_to_bhsd(got), want) <= GRAD_ATOL, w
+
+
+def test_deterministic_backward_is_bitwise_reproducible(cuda_dev):
+    q, k, v, do = (_rand((1, 700, 2, 128), torch.bfloat16, s).to(cuda_dev) for s in (31, 32, 33, 34))
+    grads = []
+    for _ in range(2):
+        qd, kd, vd = (x.clone().requires_grad_(True) for x in (q, k, v))
+        fa.tilelang_flash_attn_func(qd, kd, vd, causal=True, deterministic=True).backward(do)
+        grads.append((qd.grad, kd.grad, vd.grad))
+    for a, b in zip(*grads):
+        assert torch.equal(a, b)
+
+
+def _torch_ref_slice(q, k, v, causal, bi, hi, hk_i):
+    """fp32 torch reference on the GPU for one (batch, head) slice of a large input."""
+    qs = q[bi, :, hi].float()
+    ks = k[bi, :, hk_i].float()
+    vs = v[bi, :, hk_i].float()
+    s = (qs @ ks.T) / (q.shape[-1] ** 0.5)
+    if causal:
+        m, n = s.shape
+        mask = torch.ones(m, n, device=s.device).tril(diagonal=n - m)
+        s = s.masked_fill(mask == 0, float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    return torch.softmax(s, dim=-1) @ vs, lse
+
+
+@pytest.mark.parametrize("cfg", [(4, 2048, 2048, 16, 64, torch.float16),
+                                 (8, 4096, 4096, 32, 128, torch.bfloat16),
+                                 (8, 1024, 4096, 32, 128, torch.bfloat16)],
+                         ids=["cfg2", "cfg3", "cfg3-nonsquare"])
+def test_full_size_forward_sampled(cuda_dev, cfg):
+    """BASELINE configs at full size; sampled (batch, head) slices vs fp32 torch."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    b, sq, skv, h, d, dt = cfg
+    g = torch.Generator(device=cuda_dev).manual_seed(0)
+    q = torch.randn(b, sq, h, d, generator=g, device=cuda_dev).to(dt)
+    k = torch.randn(b, skv, h, d, generator=g, device=cuda_dev).to(dt)
+    v = torch.randn(b, skv, h, d, generator=g, device=cuda_dev).to(dt)
+    out, lse = _fwd(q, k, v, True)
+    for bi, hi in ((0, 0), (b - 1, h - 1), (b // 2, h // 3)):
+        ro, rl = _torch_ref_slice(q, k, v, True, bi, hi, hi)
+        assert_close(out[bi, :, hi].float().cpu().numpy(), ro.cpu().numpy(), what="out")
+        assert_close(lse[bi, hi].cpu().numpy(), rl.cpu().numpy(), what="lse")

@@ -1,0 +1,213 @@
+// C ABI of libfa_b200.so: argument validation, the device error word, tensor-map
+// encoding and dispatch to the kernel launchers.  Nothing here allocates device
+// memory; outputs and workspaces are owned by the caller.
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <cudaTypedefs.h>
+#include "fa_internal.h"
+
+namespace fa {
+
+// Device error word: [0] code (0 = none, 1 = bounded wait expired), [1] site, [2] block.
+__device__ int g_fa_device_error[4];
+
+static std::mutex g_mu;
+static int* g_err_ptr[64] = {nullptr};
+static int g_sm_count[64] = {0};
+static int g_cc_ok[64] = {0};  // 0 unknown, 1 ok, -1 not sm_100
+static std::atomic<int64_t> g_launches{0};
+
+void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+static int current_device(int* dev) {
+  if (cudaGetDevice(dev) != cudaSuccess) return FA_ERR_CUDA;
+  if (*dev < 0 || *dev >= 64) return FA_ERR_CUDA;
+  return FA_OK;
+}
+
+// Per-device set-up: compute-capability check, SM count and the device address of
+// the error word (taken once per device, with that device current).
+static int device_setup(int** err_out) {
+  int dev;
+  if (int s = current_device(&dev)) return s;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_cc_ok[dev] == 0) {
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+      return FA_ERR_CUDA;
+    g_cc_ok[dev] = (major == 10) ? 1 : -1;
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    g_sm_count[dev] = sms;
+  }
+  if (g_cc_ok[dev] < 0) return FA_ERR_NOT_SM100;
+  if (g_err_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_fa_device_error) != cudaSuccess) return FA_ERR_CUDA;
+    g_err_ptr[dev] = static_cast<int*>(ptr);
+  }
+  *err_out = g_err_ptr[dev];
+  return FA_OK;
+}
+
+int num_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  return g_sm_count[dev] > 0 ? g_sm_count[dev] : 148;
+}
+
+CUresult encode_tmap(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
+                     const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                     CUtensorMapSwizzle swizzle) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (fn == nullptr) return CUDA_ERROR_NOT_FOUND;
+  cuuint64_t gdim[5];
+  cuuint64_t gstr[4];
+  cuuint32_t bdim[5];
+  cuuint32_t estr[5];
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    bdim[i] = box[i];
+    estr[i] = 1;
+    if (i + 1 < rank) gstr[i] = strides_bytes[i];
+  }
+  return fn(map, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), gdim, gstr, bdim, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+static bool valid_dtype(int d) { return d == FA_DTYPE_F16 || d == FA_DTYPE_BF16; }
+
+}  // namespace fa
+
+using namespace fa;
+
+extern "C" {
+
+const char* fa_version(void) { return "fa_b200 1.0.0 (sm_100a)"; }
+
+int64_t fa_launch_count(void) { return g_launches.load(); }
+
+const char* fa_status_string(int status) {
+  switch (status) {
+    case FA_OK: return "ok";
+    case FA_ERR_INVALID_ARG: return "invalid argument";
+    case FA_ERR_UNSUPPORTED: return "unsupported head_dim / dtype / page_size / GQA ratio";
+    case FA_ERR_ALIGNMENT: return "pointer or stride not 16-byte aligned";
+    case FA_ERR_WORKSPACE: return "workspace missing or too small";
+    case FA_ERR_CUDA: return "CUDA runtime/driver call failed";
+    case FA_ERR_DEVICE_TIMEOUT: return "a kernel's bounded wait expired on the device";
+    case FA_ERR_NOT_SM100: return "current device is not an sm_100 (B200-class) GPU";
+    default: return "unknown status";
+  }
+}
+
+int fa_read_device_error(int32_t* code, int32_t* site, int32_t* block, int32_t clear) {
+  int* err = nullptr;
+  if (int s = device_setup(&err)) return s;
+  int host[4] = {0, 0, 0, 0};
+  if (cudaDeviceSynchronize() != cudaSuccess) return FA_ERR_CUDA;
+  if (cudaMemcpy(host, err, sizeof(host), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return FA_ERR_CUDA;
+  if (code) *code = host[0];
+  if (site) *site = host[1];
+  if (block) *block = host[2];
+  if (clear) {
+    const int zero[4] = {0, 0, 0, 0};
+    if (cudaMemcpy(err, zero, sizeof(zero), cudaMemcpyHostToDevice) != cudaSuccess)
+      return FA_ERR_CUDA;
+  }
+  return FA_OK;
+}
+
+int fa_fwd(const fa_fwd_args_t* a, void* stream) {
+  if (a == nullptr || a->q == nullptr || a->k == nullptr || a->v == nullptr ||
+      a->out == nullptr || a->lse == nullptr)
+    return FA_ERR_INVALID_ARG;
+  if (a->batch < 0 || a->seqlen_q < 0 || a->seqlen_k < 0 || a->num_heads <= 0 ||
+      a->num_heads_k <= 0 || a->num_heads % a->num_heads_k != 0)
+    return FA_ERR_INVALID_ARG;
+  if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
+  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256) return FA_ERR_UNSUPPORTED;
+  int* err = nullptr;
+  if (int s = device_setup(&err)) return s;
+  return launch_fwd_dense(a, err, static_cast<cudaStream_t>(stream));
+}
+
+size_t fa_bwd_workspace_size(const fa_bwd_args_t* a) {
+  if (a == nullptr) return 0;
+  return bwd_workspace_bytes(a);
+}
+
+int fa_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, void* stream) {
+  if (a == nullptr || a->q == nullptr || a->k == nullptr || a->v == nullptr ||
+      a->out == nullptr || a->dout == nullptr || a->lse == nullptr || a->dq == nullptr ||
+      a->dk == nullptr || a->dv == nullptr)
+    return FA_ERR_INVALID_ARG;
+  if (a->batch < 0 || a->seqlen_q < 0 || a->seqlen_k < 0 || a->num_heads <= 0 ||
+      a->num_heads_k <= 0 || a->num_heads % a->num_heads_k != 0)
+    return FA_ERR_INVALID_ARG;
+  if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
+  if (a->head_dim != 64 && a->head_dim != 128) return FA_ERR_UNSUPPORTED;
+  if (ws_bytes < bwd_workspace_bytes(a) || (bwd_workspace_bytes(a) > 0 && ws == nullptr))
+    return FA_ERR_WORKSPACE;
+  int* err = nullptr;
+  if (int s = device_setup(&err)) return s;
+  return launch_bwd(a, ws, ws_bytes, err, static_cast<cudaStream_t>(stream));
+}
+
+int fa_paged_prefill(const fa_paged_args_t* a, void* stream) {
+  if (a == nullptr || a->q == nullptr || a->k_cache == nullptr || a->v_cache == nullptr ||
+      a->block_table == nullptr || a->seq_lens == nullptr || a->query_start_loc == nullptr ||
+      a->prefix_kv_lens == nullptr || a->out == nullptr)
+    return FA_ERR_INVALID_ARG;
+  if (a->num_tokens < 0 || a->num_seqs < 0 || a->num_heads <= 0 || a->num_kv_heads <= 0 ||
+      a->num_heads % a->num_kv_heads != 0 || a->num_pages <= 0 || a->max_blocks <= 0)
+    return FA_ERR_INVALID_ARG;
+  if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
+  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256) return FA_ERR_UNSUPPORTED;
+  int* err = nullptr;
+  if (int s = device_setup(&err)) return s;
+  return launch_paged_prefill(a, err, static_cast<cudaStream_t>(stream));
+}
+
+size_t fa_decode_workspace_size(const fa_decode_args_t* a) {
+  if (a == nullptr) return 0;
+  return decode_workspace_bytes(a);
+}
+
+int fa_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, void* stream) {
+  if (a == nullptr || a->q == nullptr || a->k_cache == nullptr || a->v_cache == nullptr ||
+      a->block_table == nullptr || a->seq_lens == nullptr || a->out == nullptr)
+    return FA_ERR_INVALID_ARG;
+  if (a->batch < 0 || a->num_heads <= 0 || a->num_kv_heads <= 0 ||
+      a->num_heads % a->num_kv_heads != 0 || a->num_pages <= 0 || a->max_blocks <= 0 ||
+      a->num_splits < 0)
+    return FA_ERR_INVALID_ARG;
+  if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
+  int* err = nullptr;
+  if (int s = device_setup(&err)) return s;
+  return launch_decode(a, ws, ws_bytes, err, static_cast<cudaStream_t>(stream));
+}
+
+int fa_selftest_umma(const void* a, const void* b, float* c, int32_t n, int32_t k, int32_t dtype,
+                     int32_t b_mn, int32_t a_tmem, void* stream) {
+  if (a == nullptr || b == nullptr || c == nullptr) return FA_ERR_INVALID_ARG;
+  if (!valid_dtype(dtype)) return FA_ERR_UNSUPPORTED;
+  int* err = nullptr;
+  if (int s = device_setup(&err)) return s;
+  return launch_selftest_umma(a, b, c, n, k, dtype, b_mn, a_tmem, err,
+                              static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,481 @@
+// Paged decode on sm_100a: split-KV + LSE-weighted combine.
+// Reference: tilelang_decode_forward -> _decode_adapter.py:15-47 -> _decode_kernel_func
+// (_kernels_paged.py:393-489), which runs one CTA per (q head, sequence) over the whole
+// sequence and re-reads every KV page once per q head of a GQA group.
+//
+// Here the work is HBM-bound (one query token per sequence), so the kernel is built to
+// read each K/V byte exactly once:
+//   * CTA = (split, kv-head group, sequence).  A split is a contiguous range of
+//     16-token chunks of one sequence; splits run in parallel across SMs.
+//   * warp 0 lane 0 streams chunks with TMA (one 16-row x 128-byte box per kv head
+//     and 64-column half) into a STAGES-deep ring of 128-byte-swizzled slots.
+//   * one compute warp per kv head: the G = H/Hkv query heads of the group are the
+//     rows of an m16n8k16 MMA, so one read of K/V serves the whole group.
+//   * per split: partial O (normalised) and LSE in an fp32 workspace; a second
+//     kernel merges the splits with LSE weights.  With one split the first kernel
+//     writes the final output directly.
+#include "fa_ptx.cuh"
+#include "fa_internal.h"
+#include <cmath>
+
+namespace fa {
+
+constexpr int kDecChunk = 16;  // tokens per pipeline chunk
+constexpr int kDecMaxGroup = 8;  // kv heads per CTA
+
+template <int D>
+struct DecCfg {
+  static constexpr int DH = D / 64;
+  static constexpr int HEAD_BYTES = kDecChunk * D * 2;  // one kv head, one chunk, K or V
+  static constexpr int STAGE_BYTES_MAX = 2 * kDecMaxGroup * HEAD_BYTES;
+  static constexpr int STAGES = (D == 64) ? 6 : 3;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES_MAX + 256;
+  static_assert(SMEM_BYTES <= 232448, "decode smem budget");
+};
+
+struct DecParams {
+  const void* q;       // [B, H, D]
+  void* out;           // [B, H, D]
+  float* lse;          // [B, H] or null
+  float* o_part;       // [B, S, H, D]
+  float* lse_part;     // [B, S, H]
+  const int32_t* block_table;
+  const int32_t* seq_lens;
+  int B, H, Hkv, G, HG;  // HG = kv heads per CTA
+  int page_size, num_pages, max_blocks;
+  int num_splits, chunks_per_split;
+  float scale_log2, scale;
+  int* err;
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+template <bool BF16>
+__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  if constexpr (BF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+// Byte offset of (row, 16-byte chunk) inside a 128-byte-swizzled [rows][64] block.
+__device__ __forceinline__ uint32_t swz(int row, int chunk16) {
+  return static_cast<uint32_t>(row * 128 + ((chunk16 ^ (row & 7)) << 4));
+}
+
+struct DecSmemCtl {
+  uint64_t full[8];
+  uint64_t empty[8];
+  int abort_flag;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(32 + 32 * kDecMaxGroup, 1)
+    fa_decode_split_kernel(const __grid_constant__ CUtensorMap tm_k,
+                           const __grid_constant__ CUtensorMap tm_v, const DecParams p) {
+  using Cfg = DecCfg<D>;
+  constexpr int ST = Cfg::STAGES;
+  constexpr bool kBf16 = Pack2<T>::kBf16;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+  const int HG = p.HG;
+  const int stage_bytes = 2 * HG * Cfg::HEAD_BYTES;  // K heads then V heads
+  DecSmemCtl* ctl = reinterpret_cast<DecSmemCtl*>(base_ptr + ST * stage_bytes);
+  volatile int* abort_flag = &ctl->abort_flag;
+
+  const int split = blockIdx.x;
+  const int hk0 = blockIdx.y * HG;
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int L = p.seq_lens[b];
+  const int c_begin = split * p.chunks_per_split;
+  const int c_end = min((L + kDecChunk - 1) / kDecChunk, c_begin + p.chunks_per_split);
+  const int nchunks = c_end - c_begin;
+  if (nchunks <= 0) {
+    // Empty split: the combine ignores it.  With a single split this CTA owns the
+    // output, so an empty sequence gets zeros and LSE = -inf.
+    if (p.num_splits == 1 && split == 0) {
+      for (int i = threadIdx.x; i < HG * p.G * D; i += blockDim.x) {
+        const int h = hk0 * p.G + i / D;
+        reinterpret_cast<T*>(p.out)[((int64_t)b * p.H + h) * D + i % D] = T(0.f);
+        if (p.lse != nullptr && i % D == 0) p.lse[(int64_t)b * p.H + h] = -INFINITY;
+      }
+    }
+    return;
+  }
+  const int ncompute = HG;
+
+  if (threadIdx.x == 0) {
+    ctl->abort_flag = 0;
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(smem_u32(&ctl->full[s]), 1);
+      mbar_init(smem_u32(&ctl->empty[s]), ncompute);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      const int n_valid_pages = min((L + p.page_size - 1) / p.page_size, p.max_blocks);
+      int it = 0;
+      for (; it < nchunks; ++it) {
+        const int s = it % ST;
+        if (!mbar_wait(smem_u32(&ctl->empty[s]), ((it / ST) & 1) ^ 1, abort_flag, p.err,
+                       FA_SITE_DEC_PRODUCER))
+          break;
+        const uint32_t fb = smem_u32(&ctl->full[s]);
+        mbar_arrive_expect_tx(fb, stage_bytes);
+        const int tok = (c_begin + it) * kDecChunk;
+        const int lp = tok / p.page_size;
+        const int in_page = tok - lp * p.page_size;
+        const int page =
+            lp < n_valid_pages ? p.block_table[(int64_t)b * p.max_blocks + lp] : p.num_pages;
+        const uint32_t dst = base + s * stage_bytes;
+        for (int w = 0; w < 2; ++w) {
+          const CUtensorMap* tm = w == 0 ? &tm_k : &tm_v;
+          for (int hh = 0; hh < HG; ++hh)
+            for (int dh = 0; dh < Cfg::DH; ++dh)
+              tma_load_4d(dst + (w * HG + hh) * Cfg::HEAD_BYTES + dh * (kDecChunk * 128), tm, fb,
+                          dh * 64, hk0 + hh, in_page, page);
+        }
+      }
+      for (int k = max(0, it - ST); k < it; ++k) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(smem_u32(&ctl->full[k % ST]), (k / ST) & 1))
+          if (globaltimer_ns() - t0 > 200000000ull) break;
+      }
+    }
+    return;
+  }
+  const int hh = warp - 1;
+  if (hh >= HG) return;
+  const int hk = hk0 + hh;
+  const int G = p.G;
+  const int g = lane >> 2;       // MMA row group (row g and g + 8)
+  const int qd = (lane & 3) * 2;  // column pair inside an 8-wide n tile
+
+  // Q fragment (A operand, rows = query heads of the group, zero beyond G).
+  uint32_t qa[D / 16][4];
+  {
+    const T* qb = reinterpret_cast<const T*>(p.q) + ((int64_t)b * p.H + hk * G) * D;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      const int k0 = ks * 16 + qd;
+      auto ld2 = [&](int row, int col) -> uint32_t {
+        if (row >= G) return 0u;
+        return *reinterpret_cast<const uint32_t*>(qb + (int64_t)row * D + col);
+      };
+      qa[ks][0] = ld2(g, k0);
+      qa[ks][1] = ld2(g + 8, k0);
+      qa[ks][2] = ld2(g, k0 + 8);
+      qa[ks][3] = ld2(g + 8, k0 + 8);
+    }
+  }
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const float c2 = p.scale_log2;
+
+  for (int it = 0; it < nchunks; ++it) {
+    const int s = it % ST;
+    const bool w_ok =
+        mbar_wait(smem_u32(&ctl->full[s]), (it / ST) & 1, abort_flag, p.err, FA_SITE_DEC_COMPUTE);
+    if (!__all_sync(0xffffffffu, w_ok)) break;
+    const uint32_t kbase = base + s * stage_bytes + hh * Cfg::HEAD_BYTES;
+    const uint32_t vbase = base + s * stage_bytes + (HG + hh) * Cfg::HEAD_BYTES;
+    // S[16 rows x 16 tokens] = Q K^T
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      // matrices: (tokens 0-7, d lo), (tokens 0-7, d hi), (tokens 8-15, d lo), (tokens 8-15, d hi)
+      const int mi = lane >> 3;
+      const int row = ((mi >> 1) << 3) + (lane & 7);
+      const int dchunk = (ks & 3) * 2 + (mi & 1);
+      const uint32_t addr = kbase + (ks >> 2) * (kDecChunk * 128) + swz(row, dchunk);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(addr, b0, b1, b2, b3);
+      mma16816<kBf16>(sc[0], qa[ks], b0, b1);
+      mma16816<kBf16>(sc[1], qa[ks], b2, b3);
+    }
+    const int tok0 = (c_begin + it) * kDecChunk;
+    if (tok0 + kDecChunk > L) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (tok0 + nt * 8 + qd + (e & 1) >= L) sc[nt][e] = -INFINITY;
+    }
+    float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+    float mx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float f0 = (mn0 == -INFINITY) ? 1.f : ex2_approx((m0 - mn0) * c2);
+    const float f1 = (mn1 == -INFINITY) ? 1.f : ex2_approx((m1 - mn1) * c2);
+    m0 = mn0;
+    m1 = mn1;
+    const float ms0 = (mn0 == -INFINITY) ? 0.f : mn0 * c2;
+    const float ms1 = (mn1 == -INFINITY) ? 0.f : mn1 * c2;
+    float pr[2][4];
+    float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      pr[nt][0] = ex2_approx(fmaf(sc[nt][0], c2, -ms0));
+      pr[nt][1] = ex2_approx(fmaf(sc[nt][1], c2, -ms0));
+      pr[nt][2] = ex2_approx(fmaf(sc[nt][2], c2, -ms1));
+      pr[nt][3] = ex2_approx(fmaf(sc[nt][3], c2, -ms1));
+      rs0 += pr[nt][0] + pr[nt][1];
+      rs1 += pr[nt][2] + pr[nt][3];
+    }
+    l0 = l0 * f0 + rs0;  // partial (per-thread) row sums, reduced across the quad at the end
+    l1 = l1 * f1 + rs1;
+    uint32_t pa[4];
+    pa[0] = Pack2<T>::pack(pr[0][0], pr[0][1]);
+    pa[1] = Pack2<T>::pack(pr[0][2], pr[0][3]);
+    pa[2] = Pack2<T>::pack(pr[1][0], pr[1][1]);
+    pa[3] = Pack2<T>::pack(pr[1][2], pr[1][3]);
+#pragma unroll
+    for (int dn = 0; dn < D / 8; ++dn) {
+      o[dn][0] *= f0;
+      o[dn][1] *= f0;
+      o[dn][2] *= f1;
+      o[dn][3] *= f1;
+    }
+    // O[16 x D] += P[16 x 16 tokens] V[16 tokens x D]
+#pragma unroll
+    for (int dp = 0; dp < D / 16; ++dp) {
+      // matrices: (tok 0-7, d 16dp..+7), (tok 8-15, same), (tok 0-7, d +8..+15), (tok 8-15, +8..)
+      const int mi = lane >> 3;
+      const int row = ((mi & 1) << 3) + (lane & 7);
+      const int dchunk = ((dp * 2) & 7) + (mi >> 1);
+      const uint32_t addr = vbase + ((dp * 16) >> 6) * (kDecChunk * 128) + swz(row, dchunk);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(addr, b0, b1, b2, b3);
+      mma16816<kBf16>(o[2 * dp], pa, b0, b1);
+      mma16816<kBf16>(o[2 * dp + 1], pa, b2, b3);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&ctl->empty[s]));
+  }
+
+  // Row sums across the quad, then write.
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
+  const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+  const float lse0 = l0 > 0.f ? m0 * p.scale + logf(l0) : -INFINITY;
+  const float lse1 = l1 > 0.f ? m1 * p.scale + logf(l1) : -INFINITY;
+  const bool direct = p.num_splits == 1;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int row = g + half * 8;
+    if (row >= G) continue;
+    const int h = hk * G + row;
+    const float inv = half ? inv1 : inv0;
+    const float lse = half ? lse1 : lse0;
+    if (direct) {
+      T* dst = reinterpret_cast<T*>(p.out) + ((int64_t)b * p.H + h) * D;
+#pragma unroll
+      for (int dn = 0; dn < D / 8; ++dn) {
+        const uint32_t v = Pack2<T>::pack(o[dn][half * 2] * inv, o[dn][half * 2 + 1] * inv);
+        *reinterpret_cast<uint32_t*>(dst + dn * 8 + qd) = v;
+      }
+      if (p.lse != nullptr && (lane & 3) == 0) p.lse[(int64_t)b * p.H + h] = lse;
+    } else {
+      float* dst = p.o_part + (((int64_t)b * p.num_splits + split) * p.H + h) * D;
+#pragma unroll
+      for (int dn = 0; dn < D / 8; ++dn)
+        *reinterpret_cast<float2*>(dst + dn * 8 + qd) =
+            make_float2(o[dn][half * 2] * inv, o[dn][half * 2 + 1] * inv);
+      if ((lane & 3) == 0) p.lse_part[((int64_t)b * p.num_splits + split) * p.H + h] = lse;
+    }
+  }
+}
+
+// Merge the splits of each (sequence, head): out = sum_s exp(lse_s - lse) * o_s.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) fa_decode_combine_kernel(const DecParams p) {
+  const int b = blockIdx.y;
+  const int L = p.seq_lens[b];
+  const int used =
+      min(p.num_splits, (((L + kDecChunk - 1) / kDecChunk) + p.chunks_per_split - 1) /
+                            p.chunks_per_split);
+  constexpr int TPH = D / 4;  // threads per head (float4 each)
+  const int h = blockIdx.x * (256 / TPH) + threadIdx.x / TPH;
+  const int d4 = (threadIdx.x % TPH) * 4;
+  if (h >= p.H) return;
+  const float* lp = p.lse_part + (int64_t)b * p.num_splits * p.H + h;
+  float mx = -INFINITY;
+  for (int s = 0; s < used; ++s) mx = fmaxf(mx, lp[(int64_t)s * p.H]);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float wsum = 0.f;
+  if (mx != -INFINITY) {
+    for (int s = 0; s < used; ++s) {
+      const float w = __expf(lp[(int64_t)s * p.H] - mx);
+      if (w == 0.f) continue;
+      const float4 v = *reinterpret_cast<const float4*>(
+          p.o_part + (((int64_t)b * p.num_splits + s) * p.H + h) * D + d4);
+      acc.x += w * v.x;
+      acc.y += w * v.y;
+      acc.z += w * v.z;
+      acc.w += w * v.w;
+      wsum += w;
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  T* dst = reinterpret_cast<T*>(p.out) + ((int64_t)b * p.H + h) * D + d4;
+  uint2 pk;
+  pk.x = Pack2<T>::pack(acc.x * inv, acc.y * inv);
+  pk.y = Pack2<T>::pack(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(dst) = pk;
+  if (p.lse != nullptr && d4 == 0)
+    p.lse[(int64_t)b * p.H + h] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
+}
+
+// ------------------------------------------------------------------- host side
+static int dec_group(int hkv) {
+  for (int g = kDecMaxGroup; g >= 1; --g)
+    if (hkv % g == 0) return g;
+  return 1;
+}
+
+int decode_num_splits(const fa_decode_args_t* a) {
+  if (a->num_splits > 0) return a->num_splits;
+  const int max_tokens = a->max_blocks * a->page_size;
+  // ~512 tokens per split: enough CTAs to fill 148 SMs several times over with a
+  // short tail, while the partial-output traffic stays a few % of the KV bytes.
+  int s = (max_tokens + 511) / 512;
+  if (s < 1) s = 1;
+  if (s > 64) s = 64;
+  return s;
+}
+
+static int chunks_per_split(const fa_decode_args_t* a, int splits) {
+  const int max_chunks = (a->max_blocks * a->page_size + kDecChunk - 1) / kDecChunk;
+  return (max_chunks + splits - 1) / splits;
+}
+
+size_t decode_workspace_bytes(const fa_decode_args_t* a) {
+  const int s = decode_num_splits(a);
+  if (s <= 1) return 0;
+  const size_t n = (size_t)a->batch * s * a->num_heads;
+  return (n * a->head_dim + n) * sizeof(float) + 256;
+}
+
+template <typename T, int D>
+static int launch_decode_impl(const CUtensorMap& tk, const CUtensorMap& tv, const DecParams& p,
+                              cudaStream_t st) {
+  using Cfg = DecCfg<D>;
+  auto kern = fa_decode_split_kernel<T, D>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  FA_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 64 && !attr_set[dev]) {
+    FA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cfg::SMEM_BYTES));
+    attr_set[dev] = true;
+  }
+  dim3 grid(p.num_splits, p.Hkv / p.HG, p.B);
+  kern<<<grid, 32 + 32 * p.HG, Cfg::SMEM_BYTES, st>>>(tk, tv, p);
+  FA_CUDA_TRY(cudaGetLastError());
+  count_launch();
+  if (p.num_splits > 1) {
+    constexpr int HPB = 256 / (D / 4);
+    dim3 g2((p.H + HPB - 1) / HPB, p.B);
+    fa_decode_combine_kernel<T, D><<<g2, 256, 0, st>>>(p);
+    FA_CUDA_TRY(cudaGetLastError());
+    count_launch();
+  }
+  return FA_OK;
+}
+
+int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err,
+                  cudaStream_t st) {
+  const int D = a->head_dim;
+  if (D != 64 && D != 128) return FA_ERR_UNSUPPORTED;
+  const int G = a->num_heads / a->num_kv_heads;
+  if (G > 16) return FA_ERR_UNSUPPORTED;
+  const int ps = a->page_size;
+  if (ps < kDecChunk || (ps & (ps - 1)) != 0) return FA_ERR_UNSUPPORTED;
+  if (a->batch == 0) return FA_OK;
+  const int splits = decode_num_splits(a);
+  if (decode_workspace_bytes(a) > ws_bytes || (splits > 1 && ws == nullptr))
+    return FA_ERR_WORKSPACE;
+  const CUtensorMapDataType dt = tmap_dtype(a->dtype);
+  CUtensorMap tk, tv;
+  const void* kv_ptr[2] = {a->k_cache, a->v_cache};
+  CUtensorMap* kv_map[2] = {&tk, &tv};
+  for (int w = 0; w < 2; ++w) {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a->num_kv_heads, (uint64_t)ps,
+                              (uint64_t)a->num_pages};
+    const uint64_t str[3] = {(uint64_t)D * 2, (uint64_t)a->num_kv_heads * D * 2,
+                             (uint64_t)ps * a->num_kv_heads * D * 2};
+    const uint32_t box[4] = {64, 1, (uint32_t)kDecChunk, 1};
+    if (encode_tmap(kv_map[w], dt, 4, kv_ptr[w], dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B) !=
+        CUDA_SUCCESS)
+      return FA_ERR_CUDA;
+  }
+  DecParams p{};
+  p.q = a->q;
+  p.out = a->out;
+  p.lse = a->lse;
+  p.block_table = a->block_table;
+  p.seq_lens = a->seq_lens;
+  p.B = a->batch;
+  p.H = a->num_heads;
+  p.Hkv = a->num_kv_heads;
+  p.G = G;
+  p.HG = dec_group(a->num_kv_heads);
+  p.page_size = ps;
+  p.num_pages = a->num_pages;
+  p.max_blocks = a->max_blocks;
+  p.num_splits = splits;
+  p.chunks_per_split = chunks_per_split(a, splits);
+  p.scale = a->softmax_scale;
+  p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  p.err = err;
+  if (splits > 1) {
+    const size_t n = (size_t)a->batch * splits * a->num_heads;
+    uintptr_t w = (reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255);
+    p.o_part = reinterpret_cast<float*>(w);
+    p.lse_part = p.o_part + n * D;
+  }
+  const bool bf16 = a->dtype == FA_DTYPE_BF16;
+  if (D == 64)
+    return bf16 ? launch_decode_impl<__nv_bfloat16, 64>(tk, tv, p, st)
+                : launch_decode_impl<__half, 64>(tk, tv, p, st);
+  return bf16 ? launch_decode_impl<__nv_bfloat16, 128>(tk, tv, p, st)
+              : launch_decode_impl<__half, 128>(tk, tv, p, st);
+}
+
+}  // namespace fa

@@ -1,0 +1,620 @@
+// Attention forward on sm_100a: tcgen05 MMAs with S, P and O in tensor memory,
+// TMA-fed K/V ring, warp-specialised roles.  One kernel template serves the dense
+// BSHD path (tilelang_flash_attn_func, reference kernel _kernels_forward.py:94-172)
+// and the paged vLLM-cache path (tilelang_paged_forward, reference kernel
+// _kernels_paged.py:193-344).
+//
+// CTA work item: NQ Q tiles of 128 rows for one kv head.  A row is a (token, head)
+// pair: the G = H / Hk query heads that share a kv head are packed into the rows
+// of a tile (row = token_local * G + head_in_group), so every K/V tile that is
+// loaded serves all of them (GQA/MQA; G = 1 for plain MHA).
+//
+// Roles (128 + 128 * NQ threads):
+//   warp 0      TMA producer: Q tiles once, then K_j, V_j into a STAGES-slot ring
+//   warp 1      TMEM allocator + single-thread MMA issuer
+//   warps 2-3   idle
+//   warpgroup t softmax + O correction + epilogue of Q tile t (thread = row)
+// TMEM (512 columns): S_t at [t*128, t*128+128) fp32, P_t aliased onto the first
+// 64 columns of S_t as packed 16-bit pairs, O_t at [NQ*128 + t*D, ... + D) fp32.
+// Per KV tile j and Q tile t:  S_t = Q_t K_j^T (SS, K-major both), softmax writes
+// P_t, O_t += P_t V_j (TS: A = P from TMEM, B = V MN-major).  tcgen05 MMAs issued
+// by one thread execute in issue order, so S_{j+1} may be issued right behind the
+// PV_j that reads P from the same columns.
+//
+// Online softmax (reference: _kernels_forward.py:147-165): running max m, row sum
+// l, p = 2^((s - m_ref) * scale * log2 e) computed with ex2; the O rescale is lazy:
+// the reference max m_ref only moves when the running max exceeds it by more than
+// 8 (log2 units), so O and l are rescaled rarely and p <= 256.  Final
+// O = acc / l, LSE = m_ref * scale + ln(l) (natural log, as _kernels_forward.py:170).
+#include "fa_ptx.cuh"
+#include "fa_internal.h"
+#include <cmath>
+
+namespace fa {
+
+constexpr int kFwdBM = 128;  // rows per Q tile = TMEM lanes
+constexpr int kFwdBN = 128;  // keys per KV tile
+
+template <int D, int NQ>
+struct FwdCfg {
+  static constexpr int DH = D / 64;                       // 128-byte column chunks
+  static constexpr int TILE_BYTES = 128 * D * 2;          // one Q, K or V tile
+  static constexpr int CHUNK_BYTES = 128 * 128;           // one 64-column chunk of a tile
+  static constexpr int STAGES = (D == 64) ? 6 : (D == 128 ? 4 : 2);
+  static constexpr int NTHREADS = 128 + 128 * NQ;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(NQ * (128 + D) <= TMEM_COLS, "TMEM budget: S + O per Q tile");
+  static constexpr int SMEM_Q = NQ * TILE_BYTES;
+  static constexpr int SMEM_KV = STAGES * TILE_BYTES;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + SMEM_Q + SMEM_KV + 1024 /*barriers*/;
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget (227 KB per CTA)");
+};
+
+struct FwdSmemCtl {
+  uint64_t q_full;
+  uint64_t kv_full[8];
+  uint64_t kv_empty[8];
+  uint64_t s_full[2];
+  uint64_t p_ready[2];
+  uint64_t o_final[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  // work item
+  int b, tok0, q_len, kv_len, off, tok_base, j0, nkv, valid;
+};
+
+// Final, abort-insensitive bounded wait used while draining in-flight copies.
+__device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > 200000000ull) return;
+  }
+}
+
+template <typename T, int D, int NQ, bool PAGED>
+__global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
+    fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+  using Cfg = FwdCfg<D, NQ>;
+  constexpr int ST = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+  const uint32_t sQ = base;
+  const uint32_t sKV = base + Cfg::SMEM_Q;
+  FwdSmemCtl* ctl = reinterpret_cast<FwdSmemCtl*>(base_ptr + Cfg::SMEM_Q + Cfg::SMEM_KV);
+  volatile int* abort_flag = &ctl->abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = p.G;
+  const int TPB = NQ * kFwdBM / G;  // tokens per CTA block
+  const int hk = blockIdx.y;
+
+  // ---------------------------------------------------------------- work item
+  if (threadIdx.x == 0) {
+    int b = 0, tile = 0, valid = 1, q_len, kv_len, off, tok_base;
+    if constexpr (PAGED) {
+      // Map blockIdx.x onto (sequence, q block) by a running count of blocks per sequence.
+      int t = blockIdx.x, cum = 0;
+      valid = 0;
+      for (int s = 0; s < p.num_seqs; ++s) {
+        const int ql = p.qsl[s + 1] - p.qsl[s];
+        const int nb = ql > 0 ? (ql + TPB - 1) / TPB : 0;
+        if (t < cum + nb) {
+          b = s;
+          tile = t - cum;
+          valid = 1;
+          break;
+        }
+        cum += nb;
+      }
+      if (valid) {
+        q_len = p.qsl[b + 1] - p.qsl[b];
+        kv_len = p.seq_lens[b];
+        off = p.pkl[b];
+        tok_base = p.qsl[b];
+      } else {
+        q_len = kv_len = off = tok_base = 0;
+      }
+    } else {
+      b = blockIdx.z;
+      tile = p.causal ? (gridDim.x - 1 - blockIdx.x) : blockIdx.x;  // heaviest blocks first
+      q_len = p.Sq;
+      kv_len = p.Skv;
+      off = p.Skv - p.Sq;
+      tok_base = 0;
+    }
+    const int tok0 = tile * TPB;
+    int j0 = 0, j1 = (kv_len + kFwdBN - 1) / kFwdBN;
+    if (valid && p.causal) {
+      const int last_lt = min(tok0 + TPB, q_len) - 1;
+      const int max_key = last_lt + off;
+      j1 = min(j1, max_key >= 0 ? max_key / kFwdBN + 1 : 0);
+      if (PAGED && p.swq > 0) j0 = max(0, tok0 - p.swq + 1) / kFwdBN;
+    }
+    ctl->b = b;
+    ctl->tok0 = tok0;
+    ctl->q_len = q_len;
+    ctl->kv_len = kv_len;
+    ctl->off = off;
+    ctl->tok_base = tok_base;
+    ctl->j0 = j0;
+    ctl->nkv = valid ? max(0, j1 - j0) : 0;
+    ctl->valid = valid;
+    ctl->abort_flag = 0;
+    mbar_init(smem_u32(&ctl->q_full), 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(smem_u32(&ctl->kv_full[s]), 1);
+      mbar_init(smem_u32(&ctl->kv_empty[s]), 1);
+    }
+    for (int t = 0; t < NQ; ++t) {
+      mbar_init(smem_u32(&ctl->s_full[t]), 1);
+      mbar_init(smem_u32(&ctl->p_ready[t]), 128);
+      mbar_init(smem_u32(&ctl->o_final[t]), 1);
+    }
+    mbar_init(smem_u32(&ctl->drain), 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (!ctl->valid) return;  // uniform: no TMEM held, no copies issued
+
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  const int b = ctl->b, tok0 = ctl->tok0, q_len = ctl->q_len, kv_len = ctl->kv_len;
+  const int off = ctl->off, tok_base = ctl->tok_base, j0 = ctl->j0, nkv = ctl->nkv;
+
+  if (warp == 0) {
+    // ============================================================ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      const uint32_t qbar = smem_u32(&ctl->q_full);
+      mbar_arrive_expect_tx(qbar, NQ * Cfg::TILE_BYTES);
+      for (int t = 0; t < NQ; ++t) {
+        const int tok = tok_base + tok0 + t * (kFwdBM / G);
+        for (int dh = 0; dh < Cfg::DH; ++dh)
+          tma_load_4d(sQ + t * Cfg::TILE_BYTES + dh * Cfg::CHUNK_BYTES, &tm_q, qbar, dh * 64,
+                      hk * G, tok, PAGED ? 0 : b);
+      }
+      const int box_rows = PAGED ? min(p.page_size, kFwdBN) : kFwdBN;
+      const int n_valid_pages =
+          PAGED ? min((kv_len + p.page_size - 1) / p.page_size, p.max_blocks) : 0;
+      int it = 0;
+      bool ok = true;
+      for (int jj = 0; jj < nkv && ok; ++jj) {
+        const int j = j0 + jj;
+        for (int w = 0; w < 2 && ok; ++w, ++it) {
+          const int s = it % ST;
+          const uint32_t ph = (it / ST) & 1;
+          ok = mbar_wait(smem_u32(&ctl->kv_empty[s]), ph ^ 1, abort_flag, p.err,
+                         FA_SITE_FWD_PRODUCER);
+          if (!ok) break;
+          const uint32_t fb = smem_u32(&ctl->kv_full[s]);
+          mbar_arrive_expect_tx(fb, Cfg::TILE_BYTES);
+          const CUtensorMap* tm = (w == 0) ? &tm_k : &tm_v;
+          const uint32_t dst = sKV + s * Cfg::TILE_BYTES;
+          if constexpr (PAGED) {
+            for (int r0 = 0; r0 < kFwdBN; r0 += box_rows) {
+              const int key = j * kFwdBN + r0;
+              const int lp = key / p.page_size;
+              const int in_page = key - lp * p.page_size;
+              // Pages past the sequence are fetched out of range: TMA fills zeros.
+              const int page =
+                  lp < n_valid_pages ? p.block_table[(int64_t)b * p.max_blocks + lp] : p.num_pages;
+              for (int dh = 0; dh < Cfg::DH; ++dh)
+                tma_load_4d(dst + dh * Cfg::CHUNK_BYTES + r0 * 128, tm, fb, dh * 64, hk, in_page,
+                            page);
+            }
+          } else {
+            for (int dh = 0; dh < Cfg::DH; ++dh)
+              tma_load_4d(dst + dh * Cfg::CHUNK_BYTES, tm, fb, dh * 64, hk, j * kFwdBN, b);
+          }
+        }
+      }
+      // Drain: every copy issued must have landed before the CTA may exit.
+      for (int k = max(0, it - ST); k < it; ++k)
+        mbar_wait_drain(smem_u32(&ctl->kv_full[k % ST]), (k / ST) & 1);
+      mbar_wait_drain(qbar, 0);
+    }
+  } else if (warp == 1) {
+    // ============================================================ MMA issuer
+    if (lane == 0) {
+      constexpr bool kBf16 = Pack2<T>::kBf16;
+      constexpr uint32_t idS = idesc_f16(128, kFwdBN, kBf16, false, false);
+      constexpr uint32_t idPV = idesc_f16(128, D, kBf16, false, true);
+      bool ok = mbar_wait(smem_u32(&ctl->q_full), 0, abort_flag, p.err, FA_SITE_FWD_MMA);
+      tc_fence_after();
+      // S_t = Q_t K^T over D in steps of 16 (K-major, 128-byte swizzle: step = +32 B
+      // inside a 64-column chunk, next chunk at +16 KB).
+      auto issue_S = [&](int t, int slot) {
+        const uint32_t qa = sQ + t * Cfg::TILE_BYTES;
+        const uint32_t ka = sKV + slot * Cfg::TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t o = (kk >> 2) * Cfg::CHUNK_BYTES + (kk & 3) * 32;
+          mma_ss(tmem + t * 128, sdesc_sw128(qa + o, 16, 1024), sdesc_sw128(ka + o, 16, 1024),
+                 idS, kk > 0 ? 1u : 0u);
+        }
+      };
+      // O_t += P_t V over 128 keys in steps of 16 (V MN-major: step = 16 rows = +2 KB,
+      // 64-column chunks of D at +16 KB = LBO).
+      auto issue_PV = [&](int t, int slot, bool acc) {
+        const uint32_t va = sKV + slot * Cfg::TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < kFwdBN / 16; ++kk) {
+          mma_ts(tmem + NQ * 128 + t * D, tmem + t * 128 + kk * 8,
+                 sdesc_sw128(va + kk * 2048, Cfg::CHUNK_BYTES, 1024), idPV,
+                 (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      int it = 0;
+      if (ok && nkv > 0) {
+        const int s = it % ST;
+        ok = mbar_wait(smem_u32(&ctl->kv_full[s]), (it / ST) & 1, abort_flag, p.err,
+                       FA_SITE_FWD_MMA);
+        if (ok) {
+          tc_fence_after();
+          for (int t = 0; t < NQ; ++t) {
+            issue_S(t, s);
+            mma_commit(smem_u32(&ctl->s_full[t]));
+          }
+          mma_commit(smem_u32(&ctl->kv_empty[s]));
+        }
+        ++it;
+      }
+      for (int jj = 0; jj < nkv && ok; ++jj) {
+        const int sv = it % ST;
+        const uint32_t phv = (it / ST) & 1;
+        ++it;
+        const bool has_next = jj + 1 < nkv;
+        const int sk = it % ST;
+        const uint32_t phk = (it / ST) & 1;
+        if (has_next) ++it;
+        ok = mbar_wait(smem_u32(&ctl->kv_full[sv]), phv, abort_flag, p.err, FA_SITE_FWD_MMA);
+        if (!ok) break;
+        for (int t = 0; t < NQ && ok; ++t) {
+          ok = mbar_wait(smem_u32(&ctl->p_ready[t]), jj & 1, abort_flag, p.err, FA_SITE_FWD_MMA);
+          if (!ok) break;
+          tc_fence_after();
+          issue_PV(t, sv, jj > 0);
+          if (has_next) {
+            if (t == 0) {
+              ok = mbar_wait(smem_u32(&ctl->kv_full[sk]), phk, abort_flag, p.err,
+                             FA_SITE_FWD_MMA);
+              if (!ok) break;
+              tc_fence_after();
+            }
+            issue_S(t, sk);
+            mma_commit(smem_u32(&ctl->s_full[t]));
+          }
+        }
+        if (!ok) break;
+        mma_commit(smem_u32(&ctl->kv_empty[sv]));
+        if (has_next) mma_commit(smem_u32(&ctl->kv_empty[sk]));
+      }
+      for (int t = 0; t < NQ; ++t) mma_commit(smem_u32(&ctl->o_final[t]));
+      mma_commit(smem_u32(&ctl->drain));
+      mbar_wait_drain(smem_u32(&ctl->drain), 0);
+    }
+  } else if (warp >= 4) {
+    // ============================================================ softmax / epilogue
+    const int t = (warp - 4) >> 2;
+    const int r = ((warp & 3) << 5) | lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_off + t * 128;
+    const uint32_t tO = tmem + lane_off + NQ * 128 + t * D;
+    const int R = t * kFwdBM + r;
+    const int lt = tok0 + R / G;             // token index within the sequence / query chunk
+    const int h = hk * G + (R - (R / G) * G);  // query head
+    const bool row_valid = lt < q_len;
+    const int limit = lt + off;              // causal: key <= limit
+    const bool window = PAGED && p.causal && (p.swq > 0 || p.swk > 0);
+    const float c2 = p.scale_log2;
+    const float NEG_INF = -INFINITY;
+    float m_run = NEG_INF, m_ref = NEG_INF, l = 0.f;
+    bool ok = true;
+
+    for (int jj = 0; jj < nkv; ++jj) {
+      const int j = j0 + jj;
+      bool w_ok = mbar_wait(smem_u32(&ctl->s_full[t]), jj & 1, abort_flag, p.err,
+                            FA_SITE_FWD_SOFTMAX);
+      ok = __all_sync(0xffffffffu, w_ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t s[128];
+      tmem_ld32(tS + 0, s);
+      tmem_ld32(tS + 32, s + 32);
+      tmem_ld32(tS + 64, s + 64);
+      tmem_ld32(tS + 96, s + 96);
+      tmem_wait_ld();
+      const int key0 = j * kFwdBN;
+      const bool need_mask =
+          (key0 + kFwdBN > kv_len) || (p.causal && (key0 + kFwdBN - 1 > limit)) || window;
+      if (need_mask) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          const int key = key0 + c;
+          bool vis = key < kv_len;
+          if (p.causal) {
+            vis = vis && key <= limit;
+            if (window) {
+              if (p.swq > 0) vis = vis && (lt < key + p.swq);
+              if (p.swk > 0) vis = vis && (key < lt + p.swk);
+            }
+          }
+          if (!vis) s[c] = __float_as_uint(NEG_INF);
+        }
+      }
+      float mx = NEG_INF;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+      const float m_new = fmaxf(m_run, mx);
+      m_run = m_new;
+      bool rescale_o = false;
+      float factor = 1.f;
+      if (jj == 0) {
+        m_ref = m_new;
+      } else {
+        const bool need = (m_new - m_ref) * c2 > 8.0f;
+        if (__any_sync(0xffffffffu, need)) {
+          if (m_new != NEG_INF) {
+            factor = ex2_approx((m_ref - m_new) * c2);
+            m_ref = m_new;
+          }
+          l *= factor;
+          rescale_o = true;
+        }
+      }
+      const float mref_s = (m_ref == NEG_INF) ? 0.f : m_ref * c2;
+      float rs0 = 0.f, rs1 = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float p0 = ex2_approx(fmaf(__uint_as_float(s[2 * c]), c2, -mref_s));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(s[2 * c + 1]), c2, -mref_s));
+        rs0 += p0;
+        rs1 += p1;
+        pk[c] = Pack2<T>::pack(p0, p1);
+      }
+      l += rs0 + rs1;
+      tmem_st32(tS + 0, pk);
+      tmem_st32(tS + 32, pk + 32);
+      if (rescale_o) {
+        // PV_{j-1} is complete: the commit that signalled S_j covered every earlier MMA.
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32(tO + c0, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * factor);
+          tmem_st32(tO + c0, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&ctl->p_ready[t]));
+    }
+
+    // ---------------------------------------------------------- epilogue
+    if (ok) {
+      bool w_ok = mbar_wait(smem_u32(&ctl->o_final[t]), 0, abort_flag, p.err, FA_SITE_FWD_SOFTMAX);
+      ok = __all_sync(0xffffffffu, w_ok);
+    }
+    if (ok) {
+      tc_fence_after();
+      const bool have = l > 0.f;
+      const float inv = have ? 1.f / l : 0.f;
+      T* orow = reinterpret_cast<T*>(p.out) + (PAGED ? 0 : (int64_t)b * p.o_sb) +
+                (int64_t)(tok_base + lt) * p.o_st + (int64_t)h * p.o_sh;
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t o[32];
+        if (nkv > 0) {
+          tmem_ld32(tO + c0, o);
+          tmem_wait_ld();
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float a0 = have ? __uint_as_float(o[2 * c]) * inv : 0.f;
+          const float a1 = have ? __uint_as_float(o[2 * c + 1]) * inv : 0.f;
+          pk[c] = Pack2<T>::pack(a0, a1);
+        }
+        if (row_valid) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+          dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          dst[2] = make_uint4(pk[8], pk[9], pk[10], pk[11]);
+          dst[3] = make_uint4(pk[12], pk[13], pk[14], pk[15]);
+        }
+      }
+      if (row_valid && p.lse != nullptr) {
+        const float lse = have ? m_ref * p.scale + logf(l) : NEG_INF;
+        p.lse[(PAGED ? 0 : (int64_t)b * p.lse_sb) + (int64_t)h * p.lse_sh + tok_base + lt] = lse;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------- host side
+template <typename T, int D, int NQ, bool PAGED>
+static int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                           const FwdParams& p, dim3 grid, cudaStream_t st) {
+  using Cfg = FwdCfg<D, NQ>;
+  auto kern = fa_fwd_kernel<T, D, NQ, PAGED>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  FA_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 64 && !attr_set[dev]) {
+    FA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cfg::SMEM_BYTES));
+    attr_set[dev] = true;
+  }
+  kern<<<grid, Cfg::NTHREADS, Cfg::SMEM_BYTES, st>>>(tq, tk, tv, p);
+  FA_CUDA_TRY(cudaGetLastError());
+  count_launch();
+  return FA_OK;
+}
+
+template <int D, int NQ, bool PAGED>
+static int dispatch_dtype(int dtype, const CUtensorMap& tq, const CUtensorMap& tk,
+                          const CUtensorMap& tv, const FwdParams& p, dim3 grid, cudaStream_t st) {
+  if (dtype == FA_DTYPE_BF16)
+    return launch_fwd_impl<__nv_bfloat16, D, NQ, PAGED>(tq, tk, tv, p, grid, st);
+  return launch_fwd_impl<__half, D, NQ, PAGED>(tq, tk, tv, p, grid, st);
+}
+
+static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
+  const int D = a->head_dim;
+  const int G = a->num_heads / a->num_heads_k;
+  const int NQ = (D == 256) ? 1 : 2;
+  if (128 % G != 0) return FA_ERR_UNSUPPORTED;
+  if (a->seqlen_q == 0 || a->batch == 0) return FA_OK;
+  for (int i = 0; i < 3; ++i) {
+    if ((a->q_stride[i] % 8) || (a->k_stride[i] % 8) || (a->v_stride[i] % 8) ||
+        (a->o_stride[i] % 8))
+      return FA_ERR_ALIGNMENT;
+  }
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out))
+    return FA_ERR_ALIGNMENT;
+  const CUtensorMapDataType dt = tmap_dtype(a->dtype);
+  CUtensorMap tq, tk, tv;
+  {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a->num_heads, (uint64_t)a->seqlen_q,
+                              (uint64_t)a->batch};
+    const uint64_t str[3] = {(uint64_t)a->q_stride[2] * 2, (uint64_t)a->q_stride[1] * 2,
+                             (uint64_t)a->q_stride[0] * 2};
+    const uint32_t box[4] = {64, (uint32_t)G, (uint32_t)(128 / G), 1};
+    if (encode_tmap(&tq, dt, 4, a->q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+      return FA_ERR_CUDA;
+  }
+  const void* kv_ptr[2] = {a->k, a->v};
+  const int64_t* kv_str[2] = {a->k_stride, a->v_stride};
+  CUtensorMap* kv_map[2] = {&tk, &tv};
+  for (int w = 0; w < 2; ++w) {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a->num_heads_k,
+                              (uint64_t)(a->seqlen_k > 0 ? a->seqlen_k : 1), (uint64_t)a->batch};
+    const uint64_t str[3] = {(uint64_t)kv_str[w][2] * 2, (uint64_t)kv_str[w][1] * 2,
+                             (uint64_t)kv_str[w][0] * 2};
+    const uint32_t box[4] = {64, 1, 128, 1};
+    if (encode_tmap(kv_map[w], dt, 4, kv_ptr[w], dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B) !=
+        CUDA_SUCCESS)
+      return FA_ERR_CUDA;
+  }
+  FwdParams p{};
+  p.Sq = a->seqlen_q;
+  p.Skv = a->seqlen_k;
+  p.H = a->num_heads;
+  p.Hk = a->num_heads_k;
+  p.G = G;
+  p.causal = a->causal;
+  p.scale = a->softmax_scale;
+  p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  p.out = a->out;
+  p.lse = a->lse;
+  p.o_sb = a->o_stride[0];
+  p.o_st = a->o_stride[1];
+  p.o_sh = a->o_stride[2];
+  p.lse_sb = (int64_t)a->num_heads * a->seqlen_q;
+  p.lse_sh = a->seqlen_q;
+  p.err = err;
+  const int TPB = NQ * 128 / G;
+  dim3 grid((a->seqlen_q + TPB - 1) / TPB, a->num_heads_k, a->batch);
+  switch (D) {
+    case 64: return dispatch_dtype<64, 2, false>(a->dtype, tq, tk, tv, p, grid, st);
+    case 128: return dispatch_dtype<128, 2, false>(a->dtype, tq, tk, tv, p, grid, st);
+    case 256: return dispatch_dtype<256, 1, false>(a->dtype, tq, tk, tv, p, grid, st);
+    default: return FA_ERR_UNSUPPORTED;
+  }
+}
+
+int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st) {
+  const int D = a->head_dim;
+  const int G = a->num_heads / a->num_kv_heads;
+  const int NQ = (D == 256) ? 1 : 2;
+  if (128 % G != 0) return FA_ERR_UNSUPPORTED;
+  const int ps = a->page_size;
+  if (ps < 8 || (ps & (ps - 1)) != 0) return FA_ERR_UNSUPPORTED;
+  if (a->num_tokens == 0 || a->num_seqs == 0) return FA_OK;
+  if (!aligned16(a->q) || !aligned16(a->k_cache) || !aligned16(a->v_cache) || !aligned16(a->out))
+    return FA_ERR_ALIGNMENT;
+  const CUtensorMapDataType dt = tmap_dtype(a->dtype);
+  CUtensorMap tq, tk, tv;
+  {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a->num_heads, (uint64_t)a->num_tokens, 1};
+    const uint64_t str[3] = {(uint64_t)D * 2, (uint64_t)a->num_heads * D * 2,
+                             (uint64_t)a->num_tokens * a->num_heads * D * 2};
+    const uint32_t box[4] = {64, (uint32_t)G, (uint32_t)(128 / G), 1};
+    if (encode_tmap(&tq, dt, 4, a->q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+      return FA_ERR_CUDA;
+  }
+  const void* kv_ptr[2] = {a->k_cache, a->v_cache};
+  CUtensorMap* kv_map[2] = {&tk, &tv};
+  for (int w = 0; w < 2; ++w) {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a->num_kv_heads, (uint64_t)ps,
+                              (uint64_t)a->num_pages};
+    const uint64_t str[3] = {(uint64_t)D * 2, (uint64_t)a->num_kv_heads * D * 2,
+                             (uint64_t)ps * a->num_kv_heads * D * 2};
+    const uint32_t box[4] = {64, 1, (uint32_t)(ps < 128 ? ps : 128), 1};
+    if (encode_tmap(kv_map[w], dt, 4, kv_ptr[w], dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B) !=
+        CUDA_SUCCESS)
+      return FA_ERR_CUDA;
+  }
+  FwdParams p{};
+  p.H = a->num_heads;
+  p.Hk = a->num_kv_heads;
+  p.G = G;
+  p.causal = a->causal;
+  p.scale = a->softmax_scale;
+  p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  p.out = a->out;
+  p.lse = a->lse;
+  p.o_sb = 0;
+  p.o_st = (int64_t)a->num_heads * D;
+  p.o_sh = D;
+  p.lse_sb = 0;
+  p.lse_sh = a->num_tokens;
+  p.block_table = a->block_table;
+  p.seq_lens = a->seq_lens;
+  p.qsl = a->query_start_loc;
+  p.pkl = a->prefix_kv_lens;
+  p.num_seqs = a->num_seqs;
+  p.max_blocks = a->max_blocks;
+  p.page_size = ps;
+  p.num_pages = a->num_pages;
+  p.swq = a->causal ? a->sliding_window_q : 0;
+  p.swk = a->causal ? a->sliding_window_k : 0;
+  p.err = err;
+  const int TPB = NQ * 128 / G;
+  // Sum over sequences of ceil(q_len / TPB) <= num_tokens / TPB + num_seqs.
+  dim3 grid(a->num_tokens / TPB + a->num_seqs, a->num_kv_heads, 1);
+  switch (D) {
+    case 64: return dispatch_dtype<64, 2, true>(a->dtype, tq, tk, tv, p, grid, st);
+    case 128: return dispatch_dtype<128, 2, true>(a->dtype, tq, tk, tv, p, grid, st);
+    case 256: return dispatch_dtype<256, 1, true>(a->dtype, tq, tk, tv, p, grid, st);
+    default: return FA_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace fa

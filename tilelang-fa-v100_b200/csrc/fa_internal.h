@@ -1,0 +1,60 @@
+// Host-side internals shared by the kernel translation units and the C ABI.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include "../../include/fa_b200.h"
+
+namespace fa {
+
+// Forward-kernel parameters shared by the dense and the paged (varlen) modes.
+struct FwdParams {
+  int Sq;            // dense: query length; paged: unused
+  int Skv;           // dense: key length; paged: unused
+  int H, Hk, G;      // query heads, kv heads, G = H / Hk (rows of a kv head packed per Q tile)
+  int causal;
+  float scale;       // softmax scale
+  float scale_log2;  // scale * log2(e)
+  void* out;
+  float* lse;
+  int64_t o_sb, o_st, o_sh;        // out strides (elements): batch, token, head
+  int64_t lse_sb, lse_sh;          // lse strides (elements): batch, head (token stride 1)
+  // paged mode
+  const int32_t* block_table;
+  const int32_t* seq_lens;
+  const int32_t* qsl;
+  const int32_t* pkl;
+  int num_seqs, max_blocks, page_size, num_pages;
+  int swq, swk;
+  int* err;
+};
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+CUresult encode_tmap(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
+                     const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                     CUtensorMapSwizzle swizzle);
+inline CUtensorMapDataType tmap_dtype(int dtype) {
+  return dtype == FA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+int num_sms();
+void count_launch(int n = 1);
+
+int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st);
+int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st);
+int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st);
+size_t bwd_workspace_bytes(const fa_bwd_args_t* a);
+int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st);
+size_t decode_workspace_bytes(const fa_decode_args_t* a);
+int decode_num_splits(const fa_decode_args_t* a);
+int launch_selftest_umma(const void* a, const void* b, float* c, int n, int k, int dtype, int b_mn,
+                         int a_tmem, int* err, cudaStream_t st);
+
+#define FA_CUDA_TRY(x)                              \
+  do {                                              \
+    cudaError_t e_ = (x);                           \
+    if (e_ != cudaSuccess) return FA_ERR_CUDA;      \
+  } while (0)
+
+}  // namespace fa

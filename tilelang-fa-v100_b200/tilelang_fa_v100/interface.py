@@ -1,0 +1,118 @@
+"""FA2-compatible API (mirror of the reference's tilelang_fa_v100/interface.py).
+
+Same names, signatures, defaults and error behaviour as the reference:
+``tilelang_flash_attn_func`` / ``tilelang_flash_attn_gpu`` (interface.py:59-80, 101)
+with a torch.autograd forward/backward (interface.py:12-56), ``tilelang_paged_forward``
+(interface.py:83-98) and ``tilelang_decode_forward`` (interface.py:104-117).
+
+Differences that keep results identical: the kernels read and write the BSHD layout
+directly, so the reference's permute/contiguous copies (interface.py:19-21, 38, 51)
+are gone, and gradients come back as contiguous BSHD tensors (the reference returns
+permuted views of the same values, interface.py:53-55).  ``softmax_scale`` is
+honoured (the reference kernels hard-code 1/sqrt(D), _kernels_forward.py:96; equal
+for the default).  ``deterministic=True`` selects the dQ kernel without atomics.
+"""
+import math
+
+import torch
+
+from . import _ext
+from ._paged_adapter import paged_forward as _paged_forward
+from ._decode_adapter import decode_forward as _decode_forward
+
+
+class FlashAttnTileLangVFunc(torch.autograd.Function):
+    """Autograd function for the B200 FlashAttention kernels (training)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, dropout_p, softmax_scale, causal, window_size,
+                softcap, alibi_slopes, deterministic, return_softmax):
+        D = q.shape[-1]
+        if dropout_p != 0.0:
+            raise NotImplementedError("dropout not supported")
+        if alibi_slopes is not None:
+            raise NotImplementedError("alibi not supported")
+        if softcap != 0.0:
+            raise NotImplementedError("softcap not supported")
+
+        scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
+        # window_size is accepted and ignored, as in the reference (interface.py:33).
+        out, lse = _ext.dense_forward(q, k, v, scale, causal)
+
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.causal = causal
+        ctx.softmax_scale = scale
+        ctx.deterministic = bool(deterministic)
+
+        if return_softmax:
+            return out, lse, None
+        return out
+
+    @staticmethod
+    def backward(ctx, dout, *args):
+        q, k, v, out, lse = ctx.saved_tensors
+        dq, dk, dv = _ext.dense_backward(q, k, v, out, dout, lse, ctx.softmax_scale,
+                                         ctx.causal, ctx.deterministic)
+        return dq, dk, dv, None, None, None, None, None, None, None, None, None
+
+
+def tilelang_flash_attn_func(q, k, v, dropout_p=0.0, softmax_scale=None,
+                             causal=False, window_size=(-1, -1), softcap=0.0,
+                             alibi_slopes=None, deterministic=False,
+                             return_attn_probs=False):
+    """FA2-compatible flash attention function.
+
+    Args:
+        q: [B, M, H, D]; k, v: [B, N, Hk, D] (FA2 layout, H % Hk == 0), fp16 or bf16
+        causal: bottom-right aligned causal mask (key j visible to row i iff j <= i + N - M)
+        softmax_scale: (default: 1/sqrt(D))
+        deterministic: compute dQ without atomics (bit-reproducible backward)
+        return_attn_probs: return (out, lse, None) instead of just out
+
+    Returns:
+        out: [B, M, H, D] in the input dtype, or (out, lse [B, H, M] fp32, None)
+    """
+    if softmax_scale is None:
+        softmax_scale = q.shape[-1] ** -0.5
+    return FlashAttnTileLangVFunc.apply(
+        q, k, v, dropout_p, softmax_scale, causal,
+        window_size, softcap, alibi_slopes, deterministic, return_attn_probs,
+    )
+
+
+def tilelang_paged_forward(q, k_cache, v_cache, block_table, seq_lens,
+                           query_start_loc, prefix_kv_lens, out=None,
+                           block_size=16, num_kv_heads=None,
+                           softmax_scale=None, causal=True,
+                           sliding_window_q=-1, sliding_window_k=-1):
+    """Paged FlashAttention forward for vLLM integration.
+
+    Args match the reference FA-V100 paged_fwd API.  Returns (out, softmax_lse) with
+    softmax_lse [num_heads, num_tokens] fp32 (filled, unlike the reference).
+    """
+    return _paged_forward(
+        q, k_cache, v_cache, block_table, seq_lens,
+        query_start_loc, prefix_kv_lens, out=out,
+        block_size=block_size, num_kv_heads=num_kv_heads,
+        softmax_scale=softmax_scale, causal=causal,
+        sliding_window_q=sliding_window_q, sliding_window_k=sliding_window_k,
+    )
+
+
+tilelang_flash_attn_gpu = tilelang_flash_attn_func
+
+
+def tilelang_decode_forward(q, k_cache, v_cache, block_table, seq_lens,
+                            block_size=16, num_kv_heads=None,
+                            softmax_scale=None):
+    """Paged decode forward for vLLM integration.
+
+    Args match the reference FA-V100 decode_fwd API.
+    Returns:
+        output: [batch, heads, dim] in the input dtype
+    """
+    return _decode_forward(
+        q, k_cache, v_cache, block_table, seq_lens,
+        block_size=block_size, num_kv_heads=num_kv_heads,
+        softmax_scale=softmax_scale,
+    )
