@@ -148,9 +148,18 @@ const char* fa_status_string(int status);
  * device: code (0 = none, 1 = bounded wait expired), site and block index.
  * Synchronises the device. */
 int fa_read_device_error(int32_t* code, int32_t* site, int32_t* block, int32_t clear);
+/* Text of the last CUDA call that made an entry point return FA_ERR_CUDA on this
+ * host thread (call, source line, CUDA error string); "" if none. */
+const char* fa_last_error_detail(void);
 /* Library version and the number of kernels launched by this process so far. */
 const char* fa_version(void);
 int64_t fa_launch_count(void);
+
+/* Benchmark hook: record ev_begin / ev_end (cudaEvent_t, created by the caller) on the
+ * launch stream immediately around the NEXT launch of one main kernel:
+ * 1 = dense forward, 2 = dense backward dK/dV kernel, 3 = paged prefill,
+ * 4 = decode split kernel.  One shot; process-wide; not thread-safe. */
+int fa_profile_next_launch(int32_t kind, void* ev_begin, void* ev_end);
 
 /* Self-test of the tcgen05 building blocks used by the attention kernels: one
  * 128 x N x K UMMA with the given operand majorness (0 = K-major, 1 = MN-major for

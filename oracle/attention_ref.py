@@ -35,6 +35,8 @@ NEG_INF = -np.inf
 
 def _softmax_lse(scores):
     """Row softmax and natural-log LSE; fully masked rows give P = 0, LSE = -inf."""
+    if scores.shape[-1] == 0:
+        return np.zeros_like(scores), np.full(scores.shape[:-1], NEG_INF)
     m = np.max(scores, axis=-1, keepdims=True)
     m_safe = np.where(np.isfinite(m), m, 0.0)
     e = np.exp(scores - m_safe)

@@ -35,7 +35,7 @@ def _check(cuda_dev, q, kc, vc, bt, sl, page, num_splits=0):
     torch.cuda.synchronize()
     ref_out, ref_lse = R.decode_ref(q.float().numpy(), kc.float().numpy(), vc.float().numpy(),
                                     bt, sl)
-    assert_close(out.float().cpu().numpy(), ref_out, what="out")
+    assert_close(out.float().cpu().numpy(), ref_out, what="out", dtype=q.dtype)
     assert_close(lse.cpu().numpy(), ref_lse, what="lse")
 
 
@@ -97,4 +97,4 @@ def test_benchmark_config_sampled(cuda_dev):
         vb = vc[idx].float().cpu().numpy()
         ro, _ = R.decode_ref(q[b:b + 1].float().cpu().numpy(), kb, vb,
                              np.arange(pps[b], dtype=np.int32)[None], lens[b:b + 1])
-        assert_close(out[b:b + 1].float().cpu().numpy(), ro, what="seq %d" % b)
+        assert_close(out[b:b + 1].float().cpu().numpy(), ro, what="seq %d" % b, dtype=torch.bfloat16)

@@ -69,3 +69,16 @@ def test_visible_pairs_counts():
     assert R.visible_pairs(1, 1, 4, 4, True) == 10
     assert R.visible_pairs(1, 1, 2, 4, True) == 3 + 4
     assert R.visible_pairs(2, 3, 5, 7, False) == 2 * 3 * 5 * 7
+
+
+def test_torch_restatement_matches_numpy_oracle():
+    import torch
+    from oracle import attention_ref_torch as RT
+    g = golden("dense_nonsquare_causal")
+    q, k, v, do = (torch.from_numpy(g[x]).float() for x in ("q", "k", "v", "do"))
+    out, dq, dk, dv = RT.fwd_bwd(q, k, v, do, True)
+    ro, _ = R.attention_ref(g["q"], g["k"], g["v"], True)
+    rq, rk, rv = R.attention_bwd_ref(g["q"], g["k"], g["v"], g["do"], True)
+    assert max_abs(out.numpy(), ro) < 1e-4
+    for a, b_ in ((dq, rq), (dk, rk), (dv, rv)):
+        assert max_abs(a.numpy(), b_) < 1e-3

@@ -78,7 +78,7 @@ def test_varlen_paged_vs_oracle(cuda_dev, case):
     out, lse = _run(cuda_dev, q, kc, vc, bt, sl, qsl, pkl, causal, page)
     ref_out, ref_lse = R.paged_prefill_ref(q.float().numpy(), kc.float().numpy(),
                                            vc.float().numpy(), bt, sl, qsl, pkl, causal=causal)
-    assert_close(out, ref_out, what="out")
+    assert_close(out, ref_out, what="out", dtype=dt)
     assert_close(lse, ref_lse, what="lse")
 
 

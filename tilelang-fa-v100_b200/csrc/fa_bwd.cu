@@ -1,8 +1,870 @@
+// Attention backward on sm_100a (reference: tilelang_backward,
+// _kernels_backward.py:200-208, with the dQ kernel :10-85 and the dK/dV kernel
+// :88-176).  P is recomputed from the saved LSE; dS = P * (dP - D) * scale with the
+// row-dot D = rowsum(O * dO) (:203).
+//
+// Kernels (all on the caller's stream):
+//   1. fa_bwd_prep     D = rowsum(O * dO) in fp32 and LSE * log2(e), per query row, padded
+//                      to a multiple of 128 rows (+inf / 0 in the padding so padded rows
+//                      contribute P = 0); the dQ accumulator is cleared with a memset.
+//   2. fa_bwd_dkdv     one CTA per (128-key KV tile, kv head, batch) owns dK and dV in
+//                      TMEM and loops over the G query heads of its kv head x the query
+//                      tiles that can see its keys (causal skips the rest).  Per 128-row
+//                      query tile, five tcgen05 GEMMs:
+//                        S^T  = K Q^T            (SS)      -> TMEM [0,128)
+//                        dP^T = V dO^T           (SS)      -> TMEM [128,256)
+//                        dV  += P^T dO           (TS, A = P^T from TMEM)
+//                        dK  += dS^T Q           (TS, A = dS^T from TMEM)
+//                        dQ   = dS K             (SS, A = dS from smem) -> TMEM [128,128+D)
+//                      and dQ is added to an fp32 accumulator with vector atomics
+//                      (atomic mode).  In deterministic mode the last GEMM is skipped.
+//   3. fa_bwd_dq       deterministic mode only: one CTA per (128-row Q tile, head,
+//                      batch) loops over KV tiles and accumulates dQ in TMEM
+//                      (S = Q K^T, dP = dO V^T, dQ += dS K), no atomics.
+//   4. fa_bwd_dq_conv  atomic mode: fp32 accumulator -> dq in the input dtype (BSHD).
+//
+// Roles in fa_bwd_dkdv (384 threads): warp 0 TMA producer (K, V once; Q, dO, LSE, D
+// per query tile in a 2-stage ring), warp 1 TMEM allocator + MMA issuer, warps 4-11
+// two compute warpgroups: thread = key row (TMEM lane); warpgroup c handles query
+// columns [64c, 64c+64) of S^T / dP^T, writes P^T to TMEM columns [64c, 64c+32) and
+// dS^T to [64c+32, 64c+64) (each over S^T columns it has already read), and reads
+// back half of the dQ columns for the atomics.
 #include "fa_ptx.cuh"
 #include "fa_internal.h"
+#include <cmath>
+
 namespace fa {
-size_t bwd_workspace_bytes(const fa_bwd_args_t* a) { return 0; }
-int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st) {
-  return FA_ERR_UNSUPPORTED;
+
+constexpr int kBwdBN = 128;  // keys per CTA
+constexpr int kBwdBM = 128;  // query rows per iteration
+
+template <int D>
+struct BwdCfg {
+  static constexpr int DH = D / 64;
+  static constexpr int TILE = 128 * D * 2;
+  static constexpr int CHUNK = 128 * 128;
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = TILE;
+  static constexpr int OFF_Q = 2 * TILE;           // 2 stages
+  static constexpr int OFF_DO = 4 * TILE;          // 2 stages
+  static constexpr int OFF_DS = 6 * TILE;          // [2 q chunks][128 keys][64 q] 16-bit
+  static constexpr int OFF_LSE = OFF_DS + 128 * 128 * 2;  // [2][128] fp32
+  static constexpr int OFF_DI = OFF_LSE + 2 * 128 * 4;    // [2][128] fp32
+  static constexpr int OFF_CTL = OFF_DI + 2 * 128 * 4;
+  static constexpr int USED = OFF_CTL + 256;
+  static constexpr int SMEM_BYTES = (USED + 1024 <= 232448) ? USED + 1024 : 232448;
+  static_assert(USED <= 232448, "backward shared memory budget");
+  static constexpr int TMEM_COLS = 512;
+  static_assert(256 + 2 * D <= TMEM_COLS, "TMEM: S^T, dP^T, dV, dK");
+};
+
+struct BwdParams {
+  int B, Sq, Skv, H, Hk, G, Sq_pad;
+  int causal;
+  float scale, scale_log2;
+  const float* lse2;  // [B, H, Sq_pad] lse * log2(e); +inf for padded / empty rows
+  const float* dsum;  // [B, H, Sq_pad] rowsum(O * dO)
+  float* dq_acc;      // [B, H, Sq_pad, D] fp32 (atomic mode)
+  void* dq;           // deterministic mode writes here directly
+  void* dk;
+  void* dv;
+  int64_t dq_sb, dq_ss, dq_sh;
+  int64_t dk_sb, dk_ss, dk_sh;
+  int64_t dv_sb, dv_ss, dv_sh;
+  int* err;
+};
+
+struct BwdCtl {
+  uint64_t kv_full;
+  uint64_t st_full[2];
+  uint64_t st_empty[2];
+  uint64_t s_full, dp_full, p_ready, ds_ready, dq_full, dq_free, final_done, drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  int smem_ok;
+};
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
 }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer_ns() - t0 > 200000000ull) return;
+}
+
+// ---------------------------------------------------------------- 1. preprocess
+template <typename T, int D>
+__global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const T* __restrict__ o,
+                                                          const T* __restrict__ dout,
+                                                          const float* __restrict__ lse,
+                                                          float* lse2, float* dsum, int B, int Sq,
+                                                          int H, int Sq_pad, int64_t o_sb,
+                                                          int64_t o_ss, int64_t o_sh,
+                                                          int64_t do_sb, int64_t do_ss,
+                                                          int64_t do_sh) {
+  const int warp = (blockIdx.x * 256 + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = (int64_t)B * H * Sq_pad;
+  if (warp >= rows) return;
+  const int i = warp % Sq_pad;
+  const int bh = warp / Sq_pad;
+  const int h = bh % H, b = bh / H;
+  float acc = 0.f;
+  float l2 = INFINITY;
+  if (i < Sq) {
+    const T* orow = o + b * o_sb + (int64_t)i * o_ss + (int64_t)h * o_sh;
+    const T* drow = dout + b * do_sb + (int64_t)i * do_ss + (int64_t)h * do_sh;
+    constexpr int PER = D / 32;  // 2 or 4 elements per lane
+#pragma unroll
+    for (int e = 0; e < PER; e += 2) {
+      const float2 a = Pack2<T>::unpack(*reinterpret_cast<const uint32_t*>(orow + lane * PER + e));
+      const float2 c = Pack2<T>::unpack(*reinterpret_cast<const uint32_t*>(drow + lane * PER + e));
+      acc += a.x * c.x + a.y * c.y;
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
+    const float L = lse[((int64_t)b * H + h) * Sq + i];
+    l2 = (L == -INFINITY) ? INFINITY : L * 1.4426950408889634f;
+  }
+  if (lane == 0) {
+    lse2[warp] = l2;
+    dsum[warp] = acc;
+  }
+}
+
+// ---------------------------------------------------------------- 4. dQ convert
+template <typename T, int D>
+__global__ void __launch_bounds__(256) fa_bwd_dq_convert_kernel(const float* __restrict__ acc,
+                                                                T* dq, int B, int Sq, int H,
+                                                                int Sq_pad, int64_t sb,
+                                                                int64_t ss, int64_t sh) {
+  const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;  // one thread per 4 elements
+  const int64_t total = (int64_t)B * H * Sq * (D / 4);
+  if (idx >= total) return;
+  const int c4 = idx % (D / 4);
+  const int64_t row = idx / (D / 4);
+  const int h = row % H;
+  const int64_t bi = row / H;
+  const int i = bi % Sq;
+  const int b = bi / Sq;
+  const float4 v =
+      *reinterpret_cast<const float4*>(acc + (((int64_t)b * H + h) * Sq_pad + i) * D + c4 * 4);
+  uint2 pk;
+  pk.x = Pack2<T>::pack(v.x, v.y);
+  pk.y = Pack2<T>::pack(v.z, v.w);
+  *reinterpret_cast<uint2*>(dq + b * sb + (int64_t)i * ss + (int64_t)h * sh + c4 * 4) = pk;
+}
+
+// ---------------------------------------------------------------- 2. dK / dV (+ dQ atomics)
+template <typename T, int D, bool ATOMIC_DQ>
+__global__ void __launch_bounds__(384, 1)
+    fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q,
+                       const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v,
+                       const __grid_constant__ CUtensorMap tm_do, const BwdParams p) {
+  using Cfg = BwdCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+  const bool smem_ok = (base - raw_addr) + Cfg::USED <= (uint32_t)Cfg::SMEM_BYTES;
+  if (!smem_ok) {  // uniform across the CTA: the layout would not fit
+    if (threadIdx.x == 0) record_device_error(p.err, 2, FA_SITE_BWD_PRODUCER);
+    return;
+  }
+  BwdCtl* ctl = reinterpret_cast<BwdCtl*>(base_ptr + Cfg::OFF_CTL);
+  volatile int* abort_flag = &ctl->abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int nblk = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int k0 = nblk * kBwdBN;
+  const int off = p.Skv - p.Sq;
+  const int nqt_all = (p.Sq + kBwdBM - 1) / kBwdBM;
+  const int t_start = p.causal ? min(nqt_all, max(0, k0 - off) / kBwdBM) : 0;
+  const int nqt = nqt_all - t_start;
+  const int n_iter = p.G * nqt;
+
+  if (threadIdx.x == 0) {
+    ctl->abort_flag = 0;
+    mbar_init(smem_u32(&ctl->kv_full), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&ctl->st_full[s]), 1);
+      mbar_init(smem_u32(&ctl->st_empty[s]), 1);
+    }
+    mbar_init(smem_u32(&ctl->s_full), 1);
+    mbar_init(smem_u32(&ctl->dp_full), 1);
+    mbar_init(smem_u32(&ctl->p_ready), 256);
+    mbar_init(smem_u32(&ctl->ds_ready), 256);
+    mbar_init(smem_u32(&ctl->dq_full), 1);
+    mbar_init(smem_u32(&ctl->dq_free), 256);
+    mbar_init(smem_u32(&ctl->final_done), 1);
+    mbar_init(smem_u32(&ctl->drain), 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  const uint32_t sK = base + Cfg::OFF_K, sV = base + Cfg::OFF_V;
+  const uint32_t sDS = base + Cfg::OFF_DS;
+
+  if (warp == 0) {
+    // ============================================================ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+      const uint32_t kvb = smem_u32(&ctl->kv_full);
+      mbar_arrive_expect_tx(kvb, 2 * Cfg::TILE);
+      for (int dh = 0; dh < Cfg::DH; ++dh) {
+        tma_load_4d(sK + dh * Cfg::CHUNK, &tm_k, kvb, dh * 64, hk, k0, b);
+        tma_load_4d(sV + dh * Cfg::CHUNK, &tm_v, kvb, dh * 64, hk, k0, b);
+      }
+      int i = 0;
+      for (; i < n_iter; ++i) {
+        const int s = i & 1;
+        if (!mbar_wait(smem_u32(&ctl->st_empty[s]), ((i >> 1) & 1) ^ 1, abort_flag, p.err,
+                       FA_SITE_BWD_PRODUCER))
+          break;
+        const int g = i / nqt, qt = t_start + i % nqt, h = hk * p.G + g;
+        const uint32_t fb = smem_u32(&ctl->st_full[s]);
+        mbar_arrive_expect_tx(fb, 2 * Cfg::TILE + 1024);
+        const uint32_t sQ = base + Cfg::OFF_Q + s * Cfg::TILE;
+        const uint32_t sdO = base + Cfg::OFF_DO + s * Cfg::TILE;
+        for (int dh = 0; dh < Cfg::DH; ++dh) {
+          tma_load_4d(sQ + dh * Cfg::CHUNK, &tm_q, fb, dh * 64, h, qt * kBwdBM, b);
+          tma_load_4d(sdO + dh * Cfg::CHUNK, &tm_do, fb, dh * 64, h, qt * kBwdBM, b);
+        }
+        const int64_t row0 = ((int64_t)b * p.H + h) * p.Sq_pad + qt * kBwdBM;
+        bulk_load(base + Cfg::OFF_LSE + s * 512, p.lse2 + row0, 512, fb);
+        bulk_load(base + Cfg::OFF_DI + s * 512, p.dsum + row0, 512, fb);
+      }
+      drain_wait(kvb, 0);
+      for (int k = max(0, i - 2); k < i; ++k) drain_wait(smem_u32(&ctl->st_full[k & 1]), (k >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ============================================================ MMA issuer
+    if (lane == 0) {
+      constexpr bool kBf16 = Pack2<T>::kBf16;
+      constexpr uint32_t idS = idesc_f16(128, 128, kBf16, false, false);
+      constexpr uint32_t idKV = idesc_f16(128, D, kBf16, false, true);
+      constexpr uint32_t idQ = idesc_f16(128, D, kBf16, true, true);
+      const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 256 + D;
+      bool ok = mbar_wait(smem_u32(&ctl->kv_full), 0, abort_flag, p.err, FA_SITE_BWD_MMA);
+      for (int i = 0; i < n_iter && ok; ++i) {
+        const int s = i & 1;
+        const uint32_t par = i & 1;
+        ok = mbar_wait(smem_u32(&ctl->st_full[s]), (i >> 1) & 1, abort_flag, p.err,
+                       FA_SITE_BWD_MMA);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t sQ = base + Cfg::OFF_Q + s * Cfg::TILE;
+        const uint32_t sdO = base + Cfg::OFF_DO + s * Cfg::TILE;
+        // S^T = K Q^T
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
+          mma_ss(tS, sdesc_sw128(sK + o, 16, 1024), sdesc_sw128(sQ + o, 16, 1024), idS, kk > 0);
+        }
+        mma_commit(smem_u32(&ctl->s_full));
+        // dP^T = V dO^T into [128, 256): the previous dQ must have been read out.
+        if (ATOMIC_DQ && i > 0) {
+          ok = mbar_wait(smem_u32(&ctl->dq_free), (i - 1) & 1, abort_flag, p.err, FA_SITE_BWD_MMA);
+          if (!ok) break;
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
+          mma_ss(tdP, sdesc_sw128(sV + o, 16, 1024), sdesc_sw128(sdO + o, 16, 1024), idS, kk > 0);
+        }
+        mma_commit(smem_u32(&ctl->dp_full));
+        // dV += P^T dO   (P^T for q 0..63 in columns 0..31, q 64..127 in 64..95)
+        ok = mbar_wait(smem_u32(&ctl->p_ready), par, abort_flag, p.err, FA_SITE_BWD_MMA);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t acol = (kk < 4) ? kk * 8 : 64 + (kk - 4) * 8;
+          mma_ts(tdV, tS + acol, sdesc_sw128(sdO + kk * 2048, Cfg::CHUNK, 1024), idKV,
+                 (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        // dK += dS^T Q   (dS^T in columns 32..63 and 96..127)
+        ok = mbar_wait(smem_u32(&ctl->ds_ready), par, abort_flag, p.err, FA_SITE_BWD_MMA);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t acol = (kk < 4) ? 32 + kk * 8 : 96 + (kk - 4) * 8;
+          mma_ts(tdK, tS + acol, sdesc_sw128(sQ + kk * 2048, Cfg::CHUNK, 1024), idKV,
+                 (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        if (ATOMIC_DQ) {
+          // dQ = dS K  (A = dS MN-major from smem, B = K MN-major) into [128, 128 + D)
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ss(tdP, sdesc_sw128(sDS + kk * 2048, Cfg::CHUNK, 1024),
+                   sdesc_sw128(sK + kk * 2048, Cfg::CHUNK, 1024), idQ, kk > 0);
+          mma_commit(smem_u32(&ctl->dq_full));
+        }
+        mma_commit(smem_u32(&ctl->st_empty[s]));
+      }
+      mma_commit(smem_u32(&ctl->final_done));
+      mma_commit(smem_u32(&ctl->drain));
+      drain_wait(smem_u32(&ctl->drain), 0);
+    }
+  } else if (warp >= 4) {
+    // ============================================================ compute warpgroups
+    const int c = (warp - 4) >> 2;              // query-column half
+    const int j = ((warp & 3) << 5) | lane;     // key row = TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_off, tdP = tmem + lane_off + 128;
+    const int key = k0 + j;
+    const bool key_ok = key < p.Skv;
+    const float c2 = p.scale_log2;
+    bool ok = true;
+    for (int i = 0; i < n_iter; ++i) {
+      const int s = i & 1;
+      const uint32_t par = i & 1;
+      const int g = i / nqt, qt = t_start + i % nqt, h = hk * p.G + g;
+      const int q0 = qt * kBwdBM;
+      const float* sLse = reinterpret_cast<const float*>(base_ptr + Cfg::OFF_LSE + s * 512) + 64 * c;
+      const float* sDi = reinterpret_cast<const float*>(base_ptr + Cfg::OFF_DI + s * 512) + 64 * c;
+      bool w = mbar_wait(smem_u32(&ctl->st_full[s]), (i >> 1) & 1, abort_flag, p.err,
+                         FA_SITE_BWD_COMPUTE);
+      w = w && mbar_wait(smem_u32(&ctl->s_full), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+      ok = __all_sync(0xffffffffu, w);
+      if (!ok) break;
+      tc_fence_after();
+      // ---- pass A: P^T = exp2(S^T * scale*log2e - lse*log2e), masked
+      float pv[64];
+      {
+        uint32_t sv[64];
+        tmem_ld32(tS + 64 * c, sv);
+        tmem_ld32(tS + 64 * c + 32, sv + 32);
+        tmem_wait_ld();
+        const int qbase = q0 + 64 * c;
+        const bool full = key_ok && (!p.causal || key <= qbase + off);
+#pragma unroll
+        for (int x = 0; x < 64; ++x) {
+          const bool vis = full || (key_ok && key <= qbase + x + off);
+          pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -sLse[x])) : 0.f;
+        }
+        uint32_t pk[32];
+#pragma unroll
+        for (int x = 0; x < 32; ++x) pk[x] = Pack2<T>::pack(pv[2 * x], pv[2 * x + 1]);
+        tmem_st32(tS + 64 * c, pk);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&ctl->p_ready));
+      // ---- pass B: dS^T = P^T (dP^T - D) * scale
+      w = mbar_wait(smem_u32(&ctl->dp_full), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+      ok = __all_sync(0xffffffffu, w);
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t dv[32];
+        tmem_ld32(tdP + 64 * c + 32 * hf, dv);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int x = 0; x < 16; ++x) {
+          const int xx = 32 * hf + 2 * x;
+          const float d0 = pv[xx] * (__uint_as_float(dv[2 * x]) - sDi[xx]) * p.scale;
+          const float d1 = pv[xx + 1] * (__uint_as_float(dv[2 * x + 1]) - sDi[xx + 1]) * p.scale;
+          pk[x] = Pack2<T>::pack(d0, d1);
+        }
+        tmem_st16(tS + 64 * c + 32 + 16 * hf, pk);
+        if (ATOMIC_DQ) {
+          // dS^T row j, query columns 64c + 32hf .. +31 -> smem (MN-major A of dQ = dS K)
+          const uint32_t row = sDS + c * Cfg::CHUNK + j * 128;
+#pragma unroll
+          for (int m = 0; m < 4; ++m)
+            st_shared_v4(row + ((((hf << 2) + m) ^ (j & 7)) << 4), pk[4 * m], pk[4 * m + 1],
+                         pk[4 * m + 2], pk[4 * m + 3]);
+        }
+      }
+      tmem_wait_st();
+      if (ATOMIC_DQ) fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&ctl->ds_ready));
+      if (ATOMIC_DQ) {
+        // ---- dQ rows (lane = query row) -> fp32 accumulator
+        w = mbar_wait(smem_u32(&ctl->dq_full), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+        ok = __all_sync(0xffffffffu, w);
+        if (!ok) break;
+        tc_fence_after();
+        float* acc = p.dq_acc + (((int64_t)b * p.H + h) * p.Sq_pad + q0 + j) * D + c * (D / 2);
+#pragma unroll
+        for (int c0 = 0; c0 < D / 2; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld32(tdP + c * (D / 2) + c0, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int x = 0; x < 32; x += 4)
+            atomicAdd(reinterpret_cast<float4*>(acc + c0 + x),
+                      make_float4(__uint_as_float(v[x]), __uint_as_float(v[x + 1]),
+                                  __uint_as_float(v[x + 2]), __uint_as_float(v[x + 3])));
+        }
+        tc_fence_before();
+        mbar_arrive(smem_u32(&ctl->dq_free));
+      }
+    }
+    // ---- dK, dV rows (lane = key row)
+    if (ok) {
+      bool w = mbar_wait(smem_u32(&ctl->final_done), 0, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+      ok = __all_sync(0xffffffffu, w);
+    }
+    if (ok) {
+      tc_fence_after();
+      T* dkr = reinterpret_cast<T*>(p.dk) + (int64_t)b * p.dk_sb + (int64_t)key * p.dk_ss +
+               (int64_t)hk * p.dk_sh + c * (D / 2);
+      T* dvr = reinterpret_cast<T*>(p.dv) + (int64_t)b * p.dv_sb + (int64_t)key * p.dv_ss +
+               (int64_t)hk * p.dv_sh + c * (D / 2);
+#pragma unroll
+      for (int w2 = 0; w2 < 2; ++w2) {
+        const uint32_t src = tmem + lane_off + 256 + (w2 ? D : 0) + c * (D / 2);
+        T* dst = w2 ? dkr : dvr;
+#pragma unroll
+        for (int c0 = 0; c0 < D / 2; c0 += 32) {
+          uint32_t v[32];
+          if (n_iter > 0) {
+            tmem_ld32(src + c0, v);
+            tmem_wait_ld();
+          }
+          uint32_t pk[16];
+#pragma unroll
+          for (int x = 0; x < 16; ++x)
+            pk[x] = n_iter > 0 ? Pack2<T>::pack(__uint_as_float(v[2 * x]), __uint_as_float(v[2 * x + 1]))
+                               : 0u;
+          if (key_ok) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
+            d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            d4[2] = make_uint4(pk[8], pk[9], pk[10], pk[11]);
+            d4[3] = make_uint4(pk[12], pk[13], pk[14], pk[15]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- 3. deterministic dQ
+template <int D>
+struct DqCfg {
+  static constexpr int DH = D / 64;
+  static constexpr int TILE = 128 * D * 2;
+  static constexpr int CHUNK = 128 * 128;
+  static constexpr int STAGES = (D == 64) ? 4 : 2;  // K/V pairs
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_DO = TILE;
+  static constexpr int OFF_KV = 2 * TILE;          // STAGES x (K, V)
+  static constexpr int OFF_DS = OFF_KV + STAGES * 2 * TILE;  // [2 key chunks][128 q][64 keys]
+  static constexpr int OFF_CTL = OFF_DS + 128 * 128 * 2;
+  static constexpr int USED = OFF_CTL + 256;
+  static constexpr int SMEM_BYTES = (USED + 1024 <= 232448) ? USED + 1024 : 232448;
+  static_assert(USED <= 232448, "dQ kernel shared memory budget");
+};
+
+struct DqCtl {
+  uint64_t q_full;
+  uint64_t kv_full[4];
+  uint64_t kv_empty[4];
+  uint64_t s_full, dp_full, ds_ready, final_done, drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(384, 1)
+    fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q,
+                     const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v,
+                     const __grid_constant__ CUtensorMap tm_do, const BwdParams p) {
+  using Cfg = DqCfg<D>;
+  constexpr int ST = Cfg::STAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+  if ((base - raw_addr) + Cfg::USED > (uint32_t)Cfg::SMEM_BYTES) {
+    if (threadIdx.x == 0) record_device_error(p.err, 2, FA_SITE_BWD_PRODUCER);
+    return;
+  }
+  DqCtl* ctl = reinterpret_cast<DqCtl*>(base_ptr + Cfg::OFF_CTL);
+  volatile int* abort_flag = &ctl->abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y, b = blockIdx.z, hk = h / p.G;
+  const int qt = p.causal ? (gridDim.x - 1 - blockIdx.x) : blockIdx.x;
+  const int q0 = qt * kBwdBM;
+  const int off = p.Skv - p.Sq;
+  int nkv = (p.Skv + kBwdBN - 1) / kBwdBN;
+  if (p.causal) {
+    const int max_key = min(q0 + kBwdBM, p.Sq) - 1 + off;
+    nkv = min(nkv, max_key >= 0 ? max_key / kBwdBN + 1 : 0);
+  }
+
+  if (threadIdx.x == 0) {
+    ctl->abort_flag = 0;
+    mbar_init(smem_u32(&ctl->q_full), 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(smem_u32(&ctl->kv_full[s]), 1);
+      mbar_init(smem_u32(&ctl->kv_empty[s]), 1);
+    }
+    mbar_init(smem_u32(&ctl->s_full), 1);
+    mbar_init(smem_u32(&ctl->dp_full), 1);
+    mbar_init(smem_u32(&ctl->ds_ready), 256);
+    mbar_init(smem_u32(&ctl->final_done), 1);
+    mbar_init(smem_u32(&ctl->drain), 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  const uint32_t sQ = base + Cfg::OFF_Q, sdO = base + Cfg::OFF_DO, sDS = base + Cfg::OFF_DS;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t qb = smem_u32(&ctl->q_full);
+      mbar_arrive_expect_tx(qb, 2 * Cfg::TILE);
+      for (int dh = 0; dh < Cfg::DH; ++dh) {
+        tma_load_4d(sQ + dh * Cfg::CHUNK, &tm_q, qb, dh * 64, h, q0, b);
+        tma_load_4d(sdO + dh * Cfg::CHUNK, &tm_do, qb, dh * 64, h, q0, b);
+      }
+      int j = 0;
+      for (; j < nkv; ++j) {
+        const int s = j % ST;
+        if (!mbar_wait(smem_u32(&ctl->kv_empty[s]), ((j / ST) & 1) ^ 1, abort_flag, p.err,
+                       FA_SITE_BWD_PRODUCER))
+          break;
+        const uint32_t fb = smem_u32(&ctl->kv_full[s]);
+        mbar_arrive_expect_tx(fb, 2 * Cfg::TILE);
+        const uint32_t dk = base + Cfg::OFF_KV + s * 2 * Cfg::TILE;
+        for (int dh = 0; dh < Cfg::DH; ++dh) {
+          tma_load_4d(dk + dh * Cfg::CHUNK, &tm_k, fb, dh * 64, hk, j * kBwdBN, b);
+          tma_load_4d(dk + Cfg::TILE + dh * Cfg::CHUNK, &tm_v, fb, dh * 64, hk, j * kBwdBN, b);
+        }
+      }
+      drain_wait(qb, 0);
+      for (int k = max(0, j - ST); k < j; ++k) drain_wait(smem_u32(&ctl->kv_full[k % ST]), (k / ST) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr bool kBf16 = Pack2<T>::kBf16;
+      constexpr uint32_t idS = idesc_f16(128, 128, kBf16, false, false);
+      constexpr uint32_t idQ = idesc_f16(128, D, kBf16, false, true);
+      const uint32_t tS = tmem, tdP = tmem + 128, tdQ = tmem + 256;
+      bool ok = mbar_wait(smem_u32(&ctl->q_full), 0, abort_flag, p.err, FA_SITE_BWD_MMA);
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int s = j % ST;
+        ok = mbar_wait(smem_u32(&ctl->kv_full[s]), (j / ST) & 1, abort_flag, p.err, FA_SITE_BWD_MMA);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t sKt = base + Cfg::OFF_KV + s * 2 * Cfg::TILE, sVt = sKt + Cfg::TILE;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
+          mma_ss(tS, sdesc_sw128(sQ + o, 16, 1024), sdesc_sw128(sKt + o, 16, 1024), idS, kk > 0);
+        }
+        mma_commit(smem_u32(&ctl->s_full));
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
+          mma_ss(tdP, sdesc_sw128(sdO + o, 16, 1024), sdesc_sw128(sVt + o, 16, 1024), idS, kk > 0);
+        }
+        mma_commit(smem_u32(&ctl->dp_full));
+        ok = mbar_wait(smem_u32(&ctl->ds_ready), j & 1, abort_flag, p.err, FA_SITE_BWD_MMA);
+        if (!ok) break;
+        tc_fence_after();
+        // dQ += dS K: A = dS K-major from smem ([2 key chunks][128 q][64 keys]), B = K MN-major
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ss(tdQ, sdesc_sw128(sDS + (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32, 16, 1024),
+                 sdesc_sw128(sKt + kk * 2048, Cfg::CHUNK, 1024), idQ, (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(smem_u32(&ctl->kv_empty[s]));
+      }
+      mma_commit(smem_u32(&ctl->final_done));
+      mma_commit(smem_u32(&ctl->drain));
+      drain_wait(smem_u32(&ctl->drain), 0);
+    }
+  } else if (warp >= 4) {
+    const int c = (warp - 4) >> 2;           // key-column half
+    const int r = ((warp & 3) << 5) | lane;  // query row
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int qi = q0 + r;
+    const bool q_ok = qi < p.Sq;
+    const int64_t row = ((int64_t)b * p.H + h) * p.Sq_pad + qi;
+    const float lse2 = p.lse2[row];  // padded rows hold +inf -> P = 0
+    const float di = p.dsum[row];
+    const float c2 = p.scale_log2;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      bool w = mbar_wait(smem_u32(&ctl->s_full), j & 1, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+      ok = __all_sync(0xffffffffu, w);
+      if (!ok) break;
+      tc_fence_after();
+      float pv[64];
+      {
+        uint32_t sv[64];
+        tmem_ld32(tmem + lane_off + 64 * c, sv);
+        tmem_ld32(tmem + lane_off + 64 * c + 32, sv + 32);
+        tmem_wait_ld();
+        const int kb = j * kBwdBN + 64 * c;
+#pragma unroll
+        for (int x = 0; x < 64; ++x) {
+          const int key = kb + x;
+          const bool vis = q_ok && key < p.Skv && (!p.causal || key <= qi + off);
+          pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lse2)) : 0.f;
+        }
+      }
+      w = mbar_wait(smem_u32(&ctl->dp_full), j & 1, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+      ok = __all_sync(0xffffffffu, w);
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t dv[32];
+        tmem_ld32(tmem + lane_off + 128 + 64 * c + 32 * hf, dv);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int x = 0; x < 16; ++x) {
+          const int xx = 32 * hf + 2 * x;
+          pk[x] = Pack2<T>::pack(pv[xx] * (__uint_as_float(dv[2 * x]) - di) * p.scale,
+                                 pv[xx + 1] * (__uint_as_float(dv[2 * x + 1]) - di) * p.scale);
+        }
+        // dS row r, keys 64c + 32hf .. +31 -> K-major smem tile (key chunk c)
+        const uint32_t rowa = sDS + c * Cfg::CHUNK + r * 128;
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+          st_shared_v4(rowa + ((((hf << 2) + m) ^ (r & 7)) << 4), pk[4 * m], pk[4 * m + 1],
+                       pk[4 * m + 2], pk[4 * m + 3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&ctl->ds_ready));
+    }
+    if (ok) {
+      bool w = mbar_wait(smem_u32(&ctl->final_done), 0, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+      ok = __all_sync(0xffffffffu, w);
+    }
+    if (ok) {
+      tc_fence_after();
+      T* dst = reinterpret_cast<T*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)qi * p.dq_ss +
+               (int64_t)h * p.dq_sh + c * (D / 2);
+#pragma unroll
+      for (int c0 = 0; c0 < D / 2; c0 += 32) {
+        uint32_t v[32];
+        if (nkv > 0) {
+          tmem_ld32(tmem + lane_off + 256 + c * (D / 2) + c0, v);
+          tmem_wait_ld();
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int x = 0; x < 16; ++x)
+          pk[x] = nkv > 0 ? Pack2<T>::pack(__uint_as_float(v[2 * x]), __uint_as_float(v[2 * x + 1])) : 0u;
+        if (q_ok) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
+          d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          d4[2] = make_uint4(pk[8], pk[9], pk[10], pk[11]);
+          d4[3] = make_uint4(pk[12], pk[13], pk[14], pk[15]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------- host side
+static int pad128(int x) { return (x + 127) / 128 * 128; }
+
+size_t bwd_workspace_bytes(const fa_bwd_args_t* a) {
+  const size_t rows = (size_t)a->batch * a->num_heads * pad128(a->seqlen_q);
+  size_t n = 2 * (rows * 4 + 256);                         // lse2, dsum
+  if (!a->deterministic) n += rows * a->head_dim * 4 + 256;  // dQ accumulator
+  return n + 256;
+}
+
+template <typename K>
+static int set_smem(K kern, int bytes) {
+  FA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  return FA_OK;
+}
+
+template <typename T, int D>
+static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const CUtensorMap& tk,
+                           const CUtensorMap& tv, const CUtensorMap& tdo, BwdParams& p,
+                           cudaStream_t st) {
+  const int rows_blocks = (int)(((int64_t)a->batch * a->num_heads * p.Sq_pad * 32 + 255) / 256);
+  fa_bwd_prep_kernel<T, D><<<rows_blocks, 256, 0, st>>>(
+      reinterpret_cast<const T*>(a->out), reinterpret_cast<const T*>(a->dout), a->lse,
+      const_cast<float*>(p.lse2), const_cast<float*>(p.dsum), a->batch, a->seqlen_q,
+      a->num_heads, p.Sq_pad, a->o_stride[0], a->o_stride[1], a->o_stride[2], a->do_stride[0],
+      a->do_stride[1], a->do_stride[2]);
+  FA_CUDA_TRY(cudaGetLastError());
+  count_launch();
+  if (!a->deterministic) {
+    FA_CUDA_TRY(cudaMemsetAsync(p.dq_acc, 0,
+                                (size_t)a->batch * a->num_heads * p.Sq_pad * D * sizeof(float), st));
+    auto kern = fa_bwd_dkdv_kernel<T, D, true>;
+    static bool attr[64] = {false};
+    int dev = 0;
+    FA_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 64 && !attr[dev]) {
+      if (int s = set_smem(kern, BwdCfg<D>::SMEM_BYTES)) return s;
+      attr[dev] = true;
+    }
+    dim3 grid((a->seqlen_k + kBwdBN - 1) / kBwdBN, a->num_heads_k, a->batch);
+    prof_begin(FA_PROF_BWD_DKDV, st);
+    kern<<<grid, 384, BwdCfg<D>::SMEM_BYTES, st>>>(tq, tk, tv, tdo, p);
+    prof_end(FA_PROF_BWD_DKDV, st);
+    FA_CUDA_TRY(cudaGetLastError());
+    count_launch();
+    const int64_t n4 = (int64_t)a->batch * a->num_heads * a->seqlen_q * (D / 4);
+    fa_bwd_dq_convert_kernel<T, D><<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(
+        p.dq_acc, reinterpret_cast<T*>(a->dq), a->batch, a->seqlen_q, a->num_heads, p.Sq_pad,
+        a->dq_stride[0], a->dq_stride[1], a->dq_stride[2]);
+    FA_CUDA_TRY(cudaGetLastError());
+    count_launch();
+  } else {
+    auto kern = fa_bwd_dkdv_kernel<T, D, false>;
+    auto kq = fa_bwd_dq_kernel<T, D>;
+    static bool attr[64] = {false};
+    int dev = 0;
+    FA_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 64 && !attr[dev]) {
+      if (int s = set_smem(kern, BwdCfg<D>::SMEM_BYTES)) return s;
+      if (int s = set_smem(kq, DqCfg<D>::SMEM_BYTES)) return s;
+      attr[dev] = true;
+    }
+    dim3 grid((a->seqlen_k + kBwdBN - 1) / kBwdBN, a->num_heads_k, a->batch);
+    kern<<<grid, 384, BwdCfg<D>::SMEM_BYTES, st>>>(tq, tk, tv, tdo, p);
+    FA_CUDA_TRY(cudaGetLastError());
+    count_launch();
+    dim3 gq((a->seqlen_q + kBwdBM - 1) / kBwdBM, a->num_heads, a->batch);
+    kq<<<gq, 384, DqCfg<D>::SMEM_BYTES, st>>>(tq, tk, tv, tdo, p);
+    FA_CUDA_TRY(cudaGetLastError());
+    count_launch();
+  }
+  return FA_OK;
+}
+
+static uintptr_t align256(uintptr_t x) { return (x + 255) & ~uintptr_t(255); }
+
+int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st) {
+  const int D = a->head_dim;
+  if (D != 64 && D != 128) return FA_ERR_UNSUPPORTED;
+  if (a->batch == 0) return FA_OK;
+  if (a->seqlen_q == 0 || a->seqlen_k == 0) {
+    // Nothing attends: every gradient is zero (outputs are dense BSHD allocations).
+    if (a->seqlen_q > 0)
+      FA_CUDA_TRY(cudaMemsetAsync(a->dq, 0, (size_t)a->dq_stride[0] * a->batch * 2, st));
+    if (a->seqlen_k > 0) {
+      FA_CUDA_TRY(cudaMemsetAsync(a->dk, 0, (size_t)a->dk_stride[0] * a->batch * 2, st));
+      FA_CUDA_TRY(cudaMemsetAsync(a->dv, 0, (size_t)a->dv_stride[0] * a->batch * 2, st));
+    }
+    return FA_OK;
+  }
+  const void* ptrs[9] = {a->q, a->k, a->v, a->out, a->dout, a->dq, a->dk, a->dv, a->lse};
+  for (const void* q : ptrs)
+    if (reinterpret_cast<uintptr_t>(q) & 15u) return FA_ERR_ALIGNMENT;
+  const int64_t* strs[8] = {a->q_stride, a->k_stride, a->v_stride, a->o_stride,
+                            a->do_stride, a->dq_stride, a->dk_stride, a->dv_stride};
+  for (const int64_t* s : strs)
+    for (int i = 0; i < 3; ++i)
+      if (s[i] % 8) return FA_ERR_ALIGNMENT;
+  const int G = a->num_heads / a->num_heads_k;
+  const CUtensorMapDataType dt = tmap_dtype(a->dtype);
+  CUtensorMap tq, tk, tv, tdo;
+  auto enc = [&](CUtensorMap* m, const void* ptr, const int64_t* s, int heads, int seq) {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)heads, (uint64_t)(seq > 0 ? seq : 1),
+                              (uint64_t)a->batch};
+    const uint64_t str[3] = {(uint64_t)s[2] * 2, (uint64_t)s[1] * 2, (uint64_t)s[0] * 2};
+    const uint32_t box[4] = {64, 1, 128, 1};
+    return encode_tmap(m, dt, 4, ptr, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  };
+  FA_TMAP_TRY(enc(&tq, a->q, a->q_stride, a->num_heads, a->seqlen_q));
+  FA_TMAP_TRY(enc(&tdo, a->dout, a->do_stride, a->num_heads, a->seqlen_q));
+  FA_TMAP_TRY(enc(&tk, a->k, a->k_stride, a->num_heads_k, a->seqlen_k));
+  FA_TMAP_TRY(enc(&tv, a->v, a->v_stride, a->num_heads_k, a->seqlen_k));
+
+  BwdParams p{};
+  p.B = a->batch;
+  p.Sq = a->seqlen_q;
+  p.Skv = a->seqlen_k;
+  p.H = a->num_heads;
+  p.Hk = a->num_heads_k;
+  p.G = G;
+  p.Sq_pad = pad128(a->seqlen_q);
+  p.causal = a->causal;
+  p.scale = a->softmax_scale;
+  p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  const size_t rows = (size_t)a->batch * a->num_heads * p.Sq_pad;
+  uintptr_t w = align256(reinterpret_cast<uintptr_t>(ws));
+  p.lse2 = reinterpret_cast<const float*>(w);
+  w = align256(w + rows * 4);
+  p.dsum = reinterpret_cast<const float*>(w);
+  w = align256(w + rows * 4);
+  p.dq_acc = a->deterministic ? nullptr : reinterpret_cast<float*>(w);
+  p.dq = a->dq;
+  p.dk = a->dk;
+  p.dv = a->dv;
+  p.dq_sb = a->dq_stride[0];
+  p.dq_ss = a->dq_stride[1];
+  p.dq_sh = a->dq_stride[2];
+  p.dk_sb = a->dk_stride[0];
+  p.dk_ss = a->dk_stride[1];
+  p.dk_sh = a->dk_stride[2];
+  p.dv_sb = a->dv_stride[0];
+  p.dv_ss = a->dv_stride[1];
+  p.dv_sh = a->dv_stride[2];
+  p.err = err;
+  const bool bf16 = a->dtype == FA_DTYPE_BF16;
+  if (D == 64)
+    return bf16 ? launch_bwd_impl<__nv_bfloat16, 64>(a, tq, tk, tv, tdo, p, st)
+                : launch_bwd_impl<__half, 64>(a, tq, tk, tv, tdo, p, st);
+  return bf16 ? launch_bwd_impl<__nv_bfloat16, 128>(a, tq, tk, tv, tdo, p, st)
+              : launch_bwd_impl<__half, 128>(a, tq, tk, tv, tdo, p, st);
+}
+
 }  // namespace fa

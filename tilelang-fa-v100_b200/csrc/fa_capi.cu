@@ -2,6 +2,7 @@
 // encoding and dispatch to the kernel launchers.  Nothing here allocates device
 // memory; outputs and workspaces are owned by the caller.
 #include <atomic>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <cudaTypedefs.h>
@@ -20,15 +21,84 @@ static std::atomic<int64_t> g_launches{0};
 
 void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
+static thread_local char g_err_detail[512] = "";
+void set_error_detail(const char* what, const char* file, int line, const char* err) {
+  const char* base = strrchr(file, '/');
+  snprintf(g_err_detail, sizeof(g_err_detail), "%s at %s:%d: %s", what, base ? base + 1 : file,
+           line, err);
+}
+
+static int g_prof_kind = 0;
+static cudaEvent_t g_prof_begin = nullptr, g_prof_end = nullptr;
+void prof_begin(int kind, cudaStream_t st) {
+  if (g_prof_kind == kind && g_prof_begin != nullptr) cudaEventRecord(g_prof_begin, st);
+}
+void prof_end(int kind, cudaStream_t st) {
+  if (g_prof_kind == kind && g_prof_end != nullptr) {
+    cudaEventRecord(g_prof_end, st);
+    g_prof_kind = 0;
+    g_prof_begin = g_prof_end = nullptr;
+  }
+}
+
 static int current_device(int* dev) {
   if (cudaGetDevice(dev) != cudaSuccess) return FA_ERR_CUDA;
   if (*dev < 0 || *dev >= 64) return FA_ERR_CUDA;
   return FA_OK;
 }
 
-// Per-device set-up: compute-capability check, SM count and the device address of
-// the error word (taken once per device, with that device current).
-static int device_setup(int** err_out) {
+// Driver entry points used to bind the caller's context to the calling thread.
+typedef CUresult (*PFN_streamGetCtx)(CUstream, CUcontext*);
+typedef CUresult (*PFN_ctxGetCurrent)(CUcontext*);
+typedef CUresult (*PFN_ctxSetCurrent)(CUcontext);
+static PFN_streamGetCtx p_stream_get_ctx = nullptr;
+static PFN_ctxGetCurrent p_ctx_get_current = nullptr;
+static PFN_ctxSetCurrent p_ctx_set_current = nullptr;
+
+static void* driver_fn(const char* name) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return p;
+}
+
+// Makes the CUDA context of the caller's stream (or, for the default stream, the
+// primary context of the runtime's current device) current on the calling thread.
+// Needed because the library's driver calls (tensor-map encoding) need a current
+// context, and a caller's worker thread -- e.g. torch's autograd thread -- may not
+// have one bound yet even though its runtime "current device" is set.
+static int bind_context(cudaStream_t st) {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    p_stream_get_ctx = reinterpret_cast<PFN_streamGetCtx>(driver_fn("cuStreamGetCtx"));
+    p_ctx_get_current = reinterpret_cast<PFN_ctxGetCurrent>(driver_fn("cuCtxGetCurrent"));
+    p_ctx_set_current = reinterpret_cast<PFN_ctxSetCurrent>(driver_fn("cuCtxSetCurrent"));
+  });
+  const uintptr_t sv = reinterpret_cast<uintptr_t>(st);
+  if (sv > 2 && p_stream_get_ctx && p_ctx_get_current && p_ctx_set_current) {
+    CUcontext ctx = nullptr, cur = nullptr;
+    if (p_stream_get_ctx(reinterpret_cast<CUstream>(st), &ctx) == CUDA_SUCCESS && ctx != nullptr) {
+      p_ctx_get_current(&cur);
+      if (cur != ctx && p_ctx_set_current(ctx) != CUDA_SUCCESS) {
+        set_error_detail("cuCtxSetCurrent", __FILE__, __LINE__, "failed");
+        return FA_ERR_CUDA;
+      }
+      return FA_OK;
+    }
+  }
+  int dev = 0;
+  FA_CUDA_TRY(cudaGetDevice(&dev));
+  FA_CUDA_TRY(cudaSetDevice(dev));  // CUDA 12+: initialises and binds the primary context
+  return FA_OK;
+}
+
+// Per-device set-up: binds the caller's context, checks the compute capability,
+// caches the SM count and the device address of the error word (taken once per
+// device, with that device current).
+static int device_setup(int** err_out, cudaStream_t st = nullptr) {
+  if (int s = bind_context(st)) return s;
   int dev;
   if (int s = current_device(&dev)) return s;
   std::lock_guard<std::mutex> lk(g_mu);
@@ -96,6 +166,8 @@ extern "C" {
 
 const char* fa_version(void) { return "fa_b200 1.0.0 (sm_100a)"; }
 
+const char* fa_last_error_detail(void) { return g_err_detail; }
+
 int64_t fa_launch_count(void) { return g_launches.load(); }
 
 const char* fa_status_string(int status) {
@@ -140,7 +212,7 @@ int fa_fwd(const fa_fwd_args_t* a, void* stream) {
   if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
   if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256) return FA_ERR_UNSUPPORTED;
   int* err = nullptr;
-  if (int s = device_setup(&err)) return s;
+  if (int s = device_setup(&err, static_cast<cudaStream_t>(stream))) return s;
   return launch_fwd_dense(a, err, static_cast<cudaStream_t>(stream));
 }
 
@@ -162,7 +234,7 @@ int fa_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, void* stream) {
   if (ws_bytes < bwd_workspace_bytes(a) || (bwd_workspace_bytes(a) > 0 && ws == nullptr))
     return FA_ERR_WORKSPACE;
   int* err = nullptr;
-  if (int s = device_setup(&err)) return s;
+  if (int s = device_setup(&err, static_cast<cudaStream_t>(stream))) return s;
   return launch_bwd(a, ws, ws_bytes, err, static_cast<cudaStream_t>(stream));
 }
 
@@ -177,7 +249,7 @@ int fa_paged_prefill(const fa_paged_args_t* a, void* stream) {
   if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
   if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256) return FA_ERR_UNSUPPORTED;
   int* err = nullptr;
-  if (int s = device_setup(&err)) return s;
+  if (int s = device_setup(&err, static_cast<cudaStream_t>(stream))) return s;
   return launch_paged_prefill(a, err, static_cast<cudaStream_t>(stream));
 }
 
@@ -196,8 +268,16 @@ int fa_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, void* stream
     return FA_ERR_INVALID_ARG;
   if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
   int* err = nullptr;
-  if (int s = device_setup(&err)) return s;
+  if (int s = device_setup(&err, static_cast<cudaStream_t>(stream))) return s;
   return launch_decode(a, ws, ws_bytes, err, static_cast<cudaStream_t>(stream));
+}
+
+int fa_profile_next_launch(int32_t kind, void* ev_begin, void* ev_end) {
+  if (kind < 1 || kind > 4 || ev_begin == nullptr || ev_end == nullptr) return FA_ERR_INVALID_ARG;
+  g_prof_kind = kind;
+  g_prof_begin = static_cast<cudaEvent_t>(ev_begin);
+  g_prof_end = static_cast<cudaEvent_t>(ev_end);
+  return FA_OK;
 }
 
 int fa_selftest_umma(const void* a, const void* b, float* c, int32_t n, int32_t k, int32_t dtype,
@@ -205,7 +285,7 @@ int fa_selftest_umma(const void* a, const void* b, float* c, int32_t n, int32_t 
   if (a == nullptr || b == nullptr || c == nullptr) return FA_ERR_INVALID_ARG;
   if (!valid_dtype(dtype)) return FA_ERR_UNSUPPORTED;
   int* err = nullptr;
-  if (int s = device_setup(&err)) return s;
+  if (int s = device_setup(&err, static_cast<cudaStream_t>(stream))) return s;
   return launch_selftest_umma(a, b, c, n, k, dtype, b_mn, a_tmem, err,
                               static_cast<cudaStream_t>(stream));
 }

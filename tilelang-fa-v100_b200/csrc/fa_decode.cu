@@ -406,7 +406,9 @@ static int launch_decode_impl(const CUtensorMap& tk, const CUtensorMap& tv, cons
     attr_set[dev] = true;
   }
   dim3 grid(p.num_splits, p.Hkv / p.HG, p.B);
+  prof_begin(FA_PROF_DECODE, st);
   kern<<<grid, 32 + 32 * p.HG, Cfg::SMEM_BYTES, st>>>(tk, tv, p);
+  prof_end(FA_PROF_DECODE, st);
   FA_CUDA_TRY(cudaGetLastError());
   count_launch();
   if (p.num_splits > 1) {
@@ -441,9 +443,7 @@ int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err
     const uint64_t str[3] = {(uint64_t)D * 2, (uint64_t)a->num_kv_heads * D * 2,
                              (uint64_t)ps * a->num_kv_heads * D * 2};
     const uint32_t box[4] = {64, 1, (uint32_t)kDecChunk, 1};
-    if (encode_tmap(kv_map[w], dt, 4, kv_ptr[w], dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B) !=
-        CUDA_SUCCESS)
-      return FA_ERR_CUDA;
+    FA_TMAP_TRY(encode_tmap(kv_map[w], dt, 4, kv_ptr[w], dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   DecParams p{};
   p.q = a->q;

@@ -90,7 +90,8 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int G = p.G;
-  const int TPB = NQ * kFwdBM / G;  // tokens per CTA block
+  const int TPT = kFwdBM / G;       // tokens per Q tile (rows TPT*G .. 127 unused when G does not divide 128)
+  const int TPB = NQ * TPT;         // tokens per CTA block
   const int hk = blockIdx.y;
 
   // ---------------------------------------------------------------- work item
@@ -180,9 +181,9 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       const uint32_t qbar = smem_u32(&ctl->q_full);
-      mbar_arrive_expect_tx(qbar, NQ * Cfg::TILE_BYTES);
+      mbar_arrive_expect_tx(qbar, NQ * Cfg::DH * TPT * G * 128);
       for (int t = 0; t < NQ; ++t) {
-        const int tok = tok_base + tok0 + t * (kFwdBM / G);
+        const int tok = tok_base + tok0 + t * TPT;
         for (int dh = 0; dh < Cfg::DH; ++dh)
           tma_load_4d(sQ + t * Cfg::TILE_BYTES + dh * Cfg::CHUNK_BYTES, &tm_q, qbar, dh * 64,
                       hk * G, tok, PAGED ? 0 : b);
@@ -314,10 +315,10 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_off + t * 128;
     const uint32_t tO = tmem + lane_off + NQ * 128 + t * D;
-    const int R = t * kFwdBM + r;
-    const int lt = tok0 + R / G;             // token index within the sequence / query chunk
-    const int h = hk * G + (R - (R / G) * G);  // query head
-    const bool row_valid = lt < q_len;
+    const int tr = r / G;                    // token of this row inside the tile
+    const int lt = tok0 + t * TPT + tr;      // token index within the sequence / query chunk
+    const int h = hk * G + (r - tr * G);     // query head
+    const bool row_valid = tr < TPT && lt < q_len;
     const int limit = lt + off;              // causal: key <= limit
     const bool window = PAGED && p.causal && (p.swq > 0 || p.swk > 0);
     const float c2 = p.scale_log2;
@@ -469,7 +470,10 @@ static int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const C
                                      Cfg::SMEM_BYTES));
     attr_set[dev] = true;
   }
+  const int kind = PAGED ? FA_PROF_PAGED : FA_PROF_FWD;
+  prof_begin(kind, st);
   kern<<<grid, Cfg::NTHREADS, Cfg::SMEM_BYTES, st>>>(tq, tk, tv, p);
+  prof_end(kind, st);
   FA_CUDA_TRY(cudaGetLastError());
   count_launch();
   return FA_OK;
@@ -489,7 +493,7 @@ int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
   const int D = a->head_dim;
   const int G = a->num_heads / a->num_heads_k;
   const int NQ = (D == 256) ? 1 : 2;
-  if (128 % G != 0) return FA_ERR_UNSUPPORTED;
+  if (G > 128) return FA_ERR_UNSUPPORTED;
   if (a->seqlen_q == 0 || a->batch == 0) return FA_OK;
   for (int i = 0; i < 3; ++i) {
     if ((a->q_stride[i] % 8) || (a->k_stride[i] % 8) || (a->v_stride[i] % 8) ||
@@ -505,9 +509,8 @@ int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
                               (uint64_t)a->batch};
     const uint64_t str[3] = {(uint64_t)a->q_stride[2] * 2, (uint64_t)a->q_stride[1] * 2,
                              (uint64_t)a->q_stride[0] * 2};
-    const uint32_t box[4] = {64, (uint32_t)G, (uint32_t)(128 / G), 1};
-    if (encode_tmap(&tq, dt, 4, a->q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
-      return FA_ERR_CUDA;
+    const uint32_t box[4] = {64, (uint32_t)G, (uint32_t)(128 / G), 1};  // TPT tokens x G heads
+    FA_TMAP_TRY(encode_tmap(&tq, dt, 4, a->q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   const void* kv_ptr[2] = {a->k, a->v};
   const int64_t* kv_str[2] = {a->k_stride, a->v_stride};
@@ -518,9 +521,7 @@ int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
     const uint64_t str[3] = {(uint64_t)kv_str[w][2] * 2, (uint64_t)kv_str[w][1] * 2,
                              (uint64_t)kv_str[w][0] * 2};
     const uint32_t box[4] = {64, 1, 128, 1};
-    if (encode_tmap(kv_map[w], dt, 4, kv_ptr[w], dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B) !=
-        CUDA_SUCCESS)
-      return FA_ERR_CUDA;
+    FA_TMAP_TRY(encode_tmap(kv_map[w], dt, 4, kv_ptr[w], dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   FwdParams p{};
   p.Sq = a->seqlen_q;
@@ -539,7 +540,7 @@ int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
   p.lse_sb = (int64_t)a->num_heads * a->seqlen_q;
   p.lse_sh = a->seqlen_q;
   p.err = err;
-  const int TPB = NQ * 128 / G;
+  const int TPB = NQ * (128 / G);
   dim3 grid((a->seqlen_q + TPB - 1) / TPB, a->num_heads_k, a->batch);
   switch (D) {
     case 64: return dispatch_dtype<64, 2, false>(a->dtype, tq, tk, tv, p, grid, st);
@@ -553,7 +554,7 @@ int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st) {
   const int D = a->head_dim;
   const int G = a->num_heads / a->num_kv_heads;
   const int NQ = (D == 256) ? 1 : 2;
-  if (128 % G != 0) return FA_ERR_UNSUPPORTED;
+  if (G > 128) return FA_ERR_UNSUPPORTED;
   const int ps = a->page_size;
   if (ps < 8 || (ps & (ps - 1)) != 0) return FA_ERR_UNSUPPORTED;
   if (a->num_tokens == 0 || a->num_seqs == 0) return FA_OK;
@@ -565,9 +566,8 @@ int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st) {
     const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a->num_heads, (uint64_t)a->num_tokens, 1};
     const uint64_t str[3] = {(uint64_t)D * 2, (uint64_t)a->num_heads * D * 2,
                              (uint64_t)a->num_tokens * a->num_heads * D * 2};
-    const uint32_t box[4] = {64, (uint32_t)G, (uint32_t)(128 / G), 1};
-    if (encode_tmap(&tq, dt, 4, a->q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
-      return FA_ERR_CUDA;
+    const uint32_t box[4] = {64, (uint32_t)G, (uint32_t)(128 / G), 1};  // TPT tokens x G heads
+    FA_TMAP_TRY(encode_tmap(&tq, dt, 4, a->q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   const void* kv_ptr[2] = {a->k_cache, a->v_cache};
   CUtensorMap* kv_map[2] = {&tk, &tv};
@@ -577,9 +577,7 @@ int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st) {
     const uint64_t str[3] = {(uint64_t)D * 2, (uint64_t)a->num_kv_heads * D * 2,
                              (uint64_t)ps * a->num_kv_heads * D * 2};
     const uint32_t box[4] = {64, 1, (uint32_t)(ps < 128 ? ps : 128), 1};
-    if (encode_tmap(kv_map[w], dt, 4, kv_ptr[w], dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B) !=
-        CUDA_SUCCESS)
-      return FA_ERR_CUDA;
+    FA_TMAP_TRY(encode_tmap(kv_map[w], dt, 4, kv_ptr[w], dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   FwdParams p{};
   p.H = a->num_heads;
@@ -606,7 +604,7 @@ int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st) {
   p.swq = a->causal ? a->sliding_window_q : 0;
   p.swk = a->causal ? a->sliding_window_k : 0;
   p.err = err;
-  const int TPB = NQ * 128 / G;
+  const int TPB = NQ * (128 / G);
   // Sum over sequences of ceil(q_len / TPB) <= num_tokens / TPB + num_seqs.
   dim3 grid(a->num_tokens / TPB + a->num_seqs, a->num_kv_heads, 1);
   switch (D) {

@@ -40,6 +40,11 @@ inline CUtensorMapDataType tmap_dtype(int dtype) {
 
 int num_sms();
 void count_launch(int n = 1);
+enum { FA_PROF_FWD = 1, FA_PROF_BWD_DKDV = 2, FA_PROF_PAGED = 3, FA_PROF_DECODE = 4 };
+// Records the armed begin/end events around a launch of the given kind (see
+// fa_profile_next_launch); no-ops when nothing is armed.
+void prof_begin(int kind, cudaStream_t st);
+void prof_end(int kind, cudaStream_t st);
 
 int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st);
 int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st);
@@ -51,10 +56,25 @@ int decode_num_splits(const fa_decode_args_t* a);
 int launch_selftest_umma(const void* a, const void* b, float* c, int n, int k, int dtype, int b_mn,
                          int a_tmem, int* err, cudaStream_t st);
 
-#define FA_CUDA_TRY(x)                              \
-  do {                                              \
-    cudaError_t e_ = (x);                           \
-    if (e_ != cudaSuccess) return FA_ERR_CUDA;      \
+// Records the failing call (text, file:line, CUDA error) for fa_last_error_detail().
+void set_error_detail(const char* what, const char* file, int line, const char* err);
+
+#define FA_CUDA_TRY(x)                                                        \
+  do {                                                                        \
+    cudaError_t e_ = (x);                                                     \
+    if (e_ != cudaSuccess) {                                                  \
+      ::fa::set_error_detail(#x, __FILE__, __LINE__, cudaGetErrorString(e_)); \
+      return FA_ERR_CUDA;                                                     \
+    }                                                                         \
+  } while (0)
+
+#define FA_TMAP_TRY(x)                                                        \
+  do {                                                                        \
+    CUresult r_ = (x);                                                        \
+    if (r_ != CUDA_SUCCESS) {                                                 \
+      ::fa::set_error_detail(#x, __FILE__, __LINE__, "cuTensorMapEncodeTiled failed"); \
+      return FA_ERR_CUDA;                                                     \
+    }                                                                         \
   } while (0)
 
 }  // namespace fa

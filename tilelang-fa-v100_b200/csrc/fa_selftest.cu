@@ -127,21 +127,18 @@ int launch_selftest_umma(const void* a, const void* b, float* c, int n, int k, i
     const uint64_t dims[2] = {(uint64_t)k, 128};
     const uint64_t str[1] = {(uint64_t)k * 2};
     const uint32_t box[2] = {64, 128};
-    if (encode_tmap(&ta, dt, 2, a, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
-      return FA_ERR_CUDA;
+    FA_TMAP_TRY(encode_tmap(&ta, dt, 2, a, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   if (!b_mn) {
     const uint64_t dims[2] = {(uint64_t)k, (uint64_t)n};
     const uint64_t str[1] = {(uint64_t)k * 2};
     const uint32_t box[2] = {64, (uint32_t)n};
-    if (encode_tmap(&tb, dt, 2, b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
-      return FA_ERR_CUDA;
+    FA_TMAP_TRY(encode_tmap(&tb, dt, 2, b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
   } else {
     const uint64_t dims[2] = {(uint64_t)n, (uint64_t)k};
     const uint64_t str[1] = {(uint64_t)n * 2};
     const uint32_t box[2] = {64, (uint32_t)k};
-    if (encode_tmap(&tb, dt, 2, b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
-      return FA_ERR_CUDA;
+    FA_TMAP_TRY(encode_tmap(&tb, dt, 2, b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   const int smem = 1024 + 128 * k * 2 + n * k * 2 + 256;
   if (dtype == FA_DTYPE_BF16) {

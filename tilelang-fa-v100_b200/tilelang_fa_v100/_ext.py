@@ -86,9 +86,22 @@ SIGNATURES = {
     "fa_read_device_error": (_i32, [ctypes.POINTER(_i32), ctypes.POINTER(_i32),
                                     ctypes.POINTER(_i32), _i32]),
     "fa_version": (ctypes.c_char_p, []),
+    "fa_last_error_detail": (ctypes.c_char_p, []),
     "fa_launch_count": (_i64, []),
     "fa_selftest_umma": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp]),
+    "fa_profile_next_launch": (_i32, [_i32, _vp, _vp]),
 }
+
+PROF_FWD, PROF_BWD_DKDV, PROF_PAGED, PROF_DECODE = 1, 2, 3, 4
+
+
+def profile_next_launch(kind, ev_begin, ev_end):
+    """Arms torch.cuda.Event pair around the next launch of one main kernel."""
+    for ev in (ev_begin, ev_end):
+        if ev.cuda_event == 0:  # torch creates the CUDA event lazily, on first record
+            ev.record()
+    check(load().fa_profile_next_launch(kind, ctypes.c_void_p(ev_begin.cuda_event),
+                                        ctypes.c_void_p(ev_end.cuda_event)))
 
 
 def lib_path():
@@ -127,7 +140,8 @@ def check(status):
         raise NotImplementedError("libfa_b200: " + msg)
     if status == FA_ERR_INVALID_ARG:
         raise ValueError("libfa_b200: " + msg)
-    raise FaError("libfa_b200 error %d: %s" % (status, msg))
+    detail = load().fa_last_error_detail().decode() if status == FA_ERR_CUDA else ""
+    raise FaError("libfa_b200 error %d: %s%s" % (status, msg, (" (" + detail + ")") if detail else ""))
 
 
 def read_device_error(clear=True):
