@@ -476,6 +476,18 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_profile_case(args):
+    """Small case of the headline kernels for ncu captures: B=2 of configs[2]
+    (q/k/v/dO 67 MB each, 268 MB together > the 126 MB L2), fwd+bwd steps only."""
+    import tilelang_fa_v100 as fa
+    dev = torch.device("cuda", 0)
+    b, s, h, d = 2, CFG["S"], CFG["H"], CFG["D"]
+    ms, kern_ms, launches, _ = time_dense(fa, dev, b, s, h, d, torch.bfloat16, True, args.steps,
+                                          args.warmup, seed=3, profile=True)
+    print(json.dumps({"profile_case": "B2_S4096_H32_D128_bf16_causal", "ms_per_step": ms,
+                      "dkdv_ms": kern_ms, "launches": launches}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -484,10 +496,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--profile-case", action="store_true",
+                    help="small fwd+bwd case for ncu captures (no e2e / CPU / secondary)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
-    if args.impl == "reference":
+    if args.profile_case:
+        run_profile_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
