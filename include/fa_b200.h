@@ -142,6 +142,24 @@ typedef struct {
 size_t fa_decode_workspace_size(const fa_decode_args_t* args);
 int fa_decode(const fa_decode_args_t* args, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Decode that allocates nothing, not even a caller workspace.  No counterpart in the
+ * reference: it exists for callers that cannot hand the library any device memory
+ * at decode time -- e.g. a serving engine that gives all free HBM to its KV-cache
+ * pool and forbids allocations inside a decode step, or a plain C/FFI caller with no
+ * device allocator of its own -- and for latency-critical loops that must not call
+ * cudaMalloc/cudaFree, which can synchronise the device and stall other streams.
+ * Same arguments and results as fa_decode; the split partials go to a fixed
+ * 16 MiB scratch array inside the library (fa_decode_noalloc_scratch_bytes) that
+ * each GPU holds until the process exits.  With num_splits = 0 the split count is
+ * reduced until the partials fit; an explicit num_splits whose partials
+ * (batch * splits * num_heads * (head_dim + 1) * 4 bytes) exceed the scratch is
+ * rejected with FA_ERR_WORKSPACE (fa_last_error_detail says why).  The first call
+ * on a device looks up the scratch's device address, so make that first call
+ * before any stream capture.  All calls share the one array: calls that overlap on
+ * the GPU (different streams, no ordering between them) race on it. */
+int fa_decode_noalloc(const fa_decode_args_t* args, void* stream);
+size_t fa_decode_noalloc_scratch_bytes(void);
+
 /* Diagnostics. */
 const char* fa_status_string(int status);
 /* Reads (and optionally clears) the library's device error word on the current

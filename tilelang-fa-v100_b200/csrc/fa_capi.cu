@@ -272,6 +272,22 @@ int fa_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, void* stream
   return launch_decode(a, ws, ws_bytes, err, static_cast<cudaStream_t>(stream));
 }
 
+int fa_decode_noalloc(const fa_decode_args_t* a, void* stream) {
+  if (a == nullptr || a->q == nullptr || a->k_cache == nullptr || a->v_cache == nullptr ||
+      a->block_table == nullptr || a->seq_lens == nullptr || a->out == nullptr)
+    return FA_ERR_INVALID_ARG;
+  if (a->batch < 0 || a->num_heads <= 0 || a->num_kv_heads <= 0 ||
+      a->num_heads % a->num_kv_heads != 0 || a->num_pages <= 0 || a->max_blocks <= 0 ||
+      a->num_splits < 0)
+    return FA_ERR_INVALID_ARG;
+  if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
+  int* err = nullptr;
+  if (int s = device_setup(&err, static_cast<cudaStream_t>(stream))) return s;
+  return launch_decode_noalloc(a, err, static_cast<cudaStream_t>(stream));
+}
+
+size_t fa_decode_noalloc_scratch_bytes(void) { return decode_noalloc_scratch_bytes(); }
+
 int fa_profile_next_launch(int32_t kind, void* ev_begin, void* ev_end) {
   if (kind < 1 || kind > 4 || ev_begin == nullptr || ev_end == nullptr) return FA_ERR_INVALID_ARG;
   g_prof_kind = kind;

@@ -17,6 +17,8 @@
 #include "fa_ptx.cuh"
 #include "fa_internal.h"
 #include <cmath>
+#include <cstdio>
+#include <mutex>
 
 namespace fa {
 
@@ -476,6 +478,55 @@ int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err
                 : launch_decode_impl<__half, 64>(tk, tv, p, st);
   return bf16 ? launch_decode_impl<__nv_bfloat16, 128>(tk, tv, p, st)
               : launch_decode_impl<__half, 128>(tk, tv, p, st);
+}
+
+// ------------------------------------------------------------------- no-allocation decode
+// Scratch for fa_decode_noalloc: the per-split partial outputs and LSEs live in this
+// fixed device array instead of a caller-provided workspace.  Every GPU that loads the
+// library holds it until the process exits.  In host code the name is only a
+// stand-in for the symbol; its device address comes from cudaGetSymbolAddress.
+constexpr size_t kDecodeStaticScratchBytes = size_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) unsigned char g_decode_scratch[kDecodeStaticScratchBytes];
+
+static std::mutex g_scratch_mu;
+static void* g_scratch_addr[64] = {nullptr};
+
+size_t decode_noalloc_scratch_bytes() { return kDecodeStaticScratchBytes; }
+
+int launch_decode_noalloc(const fa_decode_args_t* a, int* err, cudaStream_t st) {
+  int dev = 0;
+  FA_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return FA_ERR_CUDA;
+  void* scratch = nullptr;
+  {
+    // First call on a device: look up the array's device address with that device
+    // current (the caller's context was bound by the entry point).
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (g_scratch_addr[dev] == nullptr) {
+      void* ptr = nullptr;
+      FA_CUDA_TRY(cudaGetSymbolAddress(&ptr, g_decode_scratch));
+      g_scratch_addr[dev] = ptr;
+    }
+    scratch = g_scratch_addr[dev];
+  }
+  fa_decode_args_t b = *a;
+  if (b.num_splits == 0) {
+    // Heuristic split count, reduced until the partials fit in the static scratch.
+    b.num_splits = decode_num_splits(a);
+    while (b.num_splits > 1 && decode_workspace_bytes(&b) > kDecodeStaticScratchBytes)
+      --b.num_splits;
+  }
+  const size_t need = decode_workspace_bytes(&b);
+  if (need > kDecodeStaticScratchBytes) {
+    char msg[160];
+    snprintf(msg, sizeof(msg), "needs %zu bytes of split scratch, the static scratch holds %zu",
+             need, kDecodeStaticScratchBytes);
+    set_error_detail("fa_decode_noalloc", __FILE__, __LINE__, msg);
+    return FA_ERR_WORKSPACE;
+  }
+  // The partials need no clearing: the combine reads only the splits that the split
+  // kernel wrote for the current call (derived from seq_lens).
+  return launch_decode(&b, scratch, kDecodeStaticScratchBytes, err, st);
 }
 
 }  // namespace fa

@@ -52,6 +52,8 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
 size_t bwd_workspace_bytes(const fa_bwd_args_t* a);
 int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st);
 size_t decode_workspace_bytes(const fa_decode_args_t* a);
+int launch_decode_noalloc(const fa_decode_args_t* a, int* err, cudaStream_t st);
+size_t decode_noalloc_scratch_bytes();
 int decode_num_splits(const fa_decode_args_t* a);
 int launch_selftest_umma(const void* a, const void* b, float* c, int n, int k, int dtype, int b_mn,
                          int a_tmem, int* err, cudaStream_t st);

@@ -82,6 +82,8 @@ SIGNATURES = {
     "fa_paged_prefill": (_i32, [ctypes.POINTER(PagedArgs), _vp]),
     "fa_decode_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(DecodeArgs)]),
     "fa_decode": (_i32, [ctypes.POINTER(DecodeArgs), _vp, ctypes.c_size_t, _vp]),
+    "fa_decode_noalloc": (_i32, [ctypes.POINTER(DecodeArgs), _vp]),
+    "fa_decode_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "fa_status_string": (ctypes.c_char_p, [_i32]),
     "fa_read_device_error": (_i32, [ctypes.POINTER(_i32), ctypes.POINTER(_i32),
                                     ctypes.POINTER(_i32), _i32]),
