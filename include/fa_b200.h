@@ -187,6 +187,13 @@ int fa_profile_next_launch(int32_t kind, void* ev_begin, void* ev_end);
 int fa_selftest_umma(const void* a, const void* b, float* c, int32_t n, int32_t k,
                      int32_t dtype, int32_t b_mn, int32_t a_tmem, void* stream);
 
+/* Diagnostic: tcgen05 MMA throughput.  `ctas` CTAs each issue reps x (k/16)
+ * back-to-back bf16 UMMAs of 128 x n x 16 on shared-memory operands (A from TMEM when
+ * a_tmem = 1; a_mn / b_mn select MN-major layouts); time it with events on `stream`.
+ * Used to justify the tile shapes of the attention kernels. */
+int fa_selftest_umma_rate(int32_t n, int32_t k, int32_t reps, int32_t a_tmem, int32_t a_mn,
+                          int32_t b_mn, int32_t ctas, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -101,6 +101,20 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                "r"(d)
                : "memory");
 }
+// dQaccum[tile] += smem tile (fp32 add in L2 by the TMA unit).
+__device__ __forceinline__ void tma_reduce_add_2d(const void* tmap, uint32_t src, int c0, int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::
+          "l"(reinterpret_cast<uint64_t>(tmap)),
+      "r"(c0), "r"(c1), "r"(src)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity))
@@ -171,8 +185,30 @@ __global__ void __launch_bounds__(256) fa_bwd_dq_convert_kernel(const float* __r
 }
 
 // ---------------------------------------------------------------- 2. dK / dV (+ dQ atomics)
+__device__ __forceinline__ void ld_shared_v4f(uint32_t addr, float* v) {
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
+               : "r"(addr));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// 512 threads = 4 warpgroups.  Launch: 128 registers per thread (65,536).  Warpgroup 0
+// (producer, MMA issuer, 2 idle warps) drops to 56, the other three rise to 152:
+// 128 * 56 + 384 * 152 = 65,536.
+constexpr int kBwdThreads = 512;
+constexpr int kBwdRegLow = 56;
+constexpr int kBwdRegHigh = 152;
+static_assert(128 * kBwdRegLow + 384 * kBwdRegHigh <= 65536, "register split exceeds the launch");
+
 template <typename T, int D, bool ATOMIC_DQ>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v,
@@ -211,7 +247,7 @@ __global__ void __launch_bounds__(384, 1)
     mbar_init(smem_u32(&ctl->p_ready), 256);
     mbar_init(smem_u32(&ctl->ds_ready), 256);
     mbar_init(smem_u32(&ctl->dq_full), 1);
-    mbar_init(smem_u32(&ctl->dq_free), 256);
+    mbar_init(smem_u32(&ctl->dq_free), 128);
     mbar_init(smem_u32(&ctl->final_done), 1);
     mbar_init(smem_u32(&ctl->drain), 1);
     fence_barrier_init();
@@ -226,7 +262,8 @@ __global__ void __launch_bounds__(384, 1)
   const uint32_t tmem = ctl->tmem_base;
   const uint32_t sK = base + Cfg::OFF_K, sV = base + Cfg::OFF_V;
   const uint32_t sDS = base + Cfg::OFF_DS;
-
+  if (warp < 4) {
+    setmaxnreg_dec<kBwdRegLow>();
   if (warp == 0) {
     // ============================================================ producer
     if (lane == 0) {
@@ -246,6 +283,7 @@ __global__ void __launch_bounds__(384, 1)
         if (!mbar_wait(smem_u32(&ctl->st_empty[s]), ((i >> 1) & 1) ^ 1, abort_flag, p.err,
                        FA_SITE_BWD_PRODUCER))
           break;
+        FA_TRACE_EVENT(12, i);
         const int g = i / nqt, qt = t_start + i % nqt, h = hk * p.G + g;
         const uint32_t fb = smem_u32(&ctl->st_full[s]);
         mbar_arrive_expect_tx(fb, 2 * Cfg::TILE + 1024);
@@ -270,6 +308,14 @@ __global__ void __launch_bounds__(384, 1)
       constexpr uint32_t idKV = idesc_f16(128, D, kBf16, false, true);
       constexpr uint32_t idQ = idesc_f16(128, D, kBf16, true, true);
       const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 256 + D;
+      // Descriptors built once (K-major forms for S^T / dP^T, MN-major for the rest).
+      const uint64_t dK_k = sdesc_sw128(sK, 16, 1024), dV_k = sdesc_sw128(sV, 16, 1024);
+      const uint64_t dQ_k0 = sdesc_sw128(base + Cfg::OFF_Q, 16, 1024);
+      const uint64_t ddO_k0 = sdesc_sw128(base + Cfg::OFF_DO, 16, 1024);
+      const uint64_t dQ_m0 = sdesc_sw128(base + Cfg::OFF_Q, Cfg::CHUNK, 1024);
+      const uint64_t ddO_m0 = sdesc_sw128(base + Cfg::OFF_DO, Cfg::CHUNK, 1024);
+      const uint64_t dDS_m = sdesc_sw128(sDS, Cfg::CHUNK, 1024);
+      const uint64_t dK_m = sdesc_sw128(sK, Cfg::CHUNK, 1024);
       bool ok = mbar_wait(smem_u32(&ctl->kv_full), 0, abort_flag, p.err, FA_SITE_BWD_MMA);
       for (int i = 0; i < n_iter && ok; ++i) {
         const int s = i & 1;
@@ -277,64 +323,69 @@ __global__ void __launch_bounds__(384, 1)
         ok = mbar_wait(smem_u32(&ctl->st_full[s]), (i >> 1) & 1, abort_flag, p.err,
                        FA_SITE_BWD_MMA);
         if (!ok) break;
+        FA_TRACE_EVENT(0, i);
         tc_fence_after();
-        const uint32_t sQ = base + Cfg::OFF_Q + s * Cfg::TILE;
-        const uint32_t sdO = base + Cfg::OFF_DO + s * Cfg::TILE;
+        const uint64_t dQk = desc_add(dQ_k0, s * Cfg::TILE), ddOk = desc_add(ddO_k0, s * Cfg::TILE);
+        const uint64_t dQm = desc_add(dQ_m0, s * Cfg::TILE), ddOm = desc_add(ddO_m0, s * Cfg::TILE);
         // S^T = K Q^T
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
-          mma_ss(tS, sdesc_sw128(sK + o, 16, 1024), sdesc_sw128(sQ + o, 16, 1024), idS, kk > 0);
+          mma_ss(tS, desc_add(dK_k, o), desc_add(dQk, o), idS, kk > 0);
         }
         mma_commit(smem_u32(&ctl->s_full));
-        // dP^T = V dO^T into [128, 256): the previous dQ must have been read out.
+        FA_TRACE_EVENT(1, i);
+        // dP^T = V dO^T into [128, 256): the previous dQ must have left TMEM.
         if (ATOMIC_DQ && i > 0) {
           ok = mbar_wait(smem_u32(&ctl->dq_free), (i - 1) & 1, abort_flag, p.err, FA_SITE_BWD_MMA);
           if (!ok) break;
           tc_fence_after();
         }
+        FA_TRACE_EVENT(2, i);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
-          mma_ss(tdP, sdesc_sw128(sV + o, 16, 1024), sdesc_sw128(sdO + o, 16, 1024), idS, kk > 0);
+          mma_ss(tdP, desc_add(dV_k, o), desc_add(ddOk, o), idS, kk > 0);
         }
         mma_commit(smem_u32(&ctl->dp_full));
         // dV += P^T dO   (P^T for q 0..63 in columns 0..31, q 64..127 in 64..95)
         ok = mbar_wait(smem_u32(&ctl->p_ready), par, abort_flag, p.err, FA_SITE_BWD_MMA);
         if (!ok) break;
+        FA_TRACE_EVENT(3, i);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t acol = (kk < 4) ? kk * 8 : 64 + (kk - 4) * 8;
-          mma_ts(tdV, tS + acol, sdesc_sw128(sdO + kk * 2048, Cfg::CHUNK, 1024), idKV,
-                 (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tdV, tS + acol, desc_add(ddOm, kk * 2048), idKV, (i > 0 || kk > 0) ? 1u : 0u);
         }
         // dK += dS^T Q   (dS^T in columns 32..63 and 96..127)
         ok = mbar_wait(smem_u32(&ctl->ds_ready), par, abort_flag, p.err, FA_SITE_BWD_MMA);
         if (!ok) break;
+        FA_TRACE_EVENT(4, i);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t acol = (kk < 4) ? 32 + kk * 8 : 96 + (kk - 4) * 8;
-          mma_ts(tdK, tS + acol, sdesc_sw128(sQ + kk * 2048, Cfg::CHUNK, 1024), idKV,
-                 (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tdK, tS + acol, desc_add(dQm, kk * 2048), idKV, (i > 0 || kk > 0) ? 1u : 0u);
         }
         if (ATOMIC_DQ) {
           // dQ = dS K  (A = dS MN-major from smem, B = K MN-major) into [128, 128 + D)
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            mma_ss(tdP, sdesc_sw128(sDS + kk * 2048, Cfg::CHUNK, 1024),
-                   sdesc_sw128(sK + kk * 2048, Cfg::CHUNK, 1024), idQ, kk > 0);
+            mma_ss(tdP, desc_add(dDS_m, kk * 2048), desc_add(dK_m, kk * 2048), idQ, kk > 0);
           mma_commit(smem_u32(&ctl->dq_full));
         }
         mma_commit(smem_u32(&ctl->st_empty[s]));
+        FA_TRACE_EVENT(5, i);
       }
       mma_commit(smem_u32(&ctl->final_done));
       mma_commit(smem_u32(&ctl->drain));
       drain_wait(smem_u32(&ctl->drain), 0);
     }
-  } else if (warp >= 4) {
+  }
+  } else if (warp < 12) {
     // ============================================================ compute warpgroups
+    setmaxnreg_inc<kBwdRegHigh>();
     const int c = (warp - 4) >> 2;              // query-column half
     const int j = ((warp & 3) << 5) | lane;     // key row = TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
@@ -346,30 +397,43 @@ __global__ void __launch_bounds__(384, 1)
     for (int i = 0; i < n_iter; ++i) {
       const int s = i & 1;
       const uint32_t par = i & 1;
-      const int g = i / nqt, qt = t_start + i % nqt, h = hk * p.G + g;
+      const int qt = t_start + i % nqt;
       const int q0 = qt * kBwdBM;
-      const float* sLse = reinterpret_cast<const float*>(base_ptr + Cfg::OFF_LSE + s * 512) + 64 * c;
-      const float* sDi = reinterpret_cast<const float*>(base_ptr + Cfg::OFF_DI + s * 512) + 64 * c;
+      const uint32_t lse_a = base + Cfg::OFF_LSE + s * 512 + 64 * c * 4;
+      const uint32_t di_a = base + Cfg::OFF_DI + s * 512 + 64 * c * 4;
       bool w = mbar_wait(smem_u32(&ctl->st_full[s]), (i >> 1) & 1, abort_flag, p.err,
                          FA_SITE_BWD_COMPUTE);
       w = w && mbar_wait(smem_u32(&ctl->s_full), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
       ok = __all_sync(0xffffffffu, w);
       if (!ok) break;
+      if (threadIdx.x == 128) FA_TRACE_EVENT(6, i);
       tc_fence_after();
-      // ---- pass A: P^T = exp2(S^T * scale*log2e - lse*log2e), masked
+      // ---- pass A: P^T = exp2(S^T * scale*log2e - lse*log2e), masked; 32 columns at a time
+      const int qbase = q0 + 64 * c;
+      const bool full = key_ok && (!p.causal || key <= qbase + off);
       float pv[64];
-      {
-        uint32_t sv[64];
-        tmem_ld32(tS + 64 * c, sv);
-        tmem_ld32(tS + 64 * c + 32, sv + 32);
-        tmem_wait_ld();
-        const int qbase = q0 + 64 * c;
-        const bool full = key_ok && (!p.causal || key <= qbase + off);
 #pragma unroll
-        for (int x = 0; x < 64; ++x) {
-          const bool vis = full || (key_ok && key <= qbase + x + off);
-          pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -sLse[x])) : 0.f;
+      for (int ch = 0; ch < 2; ++ch) {
+        uint32_t sv[32];
+        tmem_ld32(tS + 64 * c + 32 * ch, sv);
+        float lv[32];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) ld_shared_v4f(lse_a + (32 * ch + 4 * m) * 4, lv + 4 * m);
+        tmem_wait_ld();
+        if (full) {
+#pragma unroll
+          for (int x = 0; x < 32; ++x)
+            pv[32 * ch + x] = ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lv[x]));
+        } else {
+#pragma unroll
+          for (int x = 0; x < 32; ++x) {
+            const bool vis = key_ok && key <= qbase + 32 * ch + x + off;
+            pv[32 * ch + x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lv[x])) : 0.f;
+          }
         }
+      }
+      if (threadIdx.x == 128) FA_TRACE_EVENT(14, i);
+      {
         uint32_t pk[32];
 #pragma unroll
         for (int x = 0; x < 32; ++x) pk[x] = Pack2<T>::pack(pv[2 * x], pv[2 * x + 1]);
@@ -378,22 +442,27 @@ __global__ void __launch_bounds__(384, 1)
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl->p_ready));
+      if (threadIdx.x == 128) FA_TRACE_EVENT(7, i);
       // ---- pass B: dS^T = P^T (dP^T - D) * scale
       w = mbar_wait(smem_u32(&ctl->dp_full), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
       ok = __all_sync(0xffffffffu, w);
       if (!ok) break;
+      if (threadIdx.x == 128) FA_TRACE_EVENT(8, i);
       tc_fence_after();
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         uint32_t dv[32];
         tmem_ld32(tdP + 64 * c + 32 * hf, dv);
+        float di[32];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) ld_shared_v4f(di_a + (32 * hf + 4 * m) * 4, di + 4 * m);
         tmem_wait_ld();
         uint32_t pk[16];
 #pragma unroll
         for (int x = 0; x < 16; ++x) {
           const int xx = 32 * hf + 2 * x;
-          const float d0 = pv[xx] * (__uint_as_float(dv[2 * x]) - sDi[xx]) * p.scale;
-          const float d1 = pv[xx + 1] * (__uint_as_float(dv[2 * x + 1]) - sDi[xx + 1]) * p.scale;
+          const float d0 = pv[xx] * (__uint_as_float(dv[2 * x]) - di[2 * x]) * p.scale;
+          const float d1 = pv[xx + 1] * (__uint_as_float(dv[2 * x + 1]) - di[2 * x + 1]) * p.scale;
           pk[x] = Pack2<T>::pack(d0, d1);
         }
         tmem_st16(tS + 64 * c + 32 + 16 * hf, pk);
@@ -410,27 +479,7 @@ __global__ void __launch_bounds__(384, 1)
       if (ATOMIC_DQ) fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl->ds_ready));
-      if (ATOMIC_DQ) {
-        // ---- dQ rows (lane = query row) -> fp32 accumulator
-        w = mbar_wait(smem_u32(&ctl->dq_full), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
-        ok = __all_sync(0xffffffffu, w);
-        if (!ok) break;
-        tc_fence_after();
-        float* acc = p.dq_acc + (((int64_t)b * p.H + h) * p.Sq_pad + q0 + j) * D + c * (D / 2);
-#pragma unroll
-        for (int c0 = 0; c0 < D / 2; c0 += 32) {
-          uint32_t v[32];
-          tmem_ld32(tdP + c * (D / 2) + c0, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int x = 0; x < 32; x += 4)
-            atomicAdd(reinterpret_cast<float4*>(acc + c0 + x),
-                      make_float4(__uint_as_float(v[x]), __uint_as_float(v[x + 1]),
-                                  __uint_as_float(v[x + 2]), __uint_as_float(v[x + 3])));
-        }
-        tc_fence_before();
-        mbar_arrive(smem_u32(&ctl->dq_free));
-      }
+      if (threadIdx.x == 128) FA_TRACE_EVENT(9, i);
     }
     // ---- dK, dV rows (lane = key row)
     if (ok) {
@@ -468,6 +517,42 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
       }
+    }
+  } else {
+    setmaxnreg_inc<kBwdRegHigh>();
+    if (ATOMIC_DQ) {
+    // ============================================================ dQ warpgroup
+    // Moves each query tile's dQ (lane = query row) out of TMEM, frees the columns for
+    // the next dP^T at once, then adds it to the fp32 accumulator with vector atomics
+    // while the compute warpgroups already work on the next tile.
+    const int r = ((warp & 3) << 5) | lane;
+    const uint32_t tdP = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + 128;
+    for (int i = 0; i < n_iter; ++i) {
+      const int g = i / nqt, qt = t_start + i % nqt, h = hk * p.G + g;
+      bool w = mbar_wait(smem_u32(&ctl->dq_full), i & 1, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+      if (!__all_sync(0xffffffffu, w)) break;
+      if (threadIdx.x == 384) FA_TRACE_EVENT(10, i);
+      tc_fence_after();
+      float* acc = p.dq_acc + (((int64_t)b * p.H + h) * p.Sq_pad + qt * kBwdBM + r) * D;
+      // 64 columns at a time; the TMEM columns are released after the last load.
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 64) {
+        uint32_t v[64];
+        tmem_ld32(tdP + c0, v);
+        tmem_ld32(tdP + c0 + 32, v + 32);
+        tmem_wait_ld();
+        if (c0 + 64 == D) {
+          tc_fence_before();
+          mbar_arrive(smem_u32(&ctl->dq_free));
+        }
+#pragma unroll
+        for (int x = 0; x < 64; x += 4)
+          atomicAdd(reinterpret_cast<float4*>(acc + c0 + x),
+                    make_float4(__uint_as_float(v[x]), __uint_as_float(v[x + 1]),
+                                __uint_as_float(v[x + 2]), __uint_as_float(v[x + 3])));
+      }
+      if (threadIdx.x == 384) FA_TRACE_EVENT(11, i);
+    }
     }
   }
   tc_fence_before();
@@ -588,23 +673,29 @@ __global__ void __launch_bounds__(384, 1)
       constexpr uint32_t idS = idesc_f16(128, 128, kBf16, false, false);
       constexpr uint32_t idQ = idesc_f16(128, D, kBf16, false, true);
       const uint32_t tS = tmem, tdP = tmem + 128, tdQ = tmem + 256;
+      const uint64_t dQd = sdesc_sw128(sQ, 16, 1024), ddOd = sdesc_sw128(sdO, 16, 1024);
+      const uint64_t dKV_k0 = sdesc_sw128(base + Cfg::OFF_KV, 16, 1024);
+      const uint64_t dKV_m0 = sdesc_sw128(base + Cfg::OFF_KV, Cfg::CHUNK, 1024);
+      const uint64_t dDS_k = sdesc_sw128(sDS, 16, 1024);
       bool ok = mbar_wait(smem_u32(&ctl->q_full), 0, abort_flag, p.err, FA_SITE_BWD_MMA);
       for (int j = 0; j < nkv && ok; ++j) {
         const int s = j % ST;
         ok = mbar_wait(smem_u32(&ctl->kv_full[s]), (j / ST) & 1, abort_flag, p.err, FA_SITE_BWD_MMA);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t sKt = base + Cfg::OFF_KV + s * 2 * Cfg::TILE, sVt = sKt + Cfg::TILE;
+        const uint64_t dKk = desc_add(dKV_k0, s * 2 * Cfg::TILE);
+        const uint64_t dVk = desc_add(dKV_k0, s * 2 * Cfg::TILE + Cfg::TILE);
+        const uint64_t dKm = desc_add(dKV_m0, s * 2 * Cfg::TILE);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
-          mma_ss(tS, sdesc_sw128(sQ + o, 16, 1024), sdesc_sw128(sKt + o, 16, 1024), idS, kk > 0);
+          mma_ss(tS, desc_add(dQd, o), desc_add(dKk, o), idS, kk > 0);
         }
         mma_commit(smem_u32(&ctl->s_full));
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
-          mma_ss(tdP, sdesc_sw128(sdO + o, 16, 1024), sdesc_sw128(sVt + o, 16, 1024), idS, kk > 0);
+          mma_ss(tdP, desc_add(ddOd, o), desc_add(dVk, o), idS, kk > 0);
         }
         mma_commit(smem_u32(&ctl->dp_full));
         ok = mbar_wait(smem_u32(&ctl->ds_ready), j & 1, abort_flag, p.err, FA_SITE_BWD_MMA);
@@ -613,8 +704,8 @@ __global__ void __launch_bounds__(384, 1)
         // dQ += dS K: A = dS K-major from smem ([2 key chunks][128 q][64 keys]), B = K MN-major
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_ss(tdQ, sdesc_sw128(sDS + (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32, 16, 1024),
-                 sdesc_sw128(sKt + kk * 2048, Cfg::CHUNK, 1024), idQ, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_ss(tdQ, desc_add(dDS_k, (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32),
+                 desc_add(dKm, kk * 2048), idQ, (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit(smem_u32(&ctl->kv_empty[s]));
       }
       mma_commit(smem_u32(&ctl->final_done));
@@ -756,7 +847,7 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
     }
     dim3 grid((a->seqlen_k + kBwdBN - 1) / kBwdBN, a->num_heads_k, a->batch);
     prof_begin(FA_PROF_BWD_DKDV, st);
-    kern<<<grid, 384, BwdCfg<D>::SMEM_BYTES, st>>>(tq, tk, tv, tdo, p);
+    kern<<<grid, kBwdThreads, BwdCfg<D>::SMEM_BYTES, st>>>(tq, tk, tv, tdo, p);
     prof_end(FA_PROF_BWD_DKDV, st);
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
@@ -778,7 +869,9 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
       attr[dev] = true;
     }
     dim3 grid((a->seqlen_k + kBwdBN - 1) / kBwdBN, a->num_heads_k, a->batch);
-    kern<<<grid, 384, BwdCfg<D>::SMEM_BYTES, st>>>(tq, tk, tv, tdo, p);
+    prof_begin(FA_PROF_BWD_DKDV, st);
+    kern<<<grid, kBwdThreads, BwdCfg<D>::SMEM_BYTES, st>>>(tq, tk, tv, tdo, p);
+    prof_end(FA_PROF_BWD_DKDV, st);
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
     dim3 gq((a->seqlen_q + kBwdBM - 1) / kBwdBM, a->num_heads, a->batch);
@@ -868,3 +961,18 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
 }
 
 }  // namespace fa
+
+#ifdef FA_TRACE
+// Diagnostic build only: copies (and clears) the backward kernel's phase trace.
+extern "C" int fa_debug_trace_read(unsigned long long* dst, size_t n) {
+  using namespace fa;
+  const size_t total = sizeof(g_fa_trace) / sizeof(unsigned long long);
+  if (n > total) n = total;
+  if (cudaDeviceSynchronize() != cudaSuccess) return FA_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(dst, g_fa_trace, n * sizeof(unsigned long long)) != cudaSuccess)
+    return FA_ERR_CUDA;
+  static unsigned long long zeros[FA_TRACE_CTAS * FA_TRACE_EVENTS * FA_TRACE_ITERS];
+  if (cudaMemcpyToSymbol(g_fa_trace, zeros, sizeof(zeros)) != cudaSuccess) return FA_ERR_CUDA;
+  return FA_OK;
+}
+#endif

@@ -13,6 +13,7 @@ namespace fa {
 // Device error word: [0] code (0 = none, 1 = bounded wait expired), [1] site, [2] block.
 __device__ int g_fa_device_error[4];
 
+
 static std::mutex g_mu;
 static int* g_err_ptr[64] = {nullptr};
 static int g_sm_count[64] = {0};
@@ -31,11 +32,17 @@ void set_error_detail(const char* what, const char* file, int line, const char* 
 static int g_prof_kind = 0;
 static cudaEvent_t g_prof_begin = nullptr, g_prof_end = nullptr;
 void prof_begin(int kind, cudaStream_t st) {
-  if (g_prof_kind == kind && g_prof_begin != nullptr) cudaEventRecord(g_prof_begin, st);
+  if (g_prof_kind == kind && g_prof_begin != nullptr) {
+    if (cudaEventRecord(g_prof_begin, st) != cudaSuccess) {
+      (void)cudaGetLastError();  // a stale or foreign event: drop the request
+      g_prof_kind = 0;
+      g_prof_begin = g_prof_end = nullptr;
+    }
+  }
 }
 void prof_end(int kind, cudaStream_t st) {
   if (g_prof_kind == kind && g_prof_end != nullptr) {
-    cudaEventRecord(g_prof_end, st);
+    if (cudaEventRecord(g_prof_end, st) != cudaSuccess) (void)cudaGetLastError();
     g_prof_kind = 0;
     g_prof_begin = g_prof_end = nullptr;
   }
@@ -168,6 +175,8 @@ const char* fa_version(void) { return "fa_b200 1.0.0 (sm_100a)"; }
 
 const char* fa_last_error_detail(void) { return g_err_detail; }
 
+
+
 int64_t fa_launch_count(void) { return g_launches.load(); }
 
 const char* fa_status_string(int status) {
@@ -287,6 +296,14 @@ int fa_decode_noalloc(const fa_decode_args_t* a, void* stream) {
 }
 
 size_t fa_decode_noalloc_scratch_bytes(void) { return decode_noalloc_scratch_bytes(); }
+
+int fa_selftest_umma_rate(int32_t n, int32_t k, int32_t reps, int32_t a_tmem, int32_t a_mn,
+                          int32_t b_mn, int32_t ctas, void* stream) {
+  int* err = nullptr;
+  if (int s = device_setup(&err, static_cast<cudaStream_t>(stream))) return s;
+  return launch_umma_rate(n, k, reps, a_tmem, a_mn, b_mn, ctas, err,
+                          static_cast<cudaStream_t>(stream));
+}
 
 int fa_profile_next_launch(int32_t kind, void* ev_begin, void* ev_end) {
   if (kind < 1 || kind > 4 || ev_begin == nullptr || ev_end == nullptr) return FA_ERR_INVALID_ARG;

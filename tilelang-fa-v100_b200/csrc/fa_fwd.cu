@@ -236,26 +236,28 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
       constexpr uint32_t idPV = idesc_f16(128, D, kBf16, false, true);
       bool ok = mbar_wait(smem_u32(&ctl->q_full), 0, abort_flag, p.err, FA_SITE_FWD_MMA);
       tc_fence_after();
+      // Descriptors: built once; per slot / per K step they are base + constant.
+      const uint64_t q_desc0 = sdesc_sw128(sQ, 16, 1024);            // K-major Q tiles
+      const uint64_t k_desc0 = sdesc_sw128(sKV, 16, 1024);           // K-major K in slot 0
+      const uint64_t v_desc0 = sdesc_sw128(sKV, Cfg::CHUNK_BYTES, 1024);  // MN-major V, slot 0
       // S_t = Q_t K^T over D in steps of 16 (K-major, 128-byte swizzle: step = +32 B
       // inside a 64-column chunk, next chunk at +16 KB).
       auto issue_S = [&](int t, int slot) {
-        const uint32_t qa = sQ + t * Cfg::TILE_BYTES;
-        const uint32_t ka = sKV + slot * Cfg::TILE_BYTES;
+        const uint64_t qa = desc_add(q_desc0, t * Cfg::TILE_BYTES);
+        const uint64_t ka = desc_add(k_desc0, slot * Cfg::TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK_BYTES + (kk & 3) * 32;
-          mma_ss(tmem + t * 128, sdesc_sw128(qa + o, 16, 1024), sdesc_sw128(ka + o, 16, 1024),
-                 idS, kk > 0 ? 1u : 0u);
+          mma_ss(tmem + t * 128, desc_add(qa, o), desc_add(ka, o), idS, kk > 0 ? 1u : 0u);
         }
       };
       // O_t += P_t V over 128 keys in steps of 16 (V MN-major: step = 16 rows = +2 KB,
       // 64-column chunks of D at +16 KB = LBO).
       auto issue_PV = [&](int t, int slot, bool acc) {
-        const uint32_t va = sKV + slot * Cfg::TILE_BYTES;
+        const uint64_t va = desc_add(v_desc0, slot * Cfg::TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < kFwdBN / 16; ++kk) {
-          mma_ts(tmem + NQ * 128 + t * D, tmem + t * 128 + kk * 8,
-                 sdesc_sw128(va + kk * 2048, Cfg::CHUNK_BYTES, 1024), idPV,
+          mma_ts(tmem + NQ * 128 + t * D, tmem + t * 128 + kk * 8, desc_add(va, kk * 2048), idPV,
                  (acc || kk > 0) ? 1u : 0u);
         }
       };
@@ -287,6 +289,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
         for (int t = 0; t < NQ && ok; ++t) {
           ok = mbar_wait(smem_u32(&ctl->p_ready[t]), jj & 1, abort_flag, p.err, FA_SITE_FWD_MMA);
           if (!ok) break;
+          FA_TRACE_EVENT(8 * t + 6, jj);
           tc_fence_after();
           issue_PV(t, sv, jj > 0);
           if (has_next) {
@@ -299,6 +302,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
             issue_S(t, sk);
             mma_commit(smem_u32(&ctl->s_full[t]));
           }
+          FA_TRACE_EVENT(8 * t + 7, jj);
         }
         if (!ok) break;
         mma_commit(smem_u32(&ctl->kv_empty[sv]));
@@ -328,10 +332,13 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
 
     for (int jj = 0; jj < nkv; ++jj) {
       const int j = j0 + jj;
+      const bool tr = (threadIdx.x & 127) == 0;  // first thread of each softmax warpgroup
+      if (tr) FA_TRACE_EVENT(8 * t + 0, jj);
       bool w_ok = mbar_wait(smem_u32(&ctl->s_full[t]), jj & 1, abort_flag, p.err,
                             FA_SITE_FWD_SOFTMAX);
       ok = __all_sync(0xffffffffu, w_ok);
       if (!ok) break;
+      if (tr) FA_TRACE_EVENT(8 * t + 1, jj);
       tc_fence_after();
       uint32_t s[128];
       tmem_ld32(tS + 0, s);
@@ -339,6 +346,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
       tmem_ld32(tS + 64, s + 64);
       tmem_ld32(tS + 96, s + 96);
       tmem_wait_ld();
+      if (tr) FA_TRACE_EVENT(8 * t + 2, jj);
       const int key0 = j * kFwdBN;
       const bool need_mask =
           (key0 + kFwdBN > kv_len) || (p.causal && (key0 + kFwdBN - 1 > limit)) || window;
@@ -362,6 +370,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
       for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
       const float m_new = fmaxf(m_run, mx);
       m_run = m_new;
+      if (tr) FA_TRACE_EVENT(8 * t + 3, jj);
       bool rescale_o = false;
       float factor = 1.f;
       if (jj == 0) {
@@ -389,6 +398,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
         pk[c] = Pack2<T>::pack(p0, p1);
       }
       l += rs0 + rs1;
+      if (tr) FA_TRACE_EVENT(8 * t + 4, jj);
       tmem_st32(tS + 0, pk);
       tmem_st32(tS + 32, pk + 32);
       if (rescale_o) {
@@ -406,6 +416,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl->p_ready[t]));
+      if (tr) FA_TRACE_EVENT(8 * t + 5, jj);
     }
 
     // ---------------------------------------------------------- epilogue
@@ -616,3 +627,18 @@ int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st) {
 }
 
 }  // namespace fa
+
+#ifdef FA_TRACE
+// Diagnostic build only: copies (and clears) the forward kernel's phase trace.
+extern "C" int fa_debug_trace_read_fwd(unsigned long long* dst, size_t n) {
+  using namespace fa;
+  const size_t total = sizeof(g_fa_trace) / sizeof(unsigned long long);
+  if (n > total) n = total;
+  if (cudaDeviceSynchronize() != cudaSuccess) return FA_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(dst, g_fa_trace, n * sizeof(unsigned long long)) != cudaSuccess)
+    return FA_ERR_CUDA;
+  static unsigned long long zeros[FA_TRACE_CTAS * FA_TRACE_EVENTS * FA_TRACE_ITERS];
+  if (cudaMemcpyToSymbol(g_fa_trace, zeros, sizeof(zeros)) != cudaSuccess) return FA_ERR_CUDA;
+  return FA_OK;
+}
+#endif

@@ -55,6 +55,8 @@ size_t decode_workspace_bytes(const fa_decode_args_t* a);
 int launch_decode_noalloc(const fa_decode_args_t* a, int* err, cudaStream_t st);
 size_t decode_noalloc_scratch_bytes();
 int decode_num_splits(const fa_decode_args_t* a);
+int launch_umma_rate(int n, int k, int reps, int a_tmem, int a_mn, int b_mn, int ctas, int* err,
+                     cudaStream_t st);
 int launch_selftest_umma(const void* a, const void* b, float* c, int n, int k, int dtype, int b_mn,
                          int a_tmem, int* err, cudaStream_t st);
 

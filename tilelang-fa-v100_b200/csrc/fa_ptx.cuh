@@ -155,15 +155,18 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-// D[tmem] (+)= A[smem desc] * B[smem desc]
+// D[tmem] (+)= A[smem desc] * B[smem desc].  The issuing thread is on the critical
+// path of every attention kernel, so descriptors are built once per tile and the
+// per-K-step ones are base + constant (desc_add); no compiler memory clobber here --
+// ordering against other async tcgen05 work comes from volatile issue order and the
+// mbarrier / commit protocol.
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                        uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 // D[tmem] (+)= A[tmem] * B[smem desc]
 __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
@@ -172,8 +175,12 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+// Descriptor of a sub-tile `byte_off` bytes past the one `d` describes (the start
+// address field holds addr >> 4 in its low 14 bits; shared addresses stay < 256 KB).
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t byte_off) {
+  return d + static_cast<uint64_t>(byte_off >> 4);
 }
 // Arrive (once) on `bar` when every tcgen05 async op issued so far by this thread completes.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
@@ -257,6 +264,27 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool a
          ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
+
+// ---------------------------------------------------------------- tracing
+// Compiled in only with -DFA_TRACE (a separate diagnostic build): records
+// %globaltimer at named phases of the first FA_TRACE_CTAS CTAs so the pipeline's
+// per-phase latencies can be read back with fa_debug_trace_read().
+#ifdef FA_TRACE
+constexpr int FA_TRACE_CTAS = 2, FA_TRACE_EVENTS = 16, FA_TRACE_ITERS = 64;
+// One copy per translation unit (no relocatable device code); the unit that traces
+// also exports the reader.
+static __device__ unsigned long long g_fa_trace[FA_TRACE_CTAS][FA_TRACE_EVENTS][FA_TRACE_ITERS];
+#define FA_TRACE_EVENT(ev, it)                                                              \
+  do {                                                                                      \
+    const unsigned cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);   \
+    if (cta_ < (unsigned)FA_TRACE_CTAS && (it) < FA_TRACE_ITERS)                            \
+      g_fa_trace[cta_][(ev)][(it)] = ::fa::globaltimer_ns();                                \
+  } while (0)
+#else
+#define FA_TRACE_EVENT(ev, it) \
+  do {                         \
+  } while (0)
+#endif
 
 // ---------------------------------------------------------------- misc math
 __device__ __forceinline__ float ex2_approx(float x) {

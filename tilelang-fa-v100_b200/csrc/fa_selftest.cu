@@ -155,4 +155,87 @@ int launch_selftest_umma(const void* a, const void* b, float* c, int n, int k, i
   return FA_OK;
 }
 
+
+// Throughput probe: every CTA issues `reps` x (K/16) back-to-back UMMAs of 128 x N x 16
+// on operands already in shared memory (contents irrelevant: zero-filled), then commits
+// once.  Forms: A_TMEM (A from TMEM), A_MN / B_MN (MN-major smem operands).  All
+// descriptors are computed before the timed loop, so the loop is issue-lean.
+template <bool A_TMEM, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(128, 1)
+    fa_umma_rate_kernel(int N, int K, int reps, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+  const uint32_t sA = base, sB = base + 128 * K * 2;
+  SelftestCtl* ctl = reinterpret_cast<SelftestCtl*>(base_ptr + 128 * K * 2 + N * K * 2);
+  const int warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < (128 * K + N * K) / 8; i += blockDim.x)
+    reinterpret_cast<uint4*>(base_ptr)[i] = make_uint4(0, 0, 0, 0);
+  if (threadIdx.x == 0) {
+    ctl->abort_flag = 0;
+    mbar_init(smem_u32(&ctl->mma_bar), 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), 512);
+    tmem_relinquish();
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  if (threadIdx.x == 0) {
+    const uint32_t idesc = idesc_f16(128, N, true, A_MN, B_MN);
+    uint64_t ad[8], bd[8];
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      bd[kk] = B_MN ? sdesc_sw128(sB + kk * 2048, K * 128, 1024)
+                    : sdesc_sw128(sB + (kk >> 2) * N * 128 + (kk & 3) * 32, 16, 1024);
+      ad[kk] = A_MN ? sdesc_sw128(sA + kk * 2048, K * 128, 1024)
+                    : sdesc_sw128(sA + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
+    }
+    for (int r = 0; r < reps; ++r) {
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        if (A_TMEM)
+          mma_ts(tmem, tmem + 256 + kk * 8, bd[kk], idesc, 1);
+        else
+          mma_ss(tmem, ad[kk], bd[kk], idesc, 1);
+      }
+    }
+    mma_commit(smem_u32(&ctl->mma_bar));
+  }
+  bool done = mbar_wait(smem_u32(&ctl->mma_bar), 0, &ctl->abort_flag, err, FA_SITE_SELFTEST);
+  (void)done;
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <bool AT, bool AM, bool BM>
+static int launch_rate_t(int n, int k, int reps, int ctas, int* err, cudaStream_t st) {
+  const int smem = 1024 + 128 * k * 2 + n * k * 2 + 256;
+  FA_CUDA_TRY(cudaFuncSetAttribute(fa_umma_rate_kernel<AT, AM, BM>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  fa_umma_rate_kernel<AT, AM, BM><<<ctas, 128, smem, st>>>(n, k, reps, err);
+  FA_CUDA_TRY(cudaGetLastError());
+  count_launch();
+  return FA_OK;
+}
+
+int launch_umma_rate(int n, int k, int reps, int a_tmem, int a_mn, int b_mn, int ctas, int* err,
+                     cudaStream_t st) {
+  if (!(n == 64 || n == 128 || n == 256) || k != 128 || reps < 1) return FA_ERR_UNSUPPORTED;
+  if (a_tmem) return b_mn ? launch_rate_t<true, false, true>(n, k, reps, ctas, err, st)
+                          : launch_rate_t<true, false, false>(n, k, reps, ctas, err, st);
+  if (a_mn) return launch_rate_t<false, true, true>(n, k, reps, ctas, err, st);
+  return b_mn ? launch_rate_t<false, false, true>(n, k, reps, ctas, err, st)
+              : launch_rate_t<false, false, false>(n, k, reps, ctas, err, st);
+}
+
 }  // namespace fa

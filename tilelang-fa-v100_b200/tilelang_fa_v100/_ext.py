@@ -92,6 +92,7 @@ SIGNATURES = {
     "fa_launch_count": (_i64, []),
     "fa_selftest_umma": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp]),
     "fa_profile_next_launch": (_i32, [_i32, _vp, _vp]),
+    "fa_selftest_umma_rate": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp]),
 }
 
 PROF_FWD, PROF_BWD_DKDV, PROF_PAGED, PROF_DECODE = 1, 2, 3, 4
