@@ -200,12 +200,14 @@ __device__ __forceinline__ void setmaxnreg_dec() {
 }
 
 // 512 threads = 4 warpgroups.  Launch: 128 registers per thread (65,536).  Warpgroup 0
-// (producer, MMA issuer, 2 idle warps) drops to 56, the other three rise to 152:
-// 128 * 56 + 384 * 152 = 65,536.
+// (producer, MMA issuer, 2 idle warps) and warpgroup 3 (dQ) drop, the two compute
+// warpgroups rise; the split is sized by ptxas spill reports (none at these values).
 constexpr int kBwdThreads = 512;
-constexpr int kBwdRegLow = 56;
-constexpr int kBwdRegHigh = 152;
-static_assert(128 * kBwdRegLow + 384 * kBwdRegHigh <= 65536, "register split exceeds the launch");
+constexpr int kBwdRegLow = 104;
+constexpr int kBwdRegDq = 112;
+constexpr int kBwdRegHigh = 144;
+static_assert(128 * kBwdRegLow + 256 * kBwdRegHigh + 128 * kBwdRegDq <= 65536,
+              "register split exceeds the launch");
 
 template <typename T, int D, bool ATOMIC_DQ>
 __global__ void __launch_bounds__(kBwdThreads, 1)
@@ -519,7 +521,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
   } else {
-    setmaxnreg_inc<kBwdRegHigh>();
+    setmaxnreg_dec<kBwdRegDq>();
     if (ATOMIC_DQ) {
     // ============================================================ dQ warpgroup
     // Moves each query tile's dQ (lane = query row) out of TMEM, frees the columns for
@@ -822,6 +824,22 @@ static int set_smem(K kern, int bytes) {
   return FA_OK;
 }
 
+// setmaxnreg.inc waits until the block's own launch allocation can supply the raised
+// count, so a split whose total exceeds (registers per thread at launch) x threads
+// would never proceed.  Checked against the compiled kernel before every first launch.
+template <typename K>
+static int check_reg_split(K kern, int threads, int needed_total) {
+  cudaFuncAttributes fa_attr;
+  FA_CUDA_TRY(cudaFuncGetAttributes(&fa_attr, kern));
+  if (fa_attr.numRegs * threads < needed_total) {
+    set_error_detail("register split", __FILE__, __LINE__,
+                     "setmaxnreg split exceeds the kernel's launch register allocation");
+    return FA_ERR_CUDA;
+  }
+  return FA_OK;
+}
+constexpr int kBwdRegTotal = 128 * kBwdRegLow + 256 * kBwdRegHigh + 128 * kBwdRegDq;
+
 template <typename T, int D>
 static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const CUtensorMap& tk,
                            const CUtensorMap& tv, const CUtensorMap& tdo, BwdParams& p,
@@ -842,6 +860,7 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
     int dev = 0;
     FA_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 64 && !attr[dev]) {
+      if (int s = check_reg_split(kern, kBwdThreads, kBwdRegTotal)) return s;
       if (int s = set_smem(kern, BwdCfg<D>::SMEM_BYTES)) return s;
       attr[dev] = true;
     }
@@ -864,6 +883,7 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
     int dev = 0;
     FA_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 64 && !attr[dev]) {
+      if (int s = check_reg_split(kern, kBwdThreads, kBwdRegTotal)) return s;
       if (int s = set_smem(kern, BwdCfg<D>::SMEM_BYTES)) return s;
       if (int s = set_smem(kq, DqCfg<D>::SMEM_BYTES)) return s;
       attr[dev] = true;
