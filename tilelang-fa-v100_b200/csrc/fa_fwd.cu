@@ -365,9 +365,13 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
           if (!vis) s[c] = __float_as_uint(NEG_INF);
         }
       }
-      float mx = NEG_INF;
+      float mx8[8];
 #pragma unroll
-      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+      for (int u = 0; u < 8; ++u) mx8[u] = __uint_as_float(s[u]);
+#pragma unroll
+      for (int c = 8; c < 128; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(s[c]));
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_new = fmaxf(m_run, mx);
       m_run = m_new;
       if (tr) FA_TRACE_EVENT(8 * t + 3, jj);
@@ -387,20 +391,25 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
         }
       }
       const float mref_s = (m_ref == NEG_INF) ? 0.f : m_ref * c2;
-      float rs0 = 0.f, rs1 = 0.f;
-      uint32_t pk[64];
+      float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // P in two halves of 64 keys, each stored to TMEM as soon as it is packed.
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = ex2_approx(fmaf(__uint_as_float(s[2 * c]), c2, -mref_s));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(s[2 * c + 1]), c2, -mref_s));
-        rs0 += p0;
-        rs1 += p1;
-        pk[c] = Pack2<T>::pack(p0, p1);
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t pk[32];
+        {
+#pragma unroll
+          for (int cc = 0; cc < 32; ++cc) {
+            const int c = 32 * hf + cc;
+            const float p0 = ex2_approx(fmaf(__uint_as_float(s[2 * c]), c2, -mref_s));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(s[2 * c + 1]), c2, -mref_s));
+            rs[c & 7] += p0 + p1;
+            pk[cc] = Pack2<T>::pack(p0, p1);
+          }
+        }
+        tmem_st32(tS + 32 * hf, pk);
       }
-      l += rs0 + rs1;
+      l += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
       if (tr) FA_TRACE_EVENT(8 * t + 4, jj);
-      tmem_st32(tS + 0, pk);
-      tmem_st32(tS + 32, pk + 32);
       if (rescale_o) {
         // PV_{j-1} is complete: the commit that signalled S_j covered every earlier MMA.
 #pragma unroll

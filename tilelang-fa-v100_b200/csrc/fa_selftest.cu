@@ -29,7 +29,7 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t sB = base + a_bytes;
   const uint32_t b_bytes = N * K * 2;
   SelftestCtl* ctl = reinterpret_cast<SelftestCtl*>(base_ptr + a_bytes + b_bytes);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
 
   if (threadIdx.x == 0) {
     ctl->abort_flag = 0;
