@@ -259,23 +259,23 @@ def time_paged(dev, steps, warmup):
     return ms, 4 * 128 * visible_pairs(16, 32, 1024, 1024, True) / ms / 1e9
 
 
-def decode_problem(dev, seed):
+def decode_problem(dev, seed, batch=256):
     """256 seqs, L ~ U[512, 8192], H 32 / Hkv 8, D 128, page 16, bf16."""
     rng = np.random.default_rng(seed)
-    lens = rng.integers(512, 8193, size=256).astype(np.int32)
+    lens = rng.integers(512, 8193, size=batch).astype(np.int32)
     pps = (lens + 15) // 16
     total = int(pps.sum())
     perm = rng.permutation(total).astype(np.int32)
-    bt = np.zeros((256, 512), np.int32)
+    bt = np.zeros((batch, 512), np.int32)
     c = 0
-    for i in range(256):
+    for i in range(batch):
         bt[i, :pps[i]] = perm[c:c + pps[i]]
         c += pps[i]
     g = torch.Generator(device=dev).manual_seed(seed + 1)
     kc = torch.randn(total, 16, 8, 128, generator=g, device=dev).to(torch.bfloat16)
     vc = torch.randn(total, 16, 8, 128, generator=g, device=dev).to(torch.bfloat16)
-    q = torch.randn(256, 32, 128, generator=g, device=dev).to(torch.bfloat16)
-    nbytes = int(lens.sum()) * 8 * 128 * 2 * 2 + 2 * 256 * 32 * 128 * 2 + total * 4
+    q = torch.randn(batch, 32, 128, generator=g, device=dev).to(torch.bfloat16)
+    nbytes = int(lens.sum()) * 8 * 128 * 2 * 2 + 2 * batch * 32 * 128 * 2 + total * 4
     return q, kc, vc, torch.from_numpy(bt).to(dev), torch.from_numpy(lens).to(dev), nbytes
 
 
@@ -334,7 +334,12 @@ def run_ours(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
-    b, s, h, d, causal = CFG["B"], CFG["S"], CFG["H"], CFG["D"], CFG["causal"]
+    from tilelang_fa_v100 import sharding
+    # Weak scaling: the global batch is world x configs[2]'s batch; rank r owns batch rows
+    # [r*B, (r+1)*B) with all heads (a (batch x heads) shard, no data exchange).
+    s, h, d, causal = CFG["S"], CFG["H"], CFG["D"], CFG["causal"]
+    b0, b1 = sharding.dense_batch_slice(CFG["B"] * world, world, rank)
+    b = b1 - b0
     dtype = torch.bfloat16
     with ClockSampler(local) as clk:
         ms, kern_ms, launches, tensors = time_dense(fa, dev, b, s, h, d, dtype, causal, args.steps,
@@ -477,10 +482,18 @@ def run_reference(args):
 
 
 def run_profile_case(args):
-    """Small case of the headline kernels for ncu captures: B=2 of configs[2]
-    (q/k/v/dO 67 MB each, 268 MB together > the 126 MB L2), fwd+bwd steps only."""
+    """Small cases for ncu captures.  dense: B=2 of configs[2] (q/k/v/dO 67 MB each,
+    268 MB together > the 126 MB L2), fwd+bwd steps.  decode: 64 sequences of
+    configs[4] (L ~ U[512, 8192], ~1.1 GB of K/V pages), decode steps."""
     import tilelang_fa_v100 as fa
     dev = torch.device("cuda", 0)
+    if args.profile_case == "decode":
+        q, kc, vc, bt, sl, nbytes = decode_problem(dev, 0, batch=64)
+        for _ in range(args.warmup + args.steps):
+            fa.tilelang_decode_forward(q, kc, vc, bt, sl)
+        torch.cuda.synchronize(dev)
+        print(json.dumps({"profile_case": "decode_B64_bf16", "bytes": nbytes}), flush=True)
+        return
     b, s, h, d = 2, CFG["S"], CFG["H"], CFG["D"]
     ms, kern_ms, launches, _ = time_dense(fa, dev, b, s, h, d, torch.bfloat16, True, args.steps,
                                           args.warmup, seed=3, profile=True)
@@ -496,8 +509,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
-    ap.add_argument("--profile-case", action="store_true",
-                    help="small fwd+bwd case for ncu captures (no e2e / CPU / secondary)")
+    ap.add_argument("--profile-case", choices=["dense", "decode"], default=None,
+                    help="small case for ncu captures (no e2e / CPU / secondary)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

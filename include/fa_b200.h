@@ -11,8 +11,9 @@
  *   cache  [num_pages, page_size, Hkv, D]          (vLLM paged KV cache)
  *   paged  q/out [num_tokens, H, D], lse [H, num_tokens] fp32
  *   decode q/out [B, H, D]
- * Supported: fp16 and bf16 inputs, head_dim 64/128 (dense, decode) and
- * 64/128/256 (paged prefill), H % Hk == 0.
+ * Supported: fp16 and bf16 inputs, H % Hk == 0; head_dim 64/128/256 (dense
+ * forward, paged prefill), 64/128 (dense backward, decode; decode also needs
+ * H / Hkv <= 16).  Pointers 16-byte aligned, strides multiples of 8 elements.
  */
 #ifndef FA_B200_H_
 #define FA_B200_H_
