@@ -14,21 +14,24 @@
 //                        S^T  = K Q^T            (SS)      -> TMEM [0,128)
 //                        dP^T = V dO^T           (SS)      -> TMEM [128,256)
 //                        dV  += P^T dO           (TS, A = P^T from TMEM)
-//                        dK  += dS^T Q           (TS, A = dS^T from TMEM)
-//                        dQ   = dS K             (SS, A = dS from smem) -> TMEM [128,128+D)
+//                        dK  += dS^T Q           (SS, A = dS^T K-major in smem)
+//                        dQ   = dS K             (SS, A = dS MN-major, same smem tile)
+//                                                          -> TMEM [128,128+D)
 //                      and dQ is added to an fp32 accumulator with vector atomics
 //                      (atomic mode).  In deterministic mode the last GEMM is skipped.
+//                      Issue order per step i: dV(i), S(i+1), dK(i), dQ(i), dP(i+1), so
+//                      S(i+1) overlaps the dS pass of step i.
 //   3. fa_bwd_dq       deterministic mode only: one CTA per (128-row Q tile, head,
 //                      batch) loops over KV tiles and accumulates dQ in TMEM
 //                      (S = Q K^T, dP = dO V^T, dQ += dS K), no atomics.
 //   4. fa_bwd_dq_conv  atomic mode: fp32 accumulator -> dq in the input dtype (BSHD).
 //
-// Roles in fa_bwd_dkdv (384 threads): warp 0 TMA producer (K, V once; Q, dO, LSE, D
+// Roles in fa_bwd_dkdv (512 threads): warp 0 TMA producer (K, V once; Q, dO, LSE, D
 // per query tile in a 2-stage ring), warp 1 TMEM allocator + MMA issuer, warps 4-11
 // two compute warpgroups: thread = key row (TMEM lane); warpgroup c handles query
-// columns [64c, 64c+64) of S^T / dP^T, writes P^T to TMEM columns [64c, 64c+32) and
-// dS^T to [64c+32, 64c+64) (each over S^T columns it has already read), and reads
-// back half of the dQ columns for the atomics.
+// columns [64c, 64c+64) of S^T / dP^T, writes P^T to TMEM columns [64c, 64c+32) (over
+// S^T columns it has already read) and dS^T to the shared-memory dS tile; warps 12-15
+// (atomic mode) move dQ out of TMEM and add it to the fp32 accumulator.
 #include "fa_ptx.cuh"
 #include "fa_internal.h"
 #include <cmath>
@@ -78,11 +81,13 @@ struct BwdCtl {
   uint64_t kv_full;
   uint64_t st_full[2];
   uint64_t st_empty[2];
-  uint64_t s_full, dp_full, p_ready, ds_ready, dq_full, dq_free, final_done, drain;
+  uint64_t s_full, p_ready, ds_ready, final_done, drain;
+  uint64_t dp_full[2], dq_full[2], dq_free[2];  // per 64-query half
   uint32_t tmem_base;
   int abort_flag;
   int smem_ok;
 };
+static_assert(sizeof(BwdCtl) <= 256, "backward control block");
 
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
                                           uint32_t bar) {
@@ -245,11 +250,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(smem_u32(&ctl->st_empty[s]), 1);
     }
     mbar_init(smem_u32(&ctl->s_full), 1);
-    mbar_init(smem_u32(&ctl->dp_full), 1);
     mbar_init(smem_u32(&ctl->p_ready), 256);
     mbar_init(smem_u32(&ctl->ds_ready), 256);
-    mbar_init(smem_u32(&ctl->dq_full), 1);
-    mbar_init(smem_u32(&ctl->dq_free), 128);
+    for (int hh = 0; hh < 2; ++hh) {
+      mbar_init(smem_u32(&ctl->dp_full[hh]), 1);
+      mbar_init(smem_u32(&ctl->dq_full[hh]), 1);
+      mbar_init(smem_u32(&ctl->dq_free[hh]), 128);
+    }
     mbar_init(smem_u32(&ctl->final_done), 1);
     mbar_init(smem_u32(&ctl->drain), 1);
     fence_barrier_init();
@@ -307,8 +314,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (lane == 0) {
       constexpr bool kBf16 = Pack2<T>::kBf16;
       constexpr uint32_t idS = idesc_f16(128, 128, kBf16, false, false);
+      constexpr uint32_t idS64 = idesc_f16(128, 64, kBf16, false, false);
       constexpr uint32_t idKV = idesc_f16(128, D, kBf16, false, true);
-      constexpr uint32_t idQ = idesc_f16(128, D, kBf16, true, true);
+      // dQ^T half = K^T dS^T (M = 128 head-dim rows; at D = 64 rows 64..127 read the next
+      // 16 KB of shared memory and are ignored), N = 64 queries, both operands MN-major.
+      constexpr uint32_t idQT = idesc_f16(128, 64, kBf16, true, true);
       const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 256 + D;
       // Descriptors built once (K-major forms for S^T / dP^T, MN-major for the rest).
       const uint64_t dK_k = sdesc_sw128(sK, 16, 1024), dV_k = sdesc_sw128(sV, 16, 1024);
@@ -318,38 +328,47 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint64_t ddO_m0 = sdesc_sw128(base + Cfg::OFF_DO, Cfg::CHUNK, 1024);
       const uint64_t dDS_m = sdesc_sw128(sDS, Cfg::CHUNK, 1024);
       const uint64_t dK_m = sdesc_sw128(sK, Cfg::CHUNK, 1024);
-      bool ok = mbar_wait(smem_u32(&ctl->kv_full), 0, abort_flag, p.err, FA_SITE_BWD_MMA);
-      for (int i = 0; i < n_iter && ok; ++i) {
-        const int s = i & 1;
-        const uint32_t par = i & 1;
-        ok = mbar_wait(smem_u32(&ctl->st_full[s]), (i >> 1) & 1, abort_flag, p.err,
-                       FA_SITE_BWD_MMA);
-        if (!ok) break;
-        FA_TRACE_EVENT(0, i);
-        tc_fence_after();
-        const uint64_t dQk = desc_add(dQ_k0, s * Cfg::TILE), ddOk = desc_add(ddO_k0, s * Cfg::TILE);
-        const uint64_t dQm = desc_add(dQ_m0, s * Cfg::TILE), ddOm = desc_add(ddO_m0, s * Cfg::TILE);
-        // S^T = K Q^T
+      const uint64_t dDS_k = sdesc_sw128(sDS, 16, 1024);
+      // S^T(i) = K Q(i)^T into [0, 128).
+      auto issue_S = [&](int st) {
+        const uint64_t dQk = desc_add(dQ_k0, st * Cfg::TILE);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
           mma_ss(tS, desc_add(dK_k, o), desc_add(dQk, o), idS, kk > 0);
         }
-        mma_commit(smem_u32(&ctl->s_full));
-        FA_TRACE_EVENT(1, i);
-        // dP^T = V dO^T into [128, 256): the previous dQ must have left TMEM.
-        if (ATOMIC_DQ && i > 0) {
-          ok = mbar_wait(smem_u32(&ctl->dq_free), (i - 1) & 1, abort_flag, p.err, FA_SITE_BWD_MMA);
-          if (!ok) break;
-          tc_fence_after();
-        }
-        FA_TRACE_EVENT(2, i);
+      };
+      // dP^T(i) = V dO(i)^T for queries [64hh, 64hh + 64) into [128 + 64hh, 192 + 64hh).
+      auto issue_dP = [&](int st, int hh) {
+        const uint64_t ddOk = desc_add(ddO_k0, st * Cfg::TILE + hh * 64 * 128);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
-          mma_ss(tdP, desc_add(dV_k, o), desc_add(ddOk, o), idS, kk > 0);
+          mma_ss(tdP + 64 * hh, desc_add(dV_k, o), desc_add(ddOk, o), idS64, kk > 0);
         }
-        mma_commit(smem_u32(&ctl->dp_full));
+        mma_commit(smem_u32(&ctl->dp_full[hh]));
+      };
+      bool ok = mbar_wait(smem_u32(&ctl->kv_full), 0, abort_flag, p.err, FA_SITE_BWD_MMA);
+      if (ok && n_iter > 0) {
+        ok = mbar_wait(smem_u32(&ctl->st_full[0]), 0, abort_flag, p.err, FA_SITE_BWD_MMA);
+        if (ok) {
+          tc_fence_after();
+          issue_S(0);
+          mma_commit(smem_u32(&ctl->s_full));
+          issue_dP(0, 0);
+          issue_dP(0, 1);
+        }
+      }
+      // Step i: dV(i) as soon as P^T(i) is in TMEM, then S(i+1) (its columns are free:
+      // the tensor pipe runs MMAs in issue order, so dV(i) has read P^T first), then
+      // dK(i) and dQ^T(i) from the dS tile in shared memory, then each half of dP(i+1)
+      // once that half of dQ^T(i) has left TMEM.  The compute warpgroups find S(i+1)
+      // ready when they finish step i.
+      for (int i = 0; i < n_iter && ok; ++i) {
+        const int s = i & 1;
+        const uint32_t par = i & 1;
+        const bool has_next = i + 1 < n_iter;
+        const uint64_t dQm = desc_add(dQ_m0, s * Cfg::TILE), ddOm = desc_add(ddO_m0, s * Cfg::TILE);
         // dV += P^T dO   (P^T for q 0..63 in columns 0..31, q 64..127 in 64..95)
         ok = mbar_wait(smem_u32(&ctl->p_ready), par, abort_flag, p.err, FA_SITE_BWD_MMA);
         if (!ok) break;
@@ -360,25 +379,48 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const uint32_t acol = (kk < 4) ? kk * 8 : 64 + (kk - 4) * 8;
           mma_ts(tdV, tS + acol, desc_add(ddOm, kk * 2048), idKV, (i > 0 || kk > 0) ? 1u : 0u);
         }
-        // dK += dS^T Q   (dS^T in columns 32..63 and 96..127)
+        if (has_next) {
+          ok = mbar_wait(smem_u32(&ctl->st_full[s ^ 1]), ((i + 1) >> 1) & 1, abort_flag, p.err,
+                         FA_SITE_BWD_MMA);
+          if (!ok) break;
+          tc_fence_after();
+          issue_S(s ^ 1);
+          mma_commit(smem_u32(&ctl->s_full));
+        }
+        // dK += dS^T Q   (A = dS^T, K-major in shared memory; B = Q MN-major)
         ok = mbar_wait(smem_u32(&ctl->ds_ready), par, abort_flag, p.err, FA_SITE_BWD_MMA);
         if (!ok) break;
         FA_TRACE_EVENT(4, i);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t acol = (kk < 4) ? 32 + kk * 8 : 96 + (kk - 4) * 8;
-          mma_ts(tdK, tS + acol, desc_add(dQm, kk * 2048), idKV, (i > 0 || kk > 0) ? 1u : 0u);
+          const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
+          mma_ss(tdK, desc_add(dDS_k, o), desc_add(dQm, kk * 2048), idKV, (i > 0 || kk > 0) ? 1u : 0u);
         }
         if (ATOMIC_DQ) {
-          // dQ = dS K  (A = dS MN-major from smem, B = K MN-major) into [128, 128 + D)
+          // dQ^T = K^T dS^T, one 64-query half at a time, into the dP^T columns.
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_ss(tdP, desc_add(dDS_m, kk * 2048), desc_add(dK_m, kk * 2048), idQ, kk > 0);
-          mma_commit(smem_u32(&ctl->dq_full));
+          for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              mma_ss(tdP + 64 * hh, desc_add(dK_m, kk * 2048),
+                     desc_add(dDS_m, hh * Cfg::CHUNK + kk * 2048), idQT, kk > 0);
+            mma_commit(smem_u32(&ctl->dq_full[hh]));
+          }
         }
         mma_commit(smem_u32(&ctl->st_empty[s]));
         FA_TRACE_EVENT(5, i);
+        if (has_next) {
+#pragma unroll
+          for (int hh = 0; hh < 2 && ok; ++hh) {
+            if (ATOMIC_DQ) {
+              ok = mbar_wait(smem_u32(&ctl->dq_free[hh]), par, abort_flag, p.err, FA_SITE_BWD_MMA);
+              if (!ok) break;
+              tc_fence_after();
+            }
+            issue_dP(s ^ 1, hh);
+          }
+        }
       }
       mma_commit(smem_u32(&ctl->final_done));
       mma_commit(smem_u32(&ctl->drain));
@@ -445,8 +487,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl->p_ready));
       if (threadIdx.x == 128) FA_TRACE_EVENT(7, i);
-      // ---- pass B: dS^T = P^T (dP^T - D) * scale
-      w = mbar_wait(smem_u32(&ctl->dp_full), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+      // ---- pass B: dS^T = P^T (dP^T - D) * scale, to shared memory (K-major A of dK,
+      // MN-major B of dQ^T).  dP^T(i) was committed after dK(i-1) and dQ^T(i-1), so once
+      // dp_full(i) has fired those MMAs have finished reading the previous dS tile.
+      w = mbar_wait(smem_u32(&ctl->dp_full[c]), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
       ok = __all_sync(0xffffffffu, w);
       if (!ok) break;
       if (threadIdx.x == 128) FA_TRACE_EVENT(8, i);
@@ -467,18 +511,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const float d1 = pv[xx + 1] * (__uint_as_float(dv[2 * x + 1]) - di[2 * x + 1]) * p.scale;
           pk[x] = Pack2<T>::pack(d0, d1);
         }
-        tmem_st16(tS + 64 * c + 32 + 16 * hf, pk);
-        if (ATOMIC_DQ) {
-          // dS^T row j, query columns 64c + 32hf .. +31 -> smem (MN-major A of dQ = dS K)
-          const uint32_t row = sDS + c * Cfg::CHUNK + j * 128;
+        // dS^T row j, query columns 64c + 32hf .. +31 (128-byte swizzled rows)
+        const uint32_t row = sDS + c * Cfg::CHUNK + j * 128;
 #pragma unroll
-          for (int m = 0; m < 4; ++m)
-            st_shared_v4(row + ((((hf << 2) + m) ^ (j & 7)) << 4), pk[4 * m], pk[4 * m + 1],
-                         pk[4 * m + 2], pk[4 * m + 3]);
-        }
+        for (int m = 0; m < 4; ++m)
+          st_shared_v4(row + ((((hf << 2) + m) ^ (j & 7)) << 4), pk[4 * m], pk[4 * m + 1],
+                       pk[4 * m + 2], pk[4 * m + 3]);
       }
-      tmem_wait_st();
-      if (ATOMIC_DQ) fence_proxy_async_smem();
+      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl->ds_ready));
       if (threadIdx.x == 128) FA_TRACE_EVENT(9, i);
@@ -524,36 +564,36 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     setmaxnreg_dec<kBwdRegDq>();
     if (ATOMIC_DQ) {
     // ============================================================ dQ warpgroup
-    // Moves each query tile's dQ (lane = query row) out of TMEM, frees the columns for
-    // the next dP^T at once, then adds it to the fp32 accumulator with vector atomics
-    // while the compute warpgroups already work on the next tile.
-    const int r = ((warp & 3) << 5) | lane;
-    const uint32_t tdP = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + 128;
-    for (int i = 0; i < n_iter; ++i) {
+    // Thread = head-dim column d (TMEM lane of dQ^T).  Each 64-query half is moved out
+    // of TMEM, its columns are released for the next dP^T half at once, and the values
+    // are added to the fp32 accumulator: one warp instruction covers 32 consecutive d
+    // of one query row (128 contiguous bytes).
+    const int dl = ((warp & 3) << 5) | lane;
+    const bool d_ok = dl < D;
+    const uint32_t tq = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + 128;
+    bool ok = true;
+    for (int i = 0; i < n_iter && ok; ++i) {
       const int g = i / nqt, qt = t_start + i % nqt, h = hk * p.G + g;
-      bool w = mbar_wait(smem_u32(&ctl->dq_full), i & 1, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
-      if (!__all_sync(0xffffffffu, w)) break;
-      if (threadIdx.x == 384) FA_TRACE_EVENT(10, i);
-      tc_fence_after();
-      float* acc = p.dq_acc + (((int64_t)b * p.H + h) * p.Sq_pad + qt * kBwdBM + r) * D;
-      // 64 columns at a time; the TMEM columns are released after the last load.
+      float* acc = p.dq_acc + (((int64_t)b * p.H + h) * p.Sq_pad + qt * kBwdBM) * D + dl;
 #pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 64) {
+      for (int hh = 0; hh < 2; ++hh) {
+        bool w = mbar_wait(smem_u32(&ctl->dq_full[hh]), i & 1, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+        ok = __all_sync(0xffffffffu, w);
+        if (!ok) break;
+        if (threadIdx.x == 384) FA_TRACE_EVENT(10 + hh, i);
+        tc_fence_after();
         uint32_t v[64];
-        tmem_ld32(tdP + c0, v);
-        tmem_ld32(tdP + c0 + 32, v + 32);
+        tmem_ld32(tq + 64 * hh, v);
+        tmem_ld32(tq + 64 * hh + 32, v + 32);
         tmem_wait_ld();
-        if (c0 + 64 == D) {
-          tc_fence_before();
-          mbar_arrive(smem_u32(&ctl->dq_free));
-        }
+        tc_fence_before();
+        mbar_arrive(smem_u32(&ctl->dq_free[hh]));
+        if (d_ok) {
+          float* a = acc + (int64_t)(64 * hh) * D;
 #pragma unroll
-        for (int x = 0; x < 64; x += 4)
-          atomicAdd(reinterpret_cast<float4*>(acc + c0 + x),
-                    make_float4(__uint_as_float(v[x]), __uint_as_float(v[x + 1]),
-                                __uint_as_float(v[x + 2]), __uint_as_float(v[x + 3])));
+          for (int x = 0; x < 64; ++x) atomicAdd(a + (int64_t)x * D, __uint_as_float(v[x]));
+        }
       }
-      if (threadIdx.x == 384) FA_TRACE_EVENT(11, i);
     }
     }
   }

@@ -176,6 +176,9 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
 
   if (warp == 0) {
     // ============================================================ TMA producer
+    // Lane 0 issues every copy.  Paged: the whole warp fetches the page ids of the next
+    // KV tile (lane r: box r) while lane 0 issues the current one, so block-table reads
+    // never sit between two copies.
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
@@ -188,45 +191,63 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
           tma_load_4d(sQ + t * Cfg::TILE_BYTES + dh * Cfg::CHUNK_BYTES, &tm_q, qbar, dh * 64,
                       hk * G, tok, PAGED ? 0 : b);
       }
-      const int box_rows = PAGED ? min(p.page_size, kFwdBN) : kFwdBN;
-      const int n_valid_pages =
-          PAGED ? min((kv_len + p.page_size - 1) / p.page_size, p.max_blocks) : 0;
-      int it = 0;
-      bool ok = true;
-      for (int jj = 0; jj < nkv && ok; ++jj) {
-        const int j = j0 + jj;
-        for (int w = 0; w < 2 && ok; ++w, ++it) {
-          const int s = it % ST;
-          const uint32_t ph = (it / ST) & 1;
-          ok = mbar_wait(smem_u32(&ctl->kv_empty[s]), ph ^ 1, abort_flag, p.err,
-                         FA_SITE_FWD_PRODUCER);
-          if (!ok) break;
-          const uint32_t fb = smem_u32(&ctl->kv_full[s]);
-          mbar_arrive_expect_tx(fb, Cfg::TILE_BYTES);
-          const CUtensorMap* tm = (w == 0) ? &tm_k : &tm_v;
-          const uint32_t dst = sKV + s * Cfg::TILE_BYTES;
-          if constexpr (PAGED) {
-            for (int r0 = 0; r0 < kFwdBN; r0 += box_rows) {
-              const int key = j * kFwdBN + r0;
-              const int lp = key / p.page_size;
-              const int in_page = key - lp * p.page_size;
-              // Pages past the sequence are fetched out of range: TMA fills zeros.
-              const int page =
-                  lp < n_valid_pages ? p.block_table[(int64_t)b * p.max_blocks + lp] : p.num_pages;
+    }
+    const int box_rows = PAGED ? min(p.page_size, kFwdBN) : kFwdBN;
+    const int boxes = kFwdBN / box_rows;  // page boxes per KV tile (<= 16: page_size >= 8)
+    const int n_valid_pages =
+        PAGED ? min((kv_len + p.page_size - 1) / p.page_size, p.max_blocks) : 0;
+    // Page id of box `lane` of KV tile j; pages past the sequence are fetched out of
+    // range (page id num_pages), which TMA fills with zeros.
+    auto page_of = [&](int j) -> int {
+      int pg = p.num_pages;
+      if (PAGED && lane < boxes) {
+        const int lp = (j * kFwdBN + lane * box_rows) / p.page_size;
+        if (lp < n_valid_pages) pg = p.block_table[(int64_t)b * p.max_blocks + lp];
+      }
+      return pg;
+    };
+    int pg_next = (PAGED && nkv > 0) ? page_of(j0) : 0;
+    int it = 0;
+    bool ok = true;
+    for (int jj = 0; jj < nkv && ok; ++jj) {
+      const int j = j0 + jj;
+      const int pg_cur = pg_next;
+      if (PAGED && jj + 1 < nkv) pg_next = page_of(j + 1);
+      for (int w = 0; w < 2 && ok; ++w, ++it) {
+        const int s = it % ST;
+        const uint32_t ph = (it / ST) & 1;
+        int okl = 1;
+        if (lane == 0)
+          okl = mbar_wait(smem_u32(&ctl->kv_empty[s]), ph ^ 1, abort_flag, p.err,
+                          FA_SITE_FWD_PRODUCER);
+        ok = __shfl_sync(0xffffffffu, okl, 0) != 0;
+        if (!ok) break;
+        const uint32_t fb = smem_u32(&ctl->kv_full[s]);
+        const CUtensorMap* tm = (w == 0) ? &tm_k : &tm_v;
+        const uint32_t dst = sKV + s * Cfg::TILE_BYTES;
+        if (lane == 0) mbar_arrive_expect_tx(fb, Cfg::TILE_BYTES);
+        if constexpr (PAGED) {
+          for (int r = 0; r < boxes; ++r) {
+            const int page = __shfl_sync(0xffffffffu, pg_cur, r);
+            if (lane == 0) {
+              const int in_page = (j * kFwdBN + r * box_rows) % p.page_size;
               for (int dh = 0; dh < Cfg::DH; ++dh)
-                tma_load_4d(dst + dh * Cfg::CHUNK_BYTES + r0 * 128, tm, fb, dh * 64, hk, in_page,
-                            page);
+                tma_load_4d(dst + dh * Cfg::CHUNK_BYTES + r * box_rows * 128, tm, fb, dh * 64, hk,
+                            in_page, page);
             }
-          } else {
+          }
+        } else {
+          if (lane == 0)
             for (int dh = 0; dh < Cfg::DH; ++dh)
               tma_load_4d(dst + dh * Cfg::CHUNK_BYTES, tm, fb, dh * 64, hk, j * kFwdBN, b);
-          }
         }
       }
-      // Drain: every copy issued must have landed before the CTA may exit.
+    }
+    // Drain: every copy issued must have landed before the CTA may exit.
+    if (lane == 0) {
       for (int k = max(0, it - ST); k < it; ++k)
         mbar_wait_drain(smem_u32(&ctl->kv_full[k % ST]), (k / ST) & 1);
-      mbar_wait_drain(qbar, 0);
+      mbar_wait_drain(smem_u32(&ctl->q_full), 0);
     }
   } else if (warp == 1) {
     // ============================================================ MMA issuer
