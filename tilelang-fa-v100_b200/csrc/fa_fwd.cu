@@ -57,6 +57,7 @@ struct FwdSmemCtl {
   uint64_t s_full[2];
   uint64_t p_ready[2];
   uint64_t o_final[2];
+  uint64_t exp_turn[2];  // softmax ping-pong: warpgroup t may run its exp phase
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -155,6 +156,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
       mbar_init(smem_u32(&ctl->s_full[t]), 1);
       mbar_init(smem_u32(&ctl->p_ready[t]), 128);
       mbar_init(smem_u32(&ctl->o_final[t]), 1);
+      mbar_init(smem_u32(&ctl->exp_turn[t]), 128);
     }
     mbar_init(smem_u32(&ctl->drain), 1);
     fence_barrier_init();
@@ -350,6 +352,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
     const float NEG_INF = -INFINITY;
     float m_run = NEG_INF, m_ref = NEG_INF, l = 0.f;
     bool ok = true;
+    if (NQ == 2 && t == 1) mbar_arrive(smem_u32(&ctl->exp_turn[0]));  // tile 0 goes first
 
     for (int jj = 0; jj < nkv; ++jj) {
       const int j = j0 + jj;
@@ -412,6 +415,17 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
         }
       }
       const float mref_s = (m_ref == NEG_INF) ? 0.f : m_ref * c2;
+      // With two Q tiles the warpgroups take turns on the exponential unit: tile 0's
+      // exp phase of KV tile j, then tile 1's, then tile 0's of j + 1, ... so one
+      // tile's exponentials run while the other tile's MMAs do.
+      if (NQ == 2) {
+        const bool turn = mbar_wait(smem_u32(&ctl->exp_turn[t]), jj & 1, abort_flag, p.err,
+                                    FA_SITE_FWD_SOFTMAX);
+        if (!__all_sync(0xffffffffu, turn)) {
+          ok = false;
+          break;
+        }
+      }
       float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       // P in two halves of 64 keys, each stored to TMEM as soon as it is packed.
 #pragma unroll
@@ -429,6 +443,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
         }
         tmem_st32(tS + 32 * hf, pk);
       }
+      if (NQ == 2) mbar_arrive(smem_u32(&ctl->exp_turn[t ^ 1]));
       l += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
       if (tr) FA_TRACE_EVENT(8 * t + 4, jj);
       if (rescale_o) {
