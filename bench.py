@@ -385,7 +385,7 @@ def run_ours(args):
                      "kernel_ms": kern_ms},
         "check": {"max_abs_err_out_vs_fp32": err},
     }
-    if not args.no_secondary:
+    if not args.no_secondary and world == 1:  # secondary configs: single-GPU runs only
         sec = {}
         sms, _, _, tt = time_dense(fa, dev, 4, 2048, 16, 64, torch.float16, True, args.steps, 3,
                                    seed=7 + rank)
@@ -436,7 +436,8 @@ def run_ours(args):
         err_code = _ext.read_device_error(clear=True)
         line["device_error"] = list(err_code)
     if rank == 0:
-        line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
+        if world == 1:  # the host-core baseline is reported at N = 1 only
+            line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
