@@ -195,14 +195,6 @@ __device__ __forceinline__ void ld_shared_v4f(uint32_t addr, float* v) {
                : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
                : "r"(addr));
 }
-template <int N>
-__device__ __forceinline__ void setmaxnreg_inc() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
-}
-template <int N>
-__device__ __forceinline__ void setmaxnreg_dec() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
-}
 
 // 512 threads = 4 warpgroups.  Launch: 128 registers per thread (65,536).  Warpgroup 0
 // (producer, MMA issuer, 2 idle warps) and warpgroup 3 (dQ) drop, the two compute
@@ -864,20 +856,6 @@ static int set_smem(K kern, int bytes) {
   return FA_OK;
 }
 
-// setmaxnreg.inc waits until the block's own launch allocation can supply the raised
-// count, so a split whose total exceeds (registers per thread at launch) x threads
-// would never proceed.  Checked against the compiled kernel before every first launch.
-template <typename K>
-static int check_reg_split(K kern, int threads, int needed_total) {
-  cudaFuncAttributes fa_attr;
-  FA_CUDA_TRY(cudaFuncGetAttributes(&fa_attr, kern));
-  if (fa_attr.numRegs * threads < needed_total) {
-    set_error_detail("register split", __FILE__, __LINE__,
-                     "setmaxnreg split exceeds the kernel's launch register allocation");
-    return FA_ERR_CUDA;
-  }
-  return FA_OK;
-}
 constexpr int kBwdRegTotal = 128 * kBwdRegLow + 256 * kBwdRegHigh + 128 * kBwdRegDq;
 
 template <typename T, int D>

@@ -81,4 +81,18 @@ void set_error_detail(const char* what, const char* file, int line, const char* 
     }                                                                         \
   } while (0)
 
+// setmaxnreg.inc waits until the block's own launch allocation can supply the raised
+// count, so a split whose total exceeds (registers per thread at launch) x threads
+// would never proceed.  Checked against the compiled kernel before every first launch.
+template <typename K>
+inline int check_reg_split(K kern, int threads, int needed_total) {
+  cudaFuncAttributes fa_attr;
+  FA_CUDA_TRY(cudaFuncGetAttributes(&fa_attr, kern));
+  if (fa_attr.numRegs * threads < needed_total) {
+    set_error_detail("register split", __FILE__, __LINE__,
+                     "setmaxnreg split exceeds the kernel's launch register allocation");
+    return FA_ERR_CUDA;
+  }
+  return FA_OK;
+}
 }  // namespace fa

@@ -286,6 +286,18 @@ static __device__ unsigned long long g_fa_trace[FA_TRACE_CTAS][FA_TRACE_EVENTS][
   } while (0)
 #endif
 
+// ---------------------------------------------------------------- register split
+// setmaxnreg: executed by every warp of a warpgroup; the raised counts of all
+// warpgroups together must fit the block's launch allocation (checked on the host).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---------------------------------------------------------------- misc math
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
