@@ -23,6 +23,7 @@ causal, paged GQA prefill, split-KV decode GB/s).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
 import argparse
+import datetime
 import json
 import math
 import os
@@ -78,9 +79,10 @@ def ncu_traffic(name):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks, power and throttle reasons sampled every 20 ms; the summary
+    uses the samples taken between mark_start() and mark_stop() (the timed region)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -88,6 +90,7 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.path = None
+        self.t_start = self.t_stop = None
 
     def __enter__(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
@@ -95,15 +98,22 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu)],
+                 "-lms", "20", "-i", str(self.gpu)],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
         time.sleep(0.3)
         return self
 
+    def mark_start(self):
+        self.t_start = datetime.datetime.now()
+
+    def mark_stop(self):
+        self.t_stop = datetime.datetime.now()
+
     def __exit__(self, *exc):
         if self.proc is not None:
+            time.sleep(0.05)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -113,24 +123,27 @@ class ClockSampler:
     def summary(self):
         if self.path is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm, smax, reasons = [], None, set()
+        rows, smax = [], None
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in open(self.path):
             f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
                 continue
             try:
-                sm.append(float(f[1]))
-                smax = float(f[2])
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f")
+                mhz, smax, watts = float(f[2]), float(f[3]), float(f[4])
             except ValueError:
                 continue
-            for nm, val in zip(names, f[5:9]):
-                if val.lower() == "active":
-                    reasons.add(nm)
+            rows.append((ts, mhz, watts, [nm for nm, val in zip(names, f[6:10]) if val.lower() == "active"]))
         os.unlink(self.path)
-        loaded = [x for x in sm if smax and x > 0.3 * smax] or sm
-        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        window = [r for r in rows if self.t_start and self.t_stop and self.t_start <= r[0] <= self.t_stop]
+        if not window and self.t_start:  # region shorter than the sampling period: next sample
+            window = [r for r in rows if r[0] >= self.t_start][:1]
+        reasons = sorted({nm for r in window for nm in r[3]})
+        return {"sm_mhz": statistics.median(r[1] for r in window) if window else None,
+                "sm_max_mhz": smax, "reasons": reasons,
+                "power_w": statistics.median(r[2] for r in window) if window else None,
+                "samples": len(window), "sampling_ms": 20}
 
 
 # --------------------------------------------------------------------------- our arm
@@ -152,7 +165,8 @@ def run_dense_steps(fa, q, k, v, do, causal, n, prof_events=None):
     return out
 
 
-def time_dense(fa, dev, b, s, h, d, dtype, causal, steps, warmup, seed, dist=None, profile=False):
+def time_dense(fa, dev, b, s, h, d, dtype, causal, steps, warmup, seed, dist=None, profile=False,
+               clk=None):
     from tilelang_fa_v100 import _ext
     q, k, v, do = dense_inputs(dev, b, s, h, d, dtype, seed)
     q, k, v = (x.requires_grad_(True) for x in (q, k, v))
@@ -165,10 +179,14 @@ def time_dense(fa, dev, b, s, h, d, dtype, causal, steps, warmup, seed, dist=Non
         dist.barrier()
     torch.cuda.synchronize(dev)
     n0 = _ext.launch_count()
+    if clk is not None:
+        clk.mark_start()
     t0.record()
     out = run_dense_steps(fa, q, k, v, do, causal, steps, ev)
     t1.record()
     torch.cuda.synchronize(dev)
+    if clk is not None:
+        clk.mark_stop()
     launches = _ext.launch_count() - n0
     if dist is not None:
         dist.barrier()
@@ -344,7 +362,7 @@ def run_ours(args):
     with ClockSampler(local) as clk:
         ms, kern_ms, launches, tensors = time_dense(fa, dev, b, s, h, d, dtype, causal, args.steps,
                                                     args.warmup, seed=1000 + rank, dist=dist,
-                                                    profile=True)
+                                                    profile=True, clk=clk)
     clocks = clk.summary()
     err = check_dense(tensors, causal)
     del tensors
@@ -505,7 +523,7 @@ def run_profile_case(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true")
