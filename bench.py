@@ -314,6 +314,33 @@ def time_decode(dev, steps, warmup, seed=0):
     return ms, nbytes / ms / 1e6
 
 
+def time_kv_write(dev, steps, warmup, tokens=65536, hkv=8, d=128, page=16):
+    """Paged KV-cache write of one large prefill step: bytes = read key + value and
+    write them into the cache (slot_mapping excluded), scattered slots."""
+    from tilelang_fa_v100.cache import write_kv_cache
+    g = torch.Generator(device=dev).manual_seed(17)
+    key = torch.randn(tokens, hkv, d, generator=g, device=dev).to(torch.bfloat16)
+    value = torch.randn(tokens, hkv, d, generator=g, device=dev).to(torch.bfloat16)
+    pages = 2 * tokens // page
+    kc = torch.empty(pages, page, hkv, d, device=dev, dtype=torch.bfloat16)
+    vc = torch.empty_like(kc)
+    slots = torch.randperm(pages * page, generator=torch.Generator().manual_seed(3))[:tokens]
+    slots = slots.to(dev)
+    run = lambda: write_kv_cache(key, value, kc, vc, slots)
+    for _ in range(warmup):
+        run()
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        run()
+    t1.record()
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / steps
+    nbytes = 2 * 2 * tokens * hkv * d * 2
+    return ms, nbytes / ms / 1e6
+
+
 def cpu_baseline(budget_s=15.0):
     """The reference's PyTorch attention (fp32, autograd) on the host cores, on a bounded
     sample of the headline workload: whole (batch, head) slices of configs[2]."""
@@ -450,6 +477,9 @@ def run_ours(args):
         sec["cfg5_decode_bf16_GBps"] = {"gbs": dgbs, "ms": dms,
                                         "frac_of_hbm": dgbs / peaks.get("hbm_gbs", 6538.6),
                                         "peak_source": src + " hbm_gbs"}
+        kms, kgbs = time_kv_write(dev, args.steps, 3)
+        sec["kv_cache_write_bf16_65536tok_Hkv8_D128_GBps"] = {
+            "gbs": kgbs, "ms": kms, "frac_of_hbm": kgbs / peaks.get("hbm_gbs", 6538.6)}
         line["secondary"] = sec
         err_code = _ext.read_device_error(clear=True)
         line["device_error"] = list(err_code)

@@ -143,6 +143,28 @@ typedef struct {
 size_t fa_decode_workspace_size(const fa_decode_args_t* args);
 int fa_decode(const fa_decode_args_t* args, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Paged KV-cache write (the step before the paged path): for each token t with
+ * slot_mapping[t] >= 0, copies key[t] and value[t] (each [Hkv, D], contiguous) to
+ * k_cache / v_cache[slot / page_size][slot % page_size].  Negative slots are padding
+ * and are skipped; a slot beyond num_pages * page_size is not written and sets the
+ * device error word (code 3).  No counterpart in the reference, which reads caches
+ * that its caller filled (_kernels_paged.py:265-272, :441-448); it replaces the
+ * cache-write call a vLLM attention backend makes before attention
+ * (reshape_and_cache_flash, vllm/_custom_ops.py). */
+typedef struct {
+  const void* key;                /* [num_tokens, Hkv, D], token stride key_stride */
+  const void* value;              /* [num_tokens, Hkv, D], token stride value_stride */
+  void* k_cache;                  /* [num_pages, page_size, Hkv, D] */
+  void* v_cache;
+  const int64_t* slot_mapping;    /* [num_tokens] */
+  int64_t key_stride;             /* elements between consecutive tokens */
+  int64_t value_stride;
+  int32_t num_tokens, num_kv_heads, head_dim, page_size, num_pages;
+  int32_t dtype;                  /* fa_dtype_t (cache and inputs share it) */
+} fa_kv_write_args_t;
+
+int fa_kv_cache_write(const fa_kv_write_args_t* args, void* stream);
+
 /* Decode that allocates nothing, not even a caller workspace.  No counterpart in the
  * reference: it exists for callers that cannot hand the library any device memory
  * at decode time -- e.g. a serving engine that gives all free HBM to its KV-cache

@@ -24,6 +24,13 @@ repository's pure-PyTorch attention oracles and the semantics of its kernels:
 * ``decode_ref`` -- the decode kernel (_kernels_paged.py:393-489): one query per
   sequence, every key j < seq_lens[b] visible.
 
+* ``kv_cache_write_ref`` -- the cache-write step before the paged path (no reference
+  counterpart): token t's [Hkv, D] key / value rows land at cache[slot // page_size,
+  slot % page_size] for slot = slot_mapping[t] >= 0 (the slot addressing the paged
+  kernels read back through block_table, _kernels_paged.py:265-272); negative slots
+  are padding.  Pinned by the paged golden vectors: writing a golden sequence's tokens
+  through this function reproduces the golden cache.
+
 Pinning: tests/test_oracle_golden.py checks every function here against golden
 vectors produced by running the reference's own ``pytorch_gqa_ref`` and
 ``make_paged_gqa`` (tests/golden/make_golden.py).
@@ -182,6 +189,22 @@ def make_paged_cache(k, v, page_size=16, shuffle_seed=None, num_pages=None):
             kc[phys, : t1 - t0] = k[b, :, t0:t1].transpose(1, 0, 2)
             vc[phys, : t1 - t0] = v[b, :, t0:t1].transpose(1, 0, 2)
     return kc, vc, bt
+
+
+def kv_cache_write_ref(key, value, k_cache, v_cache, slot_mapping):
+    """In-place scatter of key / value [T, Hkv, D] into the paged caches (numpy)."""
+    page = k_cache.shape[1]
+    for t, slot in enumerate(np.asarray(slot_mapping).tolist()):
+        if slot < 0:
+            continue
+        k_cache[slot // page, slot % page] = key[t]
+        v_cache[slot // page, slot % page] = value[t]
+
+
+def slots_for(block_table_row, positions, page_size):
+    """Slot ids of token positions of one sequence under its block table row."""
+    pos = np.asarray(positions)
+    return np.asarray(block_table_row)[pos // page_size].astype(np.int64) * page_size + pos % page_size
 
 
 def flops_dense(b, h, sq, skv, d, causal):

@@ -59,7 +59,8 @@ int main(void) {
 @pytest.mark.parametrize("cname,cls", [("fa_fwd_args_t", _ext.FwdArgs),
                                        ("fa_bwd_args_t", _ext.BwdArgs),
                                        ("fa_paged_args_t", _ext.PagedArgs),
-                                       ("fa_decode_args_t", _ext.DecodeArgs)])
+                                       ("fa_decode_args_t", _ext.DecodeArgs),
+                                       ("fa_kv_write_args_t", _ext.KvWriteArgs)])
 def test_struct_layout_matches_c(cname, cls):
     fields = [f for f, _ in cls._fields_]
     lay = _c_layout(cname, fields)
@@ -87,6 +88,11 @@ def test_null_arguments_rejected_on_host():
     assert lib.fa_decode(ctypes.byref(d), None, 0, None) == _ext.FA_ERR_INVALID_ARG
     b = _ext.BwdArgs()
     assert lib.fa_bwd(ctypes.byref(b), None, 0, None) == _ext.FA_ERR_INVALID_ARG
+    w = _ext.KvWriteArgs()
+    assert lib.fa_kv_cache_write(ctypes.byref(w), None) == _ext.FA_ERR_INVALID_ARG
+    assert lib.fa_kv_cache_write(None, None) == _ext.FA_ERR_INVALID_ARG
+    w.num_tokens, w.num_kv_heads, w.head_dim, w.page_size, w.num_pages = 4, 8, 128, 16, 10
+    assert lib.fa_kv_cache_write(ctypes.byref(w), None) == _ext.FA_ERR_INVALID_ARG  # null tensors
 
 
 def test_unsupported_head_dim_rejected_on_host():

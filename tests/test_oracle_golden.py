@@ -37,6 +37,27 @@ def test_paged_matches_reference(name):
     assert_close(lse, g["lse"], atol=1e-4, rtol=1e-5, what=name + " lse")
 
 
+@pytest.mark.parametrize("name", golden_names("paged_"))
+def test_kv_cache_write_reproduces_reference_caches(name):
+    """Writing each golden sequence's tokens through slot = block_table[pos // page] * page
+    + pos % page rebuilds the cache the reference's make_paged_gqa laid out."""
+    g = golden(name)
+    kc, vc, bt, sl = g["k_cache"], g["v_cache"], g["block_table"], g["seq_lens"]
+    page = kc.shape[1]
+    k2, v2 = np.zeros_like(kc), np.zeros_like(vc)
+    for b in range(bt.shape[0]):
+        n = int(sl[b])
+        key = R.gather_pages(kc, bt[b], n).transpose(1, 0, 2)   # [n, Hkv, D]
+        val = R.gather_pages(vc, bt[b], n).transpose(1, 0, 2)
+        slots = R.slots_for(bt[b], np.arange(n), page)
+        slots[::7] = -1  # padding tokens are skipped ...
+        R.kv_cache_write_ref(key, val, k2, v2, slots)
+        slots = R.slots_for(bt[b], np.arange(n), page)[::7]
+        R.kv_cache_write_ref(key[::7], val[::7], k2, v2, slots)  # ... and written later
+        np.testing.assert_array_equal(R.gather_pages(k2, bt[b], n), R.gather_pages(kc, bt[b], n))
+        np.testing.assert_array_equal(R.gather_pages(v2, bt[b], n), R.gather_pages(vc, bt[b], n))
+
+
 def test_decode_ref_equals_prefill_with_one_query():
     g = golden("decode_gqa_16_4_d128")
     out, lse = R.decode_ref(g["q_flat"].astype(np.float32), g["k_cache"], g["v_cache"],

@@ -297,6 +297,20 @@ int fa_decode_noalloc(const fa_decode_args_t* a, void* stream) {
 
 size_t fa_decode_noalloc_scratch_bytes(void) { return decode_noalloc_scratch_bytes(); }
 
+int fa_kv_cache_write(const fa_kv_write_args_t* a, void* stream) {
+  if (a == nullptr) return FA_ERR_INVALID_ARG;
+  if (a->num_tokens < 0 || a->num_kv_heads <= 0 || a->head_dim <= 0 || a->page_size <= 0 ||
+      a->num_pages <= 0 || a->key_stride < 0 || a->value_stride < 0)
+    return FA_ERR_INVALID_ARG;
+  if (a->num_tokens > 0 && (a->key == nullptr || a->value == nullptr || a->k_cache == nullptr ||
+                            a->v_cache == nullptr || a->slot_mapping == nullptr))
+    return FA_ERR_INVALID_ARG;
+  if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
+  int* err = nullptr;
+  if (int s = device_setup(&err, static_cast<cudaStream_t>(stream))) return s;
+  return launch_kv_cache_write(a, err, static_cast<cudaStream_t>(stream));
+}
+
 int fa_selftest_umma_rate(int32_t n, int32_t k, int32_t reps, int32_t a_tmem, int32_t a_mn,
                           int32_t b_mn, int32_t ctas, void* stream) {
   int* err = nullptr;

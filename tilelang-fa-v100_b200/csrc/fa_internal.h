@@ -53,6 +53,7 @@ size_t bwd_workspace_bytes(const fa_bwd_args_t* a);
 int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st);
 size_t decode_workspace_bytes(const fa_decode_args_t* a);
 int launch_decode_noalloc(const fa_decode_args_t* a, int* err, cudaStream_t st);
+int launch_kv_cache_write(const fa_kv_write_args_t* a, int* err, cudaStream_t st);
 size_t decode_noalloc_scratch_bytes();
 int decode_num_splits(const fa_decode_args_t* a);
 int launch_umma_rate(int n, int k, int reps, int a_tmem, int a_mn, int b_mn, int ctas, int* err,

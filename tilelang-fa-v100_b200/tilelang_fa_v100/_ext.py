@@ -73,6 +73,13 @@ class DecodeArgs(ctypes.Structure):
                 ("num_splits", _i32), ("softmax_scale", _f32)]
 
 
+class KvWriteArgs(ctypes.Structure):
+    _fields_ = [("key", _vp), ("value", _vp), ("k_cache", _vp), ("v_cache", _vp),
+                ("slot_mapping", _vp), ("key_stride", _i64), ("value_stride", _i64),
+                ("num_tokens", _i32), ("num_kv_heads", _i32), ("head_dim", _i32),
+                ("page_size", _i32), ("num_pages", _i32), ("dtype", _i32)]
+
+
 # Exported symbols and their (restype, argtypes); the CPU test checks this list
 # against include/fa_b200.h.
 SIGNATURES = {
@@ -84,6 +91,7 @@ SIGNATURES = {
     "fa_decode": (_i32, [ctypes.POINTER(DecodeArgs), _vp, ctypes.c_size_t, _vp]),
     "fa_decode_noalloc": (_i32, [ctypes.POINTER(DecodeArgs), _vp]),
     "fa_decode_noalloc_scratch_bytes": (ctypes.c_size_t, []),
+    "fa_kv_cache_write": (_i32, [ctypes.POINTER(KvWriteArgs), _vp]),
     "fa_status_string": (ctypes.c_char_p, [_i32]),
     "fa_read_device_error": (_i32, [ctypes.POINTER(_i32), ctypes.POINTER(_i32),
                                     ctypes.POINTER(_i32), _i32]),
@@ -285,6 +293,19 @@ def decode(q, k_cache, v_cache, block_table, seq_lens, page_size, num_kv_heads, 
     with torch.cuda.device(dev):
         check(lib.fa_decode(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), nbytes, _stream(dev)))
     return out
+
+
+def kv_cache_write(key, value, k_cache, v_cache, slot_mapping):
+    """Scatters key/value [num_tokens, Hkv, D] into the paged caches at slot_mapping."""
+    _require_cuda(key, value, k_cache, v_cache)
+    dev = key.device
+    n, hkv, d = key.shape
+    sm = slot_mapping.to(device=dev, dtype=torch.int64).contiguous()
+    a = KvWriteArgs(key.data_ptr(), value.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                    sm.data_ptr(), key.stride(0), value.stride(0), n, hkv, d,
+                    k_cache.shape[1], k_cache.shape[0], _dtype_code(key.dtype))
+    with torch.cuda.device(dev):
+        check(load().fa_kv_cache_write(ctypes.byref(a), _stream(dev)))
 
 
 def selftest_umma(a, b, n, k, b_mn, a_tmem):
