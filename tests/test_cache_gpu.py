@@ -23,6 +23,8 @@ CACHE_CASES = [
     (37, 8, 128, 16, 40, torch.bfloat16),
     (1000, 2, 256, 32, 80, torch.float16),
     (513, 4, 64, 128, 8, torch.bfloat16),
+    (300, 1, 128, 16, 40, torch.bfloat16),   # 256-byte rows: two rows per warp
+    (77, 3, 64, 16, 10, torch.float16),      # 384-byte rows: 24 of 32 lanes busy
 ]
 
 
