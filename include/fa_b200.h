@@ -12,8 +12,8 @@
  *   paged  q/out [num_tokens, H, D], lse [H, num_tokens] fp32
  *   decode q/out [B, H, D]
  * Supported: fp16 and bf16 inputs, H % Hk == 0; head_dim 64/128/256 (dense
- * forward, paged prefill), 64/128 (dense backward, decode; decode also needs
- * H / Hkv <= 16).  Pointers 16-byte aligned, strides multiples of 8 elements.
+ * forward, paged prefill, decode with H / Hkv <= 16), 64/128 (dense backward).
+ * Pointers 16-byte aligned, strides multiples of 8 elements.
  */
 #ifndef FA_B200_H_
 #define FA_B200_H_

@@ -5,7 +5,7 @@ import torch
 
 import tilelang_fa_v100 as fa
 from tilelang_fa_v100 import _ext
-from helpers import assert_close, golden, max_abs
+from helpers import assert_close, golden, golden_names, max_abs
 from oracle import attention_ref as R
 
 pytestmark = pytest.mark.gpu
@@ -39,8 +39,9 @@ def _check(cuda_dev, q, kc, vc, bt, sl, page, num_splits=0):
     assert_close(lse.cpu().numpy(), ref_lse, what="lse")
 
 
-def test_golden_decode(cuda_dev):
-    g = golden("decode_gqa_16_4_d128")
+@pytest.mark.parametrize("name", golden_names("decode_"))
+def test_golden_decode(cuda_dev, name):
+    g = golden(name)
     t = lambda x: torch.from_numpy(x).to(cuda_dev)
     out = fa.tilelang_decode_forward(t(g["q_flat"]), t(g["k_cache"]), t(g["v_cache"]),
                                      t(g["block_table"]), t(g["seq_lens"]))
@@ -60,6 +61,10 @@ DECODE_CASES = [
     ([129, 1000], 24, 4, 64, 64, torch.bfloat16, 5),      # 6 q heads per kv head, page 64
     ([0, 50], 8, 2, 128, 16, torch.float16, 1),           # an empty sequence, single split
     ([0, 50], 8, 2, 128, 16, torch.float16, 4),           # an empty sequence, split path
+    ([64, 129, 1000, 5000], 32, 2, 256, 16, torch.bfloat16, 0),  # D = 256, 16 q heads per kv head
+    ([300, 1, 0], 8, 1, 256, 16, torch.float16, 3),       # D = 256 MQA 8:1, explicit splits
+    ([17, 4096], 16, 4, 256, 32, torch.bfloat16, 1),      # D = 256, 4 kv heads per CTA, direct
+    ([2000], 8, 8, 256, 64, torch.float16, 0),            # D = 256 MHA, 8 kv heads in 2 CTAs
 ]
 
 

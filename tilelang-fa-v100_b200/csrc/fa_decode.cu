@@ -9,8 +9,9 @@
 //     16-token chunks of one sequence; splits run in parallel across SMs.
 //   * warp 0 lane 0 streams chunks with TMA (one 16-row x 128-byte box per kv head
 //     and 64-column half) into a STAGES-deep ring of 128-byte-swizzled slots.
-//   * one compute warp per kv head: the G = H/Hkv query heads of the group are the
-//     rows of an m16n8k16 MMA, so one read of K/V serves the whole group.
+//   * one compute warp per kv head (two at D = 256, each accumulating half of the
+//     output columns): the G = H/Hkv query heads of the group are the rows of an
+//     m16n8k16 MMA, so one read of K/V serves the whole group.
 //   * per split: partial O (normalised) and LSE in an fp32 workspace; a second
 //     kernel merges the splits with LSE weights.  With one split the first kernel
 //     writes the final output directly.
@@ -23,13 +24,16 @@
 namespace fa {
 
 constexpr int kDecChunk = 16;  // tokens per pipeline chunk
-constexpr int kDecMaxGroup = 8;  // kv heads per CTA
 
 template <int D>
 struct DecCfg {
   static constexpr int DH = D / 64;
-  static constexpr int HEAD_BYTES = kDecChunk * D * 2;  // one kv head, one chunk, K or V
-  static constexpr int STAGE_BYTES_MAX = 2 * kDecMaxGroup * HEAD_BYTES;
+  static constexpr int WPH = D > 128 ? 2 : 1;             // compute warps per kv head
+  static constexpr int DW = D / WPH;                      // output columns per compute warp
+  static constexpr int MAXG = D > 128 ? 4 : 8;            // kv heads per CTA
+  static constexpr int NTHREADS = 32 + 32 * MAXG * WPH;   // producer warp + compute warps
+  static constexpr int HEAD_BYTES = kDecChunk * D * 2;    // one kv head, one chunk, K or V
+  static constexpr int STAGE_BYTES_MAX = 2 * MAXG * HEAD_BYTES;
   static constexpr int STAGES = (D == 64) ? 6 : 3;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES_MAX + 256;
   static_assert(SMEM_BYTES <= 232448, "decode smem budget");
@@ -91,7 +95,7 @@ struct DecSmemCtl {
 };
 
 template <typename T, int D>
-__global__ void __launch_bounds__(32 + 32 * kDecMaxGroup, 1)
+__global__ void __launch_bounds__(DecCfg<D>::NTHREADS, 1)
     fa_decode_split_kernel(const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v, const DecParams p) {
   using Cfg = DecCfg<D>;
@@ -127,7 +131,7 @@ __global__ void __launch_bounds__(32 + 32 * kDecMaxGroup, 1)
     }
     return;
   }
-  const int ncompute = HG;
+  const int ncompute = HG * Cfg::WPH;
 
   if (threadIdx.x == 0) {
     ctl->abort_flag = 0;
@@ -174,7 +178,8 @@ __global__ void __launch_bounds__(32 + 32 * kDecMaxGroup, 1)
     }
     return;
   }
-  const int hh = warp - 1;
+  const int hh = (warp - 1) / Cfg::WPH;    // kv head of this compute warp
+  const int part = (warp - 1) % Cfg::WPH;  // output-column half (D = 256)
   if (hh >= HG) return;
   const int hk = hk0 + hh;
   const int G = p.G;
@@ -198,9 +203,10 @@ __global__ void __launch_bounds__(32 + 32 * kDecMaxGroup, 1)
       qa[ks][3] = ld2(g + 8, k0 + 8);
     }
   }
-  float o[D / 8][4];
+  constexpr int DW = Cfg::DW;
+  float o[DW / 8][4];
 #pragma unroll
-  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  for (int i = 0; i < DW / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   const float c2 = p.scale_log2;
 
@@ -265,15 +271,16 @@ __global__ void __launch_bounds__(32 + 32 * kDecMaxGroup, 1)
     pa[2] = Pack2<T>::pack(pr[1][0], pr[1][1]);
     pa[3] = Pack2<T>::pack(pr[1][2], pr[1][3]);
 #pragma unroll
-    for (int dn = 0; dn < D / 8; ++dn) {
+    for (int dn = 0; dn < DW / 8; ++dn) {
       o[dn][0] *= f0;
       o[dn][1] *= f0;
       o[dn][2] *= f1;
       o[dn][3] *= f1;
     }
-    // O[16 x D] += P[16 x 16 tokens] V[16 tokens x D]
+    // O[16 x DW] += P[16 x 16 tokens] V[16 tokens x this warp's DW columns]
 #pragma unroll
-    for (int dp = 0; dp < D / 16; ++dp) {
+    for (int dpl = 0; dpl < DW / 16; ++dpl) {
+      const int dp = part * (DW / 16) + dpl;
       // matrices: (tok 0-7, d 16dp..+7), (tok 8-15, same), (tok 0-7, d +8..+15), (tok 8-15, +8..)
       const int mi = lane >> 3;
       const int row = ((mi & 1) << 3) + (lane & 7);
@@ -281,8 +288,8 @@ __global__ void __launch_bounds__(32 + 32 * kDecMaxGroup, 1)
       const uint32_t addr = vbase + ((dp * 16) >> 6) * (kDecChunk * 128) + swz(row, dchunk);
       uint32_t b0, b1, b2, b3;
       ldsm_x4_t(addr, b0, b1, b2, b3);
-      mma16816<kBf16>(o[2 * dp], pa, b0, b1);
-      mma16816<kBf16>(o[2 * dp + 1], pa, b2, b3);
+      mma16816<kBf16>(o[2 * dpl], pa, b0, b1);
+      mma16816<kBf16>(o[2 * dpl + 1], pa, b2, b3);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&ctl->empty[s]));
@@ -306,20 +313,21 @@ __global__ void __launch_bounds__(32 + 32 * kDecMaxGroup, 1)
     const float inv = half ? inv1 : inv0;
     const float lse = half ? lse1 : lse0;
     if (direct) {
-      T* dst = reinterpret_cast<T*>(p.out) + ((int64_t)b * p.H + h) * D;
+      T* dst = reinterpret_cast<T*>(p.out) + ((int64_t)b * p.H + h) * D + part * DW;
 #pragma unroll
-      for (int dn = 0; dn < D / 8; ++dn) {
+      for (int dn = 0; dn < DW / 8; ++dn) {
         const uint32_t v = Pack2<T>::pack(o[dn][half * 2] * inv, o[dn][half * 2 + 1] * inv);
         *reinterpret_cast<uint32_t*>(dst + dn * 8 + qd) = v;
       }
-      if (p.lse != nullptr && (lane & 3) == 0) p.lse[(int64_t)b * p.H + h] = lse;
+      if (p.lse != nullptr && (lane & 3) == 0 && part == 0) p.lse[(int64_t)b * p.H + h] = lse;
     } else {
-      float* dst = p.o_part + (((int64_t)b * p.num_splits + split) * p.H + h) * D;
+      float* dst = p.o_part + (((int64_t)b * p.num_splits + split) * p.H + h) * D + part * DW;
 #pragma unroll
-      for (int dn = 0; dn < D / 8; ++dn)
+      for (int dn = 0; dn < DW / 8; ++dn)
         *reinterpret_cast<float2*>(dst + dn * 8 + qd) =
             make_float2(o[dn][half * 2] * inv, o[dn][half * 2 + 1] * inv);
-      if ((lane & 3) == 0) p.lse_part[((int64_t)b * p.num_splits + split) * p.H + h] = lse;
+      if ((lane & 3) == 0 && part == 0)
+        p.lse_part[((int64_t)b * p.num_splits + split) * p.H + h] = lse;
     }
   }
 }
@@ -365,8 +373,8 @@ __global__ void __launch_bounds__(256) fa_decode_combine_kernel(const DecParams 
 }
 
 // ------------------------------------------------------------------- host side
-static int dec_group(int hkv) {
-  for (int g = kDecMaxGroup; g >= 1; --g)
+static int dec_group(int hkv, int max_group) {
+  for (int g = max_group; g >= 1; --g)
     if (hkv % g == 0) return g;
   return 1;
 }
@@ -408,8 +416,11 @@ static int launch_decode_impl(const CUtensorMap& tk, const CUtensorMap& tv, cons
     attr_set[dev] = true;
   }
   dim3 grid(p.num_splits, p.Hkv / p.HG, p.B);
+  // Shared memory for the actual group: small groups (few kv heads) fit several CTAs
+  // per SM, which keeps enough K/V bytes in flight.
+  const int smem = 1024 + Cfg::STAGES * 2 * p.HG * Cfg::HEAD_BYTES + 256;
   prof_begin(FA_PROF_DECODE, st);
-  kern<<<grid, 32 + 32 * p.HG, Cfg::SMEM_BYTES, st>>>(tk, tv, p);
+  kern<<<grid, 32 + 32 * p.HG * Cfg::WPH, smem, st>>>(tk, tv, p);
   prof_end(FA_PROF_DECODE, st);
   FA_CUDA_TRY(cudaGetLastError());
   count_launch();
@@ -426,7 +437,7 @@ static int launch_decode_impl(const CUtensorMap& tk, const CUtensorMap& tv, cons
 int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err,
                   cudaStream_t st) {
   const int D = a->head_dim;
-  if (D != 64 && D != 128) return FA_ERR_UNSUPPORTED;
+  if (D != 64 && D != 128 && D != 256) return FA_ERR_UNSUPPORTED;
   const int G = a->num_heads / a->num_kv_heads;
   if (G > 16) return FA_ERR_UNSUPPORTED;
   const int ps = a->page_size;
@@ -457,7 +468,7 @@ int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err
   p.H = a->num_heads;
   p.Hkv = a->num_kv_heads;
   p.G = G;
-  p.HG = dec_group(a->num_kv_heads);
+  p.HG = dec_group(a->num_kv_heads, D > 128 ? DecCfg<256>::MAXG : DecCfg<128>::MAXG);
   p.page_size = ps;
   p.num_pages = a->num_pages;
   p.max_blocks = a->max_blocks;
@@ -476,6 +487,9 @@ int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err
   if (D == 64)
     return bf16 ? launch_decode_impl<__nv_bfloat16, 64>(tk, tv, p, st)
                 : launch_decode_impl<__half, 64>(tk, tv, p, st);
+  if (D == 256)
+    return bf16 ? launch_decode_impl<__nv_bfloat16, 256>(tk, tv, p, st)
+                : launch_decode_impl<__half, 256>(tk, tv, p, st);
   return bf16 ? launch_decode_impl<__nv_bfloat16, 128>(tk, tv, p, st)
               : launch_decode_impl<__half, 128>(tk, tv, p, st);
 }
