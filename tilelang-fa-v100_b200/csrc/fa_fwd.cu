@@ -58,6 +58,7 @@ struct FwdSmemCtl {
   uint64_t p_ready[2];
   uint64_t o_final[2];
   uint64_t exp_turn[2];  // softmax ping-pong: warpgroup t may run its exp phase
+  uint64_t o_staged[2];  // output tile t written to shared memory (TMA store may start)
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -76,7 +77,8 @@ __device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
 template <typename T, int D, int NQ, bool PAGED>
 __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                  const FwdParams p) {
   using Cfg = FwdCfg<D, NQ>;
   constexpr int ST = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -157,6 +159,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
       mbar_init(smem_u32(&ctl->p_ready[t]), 128);
       mbar_init(smem_u32(&ctl->o_final[t]), 1);
       mbar_init(smem_u32(&ctl->exp_turn[t]), 128);
+      mbar_init(smem_u32(&ctl->o_staged[t]), 128);
     }
     mbar_init(smem_u32(&ctl->drain), 1);
     fence_barrier_init();
@@ -473,6 +476,13 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
       tc_fence_after();
       const bool have = l > 0.f;
       const float inv = have ? 1.f / l : 0.f;
+      // Output tile through shared memory and one TMA store per 64-column chunk (the Q
+      // tile's buffer: every MMA that read it finished before o_final).  Dense tiles
+      // always (the tensor map clips rows past Sq); paged tiles when all their tokens
+      // belong to this sequence, else per-row stores (the next rows are another
+      // sequence's).
+      const bool tma_out = PAGED ? (tok0 + t * TPT + TPT <= q_len) : true;
+      const uint32_t stage = sQ + t * Cfg::TILE_BYTES;
       T* orow = reinterpret_cast<T*>(p.out) + (PAGED ? 0 : (int64_t)b * p.o_sb) +
                 (int64_t)(tok_base + lt) * p.o_st + (int64_t)h * p.o_sh;
 #pragma unroll
@@ -489,7 +499,15 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
           const float a1 = have ? __uint_as_float(o[2 * c + 1]) * inv : 0.f;
           pk[c] = Pack2<T>::pack(a0, a1);
         }
-        if (row_valid) {
+        if (tma_out) {
+          // row r of the 128-byte-swizzled tile, 16-byte units (c0 % 64) / 8 .. + 3
+          const uint32_t rowa = stage + (c0 >> 6) * Cfg::CHUNK_BYTES + r * 128;
+          const int u0 = (c0 & 63) >> 3;
+#pragma unroll
+          for (int m = 0; m < 4; ++m)
+            st_shared_v4(rowa + (((u0 + m) ^ (r & 7)) << 4), pk[4 * m], pk[4 * m + 1],
+                         pk[4 * m + 2], pk[4 * m + 3]);
+        } else if (row_valid) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c0);
           dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
@@ -500,6 +518,19 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
       if (row_valid && p.lse != nullptr) {
         const float lse = have ? m_ref * p.scale + logf(l) : NEG_INF;
         p.lse[(PAGED ? 0 : (int64_t)b * p.lse_sb) + (int64_t)h * p.lse_sh + tok_base + lt] = lse;
+      }
+      if (tma_out) {
+        fence_async_shared();
+        mbar_arrive(smem_u32(&ctl->o_staged[t]));
+        if ((threadIdx.x & 127) == 0 &&
+            mbar_wait(smem_u32(&ctl->o_staged[t]), 0, abort_flag, p.err, FA_SITE_FWD_SOFTMAX)) {
+          const int tok = tok_base + tok0 + t * TPT;
+#pragma unroll
+          for (int dh = 0; dh < Cfg::DH; ++dh)
+            tma_store_4d(&tm_o, stage + dh * Cfg::CHUNK_BYTES, dh * 64, hk * G, tok, PAGED ? 0 : b);
+          bulk_commit_group();
+          bulk_wait_group_read();
+        }
       }
     }
   }
@@ -515,7 +546,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
 // ------------------------------------------------------------------- host side
 template <typename T, int D, int NQ, bool PAGED>
 static int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                           const FwdParams& p, dim3 grid, cudaStream_t st) {
+                           const CUtensorMap& to, const FwdParams& p, dim3 grid, cudaStream_t st) {
   using Cfg = FwdCfg<D, NQ>;
   auto kern = fa_fwd_kernel<T, D, NQ, PAGED>;
   static bool attr_set[64] = {false};
@@ -528,7 +559,7 @@ static int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const C
   }
   const int kind = PAGED ? FA_PROF_PAGED : FA_PROF_FWD;
   prof_begin(kind, st);
-  kern<<<grid, Cfg::NTHREADS, Cfg::SMEM_BYTES, st>>>(tq, tk, tv, p);
+  kern<<<grid, Cfg::NTHREADS, Cfg::SMEM_BYTES, st>>>(tq, tk, tv, to, p);
   prof_end(kind, st);
   FA_CUDA_TRY(cudaGetLastError());
   count_launch();
@@ -536,11 +567,11 @@ static int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const C
 }
 
 template <int D, int NQ, bool PAGED>
-static int dispatch_dtype(int dtype, const CUtensorMap& tq, const CUtensorMap& tk,
+static int dispatch_dtype(int dtype, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& to,
                           const CUtensorMap& tv, const FwdParams& p, dim3 grid, cudaStream_t st) {
   if (dtype == FA_DTYPE_BF16)
-    return launch_fwd_impl<__nv_bfloat16, D, NQ, PAGED>(tq, tk, tv, p, grid, st);
-  return launch_fwd_impl<__half, D, NQ, PAGED>(tq, tk, tv, p, grid, st);
+    return launch_fwd_impl<__nv_bfloat16, D, NQ, PAGED>(tq, tk, tv, to, p, grid, st);
+  return launch_fwd_impl<__half, D, NQ, PAGED>(tq, tk, tv, to, p, grid, st);
 }
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
@@ -559,7 +590,7 @@ int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out))
     return FA_ERR_ALIGNMENT;
   const CUtensorMapDataType dt = tmap_dtype(a->dtype);
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   {
     const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a->num_heads, (uint64_t)a->seqlen_q,
                               (uint64_t)a->batch};
@@ -567,6 +598,9 @@ int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
                              (uint64_t)a->q_stride[0] * 2};
     const uint32_t box[4] = {64, (uint32_t)G, (uint32_t)(128 / G), 1};  // TPT tokens x G heads
     FA_TMAP_TRY(encode_tmap(&tq, dt, 4, a->q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    const uint64_t ostr[3] = {(uint64_t)a->o_stride[2] * 2, (uint64_t)a->o_stride[1] * 2,
+                              (uint64_t)a->o_stride[0] * 2};
+    FA_TMAP_TRY(encode_tmap(&to, dt, 4, a->out, dims, ostr, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   const void* kv_ptr[2] = {a->k, a->v};
   const int64_t* kv_str[2] = {a->k_stride, a->v_stride};
@@ -599,9 +633,9 @@ int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
   const int TPB = NQ * (128 / G);
   dim3 grid((a->seqlen_q + TPB - 1) / TPB, a->num_heads_k, a->batch);
   switch (D) {
-    case 64: return dispatch_dtype<64, 2, false>(a->dtype, tq, tk, tv, p, grid, st);
-    case 128: return dispatch_dtype<128, 2, false>(a->dtype, tq, tk, tv, p, grid, st);
-    case 256: return dispatch_dtype<256, 1, false>(a->dtype, tq, tk, tv, p, grid, st);
+    case 64: return dispatch_dtype<64, 2, false>(a->dtype, tq, tk, to, tv, p, grid, st);
+    case 128: return dispatch_dtype<128, 2, false>(a->dtype, tq, tk, to, tv, p, grid, st);
+    case 256: return dispatch_dtype<256, 1, false>(a->dtype, tq, tk, to, tv, p, grid, st);
     default: return FA_ERR_UNSUPPORTED;
   }
 }
@@ -617,13 +651,14 @@ int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st) {
   if (!aligned16(a->q) || !aligned16(a->k_cache) || !aligned16(a->v_cache) || !aligned16(a->out))
     return FA_ERR_ALIGNMENT;
   const CUtensorMapDataType dt = tmap_dtype(a->dtype);
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   {
     const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a->num_heads, (uint64_t)a->num_tokens, 1};
     const uint64_t str[3] = {(uint64_t)D * 2, (uint64_t)a->num_heads * D * 2,
                              (uint64_t)a->num_tokens * a->num_heads * D * 2};
     const uint32_t box[4] = {64, (uint32_t)G, (uint32_t)(128 / G), 1};  // TPT tokens x G heads
     FA_TMAP_TRY(encode_tmap(&tq, dt, 4, a->q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    FA_TMAP_TRY(encode_tmap(&to, dt, 4, a->out, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   const void* kv_ptr[2] = {a->k_cache, a->v_cache};
   CUtensorMap* kv_map[2] = {&tk, &tv};
@@ -664,9 +699,9 @@ int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st) {
   // Sum over sequences of ceil(q_len / TPB) <= num_tokens / TPB + num_seqs.
   dim3 grid(a->num_tokens / TPB + a->num_seqs, a->num_kv_heads, 1);
   switch (D) {
-    case 64: return dispatch_dtype<64, 2, true>(a->dtype, tq, tk, tv, p, grid, st);
-    case 128: return dispatch_dtype<128, 2, true>(a->dtype, tq, tk, tv, p, grid, st);
-    case 256: return dispatch_dtype<256, 1, true>(a->dtype, tq, tk, tv, p, grid, st);
+    case 64: return dispatch_dtype<64, 2, true>(a->dtype, tq, tk, to, tv, p, grid, st);
+    case 128: return dispatch_dtype<128, 2, true>(a->dtype, tq, tk, to, tv, p, grid, st);
+    case 256: return dispatch_dtype<256, 1, true>(a->dtype, tq, tk, to, tv, p, grid, st);
     default: return FA_ERR_UNSUPPORTED;
   }
 }
