@@ -121,42 +121,76 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------- 1. preprocess
+// D / 8 lanes per row (16-byte loads), 32 / (D / 8) rows per warp and pass, kPrepPasses
+// passes per warp with every load issued before the arithmetic.  With a dQ accumulator
+// (atomic mode) the same kernel clears its rows, so no separate memset is needed.
+constexpr int kPrepPasses = 4;
+
 template <typename T, int D>
 __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const T* __restrict__ o,
                                                           const T* __restrict__ dout,
                                                           const float* __restrict__ lse,
-                                                          float* lse2, float* dsum, int B, int Sq,
-                                                          int H, int Sq_pad, int64_t o_sb,
-                                                          int64_t o_ss, int64_t o_sh,
+                                                          float* lse2, float* dsum, float* dq_acc,
+                                                          int B, int Sq, int H, int Sq_pad,
+                                                          int64_t o_sb, int64_t o_ss, int64_t o_sh,
                                                           int64_t do_sb, int64_t do_ss,
                                                           int64_t do_sh) {
-  const int warp = (blockIdx.x * 256 + threadIdx.x) >> 5;
+  constexpr int TPR = D / 8;
+  constexpr int RPW = 32 / TPR;
   const int lane = threadIdx.x & 31;
+  const int sub = lane / TPR, cl = lane % TPR;
+  const int64_t warp = ((int64_t)blockIdx.x * 256 + threadIdx.x) >> 5;
   const int64_t rows = (int64_t)B * H * Sq_pad;
-  if (warp >= rows) return;
-  const int i = warp % Sq_pad;
-  const int bh = warp / Sq_pad;
-  const int h = bh % H, b = bh / H;
-  float acc = 0.f;
-  float l2 = INFINITY;
-  if (i < Sq) {
-    const T* orow = o + b * o_sb + (int64_t)i * o_ss + (int64_t)h * o_sh;
-    const T* drow = dout + b * do_sb + (int64_t)i * do_ss + (int64_t)h * do_sh;
-    constexpr int PER = D / 32;  // 2 or 4 elements per lane
+  const int64_t row0 = warp * RPW * kPrepPasses;
+  uint4 av[kPrepPasses], dv[kPrepPasses];
+  bool live[kPrepPasses];
 #pragma unroll
-    for (int e = 0; e < PER; e += 2) {
-      const float2 a = Pack2<T>::unpack(*reinterpret_cast<const uint32_t*>(orow + lane * PER + e));
-      const float2 c = Pack2<T>::unpack(*reinterpret_cast<const uint32_t*>(drow + lane * PER + e));
-      acc += a.x * c.x + a.y * c.y;
+  for (int ps = 0; ps < kPrepPasses; ++ps) {
+    const int64_t row = row0 + ps * RPW + sub;
+    const int i = (int)(row % Sq_pad);
+    const int64_t bh = row / Sq_pad;
+    live[ps] = row < rows && i < Sq;
+    av[ps] = dv[ps] = make_uint4(0u, 0u, 0u, 0u);
+    if (live[ps]) {
+      const int h = (int)(bh % H), b = (int)(bh / H);
+      av[ps] = __ldcs(reinterpret_cast<const uint4*>(o + b * o_sb + (int64_t)i * o_ss +
+                                                     (int64_t)h * o_sh) + cl);
+      dv[ps] = __ldcs(reinterpret_cast<const uint4*>(dout + b * do_sb + (int64_t)i * do_ss +
+                                                     (int64_t)h * do_sh) + cl);
+    }
+  }
+#pragma unroll
+  for (int ps = 0; ps < kPrepPasses; ++ps) {
+    const int64_t row = row0 + ps * RPW + sub;
+    const uint32_t* a = reinterpret_cast<const uint32_t*>(&av[ps]);
+    const uint32_t* c = reinterpret_cast<const uint32_t*>(&dv[ps]);
+    float acc = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 x = Pack2<T>::unpack(a[e]);
+      const float2 y = Pack2<T>::unpack(c[e]);
+      acc = fmaf(x.x, y.x, fmaf(x.y, y.y, acc));
     }
 #pragma unroll
-    for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
-    const float L = lse[((int64_t)b * H + h) * Sq + i];
-    l2 = (L == -INFINITY) ? INFINITY : L * 1.4426950408889634f;
-  }
-  if (lane == 0) {
-    lse2[warp] = l2;
-    dsum[warp] = acc;
+    for (int sh = TPR / 2; sh > 0; sh >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, sh);
+    if (row < rows) {
+      if (cl == 0) {
+        float l2 = INFINITY;  // padded rows: P = exp2(S - inf) = 0
+        if (live[ps]) {
+          const int i = (int)(row % Sq_pad);
+          const int64_t bh = row / Sq_pad;
+          const float L = lse[bh * Sq + i];
+          l2 = (L == -INFINITY) ? INFINITY : L * 1.4426950408889634f;
+        }
+        lse2[row] = l2;
+        dsum[row] = live[ps] ? acc : 0.f;
+      }
+      if (dq_acc != nullptr) {
+        float4* z = reinterpret_cast<float4*>(dq_acc + row * D);
+#pragma unroll
+        for (int q = cl; q < D / 4; q += TPR) z[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
   }
 }
 
@@ -856,17 +890,19 @@ template <typename T, int D>
 static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const CUtensorMap& tk,
                            const CUtensorMap& tv, const CUtensorMap& tdo, BwdParams& p,
                            cudaStream_t st) {
-  const int rows_blocks = (int)(((int64_t)a->batch * a->num_heads * p.Sq_pad * 32 + 255) / 256);
-  fa_bwd_prep_kernel<T, D><<<rows_blocks, 256, 0, st>>>(
-      reinterpret_cast<const T*>(a->out), reinterpret_cast<const T*>(a->dout), a->lse,
-      const_cast<float*>(p.lse2), const_cast<float*>(p.dsum), a->batch, a->seqlen_q,
-      a->num_heads, p.Sq_pad, a->o_stride[0], a->o_stride[1], a->o_stride[2], a->do_stride[0],
-      a->do_stride[1], a->do_stride[2]);
-  FA_CUDA_TRY(cudaGetLastError());
-  count_launch();
+  {
+    const int64_t rows = (int64_t)a->batch * a->num_heads * p.Sq_pad;
+    const int64_t rows_per_block = 8 * (32 / (D / 8)) * kPrepPasses;
+    const int blocks = (int)((rows + rows_per_block - 1) / rows_per_block);
+    fa_bwd_prep_kernel<T, D><<<blocks, 256, 0, st>>>(
+        reinterpret_cast<const T*>(a->out), reinterpret_cast<const T*>(a->dout), a->lse,
+        const_cast<float*>(p.lse2), const_cast<float*>(p.dsum), p.dq_acc, a->batch, a->seqlen_q,
+        a->num_heads, p.Sq_pad, a->o_stride[0], a->o_stride[1], a->o_stride[2], a->do_stride[0],
+        a->do_stride[1], a->do_stride[2]);
+    FA_CUDA_TRY(cudaGetLastError());
+    count_launch();
+  }
   if (!a->deterministic) {
-    FA_CUDA_TRY(cudaMemsetAsync(p.dq_acc, 0,
-                                (size_t)a->batch * a->num_heads * p.Sq_pad * D * sizeof(float), st));
     auto kern = fa_bwd_dkdv_kernel<T, D, true>;
     static bool attr[64] = {false};
     int dev = 0;
