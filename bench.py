@@ -277,8 +277,9 @@ def time_paged(dev, steps, warmup):
     return ms, 4 * 128 * visible_pairs(16, 32, 1024, 1024, True) / ms / 1e9
 
 
-def decode_problem(dev, seed, batch=256):
-    """256 seqs, L ~ U[512, 8192], H 32 / Hkv 8, D 128, page 16, bf16."""
+def decode_problem(dev, seed, batch=256, hkv=8, d=128, heads=32):
+    """256 seqs, L ~ U[512, 8192], H 32 / Hkv 8, D 128, page 16, bf16
+    (other head layouts with the same length distribution on request)."""
     rng = np.random.default_rng(seed)
     lens = rng.integers(512, 8193, size=batch).astype(np.int32)
     pps = (lens + 15) // 16
@@ -290,16 +291,16 @@ def decode_problem(dev, seed, batch=256):
         bt[i, :pps[i]] = perm[c:c + pps[i]]
         c += pps[i]
     g = torch.Generator(device=dev).manual_seed(seed + 1)
-    kc = torch.randn(total, 16, 8, 128, generator=g, device=dev).to(torch.bfloat16)
-    vc = torch.randn(total, 16, 8, 128, generator=g, device=dev).to(torch.bfloat16)
-    q = torch.randn(batch, 32, 128, generator=g, device=dev).to(torch.bfloat16)
-    nbytes = int(lens.sum()) * 8 * 128 * 2 * 2 + 2 * batch * 32 * 128 * 2 + total * 4
+    kc = torch.randn(total, 16, hkv, d, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(total, 16, hkv, d, generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn(batch, heads, d, generator=g, device=dev).to(torch.bfloat16)
+    nbytes = int(lens.sum()) * hkv * d * 2 * 2 + 2 * batch * heads * d * 2 + total * 4
     return q, kc, vc, torch.from_numpy(bt).to(dev), torch.from_numpy(lens).to(dev), nbytes
 
 
-def time_decode(dev, steps, warmup, seed=0):
+def time_decode(dev, steps, warmup, seed=0, hkv=8, d=128, heads=32):
     import tilelang_fa_v100 as fa
-    q, kc, vc, bt, sl, nbytes = decode_problem(dev, seed)
+    q, kc, vc, bt, sl, nbytes = decode_problem(dev, seed, hkv=hkv, d=d, heads=heads)
     run = lambda: fa.tilelang_decode_forward(q, kc, vc, bt, sl)
     for _ in range(warmup):
         run()
@@ -477,6 +478,10 @@ def run_ours(args):
         sec["cfg5_decode_bf16_GBps"] = {"gbs": dgbs, "ms": dms,
                                         "frac_of_hbm": dgbs / peaks.get("hbm_gbs", 6538.6),
                                         "peak_source": src + " hbm_gbs"}
+        d2ms, d2gbs = time_decode(dev, args.steps, 3, seed=rank, hkv=2, d=256, heads=32)
+        sec["decode_bf16_H32_Hkv2_D256_GBps"] = {
+            "gbs": d2gbs, "ms": d2ms, "frac_of_hbm": d2gbs / peaks.get("hbm_gbs", 6538.6),
+            "note": "the reference's 32/2 D=256 test configuration, cfg5 length distribution"}
         kms, kgbs = time_kv_write(dev, args.steps, 3)
         sec["kv_cache_write_bf16_65536tok_Hkv8_D128_GBps"] = {
             "gbs": kgbs, "ms": kms, "frac_of_hbm": kgbs / peaks.get("hbm_gbs", 6538.6)}
