@@ -40,7 +40,7 @@ struct FwdCfg {
   static constexpr int DH = D / 64;                       // 128-byte column chunks
   static constexpr int TILE_BYTES = 128 * D * 2;          // one Q, K or V tile
   static constexpr int CHUNK_BYTES = 128 * 128;           // one 64-column chunk of a tile
-  static constexpr int STAGES = (D == 64) ? 6 : (D == 128 ? 4 : 2);
+  static constexpr int STAGES = (D == 64) ? 6 : (D == 128 ? 5 : 2);
   static constexpr int NTHREADS = 128 + 128 * NQ;
   static constexpr int TMEM_COLS = 512;
   static_assert(NQ * (128 + D) <= TMEM_COLS, "TMEM budget: S + O per Q tile");
@@ -181,9 +181,9 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
 
   if (warp == 0) {
     // ============================================================ TMA producer
-    // Lane 0 issues every copy.  Paged: the whole warp fetches the page ids of the next
-    // KV tile (lane r: box r) while lane 0 issues the current one, so block-table reads
-    // never sit between two copies.
+    // Dense: lane 0 issues every copy.  Paged: lane r fetches the page id of box r of the
+    // next KV tile while the current tile's copies go out, and issues box r's copies
+    // itself, so block-table reads never sit between two copies.
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
@@ -232,14 +232,14 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
         const uint32_t dst = sKV + s * Cfg::TILE_BYTES;
         if (lane == 0) mbar_arrive_expect_tx(fb, Cfg::TILE_BYTES);
         if constexpr (PAGED) {
-          for (int r = 0; r < boxes; ++r) {
-            const int page = __shfl_sync(0xffffffffu, pg_cur, r);
-            if (lane == 0) {
-              const int in_page = (j * kFwdBN + r * box_rows) % p.page_size;
-              for (int dh = 0; dh < Cfg::DH; ++dh)
-                tma_load_4d(dst + dh * Cfg::CHUNK_BYTES + r * box_rows * 128, tm, fb, dh * 64, hk,
-                            in_page, page);
-            }
+          // Lane r issues the copies of page box r, so the (up to 16) page copies of a
+          // tile go out in parallel instead of one after another from lane 0.
+          __syncwarp();
+          if (lane < boxes) {
+            const int in_page = (j * kFwdBN + lane * box_rows) % p.page_size;
+            for (int dh = 0; dh < Cfg::DH; ++dh)
+              tma_load_4d(dst + dh * Cfg::CHUNK_BYTES + lane * box_rows * 128, tm, fb, dh * 64, hk,
+                          in_page, pg_cur);
           }
         } else {
           if (lane == 0)
