@@ -54,18 +54,19 @@ static int current_device(int* dev) {
   return FA_OK;
 }
 
-// Driver entry points used to bind the caller's context to the calling thread.
-typedef CUresult (*PFN_streamGetCtx)(CUstream, CUcontext*);
-typedef CUresult (*PFN_ctxGetCurrent)(CUcontext*);
-typedef CUresult (*PFN_ctxSetCurrent)(CUcontext);
-static PFN_streamGetCtx p_stream_get_ctx = nullptr;
-static PFN_ctxGetCurrent p_ctx_get_current = nullptr;
-static PFN_ctxSetCurrent p_ctx_set_current = nullptr;
+// Driver entry points used to bind the caller's context to the calling thread.  Each
+// is requested at an explicit version with its matching signature: the default
+// version of cuStreamGetCtx in CUDA 12.5+ takes a third (green-context) output
+// argument, and calling it through a two-argument pointer lets the driver write
+// through an undefined pointer.
+static PFN_cuStreamGetCtx_v9020 p_stream_get_ctx = nullptr;
+static PFN_cuCtxGetCurrent_v4000 p_ctx_get_current = nullptr;
+static PFN_cuCtxSetCurrent_v4000 p_ctx_set_current = nullptr;
 
-static void* driver_fn(const char* name) {
+static void* driver_fn(const char* name, unsigned int version) {
   void* p = nullptr;
   cudaDriverEntryPointQueryResult q;
-  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess ||
+  if (cudaGetDriverEntryPointByVersion(name, &p, version, cudaEnableDefault, &q) != cudaSuccess ||
       q != cudaDriverEntryPointSuccess)
     return nullptr;
   return p;
@@ -79,9 +80,9 @@ static void* driver_fn(const char* name) {
 static int bind_context(cudaStream_t st) {
   static std::once_flag once;
   std::call_once(once, [] {
-    p_stream_get_ctx = reinterpret_cast<PFN_streamGetCtx>(driver_fn("cuStreamGetCtx"));
-    p_ctx_get_current = reinterpret_cast<PFN_ctxGetCurrent>(driver_fn("cuCtxGetCurrent"));
-    p_ctx_set_current = reinterpret_cast<PFN_ctxSetCurrent>(driver_fn("cuCtxSetCurrent"));
+    p_stream_get_ctx = reinterpret_cast<PFN_cuStreamGetCtx_v9020>(driver_fn("cuStreamGetCtx", 9020));
+    p_ctx_get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(driver_fn("cuCtxGetCurrent", 4000));
+    p_ctx_set_current = reinterpret_cast<PFN_cuCtxSetCurrent_v4000>(driver_fn("cuCtxSetCurrent", 4000));
   });
   const uintptr_t sv = reinterpret_cast<uintptr_t>(st);
   if (sv > 2 && p_stream_get_ctx && p_ctx_get_current && p_ctx_set_current) {
@@ -140,12 +141,8 @@ CUresult encode_tmap(CUtensorMap* map, CUtensorMapDataType dt, int rank, const v
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(
+        driver_fn("cuTensorMapEncodeTiled", 12000));
   });
   if (fn == nullptr) return CUDA_ERROR_NOT_FOUND;
   cuuint64_t gdim[5];
