@@ -71,7 +71,11 @@ def build(verbose=False, ptxas_verbose=False):
             if log:
                 print("== %s\n%s" % (os.path.basename(s), log), file=sys.stderr)
     tmp = LIB + ".tmp"
-    cmd = [_nvcc()] + ARCH + ["-shared", "-o", tmp] + objs + ["-lcudart_static", "-ldl", "-lrt", "-lpthread"]
+    if os.environ.get("FA_CUDART", "static") == "shared":
+        rt = ["-cudart", "shared", "-Xlinker", "-rpath=/usr/local/cuda/lib64"]
+    else:
+        rt = ["-lcudart_static", "-ldl", "-lrt", "-lpthread"]
+    cmd = [_nvcc()] + ARCH + ["-shared", "-o", tmp] + objs + rt
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError("link failed:\n%s\n%s" % (r.stdout, r.stderr))
