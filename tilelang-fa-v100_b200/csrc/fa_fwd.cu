@@ -55,7 +55,8 @@ struct FwdSmemCtl {
   uint64_t kv_full[8];
   uint64_t kv_empty[8];
   uint64_t s_full[2];
-  uint64_t p_ready[2];
+  uint64_t p_half[2];   // first 64 keys of P_t in TMEM (PV over them may start)
+  uint64_t p_ready[2];  // all of P_t in TMEM
   uint64_t o_final[2];
   uint64_t exp_turn[2];  // softmax ping-pong: warpgroup t may run its exp phase
   uint64_t o_staged[2];  // output tile t written to shared memory (TMA store may start)
@@ -81,6 +82,10 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
                   const FwdParams p) {
   using Cfg = FwdCfg<D, NQ>;
   constexpr int ST = Cfg::STAGES;
+  // Release P_t in two halves (PV over the first 64 keys overlaps the second half's
+  // exponentials).  Measured faster for dense D >= 128; for D = 64 (cheap PV) and the
+  // paged path the extra barrier costs more than the overlap gains.
+  constexpr bool kSplitP = (D >= 128) && !PAGED;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -156,6 +161,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
     }
     for (int t = 0; t < NQ; ++t) {
       mbar_init(smem_u32(&ctl->s_full[t]), 1);
+      mbar_init(smem_u32(&ctl->p_half[t]), 128);
       mbar_init(smem_u32(&ctl->p_ready[t]), 128);
       mbar_init(smem_u32(&ctl->o_final[t]), 1);
       mbar_init(smem_u32(&ctl->exp_turn[t]), 128);
@@ -277,12 +283,14 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
           mma_ss(tmem + t * 128, desc_add(qa, o), desc_add(ka, o), idS, kk > 0 ? 1u : 0u);
         }
       };
-      // O_t += P_t V over 128 keys in steps of 16 (V MN-major: step = 16 rows = +2 KB,
-      // 64-column chunks of D at +16 KB = LBO).
-      auto issue_PV = [&](int t, int slot, bool acc) {
+      // O_t += P_t V over keys [64 hf, 64 hf + 64) in steps of 16 (V MN-major: step = 16
+      // rows = +2 KB, 64-column chunks of D at +16 KB = LBO).  P's 16-bit pairs: 16 keys
+      // = 8 TMEM columns.
+      auto issue_PV = [&](int t, int slot, bool acc, int hf) {
         const uint64_t va = desc_add(v_desc0, slot * Cfg::TILE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < kFwdBN / 16; ++kk) {
+        for (int k4 = 0; k4 < kFwdBN / 32; ++k4) {
+          const int kk = hf * (kFwdBN / 32) + k4;
           mma_ts(tmem + NQ * 128 + t * D, tmem + t * 128 + kk * 8, desc_add(va, kk * 2048), idPV,
                  (acc || kk > 0) ? 1u : 0u);
         }
@@ -313,11 +321,19 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
         ok = mbar_wait(smem_u32(&ctl->kv_full[sv]), phv, abort_flag, p.err, FA_SITE_FWD_MMA);
         if (!ok) break;
         for (int t = 0; t < NQ && ok; ++t) {
+          if (kSplitP) {
+            // PV over the first 64 keys runs while the softmax computes the second half.
+            ok = mbar_wait(smem_u32(&ctl->p_half[t]), jj & 1, abort_flag, p.err, FA_SITE_FWD_MMA);
+            if (!ok) break;
+            FA_TRACE_EVENT(8 * t + 6, jj);
+            tc_fence_after();
+            issue_PV(t, sv, jj > 0, 0);
+          }
           ok = mbar_wait(smem_u32(&ctl->p_ready[t]), jj & 1, abort_flag, p.err, FA_SITE_FWD_MMA);
           if (!ok) break;
-          FA_TRACE_EVENT(8 * t + 6, jj);
           tc_fence_after();
-          issue_PV(t, sv, jj > 0);
+          if (!kSplitP) issue_PV(t, sv, jj > 0, 0);
+          issue_PV(t, sv, true, 1);
           if (has_next) {
             if (t == 0) {
               ok = mbar_wait(smem_u32(&ctl->kv_full[sk]), phk, abort_flag, p.err,
@@ -392,13 +408,19 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
           if (!vis) s[c] = __float_as_uint(NEG_INF);
         }
       }
-      float mx8[8];
+      // Row max with three-input max: four chains over columns (u, u+4, ...).
+      float mx4[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) mx8[u] = __uint_as_float(s[u]);
+      for (int u = 0; u < 4; ++u)
+        mx4[u] = fmax3(__uint_as_float(s[u]), __uint_as_float(s[u + 4]), __uint_as_float(s[u + 8]));
 #pragma unroll
-      for (int c = 8; c < 128; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(s[c]));
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      for (int c = 12; c < 124; c += 8)
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          mx4[u] = fmax3(mx4[u], __uint_as_float(s[c + u]), __uint_as_float(s[c + 4 + u]));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) mx4[u] = fmaxf(mx4[u], __uint_as_float(s[124 + u]));
+      const float mx = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]);
       const float m_new = fmaxf(m_run, mx);
       m_run = m_new;
       if (tr) FA_TRACE_EVENT(8 * t + 3, jj);
@@ -430,7 +452,10 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
         }
       }
       float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      // P in two halves of 64 keys, each stored to TMEM as soon as it is packed.
+      // P in two halves of 64 keys, each stored to TMEM as soon as it is packed.  With
+      // kSplitP the first half is released to the MMA issuer (p_half) before the second is
+      // computed, except by a warp that must rescale O first (PV_j accumulates onto the
+      // rescaled O): it arrives on p_half after its rescale.
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         uint32_t pk[32];
@@ -445,6 +470,11 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
           }
         }
         tmem_st32(tS + 32 * hf, pk);
+        if (kSplitP && hf == 0 && !rescale_o) {
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(smem_u32(&ctl->p_half[t]));
+        }
       }
       if (NQ == 2) mbar_arrive(smem_u32(&ctl->exp_turn[t ^ 1]));
       l += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
@@ -459,6 +489,11 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
 #pragma unroll
           for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * factor);
           tmem_st32(tO + c0, o);
+        }
+        if (kSplitP) {
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(smem_u32(&ctl->p_half[t]));
         }
       }
       tmem_wait_st();

@@ -329,6 +329,12 @@ __device__ __forceinline__ void setmaxnreg_dec() {
 }
 
 // ---------------------------------------------------------------- misc math
+// max(a, b, c) in one instruction (three-input max.f32, sm_100+).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float y;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+  return y;
+}
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
