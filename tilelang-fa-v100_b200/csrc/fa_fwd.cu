@@ -334,6 +334,8 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
           tc_fence_after();
           if (!kSplitP) issue_PV(t, sv, jj > 0, 0);
           issue_PV(t, sv, true, 1);
+          // V_j's slot is free once the last PV reading it completes, ahead of S_{j+1}.
+          if (t == NQ - 1) mma_commit(smem_u32(&ctl->kv_empty[sv]));
           if (has_next) {
             if (t == 0) {
               ok = mbar_wait(smem_u32(&ctl->kv_full[sk]), phk, abort_flag, p.err,
@@ -347,7 +349,6 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
           FA_TRACE_EVENT(8 * t + 7, jj);
         }
         if (!ok) break;
-        mma_commit(smem_u32(&ctl->kv_empty[sv]));
         if (has_next) mma_commit(smem_u32(&ctl->kv_empty[sk]));
       }
       for (int t = 0; t < NQ; ++t) mma_commit(smem_u32(&ctl->o_final[t]));
