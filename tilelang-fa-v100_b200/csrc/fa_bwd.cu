@@ -6,7 +6,7 @@
 // Kernels (all on the caller's stream):
 //   1. fa_bwd_prep     D = rowsum(O * dO) in fp32 and LSE * log2(e), per query row, padded
 //                      to a multiple of 128 rows (+inf / 0 in the padding so padded rows
-//                      contribute P = 0); the dQ accumulator is cleared with a memset.
+//                      contribute P = 0); in atomic mode it also clears the dQ accumulator.
 //   2. fa_bwd_dkdv     one CTA per (128-key KV tile, kv head, batch) owns dK and dV in
 //                      TMEM and loops over the G query heads of its kv head x the query
 //                      tiles that can see its keys (causal skips the rest).  Per 128-row
@@ -15,10 +15,11 @@
 //                        dP^T = V dO^T           (SS)      -> TMEM [128,256)
 //                        dV  += P^T dO           (TS, A = P^T from TMEM)
 //                        dK  += dS^T Q           (SS, A = dS^T K-major in smem)
-//                        dQ   = dS K             (SS, A = dS MN-major, same smem tile)
-//                                                          -> TMEM [128,128+D)
-//                      and dQ is added to an fp32 accumulator with vector atomics
-//                      (atomic mode).  In deterministic mode the last GEMM is skipped.
+//                        dQ^T = K^T dS^T         (SS, both MN-major, two 64-query
+//                                                 halves) -> the dP^T columns
+//                      and dQ is added to an fp32 accumulator with fp32 atomics, one
+//                      128-byte row per warp instruction (atomic mode).  In
+//                      deterministic mode the last GEMM is skipped.
 //                      Issue order per step i: dV(i), S(i+1), dK(i), dQ(i), dP(i+1), so
 //                      S(i+1) overlaps the dS pass of step i.
 //   3. fa_bwd_dq       deterministic mode only: one CTA per (128-row Q tile, head,
