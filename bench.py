@@ -281,8 +281,29 @@ def time_e2e(fa, dev, b, s, h, d, dtype, causal, steps, warmup, seed):
     t1.record(main)
     torch.cuda.synchronize(dev)
     ms = t0.elapsed_time(t1) / steps
+
+    # The host link's floor for the same bytes: one step's four uploads and four downloads
+    # issued together on the two copy streams with no compute (best of 3).
+    link_ms = float("inf")
+    for _ in range(3):
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(main)
+        s_up.wait_stream(main)
+        s_down.wait_stream(main)
+        with torch.no_grad():
+            with torch.cuda.stream(s_up):
+                for dst, src in zip(dev_in[0], host_in):
+                    dst.copy_(src, non_blocking=True)
+            with torch.cuda.stream(s_down):
+                for dst, src in zip(host_out[0], dev_out[0]):
+                    dst.copy_(src, non_blocking=True)
+        main.wait_stream(s_up)
+        main.wait_stream(s_down)
+        c1.record(main)
+        torch.cuda.synchronize(dev)
+        link_ms = min(link_ms, c0.elapsed_time(c1))
     nbytes = b * s * h * d * 2
-    return ms, 4 * nbytes, 4 * nbytes
+    return ms, 4 * nbytes, 4 * nbytes, link_ms
 
 
 def time_paged(dev, steps, warmup):
@@ -437,12 +458,12 @@ def run_ours(args):
         ms, err = float(t[0]), float(t[1])
     fl = step_flops(b, h, s, s, d, causal)
     value = world * fl / ms / 1e9  # TFLOP/s (ms -> s: /1e-3, TFLOP: /1e12)
-    e2e_ms, h2d, d2h = time_e2e(fa, dev, b, s, h, d, dtype, causal, min(args.steps, 10), 2,
-                                seed=1000 + rank)
+    e2e_ms, h2d, d2h, link_ms = time_e2e(fa, dev, b, s, h, d, dtype, causal, min(args.steps, 10),
+                                         2, seed=1000 + rank)
     if dist is not None:
-        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        t = torch.tensor([e2e_ms, link_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t[0])
+        e2e_ms, link_ms = float(t[0]), float(t[1])
     peaks, src = measured_peaks()
     bwd_fl = 10.0 * d * visible_pairs(b, h, s, s, causal)
     achieved = bwd_fl / kern_ms / 1e9
@@ -461,7 +482,10 @@ def run_ours(args):
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                 "schedule": "per step: H2D of q,k,v,dO -> fwd+bwd -> D2H of out,dq,dk,dv; "
                             "uploads / downloads of neighbouring steps overlap the compute "
-                            "(two copy streams, double-buffered device tensors)"},
+                            "(two copy streams, double-buffered device tensors)",
+                "link_floor_ms": link_ms, "frac_of_link_floor": link_ms / e2e_ms,
+                "link_floor": "the same step's uploads and downloads issued together with no "
+                              "compute: the host link bounds e2e when frac_of_link_floor ~ 1"},
         "gpu_launches": launches,
         "roofline": {"kernel": "fa_bwd_dkdv_kernel (dense backward dK/dV + fused dQ)",
                      "bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
@@ -578,9 +602,14 @@ def run_reference(args):
 def run_profile_case(args):
     """Small cases for ncu captures.  dense: B=2 of configs[2] (q/k/v/dO 67 MB each,
     268 MB together > the 126 MB L2), fwd+bwd steps.  decode: 64 sequences of
-    configs[4] (L ~ U[512, 8192], ~1.1 GB of K/V pages), decode steps."""
+    configs[4] (L ~ U[512, 8192], ~1.1 GB of K/V pages), decode steps.  paged: configs[3]
+    itself (q 134 MB > L2, K/V pages 34 MB), paged prefill steps."""
     import tilelang_fa_v100 as fa
     dev = torch.device("cuda", 0)
+    if args.profile_case == "paged":
+        ms, tflops = time_paged(dev, args.steps, args.warmup)
+        print(json.dumps({"profile_case": "paged_cfg4_fp16", "ms": ms, "tflops": tflops}), flush=True)
+        return
     if args.profile_case == "decode":
         q, kc, vc, bt, sl, nbytes = decode_problem(dev, 0, batch=64)
         for _ in range(args.warmup + args.steps):
@@ -603,7 +632,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
-    ap.add_argument("--profile-case", choices=["dense", "decode"], default=None,
+    ap.add_argument("--profile-case", choices=["dense", "decode", "paged"], default=None,
                     help="small case for ncu captures (no e2e / CPU / secondary)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
