@@ -1,8 +1,13 @@
 // Attention forward on sm_100a: tcgen05 MMAs with S, P and O in tensor memory,
-// TMA-fed K/V ring, warp-specialised roles.  One kernel template serves the dense
-// BSHD path (tilelang_flash_attn_func, reference kernel _kernels_forward.py:94-172)
-// and the paged vLLM-cache path (tilelang_paged_forward, reference kernel
-// _kernels_paged.py:193-344).
+// TMA-fed K/V ring, warp-specialised roles, for the dense BSHD path
+// (tilelang_flash_attn_func, reference kernel _kernels_forward.py:94-172) and the paged
+// vLLM-cache path (tilelang_paged_forward, reference kernel _kernels_paged.py:193-344).
+// Two schedules of the same per-item pipeline:
+//   fa_fwd_kernel          one CTA per work item (dense D = 128 / 256: long items)
+//   fa_fwd_persist_kernel  one CTA per SM claiming work items in the same order, the
+//                          next item's Q load and first S overlapping the current
+//                          item's tail (paged prefill and dense D = 64: items of a few
+//                          KV tiles, where per-item set-up is a large share)
 //
 // CTA work item: NQ Q tiles of 128 rows for one kv head.  A row is a (token, head)
 // pair: the G = H / Hk query heads that share a kv head are packed into the rows
@@ -28,6 +33,7 @@
 // O = acc / l, LSE = m_ref * scale + ln(l) (natural log, as _kernels_forward.py:170).
 #include "fa_ptx.cuh"
 #include "fa_internal.h"
+#include <atomic>
 #include <cmath>
 
 namespace fa {
@@ -579,24 +585,733 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
   }
 }
 
-// ------------------------------------------------------------------- host side
+template <int D, int NQ>
+struct FwdPersistCfg {
+  static constexpr int DH = D / 64;                       // 128-byte column chunks
+  static constexpr int TILE_BYTES = 128 * D * 2;          // one Q, K or V tile
+  static constexpr int CHUNK_BYTES = 128 * 128;           // one 64-column chunk of a tile
+  // Two sets of Q buffers where they fit next to the K/V ring: the next work item's Q
+  // tiles load while the current item finishes (its epilogue stages O in its own set).
+  static constexpr int QB = (D <= 128) ? 2 : 1;
+  static constexpr int STAGES = (D == 64) ? 6 : (D == 128 ? 3 : 2);
+  static constexpr int NTHREADS = 128 + 128 * NQ;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(NQ * (128 + D) <= TMEM_COLS, "TMEM budget: S + O per Q tile");
+  static constexpr int SMEM_Q = QB * NQ * TILE_BYTES;
+  static constexpr int SMEM_KV = STAGES * TILE_BYTES;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + SMEM_Q + SMEM_KV + 1024 /*barriers*/;
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget (227 KB per CTA)");
+};
+
+
+// One work item: NQ Q tiles (TPB tokens x the G heads of kv head hk) of one sequence.
+struct FwdItem {
+  int live;  // 0: the work list is exhausted
+  int b, hk, tok0, q_len, kv_len, off, tok_base, j0, nkv;
+};
+
+struct FwdPersistCtl {
+  uint64_t q_full[2];
+  uint64_t q_empty[2];   // Q buffer set free: its item's S MMAs done and its O stored
+  uint64_t kv_full[8];
+  uint64_t kv_empty[8];
+  uint64_t s_full[2];
+  uint64_t p_half[2];    // first 64 keys of P_t in TMEM (PV over them may start)
+  uint64_t p_ready[2];   // all of P_t in TMEM
+  uint64_t o_final[2];
+  uint64_t o_empty[2];   // O_t read out by the epilogue (the next item's PV may overwrite it)
+  uint64_t exp_turn[2];  // softmax ping-pong: warpgroup t may run its exp phase
+  uint64_t o_staged[2];  // output tile t written to shared memory (TMA store may start)
+  uint64_t item_full[2];
+  uint64_t item_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  FwdItem item[2];       // work items published by the producer, double-buffered
+};
+
+// Work list entry L -> item, in the grid order of a one-CTA-per-item launch: q block
+// fastest (causal dense: heaviest first), then kv head, then batch.  Paged: the q block
+// index runs over all sequences' blocks (p.nbx slots per kv head, the tail empty).
+// Returns false for an empty slot.
+template <int NQ, bool PAGED>
+__device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it) {
+  const int TPB = NQ * (kFwdBM / p.G);
+  const int x = L % p.nbx;
+  it.hk = (L / p.nbx) % p.Hk;
+  int tile;
+  if constexpr (PAGED) {
+    int cum = 0, s = 0;
+    for (; s < p.num_seqs; ++s) {
+      const int ql = p.qsl[s + 1] - p.qsl[s];
+      const int nb = ql > 0 ? (ql + TPB - 1) / TPB : 0;
+      if (x < cum + nb) break;
+      cum += nb;
+    }
+    if (s == p.num_seqs) return false;
+    it.b = s;
+    tile = x - cum;
+    it.q_len = p.qsl[s + 1] - p.qsl[s];
+    it.kv_len = p.seq_lens[s];
+    it.off = p.pkl[s];
+    it.tok_base = p.qsl[s];
+  } else {
+    it.b = L / (p.nbx * p.Hk);
+    tile = p.causal ? (p.nbx - 1 - x) : x;
+    it.q_len = p.Sq;
+    it.kv_len = p.Skv;
+    it.off = p.Skv - p.Sq;
+    it.tok_base = 0;
+  }
+  it.tok0 = tile * TPB;
+  int j0 = 0, j1 = (it.kv_len + kFwdBN - 1) / kFwdBN;
+  if (p.causal) {
+    const int last_lt = min(it.tok0 + TPB, it.q_len) - 1;
+    const int max_key = last_lt + it.off;
+    j1 = min(j1, max_key >= 0 ? max_key / kFwdBN + 1 : 0);
+    if (PAGED && p.swq > 0) j0 = max(0, it.tok0 - p.swq + 1) / kFwdBN;
+  }
+  it.j0 = j0;
+  it.nkv = max(0, j1 - j0);
+  it.live = 1;
+  return true;
+}
+
+// Persistent: one CTA per SM claims work items from a device counter (p.sched) in list
+// order, so the claim order matches a one-CTA-per-item launch while the next item's
+// loads and first S overlap the current item's tail.
 template <typename T, int D, int NQ, bool PAGED>
-static int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                           const CUtensorMap& to, const FwdParams& p, dim3 grid, cudaStream_t st) {
-  using Cfg = FwdCfg<D, NQ>;
-  auto kern = fa_fwd_kernel<T, D, NQ, PAGED>;
-  static bool attr_set[64] = {false};
+__global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
+    fa_fwd_persist_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                  const FwdParams p) {
+  using Cfg = FwdPersistCfg<D, NQ>;
+  constexpr int ST = Cfg::STAGES;
+  constexpr int QB = Cfg::QB;
+  // Release P_t in two halves (PV over the first 64 keys overlaps the second half's
+  // exponentials).  Measured faster for dense D >= 128; for D = 64 (cheap PV) and the
+  // paged path the extra barrier costs more than the overlap gains.
+  constexpr bool kSplitP = (D >= 128) && !PAGED;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+  const uint32_t sQ = base;  // Q buffer set q: sQ + q * NQ * TILE_BYTES
+  const uint32_t sKV = base + Cfg::SMEM_Q;
+  FwdPersistCtl* ctl = reinterpret_cast<FwdPersistCtl*>(base_ptr + Cfg::SMEM_Q + Cfg::SMEM_KV);
+  volatile int* abort_flag = &ctl->abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = p.G;
+  const int TPT = kFwdBM / G;       // tokens per Q tile (rows TPT*G .. 127 unused when G does not divide 128)
+
+  if (threadIdx.x == 0) {
+    ctl->abort_flag = 0;
+    for (int q = 0; q < 2; ++q) {
+      mbar_init(smem_u32(&ctl->q_full[q]), 1);
+      mbar_init(smem_u32(&ctl->q_empty[q]), 1 + NQ);
+      mbar_init(smem_u32(&ctl->item_full[q]), 1);
+      mbar_init(smem_u32(&ctl->item_empty[q]), 1 + 128 * NQ);
+    }
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(smem_u32(&ctl->kv_full[s]), 1);
+      mbar_init(smem_u32(&ctl->kv_empty[s]), 1);
+    }
+    for (int t = 0; t < NQ; ++t) {
+      mbar_init(smem_u32(&ctl->s_full[t]), 1);
+      mbar_init(smem_u32(&ctl->p_half[t]), 128);
+      mbar_init(smem_u32(&ctl->p_ready[t]), 128);
+      mbar_init(smem_u32(&ctl->o_final[t]), 1);
+      mbar_init(smem_u32(&ctl->o_empty[t]), 128);
+      mbar_init(smem_u32(&ctl->exp_turn[t]), 128);
+      mbar_init(smem_u32(&ctl->o_staged[t]), 128);
+    }
+    mbar_init(smem_u32(&ctl->drain), 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == 0) {
+    // ============================================================ scheduler + TMA producer
+    // Lane 0 claims and publishes each work item.  Dense: lane 0 issues every copy.
+    // Paged: lane r fetches the page id of box r of the next KV tile while the current
+    // tile's copies go out, and issues box r's copies itself, so block-table reads never
+    // sit between two copies.
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+    }
+    const int box_rows = PAGED ? min(p.page_size, kFwdBN) : kFwdBN;
+    const int boxes = kFwdBN / box_rows;  // page boxes per KV tile (<= 16: page_size >= 8)
+    int it = 0, k = 0, q_loaded = 0;
+    bool ok = true;
+    for (;; ++k) {
+      int okl = 1;
+      if (lane == 0) {
+        if (k >= 2)
+          okl = mbar_wait(smem_u32(&ctl->item_empty[k & 1]), ((k >> 1) - 1) & 1, abort_flag,
+                          p.err, FA_SITE_FWD_PRODUCER);
+        FwdItem item;
+        item.live = 0;
+        if (okl) {
+          for (;;) {
+            const int L = atomicAdd(p.sched, 1);
+            if (L >= p.n_items) break;
+            if (fwd_decode_item<NQ, PAGED>(L, p, item)) break;
+          }
+        }
+        ctl->item[k & 1] = item;
+        mbar_arrive(smem_u32(&ctl->item_full[k & 1]));
+      }
+      ok = __shfl_sync(0xffffffffu, okl, 0) != 0;
+      __syncwarp();
+      const FwdItem item = ctl->item[k & 1];
+      if (!ok || !item.live) break;
+      const int b = item.b, hk = item.hk, j0 = item.j0, nkv = item.nkv;
+      // Q tiles of item k into buffer set k % QB, once item k - QB has released it.
+      const int qb = k % QB;
+      if (lane == 0) {
+        if (k >= QB)
+          okl = mbar_wait(smem_u32(&ctl->q_empty[qb]), ((k / QB) - 1) & 1, abort_flag, p.err,
+                          FA_SITE_FWD_PRODUCER);
+        if (okl) {
+          const uint32_t qbar = smem_u32(&ctl->q_full[qb]);
+          mbar_arrive_expect_tx(qbar, NQ * Cfg::DH * TPT * G * 128);
+          for (int t = 0; t < NQ; ++t) {
+            const int tok = item.tok_base + item.tok0 + t * TPT;
+            for (int dh = 0; dh < Cfg::DH; ++dh)
+              tma_load_4d(sQ + (qb * NQ + t) * Cfg::TILE_BYTES + dh * Cfg::CHUNK_BYTES, &tm_q,
+                          qbar, dh * 64, hk * G, tok, PAGED ? 0 : b);
+          }
+          ++q_loaded;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, okl, 0) != 0;
+      if (!ok) break;
+      const int n_valid_pages =
+          PAGED ? min((item.kv_len + p.page_size - 1) / p.page_size, p.max_blocks) : 0;
+      // Page id of box `lane` of KV tile j; pages past the sequence are fetched out of
+      // range (page id num_pages), which TMA fills with zeros.
+      auto page_of = [&](int j) -> int {
+        int pg = p.num_pages;
+        if (PAGED && lane < boxes) {
+          const int lp = (j * kFwdBN + lane * box_rows) / p.page_size;
+          if (lp < n_valid_pages) pg = p.block_table[(int64_t)b * p.max_blocks + lp];
+        }
+        return pg;
+      };
+      int pg_next = (PAGED && nkv > 0) ? page_of(j0) : 0;
+      for (int jj = 0; jj < nkv && ok; ++jj) {
+        const int j = j0 + jj;
+        const int pg_cur = pg_next;
+        if (PAGED && jj + 1 < nkv) pg_next = page_of(j + 1);
+        for (int w = 0; w < 2 && ok; ++w, ++it) {
+          const int s = it % ST;
+          const uint32_t ph = (it / ST) & 1;
+          okl = 1;
+          if (lane == 0)
+            okl = mbar_wait(smem_u32(&ctl->kv_empty[s]), ph ^ 1, abort_flag, p.err,
+                            FA_SITE_FWD_PRODUCER);
+          ok = __shfl_sync(0xffffffffu, okl, 0) != 0;
+          if (!ok) break;
+          const uint32_t fb = smem_u32(&ctl->kv_full[s]);
+          const CUtensorMap* tm = (w == 0) ? &tm_k : &tm_v;
+          const uint32_t dst = sKV + s * Cfg::TILE_BYTES;
+          if (lane == 0) mbar_arrive_expect_tx(fb, Cfg::TILE_BYTES);
+          if constexpr (PAGED) {
+            __syncwarp();
+            if (lane < boxes) {
+              const int in_page = (j * kFwdBN + lane * box_rows) % p.page_size;
+              for (int dh = 0; dh < Cfg::DH; ++dh)
+                tma_load_4d(dst + dh * Cfg::CHUNK_BYTES + lane * box_rows * 128, tm, fb, dh * 64, hk,
+                            in_page, pg_cur);
+            }
+          } else {
+            if (lane == 0)
+              for (int dh = 0; dh < Cfg::DH; ++dh)
+                tma_load_4d(dst + dh * Cfg::CHUNK_BYTES, tm, fb, dh * 64, hk, j * kFwdBN, b);
+          }
+        }
+      }
+      if (!ok) break;
+    }
+    // Drain: every copy issued must have landed before the CTA may exit.
+    if (lane == 0) {
+      for (int kk = max(0, it - ST); kk < it; ++kk)
+        mbar_wait_drain(smem_u32(&ctl->kv_full[kk % ST]), (kk / ST) & 1);
+      for (int kk = max(0, q_loaded - QB); kk < q_loaded; ++kk)
+        mbar_wait_drain(smem_u32(&ctl->q_full[kk % QB]), (kk / QB) & 1);
+    }
+  } else if (warp == 1) {
+    // ============================================================ MMA issuer
+    if (lane == 0) {
+      constexpr bool kBf16 = Pack2<T>::kBf16;
+      constexpr uint32_t idS = idesc_f16(128, kFwdBN, kBf16, false, false);
+      constexpr uint32_t idPV = idesc_f16(128, D, kBf16, false, true);
+      // Descriptors: built once; per slot / per K step they are base + constant.
+      const uint64_t q_desc0 = sdesc_sw128(sQ, 16, 1024);            // K-major Q tiles
+      const uint64_t k_desc0 = sdesc_sw128(sKV, 16, 1024);           // K-major K in slot 0
+      const uint64_t v_desc0 = sdesc_sw128(sKV, Cfg::CHUNK_BYTES, 1024);  // MN-major V, slot 0
+      int qoff = 0;  // byte offset of the current item's Q buffer set
+      // S_t = Q_t K^T over D in steps of 16 (K-major, 128-byte swizzle: step = +32 B
+      // inside a 64-column chunk, next chunk at +16 KB).
+      auto issue_S = [&](int t, int slot) {
+        const uint64_t qa = desc_add(q_desc0, qoff + t * Cfg::TILE_BYTES);
+        const uint64_t ka = desc_add(k_desc0, slot * Cfg::TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t o = (kk >> 2) * Cfg::CHUNK_BYTES + (kk & 3) * 32;
+          mma_ss(tmem + t * 128, desc_add(qa, o), desc_add(ka, o), idS, kk > 0 ? 1u : 0u);
+        }
+      };
+      // O_t += P_t V over keys [64 hf, 64 hf + 64) in steps of 16 (V MN-major: step = 16
+      // rows = +2 KB, 64-column chunks of D at +16 KB = LBO).  P's 16-bit pairs: 16 keys
+      // = 8 TMEM columns.
+      auto issue_PV = [&](int t, int slot, bool acc, int hf) {
+        const uint64_t va = desc_add(v_desc0, slot * Cfg::TILE_BYTES);
+#pragma unroll
+        for (int k4 = 0; k4 < kFwdBN / 32; ++k4) {
+          const int kk = hf * (kFwdBN / 32) + k4;
+          mma_ts(tmem + NQ * 128 + t * D, tmem + t * 128 + kk * 8, desc_add(va, kk * 2048), idPV,
+                 (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      int it = 0, gj = 0;
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        ok = mbar_wait(smem_u32(&ctl->item_full[k & 1]), (k >> 1) & 1, abort_flag, p.err,
+                       FA_SITE_FWD_MMA);
+        if (!ok) break;
+        if (!ctl->item[k & 1].live) break;
+        const int nkv = ctl->item[k & 1].nkv;
+        const int qb = k % QB;
+        qoff = qb * NQ * Cfg::TILE_BYTES;
+        ok = mbar_wait(smem_u32(&ctl->q_full[qb]), (k / QB) & 1, abort_flag, p.err, FA_SITE_FWD_MMA);
+        if (!ok) break;
+        tc_fence_after();
+        if (nkv > 0) {
+          // First S of the item: its columns were last read by the previous item's final
+          // PV, issued earlier (MMAs run in issue order).
+          const int s = it % ST;
+          ok = mbar_wait(smem_u32(&ctl->kv_full[s]), (it / ST) & 1, abort_flag, p.err,
+                         FA_SITE_FWD_MMA);
+          if (!ok) break;
+          tc_fence_after();
+          for (int t = 0; t < NQ; ++t) {
+            issue_S(t, s);
+            mma_commit(smem_u32(&ctl->s_full[t]));
+          }
+          mma_commit(smem_u32(&ctl->kv_empty[s]));
+          ++it;
+        }
+        for (int jj = 0; jj < nkv && ok; ++jj, ++gj) {
+          const int sv = it % ST;
+          const uint32_t phv = (it / ST) & 1;
+          ++it;
+          const bool has_next = jj + 1 < nkv;
+          const int sk = it % ST;
+          const uint32_t phk = (it / ST) & 1;
+          if (has_next) ++it;
+          ok = mbar_wait(smem_u32(&ctl->kv_full[sv]), phv, abort_flag, p.err, FA_SITE_FWD_MMA);
+          if (!ok) break;
+          for (int t = 0; t < NQ && ok; ++t) {
+            if (jj == 0 && k > 0) {
+              // The item's first PV overwrites O_t: the previous item's epilogue must have
+              // read it out.
+              ok = mbar_wait(smem_u32(&ctl->o_empty[t]), (k - 1) & 1, abort_flag, p.err,
+                             FA_SITE_FWD_MMA);
+              if (!ok) break;
+            }
+            if (kSplitP) {
+              // PV over the first 64 keys runs while the softmax computes the second half.
+              ok = mbar_wait(smem_u32(&ctl->p_half[t]), gj & 1, abort_flag, p.err, FA_SITE_FWD_MMA);
+              if (!ok) break;
+              tc_fence_after();
+              issue_PV(t, sv, jj > 0, 0);
+            }
+            ok = mbar_wait(smem_u32(&ctl->p_ready[t]), gj & 1, abort_flag, p.err, FA_SITE_FWD_MMA);
+            if (!ok) break;
+            tc_fence_after();
+            if (!kSplitP) issue_PV(t, sv, jj > 0, 0);
+            issue_PV(t, sv, true, 1);
+            // V_j's slot is free once the last PV reading it completes, ahead of S_{j+1}.
+            if (t == NQ - 1) mma_commit(smem_u32(&ctl->kv_empty[sv]));
+            if (has_next) {
+              if (t == 0) {
+                ok = mbar_wait(smem_u32(&ctl->kv_full[sk]), phk, abort_flag, p.err,
+                               FA_SITE_FWD_MMA);
+                if (!ok) break;
+                tc_fence_after();
+              }
+              issue_S(t, sk);
+              mma_commit(smem_u32(&ctl->s_full[t]));
+            }
+          }
+          if (!ok) break;
+          if (has_next) mma_commit(smem_u32(&ctl->kv_empty[sk]));
+        }
+        if (!ok) break;
+        if (nkv == 0 && k > 0) {
+          // No PV for this item: consume the previous item's O release all the same, so
+          // the o_empty phases stay in step with the items.
+          for (int t = 0; t < NQ && ok; ++t)
+            ok = mbar_wait(smem_u32(&ctl->o_empty[t]), (k - 1) & 1, abort_flag, p.err,
+                           FA_SITE_FWD_MMA);
+          if (!ok) break;
+        }
+        for (int t = 0; t < NQ; ++t) mma_commit(smem_u32(&ctl->o_final[t]));
+        mma_commit(smem_u32(&ctl->q_empty[qb]));  // every S of this item has read its Q
+        mbar_arrive(smem_u32(&ctl->item_empty[k & 1]));
+      }
+      mma_commit(smem_u32(&ctl->drain));
+      mbar_wait_drain(smem_u32(&ctl->drain), 0);
+    }
+  } else if (warp >= 4) {
+    // ============================================================ softmax / epilogue
+    const int t = (warp - 4) >> 2;
+    const int r = ((warp & 3) << 5) | lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_off + t * 128;
+    const uint32_t tO = tmem + lane_off + NQ * 128 + t * D;
+    const int tr = r / G;                    // token of this row inside the tile
+    const float c2 = p.scale_log2;
+    const float NEG_INF = -INFINITY;
+    const bool window = PAGED && p.causal && (p.swq > 0 || p.swk > 0);
+    bool ok = true;
+    int gj = 0, n_staged = 0;
+    if (NQ == 2 && t == 1) mbar_arrive(smem_u32(&ctl->exp_turn[0]));  // tile 0 goes first
+
+    for (int k = 0; ok; ++k) {
+      bool w_ok = mbar_wait(smem_u32(&ctl->item_full[k & 1]), (k >> 1) & 1, abort_flag, p.err,
+                            FA_SITE_FWD_SOFTMAX);
+      ok = __all_sync(0xffffffffu, w_ok);
+      if (!ok) break;
+      // The item stays in its slot until this item's end (item_empty is arrived after the
+      // epilogue), so its fields are read from shared memory where they are used.
+      const FwdItem* itp = &ctl->item[k & 1];
+      if (!itp->live) break;
+      const int nkv = itp->nkv;
+      float m_run = NEG_INF, m_ref = NEG_INF, l = 0.f;
+
+      for (int jj = 0; jj < nkv; ++jj, ++gj) {
+        const int j = itp->j0 + jj;
+        w_ok = mbar_wait(smem_u32(&ctl->s_full[t]), gj & 1, abort_flag, p.err, FA_SITE_FWD_SOFTMAX);
+        ok = __all_sync(0xffffffffu, w_ok);
+        if (!ok) break;
+        tc_fence_after();
+        // Visible keys of this row form one range [lo, hi): key < kv_len; causal: key <=
+        // lt + off; sliding window (paged, causal): lt - swq < key and key < lt + swk.
+        const int key0 = j * kFwdBN;
+        const int lt = itp->tok0 + t * TPT + tr;  // token index within the sequence / chunk
+        int lo = 0, hi = itp->kv_len;
+        if (p.causal) {
+          hi = min(hi, lt + itp->off + 1);
+          if (window) {
+            if (p.swq > 0) lo = lt - p.swq + 1;
+            if (p.swk > 0) hi = min(hi, lt + p.swk);
+          }
+        }
+        const int clo = lo - key0, chi = hi - key0;  // visible columns [clo, chi)
+        const bool masked = clo > 0 || chi < kFwdBN;
+        // 64 S values at a time stay in registers: keys 64..127 for their max, then keys
+        // 0..63 (kept for the first half of P); keys 64..127 are loaded again during the
+        // first half's exponentials.  P overwrites only S columns already read.
+        auto mask64 = [&](uint32_t* v, int c0) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (c0 + c < clo || c0 + c >= chi) v[c] = __float_as_uint(NEG_INF);
+        };
+        // Row max with three-input max over 64 values: four chains (u, u+4, ...).
+        auto max64 = [&](const uint32_t* v) -> float {
+          float mx4[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            mx4[u] = fmax3(__uint_as_float(v[u]), __uint_as_float(v[u + 4]), __uint_as_float(v[u + 8]));
+#pragma unroll
+          for (int c = 12; c < 60; c += 8)
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              mx4[u] = fmax3(mx4[u], __uint_as_float(v[c + u]), __uint_as_float(v[c + 4 + u]));
+#pragma unroll
+          for (int u = 0; u < 4; ++u) mx4[u] = fmaxf(mx4[u], __uint_as_float(v[60 + u]));
+          return fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]);
+        };
+        uint32_t s[64];
+        tmem_ld32(tS + 64, s);
+        tmem_ld32(tS + 96, s + 32);
+        tmem_wait_ld();
+        if (masked) mask64(s, 64);
+        const float mx_hi = max64(s);
+        tmem_ld32(tS + 0, s);
+        tmem_ld32(tS + 32, s + 32);
+        tmem_wait_ld();
+        if (masked) mask64(s, 0);
+        const float mx = fmaxf(mx_hi, max64(s));
+        const float m_new = fmaxf(m_run, mx);
+        m_run = m_new;
+        bool rescale_o = false;
+        float factor = 1.f;
+        if (jj == 0) {
+          m_ref = m_new;
+        } else {
+          const bool need = (m_new - m_ref) * c2 > 8.0f;
+          if (__any_sync(0xffffffffu, need)) {
+            if (m_new != NEG_INF) {
+              factor = ex2_approx((m_ref - m_new) * c2);
+              m_ref = m_new;
+            }
+            l *= factor;
+            rescale_o = true;
+          }
+        }
+        const float mref_s = (m_ref == NEG_INF) ? 0.f : m_ref * c2;
+        // With two Q tiles the warpgroups take turns on the exponential unit: tile 0's
+        // exp phase of KV tile j, then tile 1's, then tile 0's of j + 1, ... so one
+        // tile's exponentials run while the other tile's MMAs do.
+        if (NQ == 2) {
+          const bool turn = mbar_wait(smem_u32(&ctl->exp_turn[t]), gj & 1, abort_flag, p.err,
+                                      FA_SITE_FWD_SOFTMAX);
+          if (!__all_sync(0xffffffffu, turn)) {
+            ok = false;
+            break;
+          }
+        }
+        float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        // P in two halves of 64 keys, each stored to TMEM as soon as it is packed.  With
+        // kSplitP the first half is released to the MMA issuer (p_half) before the second is
+        // computed, except by a warp that must rescale O first (PV_j accumulates onto the
+        // rescaled O): it arrives on p_half after its rescale.
+        uint32_t s_hi[64];
+        {
+          uint32_t pk[32];
+#pragma unroll
+          for (int cc = 0; cc < 32; ++cc) {
+            const float p0 = ex2_approx(fmaf(__uint_as_float(s[2 * cc]), c2, -mref_s));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(s[2 * cc + 1]), c2, -mref_s));
+            rs[cc & 7] += p0 + p1;
+            pk[cc] = Pack2<T>::pack(p0, p1);
+            if (cc == 15) {
+              // keys 0..31 are consumed: bring keys 64..127 back while 32..63 are computed
+              tmem_ld32(tS + 64, s_hi);
+              tmem_ld32(tS + 96, s_hi + 32);
+            }
+          }
+          tmem_st32(tS, pk);
+        }
+        if (kSplitP && !rescale_o) {
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(smem_u32(&ctl->p_half[t]));
+        }
+        tmem_wait_ld();
+        if (masked) mask64(s_hi, 64);
+        {
+          uint32_t pk[32];
+#pragma unroll
+          for (int cc = 0; cc < 32; ++cc) {
+            const float p0 = ex2_approx(fmaf(__uint_as_float(s_hi[2 * cc]), c2, -mref_s));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(s_hi[2 * cc + 1]), c2, -mref_s));
+            rs[cc & 7] += p0 + p1;
+            pk[cc] = Pack2<T>::pack(p0, p1);
+          }
+          tmem_st32(tS + 32, pk);
+        }
+        if (NQ == 2) mbar_arrive(smem_u32(&ctl->exp_turn[t ^ 1]));
+        l += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
+        if (rescale_o) {
+          // PV_{j-1} is complete: the commit that signalled S_j covered every earlier MMA.
+#pragma unroll
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            uint32_t o[32];
+            tmem_ld32(tO + c0, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * factor);
+            tmem_st32(tO + c0, o);
+          }
+          if (kSplitP) {
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(smem_u32(&ctl->p_half[t]));
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(smem_u32(&ctl->p_ready[t]));
+      }
+      if (!ok) break;
+
+      // -------------------------------------------------------- epilogue of item k
+      w_ok = mbar_wait(smem_u32(&ctl->o_final[t]), k & 1, abort_flag, p.err, FA_SITE_FWD_SOFTMAX);
+      ok = __all_sync(0xffffffffu, w_ok);
+      if (!ok) break;
+      tc_fence_after();
+      const bool have = l > 0.f;
+      const float inv = have ? 1.f / l : 0.f;
+      const int b = itp->b, tok0 = itp->tok0, q_len = itp->q_len, tok_base = itp->tok_base;
+      const int qb = k % QB;
+      const int lt = tok0 + t * TPT + tr;
+      const int h = itp->hk * G + (r - tr * G);  // query head
+      const bool row_valid = tr < TPT && lt < q_len;
+      // Output tile through shared memory (this item's Q tile buffer: every MMA that read
+      // it finished before o_final) and one TMA store per 64-column chunk.  Dense tiles
+      // always (the tensor map clips rows past Sq); paged tiles when all their tokens
+      // belong to this sequence, else per-row stores (the next rows are another
+      // sequence's).
+      const bool tma_out = PAGED ? (tok0 + t * TPT + TPT <= q_len) : true;
+      const uint32_t stage = sQ + (qb * NQ + t) * Cfg::TILE_BYTES;
+      T* orow = reinterpret_cast<T*>(p.out) + (PAGED ? 0 : (int64_t)b * p.o_sb) +
+                (int64_t)(tok_base + lt) * p.o_st + (int64_t)h * p.o_sh;
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t o[32];
+        if (nkv > 0) {
+          tmem_ld32(tO + c0, o);
+          tmem_wait_ld();
+        }
+        if (c0 + 32 == D) {
+          // All of O_t is in registers: the next item's first PV may overwrite it.
+          tc_fence_before();
+          mbar_arrive(smem_u32(&ctl->o_empty[t]));
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float a0 = have ? __uint_as_float(o[2 * c]) * inv : 0.f;
+          const float a1 = have ? __uint_as_float(o[2 * c + 1]) * inv : 0.f;
+          pk[c] = Pack2<T>::pack(a0, a1);
+        }
+        if (tma_out) {
+          // row r of the 128-byte-swizzled tile, 16-byte units (c0 % 64) / 8 .. + 3
+          const uint32_t rowa = stage + (c0 >> 6) * Cfg::CHUNK_BYTES + r * 128;
+          const int u0 = (c0 & 63) >> 3;
+#pragma unroll
+          for (int m = 0; m < 4; ++m)
+            st_shared_v4(rowa + (((u0 + m) ^ (r & 7)) << 4), pk[4 * m], pk[4 * m + 1],
+                         pk[4 * m + 2], pk[4 * m + 3]);
+        } else if (row_valid) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+          dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          dst[2] = make_uint4(pk[8], pk[9], pk[10], pk[11]);
+          dst[3] = make_uint4(pk[12], pk[13], pk[14], pk[15]);
+        }
+      }
+      if (row_valid && p.lse != nullptr) {
+        const float lse = have ? m_ref * p.scale + logf(l) : NEG_INF;
+        p.lse[(PAGED ? 0 : (int64_t)b * p.lse_sb) + (int64_t)h * p.lse_sh + tok_base + lt] = lse;
+      }
+      const bool leader = (threadIdx.x & 127) == 0;
+      if (tma_out) {
+        fence_async_shared();
+        mbar_arrive(smem_u32(&ctl->o_staged[t]));
+        if (leader) {
+          if (mbar_wait(smem_u32(&ctl->o_staged[t]), n_staged & 1, abort_flag, p.err,
+                        FA_SITE_FWD_SOFTMAX)) {
+            const int tok = tok_base + tok0 + t * TPT;
+#pragma unroll
+            for (int dh = 0; dh < Cfg::DH; ++dh)
+              tma_store_4d(&tm_o, stage + dh * Cfg::CHUNK_BYTES, dh * 64, itp->hk * G, tok,
+                           PAGED ? 0 : b);
+            bulk_commit_group();
+            bulk_wait_group_read();
+          }
+        }
+        ++n_staged;
+      }
+      // The Q buffer set is free for item k + QB once the staged tile has been read.
+      if (leader) mbar_arrive(smem_u32(&ctl->q_empty[qb]));
+      mbar_arrive(smem_u32(&ctl->item_empty[k & 1]));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------- host side
+// Work-item counters of the persistent kernel: each launch takes the next of
+// kFwdSchedSlots device words and zeroes it on its stream first, so launches in flight
+// on other streams use other words (kFwdSchedSlots launches would have to overlap on
+// the GPU for two to share one).
+constexpr int kFwdSchedSlots = 64;
+__device__ int g_fwd_sched[kFwdSchedSlots];
+
+static int* fwd_sched_counter(cudaStream_t st) {
+  static std::atomic<unsigned> next{0};
+  static int* base_of[64] = {nullptr};  // per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  int* base = dev < 64 ? base_of[dev] : nullptr;
+  if (base == nullptr) {
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&base), g_fwd_sched) != cudaSuccess)
+      return nullptr;
+    if (dev < 64) base_of[dev] = base;
+  }
+  int* c = base + (next.fetch_add(1) % kFwdSchedSlots);
+  if (cudaMemsetAsync(c, 0, sizeof(int), st) != cudaSuccess) return nullptr;
+  return c;
+}
+// Which schedule serves a launch: the persistent kernel for the paged path and D = 64
+// (work items of a few KV tiles, where per-item set-up is a large share), one CTA per
+// work item for dense D >= 128 (long items; the smaller kernel keeps its instruction
+// footprint, measured faster there).
+template <int D, bool PAGED>
+constexpr bool fwd_persistent() {
+  return PAGED || D == 64;
+}
+
+template <typename K>
+static int fwd_smem_attr(K kern, int bytes, bool* done) {
   int dev = 0;
   FA_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 64 && !attr_set[dev]) {
-    FA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Cfg::SMEM_BYTES));
-    attr_set[dev] = true;
+  if (dev < 64 && !done[dev]) {
+    FA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done[dev] = true;
   }
+  return FA_OK;
+}
+
+template <typename T, int D, int NQ, bool PAGED>
+static int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                           const CUtensorMap& to, const FwdParams& p, cudaStream_t st) {
   const int kind = PAGED ? FA_PROF_PAGED : FA_PROF_FWD;
-  prof_begin(kind, st);
-  kern<<<grid, Cfg::NTHREADS, Cfg::SMEM_BYTES, st>>>(tq, tk, tv, to, p);
-  prof_end(kind, st);
+  if constexpr (fwd_persistent<D, PAGED>()) {
+    using Cfg = FwdPersistCfg<D, NQ>;
+    auto kern = fa_fwd_persist_kernel<T, D, NQ, PAGED>;
+    static bool attr_set[64] = {false};
+    if (int s = fwd_smem_attr(kern, Cfg::SMEM_BYTES, attr_set)) return s;
+    FwdParams q = p;
+    q.sched = fwd_sched_counter(st);
+    if (q.sched == nullptr) return FA_ERR_CUDA;
+    const dim3 grid(p.n_items < num_sms() ? p.n_items : num_sms());
+    prof_begin(kind, st);
+    kern<<<grid, Cfg::NTHREADS, Cfg::SMEM_BYTES, st>>>(tq, tk, tv, to, q);
+    prof_end(kind, st);
+  } else {
+    using Cfg = FwdCfg<D, NQ>;
+    auto kern = fa_fwd_kernel<T, D, NQ, PAGED>;
+    static bool attr_set[64] = {false};
+    if (int s = fwd_smem_attr(kern, Cfg::SMEM_BYTES, attr_set)) return s;
+    // one CTA per work item: q blocks x kv heads x batch
+    const dim3 grid(p.nbx, p.Hk, p.n_items / (p.nbx * p.Hk));
+    prof_begin(kind, st);
+    kern<<<grid, Cfg::NTHREADS, Cfg::SMEM_BYTES, st>>>(tq, tk, tv, to, p);
+    prof_end(kind, st);
+  }
   FA_CUDA_TRY(cudaGetLastError());
   count_launch();
   return FA_OK;
@@ -604,10 +1319,10 @@ static int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const C
 
 template <int D, int NQ, bool PAGED>
 static int dispatch_dtype(int dtype, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& to,
-                          const CUtensorMap& tv, const FwdParams& p, dim3 grid, cudaStream_t st) {
+                          const CUtensorMap& tv, const FwdParams& p, cudaStream_t st) {
   if (dtype == FA_DTYPE_BF16)
-    return launch_fwd_impl<__nv_bfloat16, D, NQ, PAGED>(tq, tk, tv, to, p, grid, st);
-  return launch_fwd_impl<__half, D, NQ, PAGED>(tq, tk, tv, to, p, grid, st);
+    return launch_fwd_impl<__nv_bfloat16, D, NQ, PAGED>(tq, tk, tv, to, p, st);
+  return launch_fwd_impl<__half, D, NQ, PAGED>(tq, tk, tv, to, p, st);
 }
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
@@ -667,11 +1382,12 @@ int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
   p.lse_sh = a->seqlen_q;
   p.err = err;
   const int TPB = NQ * (128 / G);
-  dim3 grid((a->seqlen_q + TPB - 1) / TPB, a->num_heads_k, a->batch);
+  p.nbx = (a->seqlen_q + TPB - 1) / TPB;
+  p.n_items = p.nbx * a->num_heads_k * a->batch;
   switch (D) {
-    case 64: return dispatch_dtype<64, 2, false>(a->dtype, tq, tk, to, tv, p, grid, st);
-    case 128: return dispatch_dtype<128, 2, false>(a->dtype, tq, tk, to, tv, p, grid, st);
-    case 256: return dispatch_dtype<256, 1, false>(a->dtype, tq, tk, to, tv, p, grid, st);
+    case 64: return dispatch_dtype<64, 2, false>(a->dtype, tq, tk, to, tv, p, st);
+    case 128: return dispatch_dtype<128, 2, false>(a->dtype, tq, tk, to, tv, p, st);
+    case 256: return dispatch_dtype<256, 1, false>(a->dtype, tq, tk, to, tv, p, st);
     default: return FA_ERR_UNSUPPORTED;
   }
 }
@@ -733,11 +1449,12 @@ int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st) {
   p.err = err;
   const int TPB = NQ * (128 / G);
   // Sum over sequences of ceil(q_len / TPB) <= num_tokens / TPB + num_seqs.
-  dim3 grid(a->num_tokens / TPB + a->num_seqs, a->num_kv_heads, 1);
+  p.nbx = a->num_tokens / TPB + a->num_seqs;
+  p.n_items = p.nbx * a->num_kv_heads;
   switch (D) {
-    case 64: return dispatch_dtype<64, 2, true>(a->dtype, tq, tk, to, tv, p, grid, st);
-    case 128: return dispatch_dtype<128, 2, true>(a->dtype, tq, tk, to, tv, p, grid, st);
-    case 256: return dispatch_dtype<256, 1, true>(a->dtype, tq, tk, to, tv, p, grid, st);
+    case 64: return dispatch_dtype<64, 2, true>(a->dtype, tq, tk, to, tv, p, st);
+    case 128: return dispatch_dtype<128, 2, true>(a->dtype, tq, tk, to, tv, p, st);
+    case 256: return dispatch_dtype<256, 1, true>(a->dtype, tq, tk, to, tv, p, st);
     default: return FA_ERR_UNSUPPORTED;
   }
 }

@@ -26,6 +26,9 @@ struct FwdParams {
   const int32_t* pkl;
   int num_seqs, max_blocks, page_size, num_pages;
   int swq, swk;
+  // persistent scheduling: the work list is nbx q-block slots x kv heads (x batch, dense)
+  int nbx, n_items;
+  int* sched;  // device counter of claimed work-list entries (zeroed before the launch)
   int* err;
 };
 
