@@ -41,6 +41,7 @@ namespace fa {
 
 constexpr int kBwdBN = 128;  // keys per CTA
 constexpr int kBwdBM = 128;  // query rows per iteration
+constexpr int kBwdOrderGroup = 8;  // (batch, kv head) units ordered together, heaviest tile first
 
 template <int D>
 struct BwdCfg {
@@ -255,7 +256,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   volatile int* abort_flag = &ctl->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  const int nblk = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  // Work order: the grid's linear index walks groups of kBwdOrderGroup (batch, kv head)
+  // units, and inside a group the kv tiles heaviest first (causal: tile 0 sees every query
+  // tile) across all its units, so the last CTAs to start are light ones; a group's units
+  // run together and share their Q / dO in L2.  (Per-unit heaviest-first left long CTAs
+  // for the end when CTAs are long, e.g. GQA looping over several query heads.)
+  const int n_t = gridDim.x, n_u = gridDim.y * gridDim.z;
+  const int L = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int gsz = min(kBwdOrderGroup, n_u);
+  const int grp = L / (gsz * n_t), within = L % (gsz * n_t);
+  const int gbase = grp * gsz, gcount = min(gsz, n_u - gbase);
+  const int nblk = within / gcount;
+  const int unit = gbase + within % gcount;
+  const int hk = unit % gridDim.y, b = unit / gridDim.y;
   const int k0 = nblk * kBwdBN;
   const int off = p.Skv - p.Sq;
   const int nqt_all = (p.Sq + kBwdBM - 1) / kBwdBM;
