@@ -40,6 +40,20 @@ namespace fa {
 
 constexpr int kFwdBM = 128;  // rows per Q tile = TMEM lanes
 constexpr int kFwdBN = 128;  // keys per KV tile
+constexpr int kFwdOrderGroup = 8;  // (batch, kv head) units ordered together (dense)
+
+// Dense work order over n_t q blocks x n_u (batch, kv head) units: linear index L walks
+// groups of kFwdOrderGroup units and, inside a group, the q block ranks across all its
+// units (causal: rank 0 = the heaviest block), so the last work to start is light; a
+// group's units run together and share their K/V in L2.  Returns the q block rank x and
+// the unit.
+__device__ __forceinline__ void fwd_dense_order(int L, int n_t, int n_u, int& x, int& unit) {
+  const int gsz = min(kFwdOrderGroup, n_u);
+  const int grp = L / (gsz * n_t), within = L % (gsz * n_t);
+  const int gbase = grp * gsz, gcount = min(gsz, n_u - gbase);
+  x = within / gcount;
+  unit = gbase + within % gcount;
+}
 
 template <int D, int NQ>
 struct FwdCfg {
@@ -106,7 +120,15 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
   const int G = p.G;
   const int TPT = kFwdBM / G;       // tokens per Q tile (rows TPT*G .. 127 unused when G does not divide 128)
   const int TPB = NQ * TPT;         // tokens per CTA block
-  const int hk = blockIdx.y;
+  // Dense: grouped order (fwd_dense_order); paged: blockIdx.x is the sequence block.
+  int hk = blockIdx.y, dense_b = blockIdx.z, dense_x = blockIdx.x;
+  if constexpr (!PAGED) {
+    int unit;
+    fwd_dense_order(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), gridDim.x,
+                     gridDim.y * gridDim.z, dense_x, unit);
+    hk = unit % gridDim.y;
+    dense_b = unit / gridDim.y;
+  }
 
   // ---------------------------------------------------------------- work item
   if (threadIdx.x == 0) {
@@ -135,8 +157,8 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
         q_len = kv_len = off = tok_base = 0;
       }
     } else {
-      b = blockIdx.z;
-      tile = p.causal ? (gridDim.x - 1 - blockIdx.x) : blockIdx.x;  // heaviest blocks first
+      b = dense_b;
+      tile = p.causal ? (gridDim.x - 1 - dense_x) : dense_x;  // heaviest blocks first
       q_len = p.Sq;
       kv_len = p.Skv;
       off = p.Skv - p.Sq;
@@ -630,16 +652,19 @@ struct FwdPersistCtl {
   FwdItem item[2];       // work items published by the producer, double-buffered
 };
 
-// Work list entry L -> item, in the grid order of a one-CTA-per-item launch: q block
-// fastest (causal dense: heaviest first), then kv head, then batch.  Paged: the q block
-// index runs over all sequences' blocks (p.nbx slots per kv head, the tail empty).
-// Returns false for an empty slot.
+// Work list entry L -> item, in the order of the one-CTA-per-item launch: dense in the
+// grouped order of fwd_dense_order (q block ranks, kv heads, batches).  Paged: the q block index runs over all sequences' blocks (p.nbx
+// slots per kv head, the tail empty).  Returns false for an empty slot.
 template <int NQ, bool PAGED>
 __device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it) {
   const int TPB = NQ * (kFwdBM / p.G);
-  const int x = L % p.nbx;
+  int x = L % p.nbx;
   it.hk = (L / p.nbx) % p.Hk;
-  int tile;
+  int tile, unit = L / p.nbx;
+  if constexpr (!PAGED) {
+    fwd_dense_order(L, p.nbx, p.n_items / p.nbx, x, unit);
+    it.hk = unit % p.Hk;
+  }
   if constexpr (PAGED) {
     int cum = 0, s = 0;
     for (; s < p.num_seqs; ++s) {
@@ -656,7 +681,7 @@ __device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it) {
     it.off = p.pkl[s];
     it.tok_base = p.qsl[s];
   } else {
-    it.b = L / (p.nbx * p.Hk);
+    it.b = unit / p.Hk;
     tile = p.causal ? (p.nbx - 1 - x) : x;
     it.q_len = p.Sq;
     it.kv_len = p.Skv;
