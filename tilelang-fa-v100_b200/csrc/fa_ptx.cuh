@@ -137,9 +137,6 @@ __device__ __forceinline__ void tma_store_4d(const void* tmap, uint32_t src, int
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
-__device__ __forceinline__ void bulk_wait_group_all() {
-  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-}
 // Waits until the committed bulk stores have read their shared-memory source (the
 // global writes then complete on their own before the grid completes).
 __device__ __forceinline__ void bulk_wait_group_read() {
@@ -225,16 +222,7 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// 32 lanes x 32-bit, 16 consecutive columns per thread.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
+// 32 lanes x 32-bit: thread i of the warp receives 32 consecutive columns of lane i.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
