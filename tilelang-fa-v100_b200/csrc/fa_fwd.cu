@@ -654,9 +654,11 @@ struct FwdPersistCtl {
 
 // Work list entry L -> item, in the order of the one-CTA-per-item launch: dense in the
 // grouped order of fwd_dense_order (q block ranks, kv heads, batches).  Paged: the q block index runs over all sequences' blocks (p.nbx
-// slots per kv head, the tail empty).  Returns false for an empty slot.
+// slots per kv head, the tail empty).  Returns false for an empty slot.  Called by all 32
+// lanes of a warp (the paged scan over sequences takes 32 of them per step); the result is
+// the same in every lane.
 template <int NQ, bool PAGED>
-__device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it) {
+__device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it, int lane) {
   const int TPB = NQ * (kFwdBM / p.G);
   int x = L % p.nbx;
   it.hk = (L / p.nbx) % p.Hk;
@@ -666,14 +668,32 @@ __device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it) {
     it.hk = unit % p.Hk;
   }
   if constexpr (PAGED) {
-    int cum = 0, s = 0;
-    for (; s < p.num_seqs; ++s) {
-      const int ql = p.qsl[s + 1] - p.qsl[s];
-      const int nb = ql > 0 ? (ql + TPB - 1) / TPB : 0;
-      if (x < cum + nb) break;
-      cum += nb;
+    // Sequence s owns q block slots [cum_s, cum_s + nb_s); find the first whose end > x.
+    int s = -1, cum = 0, base = 0;
+    for (int s0 = 0; s0 < p.num_seqs; s0 += 32) {
+      const int sl = s0 + lane;
+      int nb = 0;
+      if (sl < p.num_seqs) {
+        const int ql = p.qsl[sl + 1] - p.qsl[sl];
+        nb = ql > 0 ? (ql + TPB - 1) / TPB : 0;
+      }
+      int incl = nb;  // inclusive prefix sum of block counts across the warp
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += v;
+      }
+      const int end = base + incl;
+      const unsigned hit = __ballot_sync(0xffffffffu, sl < p.num_seqs && x < end);
+      if (hit != 0u) {
+        const int l = __ffs(hit) - 1;
+        s = s0 + l;
+        cum = __shfl_sync(0xffffffffu, end - nb, l);
+        break;
+      }
+      base += __shfl_sync(0xffffffffu, incl, 31);
     }
-    if (s == p.num_seqs) return false;
+    if (s < 0) return false;
     it.b = s;
     tile = x - cum;
     it.q_len = p.qsl[s + 1] - p.qsl[s];
@@ -781,25 +801,27 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
     bool ok = true;
     for (;; ++k) {
       int okl = 1;
-      if (lane == 0) {
-        if (k >= 2)
-          okl = mbar_wait(smem_u32(&ctl->item_empty[k & 1]), ((k >> 1) - 1) & 1, abort_flag,
-                          p.err, FA_SITE_FWD_PRODUCER);
-        FwdItem item;
-        item.live = 0;
-        if (okl) {
-          for (;;) {
-            const int L = atomicAdd(p.sched, 1);
-            if (L >= p.n_items) break;
-            if (fwd_decode_item<NQ, PAGED>(L, p, item)) break;
-          }
+      if (lane == 0 && k >= 2)
+        okl = mbar_wait(smem_u32(&ctl->item_empty[k & 1]), ((k >> 1) - 1) & 1, abort_flag,
+                        p.err, FA_SITE_FWD_PRODUCER);
+      okl = __shfl_sync(0xffffffffu, okl, 0);
+      // The whole warp claims (lane 0's ticket) and decodes the next item with work.
+      FwdItem item;
+      item.live = 0;
+      if (okl) {
+        for (;;) {
+          int L = 0;
+          if (lane == 0) L = atomicAdd(p.sched, 1);
+          L = __shfl_sync(0xffffffffu, L, 0);
+          if (L >= p.n_items) break;
+          if (fwd_decode_item<NQ, PAGED>(L, p, item, lane)) break;
         }
+      }
+      if (lane == 0) {
         ctl->item[k & 1] = item;
         mbar_arrive(smem_u32(&ctl->item_full[k & 1]));
       }
-      ok = __shfl_sync(0xffffffffu, okl, 0) != 0;
-      __syncwarp();
-      const FwdItem item = ctl->item[k & 1];
+      ok = okl != 0;
       if (!ok || !item.live) break;
       const int b = item.b, hk = item.hk, j0 = item.j0, nkv = item.nkv;
       // Q tiles of item k into buffer set k % QB, once item k - QB has released it.
