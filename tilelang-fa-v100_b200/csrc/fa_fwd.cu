@@ -3,11 +3,10 @@
 // (tilelang_flash_attn_func, reference kernel _kernels_forward.py:94-172) and the paged
 // vLLM-cache path (tilelang_paged_forward, reference kernel _kernels_paged.py:193-344).
 // Two schedules of the same per-item pipeline:
-//   fa_fwd_kernel          one CTA per work item (dense D = 128 / 256: long items)
+//   fa_fwd_kernel          one CTA per work item (dense D = 128, dense D = 256 non-causal)
 //   fa_fwd_persist_kernel  one CTA per SM claiming work items in the same order, the
 //                          next item's Q load and first S overlapping the current
-//                          item's tail (paged prefill and dense D = 64: items of a few
-//                          KV tiles, where per-item set-up is a large share)
+//                          item's tail (paged prefill, dense D = 64, dense D = 256 causal)
 //
 // CTA work item: NQ Q tiles of 128 rows for one kv head.  A row is a (token, head)
 // pair: the G = H / Hk query heads that share a kv head are packed into the rows
@@ -733,6 +732,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
   using Cfg = FwdPersistCfg<D, NQ>;
   constexpr int ST = Cfg::STAGES;
   constexpr int QB = Cfg::QB;
+  constexpr bool kReloadS = NQ == 2;  // S values re-read from TMEM to stay within 168 registers
   // Release P_t in two halves (PV over the first 64 keys overlaps the second half's
   // exponentials).  Measured faster for dense D >= 128; for D = 64 (cheap PV) and the
   // paged path the extra barrier costs more than the overlap gains.
@@ -1069,9 +1069,10 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
         }
         const int clo = lo - key0, chi = hi - key0;  // visible columns [clo, chi)
         const bool masked = clo > 0 || chi < kFwdBN;
-        // 64 S values at a time stay in registers: keys 64..127 for their max, then keys
-        // 0..63 (kept for the first half of P); keys 64..127 are loaded again during the
-        // first half's exponentials.  P overwrites only S columns already read.
+        // Keys 64..127 are read first (their max), then keys 0..63 (kept for the first half
+        // of P).  Two-tile CTAs (168 registers a thread) keep 64 S values at a time and load
+        // keys 64..127 again during the first half's exponentials; one-tile CTAs keep all
+        // 128.  P overwrites only S columns already read.
         auto mask64 = [&](uint32_t* v, int c0) {
 #pragma unroll
           for (int c = 0; c < 64; ++c)
@@ -1092,12 +1093,12 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
           for (int u = 0; u < 4; ++u) mx4[u] = fmaxf(mx4[u], __uint_as_float(v[60 + u]));
           return fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]);
         };
-        uint32_t s[64];
-        tmem_ld32(tS + 64, s);
-        tmem_ld32(tS + 96, s + 32);
+        uint32_t s[64], s_hi[64];
+        tmem_ld32(tS + 64, s_hi);
+        tmem_ld32(tS + 96, s_hi + 32);
         tmem_wait_ld();
-        if (masked) mask64(s, 64);
-        const float mx_hi = max64(s);
+        if (masked) mask64(s_hi, 64);
+        const float mx_hi = max64(s_hi);
         tmem_ld32(tS + 0, s);
         tmem_ld32(tS + 32, s + 32);
         tmem_wait_ld();
@@ -1137,7 +1138,6 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
         // kSplitP the first half is released to the MMA issuer (p_half) before the second is
         // computed, except by a warp that must rescale O first (PV_j accumulates onto the
         // rescaled O): it arrives on p_half after its rescale.
-        uint32_t s_hi[64];
         {
           uint32_t pk[32];
 #pragma unroll
@@ -1146,7 +1146,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
             const float p1 = ex2_approx(fmaf(__uint_as_float(s[2 * cc + 1]), c2, -mref_s));
             rs[cc & 7] += p0 + p1;
             pk[cc] = Pack2<T>::pack(p0, p1);
-            if (cc == 15) {
+            if (kReloadS && cc == 15) {
               // keys 0..31 are consumed: bring keys 64..127 back while 32..63 are computed
               tmem_ld32(tS + 64, s_hi);
               tmem_ld32(tS + 96, s_hi + 32);
@@ -1159,8 +1159,10 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
           tc_fence_before();
           mbar_arrive(smem_u32(&ctl->p_half[t]));
         }
-        tmem_wait_ld();
-        if (masked) mask64(s_hi, 64);
+        if (kReloadS) {
+          tmem_wait_ld();
+          if (masked) mask64(s_hi, 64);
+        }
         {
           uint32_t pk[32];
 #pragma unroll
@@ -1312,13 +1314,21 @@ static int* fwd_sched_counter(cudaStream_t st) {
   if (cudaMemsetAsync(c, 0, sizeof(int), st) != cudaSuccess) return nullptr;
   return c;
 }
-// Which schedule serves a launch: the persistent kernel for the paged path and D = 64
-// (work items of a few KV tiles, where per-item set-up is a large share), one CTA per
-// work item for dense D >= 128 (long items; the smaller kernel keeps its instruction
-// footprint, measured faster there).
+// Which schedule serves a launch.  Persistent: paged prefill, dense D = 64, dense D = 256
+// causal (work items of a few to a few dozen KV tiles, where per-item set-up is a large
+// share).  One CTA per work item: dense D = 128, where it measured faster (the two-tile
+// softmax at 168 registers needs the two-pass S loads in the persistent kernel, and its
+// larger code misses the instruction cache more; the items are long), and dense D = 256
+// non-causal (long equal items: 1129 vs 1103 TFLOP/s).
 template <int D, bool PAGED>
-constexpr bool fwd_persistent() {
-  return PAGED || D == 64;
+constexpr bool fwd_may_persist() { return PAGED || D != 128; }
+template <int D, bool PAGED>
+constexpr bool fwd_may_direct() { return !PAGED && D != 64; }
+template <int D, bool PAGED>
+static bool fwd_persistent(bool causal) {
+  if (!fwd_may_direct<D, PAGED>()) return true;
+  if (!fwd_may_persist<D, PAGED>()) return false;
+  return causal;  // dense D = 256
 }
 
 template <typename K>
@@ -1333,32 +1343,50 @@ static int fwd_smem_attr(K kern, int bytes, bool* done) {
 }
 
 template <typename T, int D, int NQ, bool PAGED>
+static int launch_fwd_persist(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                              const CUtensorMap& to, const FwdParams& p, int kind, cudaStream_t st) {
+  using Cfg = FwdPersistCfg<D, NQ>;
+  auto kern = fa_fwd_persist_kernel<T, D, NQ, PAGED>;
+  static bool attr_set[64] = {false};
+  if (int s = fwd_smem_attr(kern, Cfg::SMEM_BYTES, attr_set)) return s;
+  FwdParams q = p;
+  q.sched = fwd_sched_counter(st);
+  if (q.sched == nullptr) return FA_ERR_CUDA;
+  const dim3 grid(p.n_items < num_sms() ? p.n_items : num_sms());
+  prof_begin(kind, st);
+  kern<<<grid, Cfg::NTHREADS, Cfg::SMEM_BYTES, st>>>(tq, tk, tv, to, q);
+  prof_end(kind, st);
+  return FA_OK;
+}
+
+template <typename T, int D, int NQ, bool PAGED>
+static int launch_fwd_direct(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                             const CUtensorMap& to, const FwdParams& p, int kind, cudaStream_t st) {
+  using Cfg = FwdCfg<D, NQ>;
+  auto kern = fa_fwd_kernel<T, D, NQ, PAGED>;
+  static bool attr_set[64] = {false};
+  if (int s = fwd_smem_attr(kern, Cfg::SMEM_BYTES, attr_set)) return s;
+  // one CTA per work item: q blocks x kv heads x batch
+  const dim3 grid(p.nbx, p.Hk, p.n_items / (p.nbx * p.Hk));
+  prof_begin(kind, st);
+  kern<<<grid, Cfg::NTHREADS, Cfg::SMEM_BYTES, st>>>(tq, tk, tv, to, p);
+  prof_end(kind, st);
+  return FA_OK;
+}
+
+template <typename T, int D, int NQ, bool PAGED>
 static int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                            const CUtensorMap& to, const FwdParams& p, cudaStream_t st) {
   const int kind = PAGED ? FA_PROF_PAGED : FA_PROF_FWD;
-  if constexpr (fwd_persistent<D, PAGED>()) {
-    using Cfg = FwdPersistCfg<D, NQ>;
-    auto kern = fa_fwd_persist_kernel<T, D, NQ, PAGED>;
-    static bool attr_set[64] = {false};
-    if (int s = fwd_smem_attr(kern, Cfg::SMEM_BYTES, attr_set)) return s;
-    FwdParams q = p;
-    q.sched = fwd_sched_counter(st);
-    if (q.sched == nullptr) return FA_ERR_CUDA;
-    const dim3 grid(p.n_items < num_sms() ? p.n_items : num_sms());
-    prof_begin(kind, st);
-    kern<<<grid, Cfg::NTHREADS, Cfg::SMEM_BYTES, st>>>(tq, tk, tv, to, q);
-    prof_end(kind, st);
+  int s = FA_OK;
+  if (fwd_persistent<D, PAGED>(p.causal != 0)) {
+    if constexpr (fwd_may_persist<D, PAGED>())
+      s = launch_fwd_persist<T, D, NQ, PAGED>(tq, tk, tv, to, p, kind, st);
   } else {
-    using Cfg = FwdCfg<D, NQ>;
-    auto kern = fa_fwd_kernel<T, D, NQ, PAGED>;
-    static bool attr_set[64] = {false};
-    if (int s = fwd_smem_attr(kern, Cfg::SMEM_BYTES, attr_set)) return s;
-    // one CTA per work item: q blocks x kv heads x batch
-    const dim3 grid(p.nbx, p.Hk, p.n_items / (p.nbx * p.Hk));
-    prof_begin(kind, st);
-    kern<<<grid, Cfg::NTHREADS, Cfg::SMEM_BYTES, st>>>(tq, tk, tv, to, p);
-    prof_end(kind, st);
+    if constexpr (fwd_may_direct<D, PAGED>())
+      s = launch_fwd_direct<T, D, NQ, PAGED>(tq, tk, tv, to, p, kind, st);
   }
+  if (s != FA_OK) return s;
   FA_CUDA_TRY(cudaGetLastError());
   count_launch();
   return FA_OK;
