@@ -53,6 +53,12 @@ FWD_CASES = [
     (2, 512, 512, 2, 2, 64, True, torch.float16),
     (1, 1000, 1000, 1, 1, 128, True, torch.bfloat16),
     (1, 384, 1024, 2, 2, 128, False, torch.float16),
+    # long keys: work items of more than 12 KV tiles take the one-CTA-per-item kernel
+    (1, 64, 4096, 2, 2, 128, True, torch.bfloat16),     # non-square causal
+    (1, 3300, 3300, 4, 1, 128, True, torch.bfloat16),   # MQA
+    (1, 4200, 4100, 2, 2, 128, True, torch.float16),    # Sq > Skv
+    (1, 2000, 2000, 8, 2, 128, False, torch.float16),   # GQA 4:1, non-causal
+    (1, 1700, 1700, 2, 2, 256, False, torch.bfloat16),  # D = 256 non-causal
 ]
 
 

@@ -2,11 +2,12 @@
 // TMA-fed K/V ring, warp-specialised roles, for the dense BSHD path
 // (tilelang_flash_attn_func, reference kernel _kernels_forward.py:94-172) and the paged
 // vLLM-cache path (tilelang_paged_forward, reference kernel _kernels_paged.py:193-344).
-// Two schedules of the same per-item pipeline:
-//   fa_fwd_kernel          one CTA per work item (dense D = 128, dense D = 256 non-causal)
+// Two schedules of the same per-item pipeline, chosen per launch (fwd_persistent):
+//   fa_fwd_kernel          one CTA per work item (dense D = 128 / 256 with long items)
 //   fa_fwd_persist_kernel  one CTA per SM claiming work items in the same order, the
 //                          next item's Q load and first S overlapping the current
-//                          item's tail (paged prefill, dense D = 64, dense D = 256 causal)
+//                          item's tail (paged prefill, dense D = 64, short dense items,
+//                          dense D = 256 causal)
 //
 // CTA work item: NQ Q tiles of 128 rows for one kv head.  A row is a (token, head)
 // pair: the G = H / Hk query heads that share a kv head are packed into the rows
@@ -1314,21 +1315,27 @@ static int* fwd_sched_counter(cudaStream_t st) {
   if (cudaMemsetAsync(c, 0, sizeof(int), st) != cudaSuccess) return nullptr;
   return c;
 }
-// Which schedule serves a launch.  Persistent: paged prefill, dense D = 64, dense D = 256
-// causal (work items of a few to a few dozen KV tiles, where per-item set-up is a large
-// share).  One CTA per work item: dense D = 128, where it measured faster (the two-tile
-// softmax at 168 registers needs the two-pass S loads in the persistent kernel, and its
-// larger code misses the instruction cache more; the items are long), and dense D = 256
-// non-causal (long equal items: 1129 vs 1103 TFLOP/s).
+// Which schedule serves a launch.  The persistent kernel hides each work item's set-up
+// (Q load, first S, epilogue) behind the previous item, which pays when items are short;
+// the one-CTA-per-item kernel runs each KV step faster at D = 128 (there the persistent
+// kernel's two-tile softmax needs two-pass S loads to fit 168 registers and its larger
+// code misses the instruction cache more).  Measured (bf16, TFLOP/s, direct -> persistent):
+// D = 128 causal S = 512 238 -> 338, 1024 404 -> 496, 2048 620 -> 662, 4096 855 -> 777;
+// non-causal S = 1024 946 -> 959, 4096 1195 -> 1127; D = 256 causal S = 4096 860 -> 945,
+// non-causal 1112 -> 1103.  Hence: paged and D = 64 always persistent; dense D = 128 / 256
+// persistent when a work item averages at most 12 KV tiles, and D = 256 causal always.
+constexpr int kFwdPersistMaxTiles = 12;
 template <int D, bool PAGED>
-constexpr bool fwd_may_persist() { return PAGED || D != 128; }
+constexpr bool fwd_may_persist() { return true; }
 template <int D, bool PAGED>
 constexpr bool fwd_may_direct() { return !PAGED && D != 64; }
 template <int D, bool PAGED>
-static bool fwd_persistent(bool causal) {
+static bool fwd_persistent(bool causal, int kv_len) {
   if (!fwd_may_direct<D, PAGED>()) return true;
-  if (!fwd_may_persist<D, PAGED>()) return false;
-  return causal;  // dense D = 256
+  const int tiles = (kv_len + kFwdBN - 1) / kFwdBN;
+  const int avg_tiles = causal ? (tiles + 1) / 2 : tiles;  // per work item
+  if (D == 256 && causal) return true;
+  return avg_tiles <= kFwdPersistMaxTiles;
 }
 
 template <typename K>
@@ -1379,7 +1386,7 @@ static int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const C
                            const CUtensorMap& to, const FwdParams& p, cudaStream_t st) {
   const int kind = PAGED ? FA_PROF_PAGED : FA_PROF_FWD;
   int s = FA_OK;
-  if (fwd_persistent<D, PAGED>(p.causal != 0)) {
+  if (fwd_persistent<D, PAGED>(p.causal != 0, p.Skv)) {
     if constexpr (fwd_may_persist<D, PAGED>())
       s = launch_fwd_persist<T, D, NQ, PAGED>(tq, tk, tv, to, p, kind, st);
   } else {
