@@ -458,8 +458,10 @@ def run_ours(args):
         ms, err = float(t[0]), float(t[1])
     fl = step_flops(b, h, s, s, d, causal)
     value = world * fl / ms / 1e9  # TFLOP/s (ms -> s: /1e-3, TFLOP: /1e12)
-    e2e_ms, h2d, d2h, link_ms = time_e2e(fa, dev, b, s, h, d, dtype, causal, min(args.steps, 10),
-                                         2, seed=1000 + rank)
+    # as many e2e steps as timed steps: the first upload and the last download of a
+    # pipelined run are exposed once, so short runs understate the streaming rate
+    e2e_ms, h2d, d2h, link_ms = time_e2e(fa, dev, b, s, h, d, dtype, causal, args.steps, 2,
+                                         seed=1000 + rank)
     if dist is not None:
         t = torch.tensor([e2e_ms, link_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
