@@ -105,6 +105,11 @@ BWD_CASES = [
     (1, 257, 257, 4, 1, 128, True, torch.bfloat16),
     (1, 190, 190, 4, 2, 64, True, torch.float16),
     (1, 512, 512, 2, 2, 64, True, torch.bfloat16),
+    # causal with seqlen_q > seqlen_k + 128: query tile 0 sees no key (dq = 0 from prep)
+    (1, 400, 150, 2, 2, 128, True, torch.bfloat16),
+    # several KV tiles add into each query tile; ragged last tile; GQA 4:2
+    (2, 1000, 1000, 4, 2, 128, True, torch.float16),
+    (1, 300, 700, 2, 1, 64, False, torch.bfloat16),
 ]
 
 
