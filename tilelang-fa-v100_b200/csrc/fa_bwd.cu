@@ -17,8 +17,9 @@
 //                        dK  += dS^T Q           (SS, A = dS^T K-major in smem)
 //                        dQ^T = K^T dS^T         (SS, both MN-major, two 64-query
 //                                                 halves) -> the dP^T columns
-//                      and dQ is added to an fp32 accumulator with fp32 atomics, one
-//                      128-byte row per warp instruction (atomic mode).  In
+//                      and dQ is added to an fp32 accumulator (atomic mode): at D = 128
+//                      each 64-query half is staged in shared memory and added by one
+//                      bulk reduce-add, at D = 64 by per-thread fp32 atomics.  In
 //                      deterministic mode the last GEMM is skipped.
 //                      Issue order per step i: dV(i), S(i+1), dK(i), dQ(i), dP(i+1), so
 //                      S(i+1) overlaps the dS pass of step i.
@@ -27,12 +28,13 @@
 //                      (S = Q K^T, dP = dO V^T, dQ += dS K), no atomics.
 //   4. fa_bwd_dq_conv  atomic mode: fp32 accumulator -> dq in the input dtype (BSHD).
 //
-// Roles in fa_bwd_dkdv (512 threads): warp 0 TMA producer (K, V once; Q, dO, LSE, D
-// per query tile in a 2-stage ring), warp 1 TMEM allocator + MMA issuer, warps 4-11
-// two compute warpgroups: thread = key row (TMEM lane); warpgroup c handles query
-// columns [64c, 64c+64) of S^T / dP^T, writes P^T to TMEM columns [64c, 64c+32) (over
-// S^T columns it has already read) and dS^T to the shared-memory dS tile; warps 12-15
-// (atomic mode) move dQ out of TMEM and add it to the fp32 accumulator.
+// Roles in fa_bwd_dkdv (512 threads): warp 0 TMA producer (K, V once; Q, LSE, D per
+// query tile in a 2-stage ring; dO in its own 1- or 2-slot ring), warp 1 TMEM allocator
+// + MMA issuer, warps 4-11 two compute warpgroups: thread = key row (TMEM lane);
+// warpgroup c handles query columns [64c, 64c+64) of S^T / dP^T, writes P^T to TMEM
+// columns [64c, 64c+32) (over S^T columns it has already read) and dS^T to the
+// shared-memory dS tile; warps 12-15 (atomic mode) move dQ out of TMEM and add it to
+// the fp32 accumulator.
 #include "fa_ptx.cuh"
 #include "fa_internal.h"
 #include <cmath>
@@ -50,9 +52,17 @@ struct BwdCfg {
   static constexpr int CHUNK = 128 * 128;
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = TILE;
+  // D = 128: dQ halves are staged in shared memory ([64 q][D] fp32 = TILE bytes) and
+  // added by bulk reduce; the staging tile is the room a second dO buffer would take,
+  // so dO has one buffer (loaded after dV(i), its last reader, in time for dP(i+1)).
+  // D = 64: per-thread fp32 atomics (measured equal or faster there) and two dO buffers.
+  static constexpr bool BULK_DQ = D == 128;
+  static constexpr int DO_ST = BULK_DQ ? 1 : 2;
+  static constexpr int STG_N = BULK_DQ ? 1 : 0;
   static constexpr int OFF_Q = 2 * TILE;           // 2 stages
-  static constexpr int OFF_DO = 4 * TILE;          // 2 stages
-  static constexpr int OFF_DS = 6 * TILE;          // [2 q chunks][128 keys][64 q] 16-bit
+  static constexpr int OFF_DO = 4 * TILE;
+  static constexpr int OFF_STG = OFF_DO + DO_ST * TILE;
+  static constexpr int OFF_DS = OFF_STG + STG_N * TILE;  // [2 q chunks][128 keys][64 q] 16-bit
   static constexpr int OFF_LSE = OFF_DS + 128 * 128 * 2;  // [2][128] fp32
   static constexpr int OFF_DI = OFF_LSE + 2 * 128 * 4;    // [2][128] fp32
   static constexpr int OFF_CTL = OFF_DI + 2 * 128 * 4;
@@ -85,6 +95,7 @@ struct BwdCtl {
   uint64_t st_empty[2];
   uint64_t s_full, p_ready, ds_ready, final_done, drain;
   uint64_t dp_full[2], dq_full[2], dq_free[2];  // per 64-query half
+  uint64_t do_full[2], do_empty[2];
   uint32_t tmem_base;
   int abort_flag;
   int smem_ok;
@@ -277,6 +288,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(smem_u32(&ctl->dq_full[hh]), 1);
       mbar_init(smem_u32(&ctl->dq_free[hh]), 128);
     }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&ctl->do_full[s]), 1);
+      mbar_init(smem_u32(&ctl->do_empty[s]), 1);
+    }
     mbar_init(smem_u32(&ctl->final_done), 1);
     mbar_init(smem_u32(&ctl->drain), 1);
     fence_barrier_init();
@@ -306,7 +321,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tma_load_4d(sK + dh * Cfg::CHUNK, &tm_k, kvb, dh * 64, hk, k0, b);
         tma_load_4d(sV + dh * Cfg::CHUNK, &tm_v, kvb, dh * 64, hk, k0, b);
       }
-      int i = 0;
+      int i = 0, n_do = 0;
       for (; i < n_iter; ++i) {
         const int s = i & 1;
         if (!mbar_wait(smem_u32(&ctl->st_empty[s]), ((i >> 1) & 1) ^ 1, abort_flag, p.err,
@@ -315,19 +330,31 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         FA_TRACE_EVENT(12, i);
         const int g = i / nqt, qt = t_start + i % nqt, h = hk * p.G + g;
         const uint32_t fb = smem_u32(&ctl->st_full[s]);
-        mbar_arrive_expect_tx(fb, 2 * Cfg::TILE + 1024);
+        mbar_arrive_expect_tx(fb, Cfg::TILE + 1024);
         const uint32_t sQ = base + Cfg::OFF_Q + s * Cfg::TILE;
-        const uint32_t sdO = base + Cfg::OFF_DO + s * Cfg::TILE;
-        for (int dh = 0; dh < Cfg::DH; ++dh) {
+        for (int dh = 0; dh < Cfg::DH; ++dh)
           tma_load_4d(sQ + dh * Cfg::CHUNK, &tm_q, fb, dh * 64, h, qt * kBwdBM, b);
-          tma_load_4d(sdO + dh * Cfg::CHUNK, &tm_do, fb, dh * 64, h, qt * kBwdBM, b);
-        }
         const int64_t row0 = ((int64_t)b * p.H + h) * p.Sq_pad + qt * kBwdBM;
         bulk_load(base + Cfg::OFF_LSE + s * 512, p.lse2 + row0, 512, fb);
         bulk_load(base + Cfg::OFF_DI + s * 512, p.dsum + row0, 512, fb);
+        // dO(i) goes into its slot once dV(i - DO_ST), the slot's last reader, completed.
+        const int ds = i % Cfg::DO_ST, du = i / Cfg::DO_ST;
+        if (!mbar_wait(smem_u32(&ctl->do_empty[ds]), (du & 1) ^ 1, abort_flag, p.err,
+                       FA_SITE_BWD_PRODUCER)) {
+          ++i;  // Q(i) is in flight: drain it below
+          break;
+        }
+        const uint32_t db = smem_u32(&ctl->do_full[ds]);
+        mbar_arrive_expect_tx(db, Cfg::TILE);
+        for (int dh = 0; dh < Cfg::DH; ++dh)
+          tma_load_4d(base + Cfg::OFF_DO + ds * Cfg::TILE + dh * Cfg::CHUNK, &tm_do, db, dh * 64,
+                      h, qt * kBwdBM, b);
+        n_do = i + 1;
       }
       drain_wait(kvb, 0);
       for (int k = max(0, i - 2); k < i; ++k) drain_wait(smem_u32(&ctl->st_full[k & 1]), (k >> 1) & 1);
+      for (int k = max(0, n_do - Cfg::DO_ST); k < n_do; ++k)
+        drain_wait(smem_u32(&ctl->do_full[k % Cfg::DO_ST]), (k / Cfg::DO_ST) & 1);
     }
   } else if (warp == 1) {
     // ============================================================ MMA issuer
@@ -359,8 +386,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       };
       // dP^T(i) = V dO(i)^T for queries [64hh, 64hh + 64) into [128 + 64hh, 192 + 64hh).
-      auto issue_dP = [&](int st, int hh) {
-        const uint64_t ddOk = desc_add(ddO_k0, st * Cfg::TILE + hh * 64 * 128);
+      auto issue_dP = [&](int ds, int hh) {
+        const uint64_t ddOk = desc_add(ddO_k0, ds * Cfg::TILE + hh * 64 * 128);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
@@ -375,8 +402,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           tc_fence_after();
           issue_S(0);
           mma_commit(smem_u32(&ctl->s_full));
-          issue_dP(0, 0);
-          issue_dP(0, 1);
+          ok = mbar_wait(smem_u32(&ctl->do_full[0]), 0, abort_flag, p.err, FA_SITE_BWD_MMA);
+          if (ok) {
+            tc_fence_after();
+            issue_dP(0, 0);
+            issue_dP(0, 1);
+          }
         }
       }
       // Step i: dV(i) as soon as P^T(i) is in TMEM, then S(i+1) (its columns are free:
@@ -388,7 +419,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int s = i & 1;
         const uint32_t par = i & 1;
         const bool has_next = i + 1 < n_iter;
-        const uint64_t dQm = desc_add(dQ_m0, s * Cfg::TILE), ddOm = desc_add(ddO_m0, s * Cfg::TILE);
+        const int ds = i % Cfg::DO_ST, ds1 = (i + 1) % Cfg::DO_ST;
+        const uint64_t dQm = desc_add(dQ_m0, s * Cfg::TILE), ddOm = desc_add(ddO_m0, ds * Cfg::TILE);
         // dV += P^T dO   (P^T for q 0..63 in columns 0..31, q 64..127 in 64..95)
         ok = mbar_wait(smem_u32(&ctl->p_ready), par, abort_flag, p.err, FA_SITE_BWD_MMA);
         if (!ok) break;
@@ -399,6 +431,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const uint32_t acol = (kk < 4) ? kk * 8 : 64 + (kk - 4) * 8;
           mma_ts(tdV, tS + acol, desc_add(ddOm, kk * 2048), idKV, (i > 0 || kk > 0) ? 1u : 0u);
         }
+        mma_commit(smem_u32(&ctl->do_empty[ds]));  // dO(i) read by dP(i) and dV(i)
         if (has_next) {
           ok = mbar_wait(smem_u32(&ctl->st_full[s ^ 1]), ((i + 1) >> 1) & 1, abort_flag, p.err,
                          FA_SITE_BWD_MMA);
@@ -431,14 +464,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         mma_commit(smem_u32(&ctl->st_empty[s]));
         FA_TRACE_EVENT(5, i);
         if (has_next) {
+          ok = mbar_wait(smem_u32(&ctl->do_full[ds1]), ((i + 1) / Cfg::DO_ST) & 1, abort_flag, p.err,
+                         FA_SITE_BWD_MMA);
 #pragma unroll
           for (int hh = 0; hh < 2 && ok; ++hh) {
             if (ATOMIC_DQ) {
               ok = mbar_wait(smem_u32(&ctl->dq_free[hh]), par, abort_flag, p.err, FA_SITE_BWD_MMA);
               if (!ok) break;
-              tc_fence_after();
             }
-            issue_dP(s ^ 1, hh);
+            tc_fence_after();
+            issue_dP(ds1, hh);
           }
         }
       }
@@ -585,36 +620,64 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (ATOMIC_DQ) {
     // ============================================================ dQ warpgroup
     // Thread = head-dim column d (TMEM lane of dQ^T).  Each 64-query half is moved out
-    // of TMEM, its columns are released for the next dP^T half at once, and the values
-    // are added to the fp32 accumulator: one warp instruction covers 32 consecutive d
-    // of one query row (128 contiguous bytes).
+    // of TMEM (its columns are released for the next dP^T half at once) and added to the
+    // fp32 accumulator.  D = 128: the half is written to the staging tile [64 q][D] fp32
+    // in shared memory (a warp stores 32 consecutive d of a row: 128 contiguous bytes)
+    // and added by one bulk reduce-add (the 64 accumulator rows of a half are
+    // contiguous), so the adds run in the TMA unit and L2 instead of as per-thread
+    // atomics (cfg3 backward 3.71 -> 3.39 ms).  Thread 384 issues the reduce and waits
+    // for its read of the staging tile before the tile is written again; named barrier 1
+    // (these 128 threads) orders both, and its AND ends the loop for all four warps
+    // together when a wait fails in any of them, so none is left at the barrier.
+    // D = 64: per-thread atomics, one warp instruction per 128-byte row.
     const int dl = ((warp & 3) << 5) | lane;
     const bool d_ok = dl < D;
+    const bool issuer = threadIdx.x == 384;
     const uint32_t tq = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + 128;
+    const uint32_t stg = base + Cfg::OFF_STG;
     bool ok = true;
     for (int i = 0; i < n_iter && ok; ++i) {
       const int g = i / nqt, qt = t_start + i % nqt, h = hk * p.G + g;
-      float* acc = p.dq_acc + (((int64_t)b * p.H + h) * p.Sq_pad + qt * kBwdBM) * D + dl;
+      float* acc = p.dq_acc + (((int64_t)b * p.H + h) * p.Sq_pad + qt * kBwdBM) * D;
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         bool w = mbar_wait(smem_u32(&ctl->dq_full[hh]), i & 1, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
-        ok = __all_sync(0xffffffffu, w);
-        if (!ok) break;
-        if (threadIdx.x == 384) FA_TRACE_EVENT(10 + hh, i);
-        tc_fence_after();
+        w = __all_sync(0xffffffffu, w);
         uint32_t v[64];
-        tmem_ld32(tq + 64 * hh, v);
-        tmem_ld32(tq + 64 * hh + 32, v + 32);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(smem_u32(&ctl->dq_free[hh]));
-        if (d_ok) {
-          float* a = acc + (int64_t)(64 * hh) * D;
+        if (w) {
+          if (issuer) FA_TRACE_EVENT(10 + hh, i);
+          tc_fence_after();
+          tmem_ld32(tq + 64 * hh, v);
+          tmem_ld32(tq + 64 * hh + 32, v + 32);
+          tmem_wait_ld();
+          tc_fence_before();
+          mbar_arrive(smem_u32(&ctl->dq_free[hh]));
+        }
+        if constexpr (Cfg::BULK_DQ) {
+          if (issuer) bulk_wait_group_read();  // the last reduce has read the staging tile
+          ok = bar_red_and(1, 128, w);
+          if (!ok) break;
 #pragma unroll
-          for (int x = 0; x < 64; ++x) atomicAdd(a + (int64_t)x * D, __uint_as_float(v[x]));
+          for (int x = 0; x < 64; ++x)
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(stg + (x * D + dl) * 4), "r"(v[x]) : "memory");
+          fence_async_shared();
+          bar_sync_n(1, 128);
+          if (issuer) {
+            bulk_reduce_add_f32(acc + (int64_t)(64 * hh) * D, stg, 64 * D * 4);
+            bulk_commit_group();
+          }
+        } else {
+          ok = w;
+          if (!ok) break;
+          if (d_ok) {
+            float* a = acc + (int64_t)(64 * hh) * D + dl;
+#pragma unroll
+            for (int x = 0; x < 64; ++x) atomicAdd(a + (int64_t)x * D, __uint_as_float(v[x]));
+          }
         }
       }
     }
+    if (issuer) bulk_wait_group_all();  // the adds complete before the CTA's memory goes
     }
   }
   tc_fence_before();

@@ -106,6 +106,24 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// ---------------------------------------------------------------- named barriers
+// Barrier `id` (1..15; 0 is __syncthreads) over `count` threads, whole warps, every warp
+// converged.  The reduction form returns the AND of `pred` over all of them, so a
+// decision taken after it is uniform across the participating warps.
+__device__ __forceinline__ bool bar_red_and(int id, int count, bool pred) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.s32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\tselp.s32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<int>(pred)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void bar_sync_n(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
@@ -141,6 +159,19 @@ __device__ __forceinline__ void bulk_commit_group() {
 // global writes then complete on their own before the grid completes).
 __device__ __forceinline__ void bulk_wait_group_read() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Waits until every committed bulk operation of this thread has completed.
+__device__ __forceinline__ void bulk_wait_group_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Element-wise fp32 add of `bytes` (a multiple of 16; both addresses 16-byte aligned)
+// from shared memory into global memory, performed at L2 (bulk-group completion).
+__device__ __forceinline__ void bulk_reduce_add_f32(float* dst, uint32_t src, uint32_t bytes) {
+  asm volatile(
+      "cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(
+          reinterpret_cast<uint64_t>(dst)),
+      "r"(src), "r"(bytes)
+      : "memory");
 }
 __device__ __forceinline__ void fence_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
