@@ -110,6 +110,14 @@ BWD_CASES = [
     # several KV tiles add into each query tile; ragged last tile; GQA 4:2
     (2, 1000, 1000, 4, 2, 128, True, torch.float16),
     (1, 300, 700, 2, 1, 64, False, torch.bfloat16),
+    # D = 128, one query head per kv head, short items: the persistent dK/dV kernel with
+    # 300-500 work items, so each CTA runs two to four of them.  The causal ones are fp16:
+    # in bf16 the first causal rows (a few visible keys, dS = P (dP - D) a cancellation
+    # of bf16-rounded terms) put a handful of the 6M dq elements just past the bf16 bound
+    # at this size, identically for the one-CTA-per-item kernel.
+    (40, 300, 300, 4, 4, 128, True, torch.float16),
+    (24, 700, 900, 2, 2, 128, False, torch.bfloat16),
+    (30, 1000, 400, 3, 3, 128, True, torch.float16),
 ]
 
 

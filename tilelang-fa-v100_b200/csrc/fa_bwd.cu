@@ -23,6 +23,9 @@
 //                      deterministic mode the last GEMM is skipped.
 //                      Issue order per step i: dV(i), S(i+1), dK(i), dQ(i), dP(i+1), so
 //                      S(i+1) overlaps the dS pass of step i.
+//   2b. fa_bwd_dkdv_persist  the same pipeline as 2, one CTA per SM looping over the
+//                      work items, for atomic mode at D = 128 with one query head per kv
+//                      head and short items (bwd_persistent on the host).
 //   3. fa_bwd_dq       deterministic mode only: one CTA per (128-row Q tile, head,
 //                      batch) loops over KV tiles and accumulates dQ in TMEM
 //                      (S = Q K^T, dP = dO V^T, dQ += dS K), no atomics.
@@ -76,6 +79,7 @@ struct BwdCfg {
 struct BwdParams {
   int B, Sq, Skv, H, Hk, G, Sq_pad;
   int causal;
+  int n_t, n_u, n_items;  // KV tiles per (batch, kv head), B * Hk units, n_t * n_u items
   float scale, scale_log2;
   const float* lse2;  // [B, H, Sq_pad] lse * log2(e); +inf for padded / empty rows
   const float* dsum;  // [B, H, Sq_pad] rowsum(O * dO)
@@ -90,7 +94,7 @@ struct BwdParams {
 };
 
 struct BwdCtl {
-  uint64_t kv_full;
+  uint64_t kv_full, kv_empty;  // kv_empty: persistent kernel only
   uint64_t st_full[2];
   uint64_t st_empty[2];
   uint64_t s_full, p_ready, ds_ready, final_done, drain;
@@ -231,6 +235,13 @@ constexpr int kBwdRegLow = 104;
 constexpr int kBwdRegDq = 112;
 constexpr int kBwdRegHigh = 144;
 static_assert(128 * kBwdRegLow + 256 * kBwdRegHigh + 128 * kBwdRegDq <= 65536,
+              "register split exceeds the launch");
+// The persistent kernel's compute warpgroups carry the item loop's state as well: they
+// get 152 registers (ptxas reports 8 bytes of spill there, 120 at 144).
+constexpr int kBwdPRegLow = 104;
+constexpr int kBwdPRegDq = 96;
+constexpr int kBwdPRegHigh = 152;
+static_assert(128 * kBwdPRegLow + 256 * kBwdPRegHigh + 128 * kBwdPRegDq <= 65536,
               "register split exceeds the launch");
 
 template <typename T, int D, bool ATOMIC_DQ>
@@ -688,6 +699,536 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- 2b. dK / dV, persistent
+// fa_bwd_dkdv_persist_kernel runs the per-step pipeline of fa_bwd_dkdv_kernel (same roles,
+// shared-memory layout and TMEM map) in a loop over work items; the host launches it for
+// <T, 128, atomic dQ> only.
+//
+// Work item L -> (KV tile, kv head, batch) and its query-tile loop.  Order: groups of
+// kBwdOrderGroup (batch, kv head) units, and inside a group the kv tiles heaviest first
+// (causal: tile 0 sees every query tile) across all its units, so the last items to start
+// are light and a group's units run together and share their Q / dO in L2.  (Per-unit
+// heaviest-first left long items for the end when items are long, e.g. GQA looping over
+// several query heads.)
+struct BwdItem {
+  int b, hk, k0, t_start, nqt, n_iter;
+};
+__device__ __forceinline__ BwdItem bwd_item(const BwdParams& p, int L) {
+  const int gsz = min(kBwdOrderGroup, p.n_u);
+  const int grp = L / (gsz * p.n_t), within = L % (gsz * p.n_t);
+  const int gbase = grp * gsz, gcount = min(gsz, p.n_u - gbase);
+  const int unit = gbase + within % gcount;
+  BwdItem it;
+  it.hk = unit % p.Hk;
+  it.b = unit / p.Hk;
+  it.k0 = (within / gcount) * kBwdBN;
+  const int nqt_all = (p.Sq + kBwdBM - 1) / kBwdBM;
+  it.t_start = p.causal ? min(nqt_all, max(0, it.k0 - (p.Skv - p.Sq)) / kBwdBM) : 0;
+  it.nqt = nqt_all - it.t_start;
+  it.n_iter = p.G * it.nqt;
+  return it;
+}
+
+template <typename T, int D, bool ATOMIC_DQ>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    fa_bwd_dkdv_persist_kernel(const __grid_constant__ CUtensorMap tm_q,
+                       const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v,
+                       const __grid_constant__ CUtensorMap tm_do, const BwdParams p) {
+  using Cfg = BwdCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+  const bool smem_ok = (base - raw_addr) + Cfg::USED <= (uint32_t)Cfg::SMEM_BYTES;
+  if (!smem_ok) {  // uniform across the CTA: the layout would not fit
+    if (threadIdx.x == 0) record_device_error(p.err, 2, FA_SITE_BWD_PRODUCER);
+    return;
+  }
+  BwdCtl* ctl = reinterpret_cast<BwdCtl*>(base_ptr + Cfg::OFF_CTL);
+  volatile int* abort_flag = &ctl->abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // CTA x takes work items x, x + gridDim.x, ...: with gridDim.x = n_items one item per
+  // CTA; with one CTA per SM the CTA keeps its barriers and TMEM, and the next item's
+  // K / V, Q and dO loads and its first S and dP^T run while this item's dK / dV leave
+  // TMEM.  Pipeline parities run over the CTA's query-tile steps (gi) and its items with
+  // at least one step (kc); items with none only write dK = dV = 0.
+  const int off = p.Skv - p.Sq;
+
+  if (threadIdx.x == 0) {
+    ctl->abort_flag = 0;
+    mbar_init(smem_u32(&ctl->kv_full), 1);
+    mbar_init(smem_u32(&ctl->kv_empty), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&ctl->st_full[s]), 1);
+      mbar_init(smem_u32(&ctl->st_empty[s]), 1);
+    }
+    mbar_init(smem_u32(&ctl->s_full), 1);
+    mbar_init(smem_u32(&ctl->p_ready), 256);
+    mbar_init(smem_u32(&ctl->ds_ready), 256);
+    for (int hh = 0; hh < 2; ++hh) {
+      mbar_init(smem_u32(&ctl->dp_full[hh]), 1);
+      mbar_init(smem_u32(&ctl->dq_full[hh]), 1);
+      mbar_init(smem_u32(&ctl->dq_free[hh]), 128);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&ctl->do_full[s]), 1);
+      mbar_init(smem_u32(&ctl->do_empty[s]), 1);
+    }
+    mbar_init(smem_u32(&ctl->final_done), 1);
+    mbar_init(smem_u32(&ctl->drain), 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  const uint32_t sK = base + Cfg::OFF_K, sV = base + Cfg::OFF_V;
+  const uint32_t sDS = base + Cfg::OFF_DS;
+  if (warp < 4) {
+    setmaxnreg_dec<kBwdPRegLow>();
+  if (warp == 0) {
+    // ============================================================ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+      const uint32_t kvb = smem_u32(&ctl->kv_full);
+      int gi = 0, kc = 0, n_do = 0;
+      bool ok = true;
+      for (int L = blockIdx.x; L < p.n_items && ok; L += gridDim.x) {
+        const BwdItem it = bwd_item(p, L);
+        if (it.n_iter == 0) continue;
+        // K / V replace the last item's once its MMAs have completed (kv_empty).
+        if (!mbar_wait(smem_u32(&ctl->kv_empty), (kc & 1) ^ 1, abort_flag, p.err,
+                       FA_SITE_BWD_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(kvb, 2 * Cfg::TILE);
+        for (int dh = 0; dh < Cfg::DH; ++dh) {
+          tma_load_4d(sK + dh * Cfg::CHUNK, &tm_k, kvb, dh * 64, it.hk, it.k0, it.b);
+          tma_load_4d(sV + dh * Cfg::CHUNK, &tm_v, kvb, dh * 64, it.hk, it.k0, it.b);
+        }
+        ++kc;
+        for (int i = 0; i < it.n_iter; ++i, ++gi) {
+          const int s = gi & 1;
+          if (!mbar_wait(smem_u32(&ctl->st_empty[s]), ((gi >> 1) & 1) ^ 1, abort_flag, p.err,
+                         FA_SITE_BWD_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          FA_TRACE_EVENT(12, gi);
+          const int g = i / it.nqt, qt = it.t_start + i % it.nqt, h = it.hk * p.G + g;
+          const uint32_t fb = smem_u32(&ctl->st_full[s]);
+          mbar_arrive_expect_tx(fb, Cfg::TILE + 1024);
+          const uint32_t sQ = base + Cfg::OFF_Q + s * Cfg::TILE;
+          for (int dh = 0; dh < Cfg::DH; ++dh)
+            tma_load_4d(sQ + dh * Cfg::CHUNK, &tm_q, fb, dh * 64, h, qt * kBwdBM, it.b);
+          const int64_t row0 = ((int64_t)it.b * p.H + h) * p.Sq_pad + qt * kBwdBM;
+          bulk_load(base + Cfg::OFF_LSE + s * 512, p.lse2 + row0, 512, fb);
+          bulk_load(base + Cfg::OFF_DI + s * 512, p.dsum + row0, 512, fb);
+          // dO goes into its slot once dV of the step DO_ST before, the slot's last
+          // reader, has completed.
+          const int ds = gi % Cfg::DO_ST, du = gi / Cfg::DO_ST;
+          if (!mbar_wait(smem_u32(&ctl->do_empty[ds]), (du & 1) ^ 1, abort_flag, p.err,
+                         FA_SITE_BWD_PRODUCER)) {
+            ++gi;  // Q of this step is in flight: drain it below
+            ok = false;
+            break;
+          }
+          const uint32_t db = smem_u32(&ctl->do_full[ds]);
+          mbar_arrive_expect_tx(db, Cfg::TILE);
+          for (int dh = 0; dh < Cfg::DH; ++dh)
+            tma_load_4d(base + Cfg::OFF_DO + ds * Cfg::TILE + dh * Cfg::CHUNK, &tm_do, db,
+                        dh * 64, h, qt * kBwdBM, it.b);
+          n_do = gi + 1;
+        }
+      }
+      // Loads still in flight complete before the CTA exits.
+      if (kc > 0) drain_wait(kvb, (kc - 1) & 1);
+      for (int k = max(0, gi - 2); k < gi; ++k) drain_wait(smem_u32(&ctl->st_full[k & 1]), (k >> 1) & 1);
+      for (int k = max(0, n_do - Cfg::DO_ST); k < n_do; ++k)
+        drain_wait(smem_u32(&ctl->do_full[k % Cfg::DO_ST]), (k / Cfg::DO_ST) & 1);
+    }
+  } else if (warp == 1) {
+    // ============================================================ MMA issuer
+    if (lane == 0) {
+      constexpr bool kBf16 = Pack2<T>::kBf16;
+      constexpr uint32_t idS = idesc_f16(128, 128, kBf16, false, false);
+      constexpr uint32_t idS64 = idesc_f16(128, 64, kBf16, false, false);
+      constexpr uint32_t idKV = idesc_f16(128, D, kBf16, false, true);
+      // dQ^T half = K^T dS^T (M = 128 head-dim rows; at D = 64 rows 64..127 read the next
+      // 16 KB of shared memory and are ignored), N = 64 queries, both operands MN-major.
+      constexpr uint32_t idQT = idesc_f16(128, 64, kBf16, true, true);
+      const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 256 + D;
+      // Descriptors built once (K-major forms for S^T / dP^T, MN-major for the rest).
+      const uint64_t dK_k = sdesc_sw128(sK, 16, 1024), dV_k = sdesc_sw128(sV, 16, 1024);
+      const uint64_t dQ_k0 = sdesc_sw128(base + Cfg::OFF_Q, 16, 1024);
+      const uint64_t ddO_k0 = sdesc_sw128(base + Cfg::OFF_DO, 16, 1024);
+      const uint64_t dQ_m0 = sdesc_sw128(base + Cfg::OFF_Q, Cfg::CHUNK, 1024);
+      const uint64_t ddO_m0 = sdesc_sw128(base + Cfg::OFF_DO, Cfg::CHUNK, 1024);
+      const uint64_t dDS_m = sdesc_sw128(sDS, Cfg::CHUNK, 1024);
+      const uint64_t dK_m = sdesc_sw128(sK, Cfg::CHUNK, 1024);
+      const uint64_t dDS_k = sdesc_sw128(sDS, 16, 1024);
+      // S^T(i) = K Q(i)^T into [0, 128).
+      auto issue_S = [&](int st) {
+        const uint64_t dQk = desc_add(dQ_k0, st * Cfg::TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
+          mma_ss(tS, desc_add(dK_k, o), desc_add(dQk, o), idS, kk > 0);
+        }
+      };
+      // dP^T(i) = V dO(i)^T for queries [64hh, 64hh + 64) into [128 + 64hh, 192 + 64hh).
+      auto issue_dP = [&](int ds, int hh) {
+        const uint64_t ddOk = desc_add(ddO_k0, ds * Cfg::TILE + hh * 64 * 128);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
+          mma_ss(tdP + 64 * hh, desc_add(dV_k, o), desc_add(ddOk, o), idS64, kk > 0);
+        }
+        mma_commit(smem_u32(&ctl->dp_full[hh]));
+      };
+      // Per item: wait for its K / V, issue S and dP^T of its first step (the first dP^T
+      // half waits until the dQ warpgroup has moved the last step's dQ^T half out of
+      // those columns), then the steps.  Step g: dV(g) as soon as P^T(g) is in TMEM, then
+      // S(g+1) (its columns are free: the tensor pipe runs MMAs in issue order, so dV(g)
+      // has read P^T first), then dK(g) and dQ^T(g) from the dS tile in shared memory,
+      // then each half of dP(g+1) once that half of dQ^T(g) has left TMEM.  The compute
+      // warpgroups find S(g+1) ready when they finish step g.  After the item's last step:
+      // final_done (its dK / dV are complete in TMEM) and kv_empty (K / V are free).  The
+      // next item's first dV / dK overwrite the accumulators only after its p_ready /
+      // ds_ready, which the compute warpgroups give after they have read dK / dV out.
+      bool ok = true;
+      int gi = 0, kc = 0;
+      for (int L = blockIdx.x; L < p.n_items && ok; L += gridDim.x) {
+        const int n_iter = bwd_item(p, L).n_iter;
+        if (n_iter == 0) continue;
+        ok = mbar_wait(smem_u32(&ctl->kv_full), kc & 1, abort_flag, p.err, FA_SITE_BWD_MMA);
+        ok = ok && mbar_wait(smem_u32(&ctl->st_full[gi & 1]), (gi >> 1) & 1, abort_flag, p.err,
+                             FA_SITE_BWD_MMA);
+        if (!ok) break;
+        tc_fence_after();
+        issue_S(gi & 1);
+        mma_commit(smem_u32(&ctl->s_full));
+        ok = mbar_wait(smem_u32(&ctl->do_full[gi % Cfg::DO_ST]), (gi / Cfg::DO_ST) & 1, abort_flag,
+                       p.err, FA_SITE_BWD_MMA);
+#pragma unroll
+        for (int hh = 0; hh < 2 && ok; ++hh) {
+          if (ATOMIC_DQ && gi > 0) {
+            ok = mbar_wait(smem_u32(&ctl->dq_free[hh]), (gi - 1) & 1, abort_flag, p.err,
+                           FA_SITE_BWD_MMA);
+            if (!ok) break;
+          }
+          tc_fence_after();
+          issue_dP(gi % Cfg::DO_ST, hh);
+        }
+        for (int i = 0; i < n_iter && ok; ++i) {
+          const int g = gi + i;
+          const int s = g & 1;
+          const uint32_t par = g & 1;
+          const bool has_next = i + 1 < n_iter;
+          const int ds = g % Cfg::DO_ST, ds1 = (g + 1) % Cfg::DO_ST;
+          const uint64_t dQm = desc_add(dQ_m0, s * Cfg::TILE), ddOm = desc_add(ddO_m0, ds * Cfg::TILE);
+          // dV += P^T dO   (P^T for q 0..63 in columns 0..31, q 64..127 in 64..95)
+          ok = mbar_wait(smem_u32(&ctl->p_ready), par, abort_flag, p.err, FA_SITE_BWD_MMA);
+          if (!ok) break;
+          FA_TRACE_EVENT(3, g);
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t acol = (kk < 4) ? kk * 8 : 64 + (kk - 4) * 8;
+            mma_ts(tdV, tS + acol, desc_add(ddOm, kk * 2048), idKV, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(smem_u32(&ctl->do_empty[ds]));  // dO(g) read by dP(g) and dV(g)
+          if (has_next) {
+            ok = mbar_wait(smem_u32(&ctl->st_full[s ^ 1]), ((g + 1) >> 1) & 1, abort_flag, p.err,
+                           FA_SITE_BWD_MMA);
+            if (!ok) break;
+            tc_fence_after();
+            issue_S(s ^ 1);
+            mma_commit(smem_u32(&ctl->s_full));
+          }
+          // dK += dS^T Q   (A = dS^T, K-major in shared memory; B = Q MN-major)
+          ok = mbar_wait(smem_u32(&ctl->ds_ready), par, abort_flag, p.err, FA_SITE_BWD_MMA);
+          if (!ok) break;
+          FA_TRACE_EVENT(4, g);
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
+            mma_ss(tdK, desc_add(dDS_k, o), desc_add(dQm, kk * 2048), idKV, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          if (ATOMIC_DQ) {
+            // dQ^T = K^T dS^T, one 64-query half at a time, into the dP^T columns.
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk)
+                mma_ss(tdP + 64 * hh, desc_add(dK_m, kk * 2048),
+                       desc_add(dDS_m, hh * Cfg::CHUNK + kk * 2048), idQT, kk > 0);
+              mma_commit(smem_u32(&ctl->dq_full[hh]));
+            }
+          }
+          mma_commit(smem_u32(&ctl->st_empty[s]));
+          FA_TRACE_EVENT(5, g);
+          if (has_next) {
+            ok = mbar_wait(smem_u32(&ctl->do_full[ds1]), ((g + 1) / Cfg::DO_ST) & 1, abort_flag,
+                           p.err, FA_SITE_BWD_MMA);
+#pragma unroll
+            for (int hh = 0; hh < 2 && ok; ++hh) {
+              if (ATOMIC_DQ) {
+                ok = mbar_wait(smem_u32(&ctl->dq_free[hh]), par, abort_flag, p.err, FA_SITE_BWD_MMA);
+                if (!ok) break;
+              }
+              tc_fence_after();
+              issue_dP(ds1, hh);
+            }
+          }
+        }
+        if (!ok) break;
+        gi += n_iter;
+        ++kc;
+        mma_commit(smem_u32(&ctl->final_done));
+        mma_commit(smem_u32(&ctl->kv_empty));
+      }
+      mma_commit(smem_u32(&ctl->drain));
+      drain_wait(smem_u32(&ctl->drain), 0);
+    }
+  }
+  } else if (warp < 12) {
+    // ============================================================ compute warpgroups
+    setmaxnreg_inc<kBwdPRegHigh>();
+    const int c = (warp - 4) >> 2;              // query-column half
+    const int j = ((warp & 3) << 5) | lane;     // key row = TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_off, tdP = tmem + lane_off + 128;
+    const float c2 = p.scale_log2;
+    bool ok = true;
+    int gi = 0, kc = 0;
+    for (int L = blockIdx.x; L < p.n_items && ok; L += gridDim.x) {
+    const BwdItem it = bwd_item(p, L);
+    const int key = it.k0 + j;
+    const bool key_ok = key < p.Skv;
+    for (int i = 0; i < it.n_iter; ++i) {
+      const int g = gi + i;
+      const int s = g & 1;
+      const uint32_t par = g & 1;
+      const int qt = it.t_start + i % it.nqt;
+      const int q0 = qt * kBwdBM;
+      const uint32_t lse_a = base + Cfg::OFF_LSE + s * 512 + 64 * c * 4;
+      const uint32_t di_a = base + Cfg::OFF_DI + s * 512 + 64 * c * 4;
+      bool w = mbar_wait(smem_u32(&ctl->st_full[s]), (g >> 1) & 1, abort_flag, p.err,
+                         FA_SITE_BWD_COMPUTE);
+      w = w && mbar_wait(smem_u32(&ctl->s_full), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+      ok = __all_sync(0xffffffffu, w);
+      if (!ok) break;
+      if (threadIdx.x == 128) FA_TRACE_EVENT(6, g);
+      tc_fence_after();
+      // ---- pass A: P^T = exp2(S^T * scale*log2e - lse*log2e), masked; 32 columns at a time
+      const int qbase = q0 + 64 * c;
+      const bool full = key_ok && (!p.causal || key <= qbase + off);
+      float pv[64];
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+        uint32_t sv[32];
+        tmem_ld32(tS + 64 * c + 32 * ch, sv);
+        float lv[32];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) ld_shared_v4f(lse_a + (32 * ch + 4 * m) * 4, lv + 4 * m);
+        tmem_wait_ld();
+        if (full) {
+#pragma unroll
+          for (int x = 0; x < 32; ++x)
+            pv[32 * ch + x] = ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lv[x]));
+        } else {
+#pragma unroll
+          for (int x = 0; x < 32; ++x) {
+            const bool vis = key_ok && key <= qbase + 32 * ch + x + off;
+            pv[32 * ch + x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lv[x])) : 0.f;
+          }
+        }
+      }
+      if (threadIdx.x == 128) FA_TRACE_EVENT(14, g);
+      {
+        uint32_t pk[32];
+#pragma unroll
+        for (int x = 0; x < 32; ++x) pk[x] = Pack2<T>::pack(pv[2 * x], pv[2 * x + 1]);
+        tmem_st32(tS + 64 * c, pk);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&ctl->p_ready));
+      if (threadIdx.x == 128) FA_TRACE_EVENT(7, g);
+      // ---- pass B: dS^T = P^T (dP^T - D) * scale, to shared memory (K-major A of dK,
+      // MN-major B of dQ^T).  dP^T(i) was committed after dK(i-1) and dQ^T(i-1), so once
+      // dp_full(i) has fired those MMAs have finished reading the previous dS tile.
+      w = mbar_wait(smem_u32(&ctl->dp_full[c]), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+      ok = __all_sync(0xffffffffu, w);
+      if (!ok) break;
+      if (threadIdx.x == 128) FA_TRACE_EVENT(8, g);
+      tc_fence_after();
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t dv[32];
+        tmem_ld32(tdP + 64 * c + 32 * hf, dv);
+        float di[32];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) ld_shared_v4f(di_a + (32 * hf + 4 * m) * 4, di + 4 * m);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int x = 0; x < 16; ++x) {
+          const int xx = 32 * hf + 2 * x;
+          const float d0 = pv[xx] * (__uint_as_float(dv[2 * x]) - di[2 * x]) * p.scale;
+          const float d1 = pv[xx + 1] * (__uint_as_float(dv[2 * x + 1]) - di[2 * x + 1]) * p.scale;
+          pk[x] = Pack2<T>::pack(d0, d1);
+        }
+        // dS^T row j, query columns 64c + 32hf .. +31 (128-byte swizzled rows)
+        const uint32_t row = sDS + c * Cfg::CHUNK + j * 128;
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+          st_shared_v4(row + ((((hf << 2) + m) ^ (j & 7)) << 4), pk[4 * m], pk[4 * m + 1],
+                       pk[4 * m + 2], pk[4 * m + 3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&ctl->ds_ready));
+      if (threadIdx.x == 128) FA_TRACE_EVENT(9, g);
+    }
+    if (!ok) break;
+    // ---- dK, dV rows (lane = key row); an item with no step writes zeros
+    const int n_iter = it.n_iter;
+    if (n_iter > 0) {
+      bool w = mbar_wait(smem_u32(&ctl->final_done), kc & 1, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+      ok = __all_sync(0xffffffffu, w);
+      if (!ok) break;
+      tc_fence_after();
+    }
+    {
+      const BwdItem ie = bwd_item(p, L);  // recomputed: b, hk need no register in the steps
+      T* dkr = reinterpret_cast<T*>(p.dk) + (int64_t)ie.b * p.dk_sb + (int64_t)key * p.dk_ss +
+               (int64_t)ie.hk * p.dk_sh + c * (D / 2);
+      T* dvr = reinterpret_cast<T*>(p.dv) + (int64_t)ie.b * p.dv_sb + (int64_t)key * p.dv_ss +
+               (int64_t)ie.hk * p.dv_sh + c * (D / 2);
+#pragma unroll
+      for (int w2 = 0; w2 < 2; ++w2) {
+        const uint32_t src = tmem + lane_off + 256 + (w2 ? D : 0) + c * (D / 2);
+        T* dst = w2 ? dkr : dvr;
+#pragma unroll
+        for (int c0 = 0; c0 < D / 2; c0 += 32) {
+          uint32_t v[32];
+          if (n_iter > 0) {
+            tmem_ld32(src + c0, v);
+            tmem_wait_ld();
+          }
+          uint32_t pk[16];
+#pragma unroll
+          for (int x = 0; x < 16; ++x)
+            pk[x] = n_iter > 0 ? Pack2<T>::pack(__uint_as_float(v[2 * x]), __uint_as_float(v[2 * x + 1]))
+                               : 0u;
+          if (key_ok) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
+            d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            d4[2] = make_uint4(pk[8], pk[9], pk[10], pk[11]);
+            d4[3] = make_uint4(pk[12], pk[13], pk[14], pk[15]);
+          }
+        }
+      }
+    }
+    if (n_iter > 0) {
+      tc_fence_before();  // dK / dV reads ordered before this item's next p_ready
+      gi += n_iter;
+      ++kc;
+    }
+    }
+  } else {
+    setmaxnreg_dec<kBwdPRegDq>();
+    if (ATOMIC_DQ) {
+    // ============================================================ dQ warpgroup
+    // Thread = head-dim column d (TMEM lane of dQ^T).  Each 64-query half is moved out
+    // of TMEM (its columns are released for the next dP^T half at once) and added to the
+    // fp32 accumulator.  D = 128: the half is written to the staging tile [64 q][D] fp32
+    // in shared memory (a warp stores 32 consecutive d of a row: 128 contiguous bytes)
+    // and added by one bulk reduce-add (the 64 accumulator rows of a half are
+    // contiguous), so the adds run in the TMA unit and L2 instead of as per-thread
+    // atomics (cfg3 backward 3.71 -> 3.39 ms).  Thread 384 issues the reduce and waits
+    // for its read of the staging tile before the tile is written again; named barrier 1
+    // (these 128 threads) orders both, and its AND ends the loop for all four warps
+    // together when a wait fails in any of them, so none is left at the barrier.
+    // D = 64: per-thread atomics, one warp instruction per 128-byte row.
+    const int dl = ((warp & 3) << 5) | lane;
+    const bool d_ok = dl < D;
+    const bool issuer = threadIdx.x == 384;
+    const uint32_t tq = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + 128;
+    const uint32_t stg = base + Cfg::OFF_STG;
+    bool ok = true;
+    int gi = 0;
+    for (int L = blockIdx.x; L < p.n_items && ok; L += gridDim.x) {
+    const BwdItem it = bwd_item(p, L);
+    for (int i = 0; i < it.n_iter && ok; ++i) {
+      const int gs = gi + i;
+      const int g = i / it.nqt, qt = it.t_start + i % it.nqt, h = it.hk * p.G + g;
+      float* acc = p.dq_acc + (((int64_t)it.b * p.H + h) * p.Sq_pad + qt * kBwdBM) * D;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        bool w = mbar_wait(smem_u32(&ctl->dq_full[hh]), gs & 1, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+        w = __all_sync(0xffffffffu, w);
+        uint32_t v[64];
+        if (w) {
+          if (issuer) FA_TRACE_EVENT(10 + hh, gs);
+          tc_fence_after();
+          tmem_ld32(tq + 64 * hh, v);
+          tmem_ld32(tq + 64 * hh + 32, v + 32);
+          tmem_wait_ld();
+          tc_fence_before();
+          mbar_arrive(smem_u32(&ctl->dq_free[hh]));
+        }
+        if constexpr (Cfg::BULK_DQ) {
+          if (issuer) bulk_wait_group_read();  // the last reduce has read the staging tile
+          ok = bar_red_and(1, 128, w);
+          if (!ok) break;
+#pragma unroll
+          for (int x = 0; x < 64; ++x)
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(stg + (x * D + dl) * 4), "r"(v[x]) : "memory");
+          fence_async_shared();
+          bar_sync_n(1, 128);
+          if (issuer) {
+            bulk_reduce_add_f32(acc + (int64_t)(64 * hh) * D, stg, 64 * D * 4);
+            bulk_commit_group();
+          }
+        } else {
+          ok = w;
+          if (!ok) break;
+          if (d_ok) {
+            float* a = acc + (int64_t)(64 * hh) * D + dl;
+#pragma unroll
+            for (int x = 0; x < 64; ++x) atomicAdd(a + (int64_t)x * D, __uint_as_float(v[x]));
+          }
+        }
+      }
+    }
+    gi += it.n_iter;
+    }
+    if (issuer) bulk_wait_group_all();  // the adds complete before the CTA's memory goes
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
 // ---------------------------------------------------------------- 3. deterministic dQ
 template <int D>
 struct DqCfg {
@@ -948,6 +1489,23 @@ static int set_smem(K kern, int bytes) {
 }
 
 constexpr int kBwdRegTotal = 128 * kBwdRegLow + 256 * kBwdRegHigh + 128 * kBwdRegDq;
+constexpr int kBwdPRegTotal = 128 * kBwdPRegLow + 256 * kBwdPRegHigh + 128 * kBwdPRegDq;
+
+// Atomic-mode dK / dV at D = 128 with one query head per kv head runs on the persistent
+// kernel (one CTA per SM looping over the work items) when an item averages at most
+// kBwdPersistMaxSteps query-tile steps: its fixed costs (K / V load, first MMAs, dK / dV
+// epilogue) then weigh more and the loop overlaps them.  Measured (bf16 causal backward,
+// B x S = 64 x 512: 1.38-1.43 -> 1.19 ms; 32 x 1024: 1.67 -> 1.46; 16 x 2048: 2.25 ->
+// 2.12; 128 x 256: 1.13 -> 0.99).  Longer items gain nothing (S = 4096: 3.39 -> 3.37), and
+// GQA (G query heads per item) and D = 64 lost 10-20 % to the static item assignment.
+constexpr int kBwdPersistMaxSteps = 8;
+template <int D>
+static bool bwd_persistent(const BwdParams& p) {
+  if (D != 128 || p.G != 1) return false;
+  const int nqt_all = (p.Sq + kBwdBM - 1) / kBwdBM;
+  const int avg_steps = p.causal ? (nqt_all + 1) / 2 : nqt_all;
+  return avg_steps <= kBwdPersistMaxSteps;
+}
 
 template <typename T, int D>
 static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const CUtensorMap& tk,
@@ -965,7 +1523,29 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
   }
-  if (!a->deterministic) {
+  if (!a->deterministic && bwd_persistent<D>(p)) {
+    auto kern = fa_bwd_dkdv_persist_kernel<T, 128, true>;
+    static bool attr[64] = {false};
+    int dev = 0;
+    FA_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 64 && !attr[dev]) {
+      if (int s = check_reg_split(kern, kBwdThreads, kBwdPRegTotal)) return s;
+      if (int s = set_smem(kern, BwdCfg<128>::SMEM_BYTES)) return s;
+      attr[dev] = true;
+    }
+    const unsigned grid = (unsigned)min(p.n_items, num_sms());
+    prof_begin(FA_PROF_BWD_DKDV, st);
+    kern<<<grid, kBwdThreads, BwdCfg<128>::SMEM_BYTES, st>>>(tq, tk, tv, tdo, p);
+    prof_end(FA_PROF_BWD_DKDV, st);
+    FA_CUDA_TRY(cudaGetLastError());
+    count_launch();
+    const int64_t n4 = (int64_t)a->batch * a->num_heads * a->seqlen_q * (D / 4);
+    fa_bwd_dq_convert_kernel<T, D><<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(
+        p.dq_acc, reinterpret_cast<T*>(a->dq), a->batch, a->seqlen_q, a->num_heads, p.Sq_pad,
+        a->dq_stride[0], a->dq_stride[1], a->dq_stride[2]);
+    FA_CUDA_TRY(cudaGetLastError());
+    count_launch();
+  } else if (!a->deterministic) {
     auto kern = fa_bwd_dkdv_kernel<T, D, true>;
     static bool attr[64] = {false};
     int dev = 0;
@@ -1061,6 +1641,9 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
   p.G = G;
   p.Sq_pad = pad128(a->seqlen_q);
   p.causal = a->causal;
+  p.n_t = (a->seqlen_k + kBwdBN - 1) / kBwdBN;
+  p.n_u = a->num_heads_k * a->batch;
+  p.n_items = p.n_t * p.n_u;
   p.scale = a->softmax_scale;
   p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
   const size_t rows = (size_t)a->batch * a->num_heads * p.Sq_pad;
