@@ -186,8 +186,10 @@ size_t fa_decode_noalloc_scratch_bytes(void);
 /* Diagnostics. */
 const char* fa_status_string(int status);
 /* Reads (and optionally clears) the library's device error word on the current
- * device: code (0 = none, 1 = bounded wait expired), site and block index.
- * Synchronises the device. */
+ * device: code, site and block index of the first error recorded.  Codes: 0 = none,
+ * 1 = a bounded wait expired, 3 = fa_kv_cache_write got a slot past the cache,
+ * 4 = a paged / decode call got seq_lens[b] > max_blocks * page_size (the keys were
+ * clamped to the pages the block-table row maps).  Synchronises the device. */
 int fa_read_device_error(int32_t* code, int32_t* site, int32_t* block, int32_t clear);
 /* Text of the last CUDA call that made an entry point return FA_ERR_CUDA on this
  * host thread (call, source line, CUDA error string); "" if none. */
@@ -199,7 +201,9 @@ int64_t fa_launch_count(void);
 /* Benchmark hook: record ev_begin / ev_end (cudaEvent_t, created by the caller) on the
  * launch stream immediately around the NEXT launch of one main kernel:
  * 1 = dense forward, 2 = dense backward dK/dV kernel, 3 = paged prefill,
- * 4 = decode split kernel.  One shot; process-wide; not thread-safe. */
+ * 4 = decode split kernel.  One shot and process-wide: the first matching launch
+ * from any host thread takes the request (a new request replaces an unused one);
+ * safe to call from several threads. */
 int fa_profile_next_launch(int32_t kind, void* ev_begin, void* ev_end);
 
 /* Self-test of the tcgen05 building blocks used by the attention kernels: one

@@ -5,7 +5,7 @@ import torch
 
 import tilelang_fa_v100 as fa
 from tilelang_fa_v100 import _ext
-from helpers import assert_close, golden, golden_names, max_abs
+from helpers import assert_close, assert_out_close, golden, golden_names, max_abs, unit_roundoff
 from oracle import attention_ref as R
 
 pytestmark = pytest.mark.gpu
@@ -33,9 +33,10 @@ def _check(cuda_dev, q, kc, vc, bt, sl, page, num_splits=0):
     out = _ext.decode(t(q), t(kc), t(vc), t(bt), t(sl), page, kc.shape[2],
                       _ext.default_scale(q.shape[-1]), num_splits=num_splits, lse=lse)
     torch.cuda.synchronize()
-    ref_out, ref_lse = R.decode_ref(q.float().numpy(), kc.float().numpy(), vc.float().numpy(),
-                                    bt, sl)
-    assert_close(out.float().cpu().numpy(), ref_out, what="out", dtype=q.dtype)
+    ref_out, ref_lse, bound = R.decode_ref(q.float().numpy(), kc.float().numpy(),
+                                           vc.float().numpy(), bt, sl,
+                                           unit_roundoff=unit_roundoff(q.dtype))
+    assert_out_close(out.float().cpu().numpy(), ref_out, q.dtype, bound, what="out")
     assert_close(lse.cpu().numpy(), ref_lse, what="lse")
 
 
@@ -61,7 +62,8 @@ DECODE_CASES = [
     ([129, 1000], 24, 4, 64, 64, torch.bfloat16, 5),      # 6 q heads per kv head, page 64
     ([0, 50], 8, 2, 128, 16, torch.float16, 1),           # an empty sequence, single split
     ([0, 50], 8, 2, 128, 16, torch.float16, 4),           # an empty sequence, split path
-    ([64, 129, 1000, 5000], 32, 2, 256, 16, torch.bfloat16, 0),  # D = 256, 16 q heads per kv head
+    ([64, 129, 1000, 5000], 48, 3, 256, 16, torch.bfloat16, 0),  # D = 256, 16 q heads per kv head
+    ([64, 129, 1000, 5000], 8, 1, 256, 16, torch.bfloat16, 0),   # D = 256 MQA 8:1 (reference synthetic row)
     ([300, 1, 0], 8, 1, 256, 16, torch.float16, 3),       # D = 256 MQA 8:1, explicit splits
     ([17, 4096], 16, 4, 256, 32, torch.bfloat16, 1),      # D = 256, 4 kv heads per CTA, direct
     ([2000], 8, 8, 256, 64, torch.float16, 0),            # D = 256 MHA, 8 kv heads in 2 CTAs
@@ -100,6 +102,30 @@ def test_benchmark_config_sampled(cuda_dev):
         idx = torch.from_numpy(bt[b, :pps[b]].astype(np.int64)).to(cuda_dev)
         kb = kc[idx].float().cpu().numpy()
         vb = vc[idx].float().cpu().numpy()
-        ro, _ = R.decode_ref(q[b:b + 1].float().cpu().numpy(), kb, vb,
-                             np.arange(pps[b], dtype=np.int32)[None], lens[b:b + 1])
-        assert_close(out[b:b + 1].float().cpu().numpy(), ro, what="seq %d" % b, dtype=torch.bfloat16)
+        ro, _, bnd = R.decode_ref(q[b:b + 1].float().cpu().numpy(), kb, vb,
+                                  np.arange(pps[b], dtype=np.int32)[None], lens[b:b + 1],
+                                  unit_roundoff=2.0 ** -8)
+        assert_out_close(out[b:b + 1].float().cpu().numpy(), ro, torch.bfloat16, bnd,
+                         what="seq %d" % b)
+
+
+@pytest.mark.parametrize("num_splits", [0, 1, 3])
+def test_seq_len_past_block_table_is_clamped_and_reported(cuda_dev, num_splits):
+    """seq_lens[b] larger than the keys its block-table row maps (max_blocks * page): the
+    kernels clamp it to the mapped keys (instead of counting zero-filled out-of-range
+    loads as keys) and record device error 4."""
+    q, kc, vc, bt, sl = _case(91, [40, 300], 8, 2, 128, 16, torch.bfloat16, extra_cols=0)
+    cap = bt.shape[1] * 16
+    claimed = sl.copy()
+    claimed[1] = cap + 100  # sequence 1 claims 100 keys more than its row maps
+    t = lambda x: torch.as_tensor(x).to(cuda_dev)
+    _ext.read_device_error(clear=True)
+    out = _ext.decode(t(q), t(kc), t(vc), t(bt), t(claimed), 16, kc.shape[2],
+                      _ext.default_scale(q.shape[-1]), num_splits=num_splits)
+    torch.cuda.synchronize()
+    code, _, _ = _ext.read_device_error(clear=True)
+    assert code == 4
+    clamped = np.minimum(claimed, cap).astype(np.int32)
+    ref_out, _, bound = R.decode_ref(q.float().numpy(), kc.float().numpy(), vc.float().numpy(),
+                                     bt, clamped, unit_roundoff=unit_roundoff(q.dtype))
+    assert_out_close(out.float().cpu().numpy(), ref_out, q.dtype, bound, what="out")

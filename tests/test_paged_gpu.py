@@ -5,7 +5,7 @@ import pytest
 import torch
 
 import tilelang_fa_v100 as fa
-from helpers import assert_close, golden, golden_names, max_abs
+from helpers import assert_close, assert_out_close, golden, golden_names, max_abs, unit_roundoff
 from oracle import attention_ref as R
 
 pytestmark = pytest.mark.gpu
@@ -76,9 +76,10 @@ def test_varlen_paged_vs_oracle(cuda_dev, case):
     q, kc, vc, bt, sl, qsl, pkl = _varlen_case(hash(str(case)) % 1000, q_lens, kv_lens, h, hkv,
                                                d, page, dt)
     out, lse = _run(cuda_dev, q, kc, vc, bt, sl, qsl, pkl, causal, page)
-    ref_out, ref_lse = R.paged_prefill_ref(q.float().numpy(), kc.float().numpy(),
-                                           vc.float().numpy(), bt, sl, qsl, pkl, causal=causal)
-    assert_close(out, ref_out, what="out", dtype=dt)
+    ref_out, ref_lse, bound = R.paged_prefill_ref(q.float().numpy(), kc.float().numpy(),
+                                                  vc.float().numpy(), bt, sl, qsl, pkl,
+                                                  causal=causal, unit_roundoff=unit_roundoff(dt))
+    assert_out_close(out, ref_out, dt, bound, what="out")
     assert_close(lse, ref_lse, what="lse")
 
 
@@ -125,3 +126,26 @@ def test_benchmark_config_sampled(cuda_dev):
                                      np.array([0, L], np.int32), pkl[b:b + 1], causal=True)
         assert_close(out[sel], ro, what="out seq %d" % b)
         assert_close(lse[:, sel], rl, what="lse seq %d" % b)
+
+
+def test_seq_len_past_block_table_is_clamped_and_reported(cuda_dev):
+    """Paged prefill with seq_lens[b] beyond max_blocks * page_size: keys are clamped to
+    the mapped pages and device error 4 is recorded (non-causal, so every mapped key is
+    visible to every query row)."""
+    from tilelang_fa_v100 import _ext
+    q, kc, vc, bt, sl, qsl, pkl = _varlen_case(93, [20, 33], [20, 200], 8, 2, 128, 16,
+                                               torch.float16)
+    bt = bt[:, :-1].copy()                      # drop the spare column: row 1 maps 208 keys
+    cap = bt.shape[1] * 16
+    claimed = sl.copy()
+    claimed[1] = cap + 64
+    _ext.read_device_error(clear=True)
+    out, lse = _run(cuda_dev, q, kc, vc, bt, claimed, qsl, np.zeros_like(pkl), False, 16)
+    code, _, _ = _ext.read_device_error(clear=True)
+    assert code == 4
+    clamped = np.minimum(claimed, cap).astype(np.int32)
+    ref_out, ref_lse = R.paged_prefill_ref(q.float().numpy(), kc.float().numpy(),
+                                           vc.float().numpy(), bt, clamped, qsl,
+                                           np.zeros_like(pkl), causal=False)
+    assert_close(out, ref_out, what="out")
+    assert_close(lse, ref_lse, what="lse")

@@ -1525,13 +1525,13 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
   }
   if (!a->deterministic && bwd_persistent<D>(p)) {
     auto kern = fa_bwd_dkdv_persist_kernel<T, 128, true>;
-    static bool attr[64] = {false};
-    int dev = 0;
-    FA_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 64 && !attr[dev]) {
+    static std::atomic<bool> attr[kMaxContexts];
+    const int slot = call_context_slot();
+    if (slot < 0 || slot >= kMaxContexts) return FA_ERR_CUDA;
+    if (!attr[slot].load(std::memory_order_acquire)) {
       if (int s = check_reg_split(kern, kBwdThreads, kBwdPRegTotal)) return s;
       if (int s = set_smem(kern, BwdCfg<128>::SMEM_BYTES)) return s;
-      attr[dev] = true;
+      attr[slot].store(true, std::memory_order_release);
     }
     const unsigned grid = (unsigned)min(p.n_items, num_sms());
     prof_begin(FA_PROF_BWD_DKDV, st);
@@ -1547,13 +1547,13 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
     count_launch();
   } else if (!a->deterministic) {
     auto kern = fa_bwd_dkdv_kernel<T, D, true>;
-    static bool attr[64] = {false};
-    int dev = 0;
-    FA_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 64 && !attr[dev]) {
+    static std::atomic<bool> attr[kMaxContexts];
+    const int slot = call_context_slot();
+    if (slot < 0 || slot >= kMaxContexts) return FA_ERR_CUDA;
+    if (!attr[slot].load(std::memory_order_acquire)) {
       if (int s = check_reg_split(kern, kBwdThreads, kBwdRegTotal)) return s;
       if (int s = set_smem(kern, BwdCfg<D>::SMEM_BYTES)) return s;
-      attr[dev] = true;
+      attr[slot].store(true, std::memory_order_release);
     }
     dim3 grid((a->seqlen_k + kBwdBN - 1) / kBwdBN, a->num_heads_k, a->batch);
     prof_begin(FA_PROF_BWD_DKDV, st);
@@ -1570,14 +1570,14 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
   } else {
     auto kern = fa_bwd_dkdv_kernel<T, D, false>;
     auto kq = fa_bwd_dq_kernel<T, D>;
-    static bool attr[64] = {false};
-    int dev = 0;
-    FA_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 64 && !attr[dev]) {
+    static std::atomic<bool> attr[kMaxContexts];
+    const int slot = call_context_slot();
+    if (slot < 0 || slot >= kMaxContexts) return FA_ERR_CUDA;
+    if (!attr[slot].load(std::memory_order_acquire)) {
       if (int s = check_reg_split(kern, kBwdThreads, kBwdRegTotal)) return s;
       if (int s = set_smem(kern, BwdCfg<D>::SMEM_BYTES)) return s;
       if (int s = set_smem(kq, DqCfg<D>::SMEM_BYTES)) return s;
-      attr[dev] = true;
+      attr[slot].store(true, std::memory_order_release);
     }
     dim3 grid((a->seqlen_k + kBwdBN - 1) / kBwdBN, a->num_heads_k, a->batch);
     prof_begin(FA_PROF_BWD_DKDV, st);

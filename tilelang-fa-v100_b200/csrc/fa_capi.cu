@@ -15,9 +15,9 @@ __device__ int g_fa_device_error[4];
 
 
 static std::mutex g_mu;
-static int* g_err_ptr[64] = {nullptr};
-static int g_sm_count[64] = {0};
-static int g_cc_ok[64] = {0};  // 0 unknown, 1 ok, -1 not sm_100
+static int* g_err_ptr[kMaxContexts] = {nullptr};  // per context slot
+static int g_sm_count[64] = {0};                  // per device
+static int g_cc_ok[64] = {0};  // per device: 0 unknown, 1 ok, -1 not sm_100
 static std::atomic<int64_t> g_launches{0};
 
 void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
@@ -29,23 +29,38 @@ void set_error_detail(const char* what, const char* file, int line, const char* 
            line, err);
 }
 
-static int g_prof_kind = 0;
+// Benchmark hook state (fa_profile_next_launch).  The armed request is taken by the
+// first matching launch from any thread: prof_begin claims it under the mutex and
+// hands the end event to the same thread's prof_end, so two threads never record
+// the same request.
+static std::mutex g_prof_mu;
+static std::atomic<int> g_prof_kind{0};
 static cudaEvent_t g_prof_begin = nullptr, g_prof_end = nullptr;
+static thread_local cudaEvent_t t_prof_end = nullptr;
+static thread_local int t_prof_kind = 0;
 void prof_begin(int kind, cudaStream_t st) {
-  if (g_prof_kind == kind && g_prof_begin != nullptr) {
-    if (cudaEventRecord(g_prof_begin, st) != cudaSuccess) {
-      (void)cudaGetLastError();  // a stale or foreign event: drop the request
-      g_prof_kind = 0;
-      g_prof_begin = g_prof_end = nullptr;
-    }
-  }
-}
-void prof_end(int kind, cudaStream_t st) {
-  if (g_prof_kind == kind && g_prof_end != nullptr) {
-    if (cudaEventRecord(g_prof_end, st) != cudaSuccess) (void)cudaGetLastError();
-    g_prof_kind = 0;
+  if (g_prof_kind.load(std::memory_order_relaxed) != kind) return;
+  cudaEvent_t b = nullptr, e = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (g_prof_kind.load(std::memory_order_relaxed) != kind) return;
+    b = g_prof_begin;
+    e = g_prof_end;
+    g_prof_kind.store(0, std::memory_order_relaxed);
     g_prof_begin = g_prof_end = nullptr;
   }
+  if (cudaEventRecord(b, st) != cudaSuccess) {
+    (void)cudaGetLastError();  // a stale or foreign event: drop the request
+    return;
+  }
+  t_prof_end = e;
+  t_prof_kind = kind;
+}
+void prof_end(int kind, cudaStream_t st) {
+  if (t_prof_kind != kind || t_prof_end == nullptr) return;
+  if (cudaEventRecord(t_prof_end, st) != cudaSuccess) (void)cudaGetLastError();
+  t_prof_end = nullptr;
+  t_prof_kind = 0;
 }
 
 static int current_device(int* dev) {
@@ -62,6 +77,7 @@ static int current_device(int* dev) {
 static PFN_cuStreamGetCtx_v9020 p_stream_get_ctx = nullptr;
 static PFN_cuCtxGetCurrent_v4000 p_ctx_get_current = nullptr;
 static PFN_cuCtxSetCurrent_v4000 p_ctx_set_current = nullptr;
+static PFN_cuCtxGetId_v12000 p_ctx_get_id = nullptr;
 
 static void* driver_fn(const char* name, unsigned int version) {
   void* p = nullptr;
@@ -83,6 +99,7 @@ static int bind_context(cudaStream_t st) {
     p_stream_get_ctx = reinterpret_cast<PFN_cuStreamGetCtx_v9020>(driver_fn("cuStreamGetCtx", 9020));
     p_ctx_get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(driver_fn("cuCtxGetCurrent", 4000));
     p_ctx_set_current = reinterpret_cast<PFN_cuCtxSetCurrent_v4000>(driver_fn("cuCtxSetCurrent", 4000));
+    p_ctx_get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(driver_fn("cuCtxGetId", 12000));
   });
   const uintptr_t sv = reinterpret_cast<uintptr_t>(st);
   if (sv > 2 && p_stream_get_ctx && p_ctx_get_current && p_ctx_set_current) {
@@ -102,13 +119,63 @@ static int bind_context(cudaStream_t st) {
   return FA_OK;
 }
 
-// Per-device set-up: binds the caller's context, checks the compute capability,
-// caches the SM count and the device address of the error word (taken once per
-// device, with that device current).
+// Context slots.  A module global (the error word, the persistent scheduler's
+// counters, the no-allocation decode scratch) has its own device address in every CUDA
+// context, and kernel attributes are set per context, so whatever the library caches
+// is keyed by the context a call runs in: by its id (cuCtxGetId), which is unique for
+// the context's lifetime, whereas a destroyed context's handle may be reused.  Slots
+// are never recycled; a process that creates more than kMaxContexts contexts gets
+// FA_ERR_CUDA from the calls made in the extra ones.
+static unsigned long long g_ctx_id[kMaxContexts] = {0};
+static int g_ctx_count = 0;
+static thread_local unsigned long long t_last_ctx_id = 0;
+static thread_local int t_last_slot = -1;
+static thread_local int t_call_slot = -1;
+
+static int find_context_slot(int* slot) {
+  CUcontext cur = nullptr;
+  unsigned long long id = 0;
+  if (p_ctx_get_current == nullptr || p_ctx_get_id == nullptr ||
+      p_ctx_get_current(&cur) != CUDA_SUCCESS || cur == nullptr ||
+      p_ctx_get_id(cur, &id) != CUDA_SUCCESS) {
+    set_error_detail("cuCtxGetCurrent / cuCtxGetId", __FILE__, __LINE__, "no current context");
+    return FA_ERR_CUDA;
+  }
+  if (id == t_last_ctx_id && t_last_slot >= 0) {
+    *slot = t_last_slot;
+    return FA_OK;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  int found = -1;
+  for (int i = 0; i < g_ctx_count; ++i)
+    if (g_ctx_id[i] == id) found = i;
+  if (found < 0) {
+    if (g_ctx_count == kMaxContexts) {
+      set_error_detail("context slot", __FILE__, __LINE__, "more CUDA contexts than kMaxContexts");
+      return FA_ERR_CUDA;
+    }
+    found = g_ctx_count++;
+    g_ctx_id[found] = id;
+  }
+  t_last_ctx_id = id;
+  t_last_slot = found;
+  *slot = found;
+  return FA_OK;
+}
+
+int call_context_slot() { return t_call_slot; }
+
+// Per-call set-up: binds the caller's context and records its slot for the launchers
+// (call_context_slot), checks the compute capability, caches the SM count (per
+// device) and the device address of the error word (per context, looked up with that
+// context current).
 static int device_setup(int** err_out, cudaStream_t st = nullptr) {
   if (int s = bind_context(st)) return s;
   int dev;
   if (int s = current_device(&dev)) return s;
+  int slot = -1;
+  if (int s = find_context_slot(&slot)) return s;
+  t_call_slot = slot;
   std::lock_guard<std::mutex> lk(g_mu);
   if (g_cc_ok[dev] == 0) {
     int major = 0;
@@ -120,12 +187,12 @@ static int device_setup(int** err_out, cudaStream_t st = nullptr) {
     g_sm_count[dev] = sms;
   }
   if (g_cc_ok[dev] < 0) return FA_ERR_NOT_SM100;
-  if (g_err_ptr[dev] == nullptr) {
+  if (g_err_ptr[slot] == nullptr) {
     void* ptr = nullptr;
     if (cudaGetSymbolAddress(&ptr, g_fa_device_error) != cudaSuccess) return FA_ERR_CUDA;
-    g_err_ptr[dev] = static_cast<int*>(ptr);
+    g_err_ptr[slot] = static_cast<int*>(ptr);
   }
-  *err_out = g_err_ptr[dev];
+  *err_out = g_err_ptr[slot];
   return FA_OK;
 }
 
@@ -318,9 +385,10 @@ int fa_selftest_umma_rate(int32_t n, int32_t k, int32_t reps, int32_t a_tmem, in
 
 int fa_profile_next_launch(int32_t kind, void* ev_begin, void* ev_end) {
   if (kind < 1 || kind > 4 || ev_begin == nullptr || ev_end == nullptr) return FA_ERR_INVALID_ARG;
-  g_prof_kind = kind;
+  std::lock_guard<std::mutex> lk(g_prof_mu);
   g_prof_begin = static_cast<cudaEvent_t>(ev_begin);
   g_prof_end = static_cast<cudaEvent_t>(ev_end);
+  g_prof_kind.store(kind, std::memory_order_relaxed);
   return FA_OK;
 }
 

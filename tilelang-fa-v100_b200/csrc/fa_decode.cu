@@ -115,7 +115,8 @@ __global__ void __launch_bounds__(DecCfg<D>::NTHREADS, 1)
   const int b = blockIdx.z;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int L = p.seq_lens[b];
+  const int L = clamp_seq_len(p.seq_lens[b], p.max_blocks, p.page_size, p.err,
+                              FA_SITE_DEC_SEQLEN, threadIdx.x == 0);
   const int c_begin = split * p.chunks_per_split;
   const int c_end = min((L + kDecChunk - 1) / kDecChunk, c_begin + p.chunks_per_split);
   const int nchunks = c_end - c_begin;
@@ -336,7 +337,8 @@ __global__ void __launch_bounds__(DecCfg<D>::NTHREADS, 1)
 template <typename T, int D>
 __global__ void __launch_bounds__(256) fa_decode_combine_kernel(const DecParams p) {
   const int b = blockIdx.y;
-  const int L = p.seq_lens[b];
+  const int L = clamp_seq_len(p.seq_lens[b], p.max_blocks, p.page_size, p.err,
+                              FA_SITE_DEC_SEQLEN, false);
   const int used =
       min(p.num_splits, (((L + kDecChunk - 1) / kDecChunk) + p.chunks_per_split - 1) /
                             p.chunks_per_split);
@@ -407,14 +409,8 @@ static int launch_decode_impl(const CUtensorMap& tk, const CUtensorMap& tv, cons
                               cudaStream_t st) {
   using Cfg = DecCfg<D>;
   auto kern = fa_decode_split_kernel<T, D>;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  FA_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 64 && !attr_set[dev]) {
-    FA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Cfg::SMEM_BYTES));
-    attr_set[dev] = true;
-  }
+  static std::atomic<bool> attr_set[kMaxContexts];
+  if (int s = smem_attr_once(kern, Cfg::SMEM_BYTES, attr_set)) return s;
   dim3 grid(p.num_splits, p.Hkv / p.HG, p.B);
   // Shared memory for the actual group: small groups (few kv heads) fit several CTAs
   // per SM, which keeps enough K/V bytes in flight.
@@ -503,25 +499,25 @@ constexpr size_t kDecodeStaticScratchBytes = size_t(16) << 20;  // 16 MiB
 static __device__ __align__(256) unsigned char g_decode_scratch[kDecodeStaticScratchBytes];
 
 static std::mutex g_scratch_mu;
-static void* g_scratch_addr[64] = {nullptr};
+static void* g_scratch_addr[kMaxContexts] = {nullptr};  // per context slot
 
 size_t decode_noalloc_scratch_bytes() { return kDecodeStaticScratchBytes; }
 
 int launch_decode_noalloc(const fa_decode_args_t* a, int* err, cudaStream_t st) {
-  int dev = 0;
-  FA_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) return FA_ERR_CUDA;
+  const int slot = call_context_slot();
+  if (slot < 0 || slot >= kMaxContexts) return FA_ERR_CUDA;
   void* scratch = nullptr;
   {
-    // First call on a device: look up the array's device address with that device
-    // current (the caller's context was bound by the entry point).
+    // First call in a context (each GPU's primary context, or any other context the
+    // caller's stream belongs to): look up the array's device address with that
+    // context current -- the entry point bound it.
     std::lock_guard<std::mutex> lk(g_scratch_mu);
-    if (g_scratch_addr[dev] == nullptr) {
+    if (g_scratch_addr[slot] == nullptr) {
       void* ptr = nullptr;
       FA_CUDA_TRY(cudaGetSymbolAddress(&ptr, g_decode_scratch));
-      g_scratch_addr[dev] = ptr;
+      g_scratch_addr[slot] = ptr;
     }
-    scratch = g_scratch_addr[dev];
+    scratch = g_scratch_addr[slot];
   }
   fa_decode_args_t b = *a;
   if (b.num_splits == 0) {

@@ -150,7 +150,8 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
       }
       if (valid) {
         q_len = p.qsl[b + 1] - p.qsl[b];
-        kv_len = p.seq_lens[b];
+        kv_len = clamp_seq_len(p.seq_lens[b], p.max_blocks, p.page_size, p.err,
+                               FA_SITE_PAGED_SEQLEN, true);
         off = p.pkl[b];
         tok_base = p.qsl[b];
       } else {
@@ -697,7 +698,8 @@ __device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it, int lane
     it.b = s;
     tile = x - cum;
     it.q_len = p.qsl[s + 1] - p.qsl[s];
-    it.kv_len = p.seq_lens[s];
+    it.kv_len = clamp_seq_len(p.seq_lens[s], p.max_blocks, p.page_size, p.err,
+                              FA_SITE_PAGED_SEQLEN, lane == 0);
     it.off = p.pkl[s];
     it.tok_base = p.qsl[s];
   } else {
@@ -1302,14 +1304,15 @@ __device__ int g_fwd_sched[kFwdSchedSlots];
 
 static int* fwd_sched_counter(cudaStream_t st) {
   static std::atomic<unsigned> next{0};
-  static int* base_of[64] = {nullptr};  // per device
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
-  int* base = dev < 64 ? base_of[dev] : nullptr;
+  static std::atomic<int*> base_of[kMaxContexts];  // the counters' address per context
+  const int slot = call_context_slot();
+  if (slot < 0 || slot >= kMaxContexts) return nullptr;
+  int* base = base_of[slot].load(std::memory_order_acquire);
   if (base == nullptr) {
+    // Every thread that gets here stores the same address.
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&base), g_fwd_sched) != cudaSuccess)
       return nullptr;
-    if (dev < 64) base_of[dev] = base;
+    base_of[slot].store(base, std::memory_order_release);
   }
   int* c = base + (next.fetch_add(1) % kFwdSchedSlots);
   if (cudaMemsetAsync(c, 0, sizeof(int), st) != cudaSuccess) return nullptr;
@@ -1338,24 +1341,13 @@ static bool fwd_persistent(bool causal, int kv_len) {
   return avg_tiles <= kFwdPersistMaxTiles;
 }
 
-template <typename K>
-static int fwd_smem_attr(K kern, int bytes, bool* done) {
-  int dev = 0;
-  FA_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 64 && !done[dev]) {
-    FA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-    done[dev] = true;
-  }
-  return FA_OK;
-}
-
 template <typename T, int D, int NQ, bool PAGED>
 static int launch_fwd_persist(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                               const CUtensorMap& to, const FwdParams& p, int kind, cudaStream_t st) {
   using Cfg = FwdPersistCfg<D, NQ>;
   auto kern = fa_fwd_persist_kernel<T, D, NQ, PAGED>;
-  static bool attr_set[64] = {false};
-  if (int s = fwd_smem_attr(kern, Cfg::SMEM_BYTES, attr_set)) return s;
+  static std::atomic<bool> attr_set[kMaxContexts];
+  if (int s = smem_attr_once(kern, Cfg::SMEM_BYTES, attr_set)) return s;
   FwdParams q = p;
   q.sched = fwd_sched_counter(st);
   if (q.sched == nullptr) return FA_ERR_CUDA;
@@ -1371,8 +1363,8 @@ static int launch_fwd_direct(const CUtensorMap& tq, const CUtensorMap& tk, const
                              const CUtensorMap& to, const FwdParams& p, int kind, cudaStream_t st) {
   using Cfg = FwdCfg<D, NQ>;
   auto kern = fa_fwd_kernel<T, D, NQ, PAGED>;
-  static bool attr_set[64] = {false};
-  if (int s = fwd_smem_attr(kern, Cfg::SMEM_BYTES, attr_set)) return s;
+  static std::atomic<bool> attr_set[kMaxContexts];
+  if (int s = smem_attr_once(kern, Cfg::SMEM_BYTES, attr_set)) return s;
   // one CTA per work item: q blocks x kv heads x batch
   const dim3 grid(p.nbx, p.Hk, p.n_items / (p.nbx * p.Hk));
   prof_begin(kind, st);

@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cstdint>
 #include "../../include/fa_b200.h"
 
@@ -43,6 +44,13 @@ inline CUtensorMapDataType tmap_dtype(int dtype) {
 
 int num_sms();
 void count_launch(int n = 1);
+
+// Whatever the library caches (module-global addresses, kernel attributes) is kept per
+// CUDA context: a module global has its own address in every context.  The entry
+// point binds the caller's context and records its slot (0 .. kMaxContexts - 1) for
+// the launchers of the same call.
+constexpr int kMaxContexts = 64;
+int call_context_slot();
 enum { FA_PROF_FWD = 1, FA_PROF_BWD_DKDV = 2, FA_PROF_PAGED = 3, FA_PROF_DECODE = 4 };
 // Records the armed begin/end events around a launch of the given kind (see
 // fa_profile_next_launch); no-ops when nothing is armed.
@@ -84,6 +92,19 @@ void set_error_detail(const char* what, const char* file, int line, const char* 
       return FA_ERR_CUDA;                                                     \
     }                                                                         \
   } while (0)
+
+// Raises a kernel's dynamic shared-memory limit once per context (`done` is a static
+// array of kMaxContexts flags that belongs to that kernel).
+template <typename K>
+inline int smem_attr_once(K kern, int bytes, std::atomic<bool>* done) {
+  const int slot = call_context_slot();
+  if (slot < 0 || slot >= kMaxContexts) return FA_ERR_CUDA;
+  if (!done[slot].load(std::memory_order_acquire)) {
+    FA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done[slot].store(true, std::memory_order_release);
+  }
+  return FA_OK;
+}
 
 // setmaxnreg.inc waits until the block's own launch allocation can supply the raised
 // count, so a split whose total exceeds (registers per thread at launch) x threads

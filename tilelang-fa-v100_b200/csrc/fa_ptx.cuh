@@ -31,8 +31,15 @@ enum : int {
   FA_SITE_DEC_PRODUCER = 21,
   FA_SITE_DEC_COMPUTE = 22,
   FA_SITE_SELFTEST = 31,
+  FA_SITE_PAGED_SEQLEN = 4,
+  FA_SITE_DEC_SEQLEN = 23,
 };
 constexpr int FA_DEVERR_TIMEOUT = 1;
+// seq_lens[b] asks for more keys than the sequence's block-table row maps
+// (max_blocks * page_size): the keys are clamped to the mapped ones and this is recorded.
+constexpr int FA_DEVERR_SEQLEN = 4;
+
+
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -52,6 +59,19 @@ __device__ __forceinline__ void record_device_error(int* err, int code, int site
       err[2] = static_cast<int>(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
     }
   }
+}
+
+// Keys of sequence b that the kernels may read: seq_lens[b] clamped to the pages its
+// block-table row maps.  A longer seq_len would otherwise make the zero-filled
+// out-of-range loads count as real keys.  `report` selects the thread that records it.
+__device__ __forceinline__ int clamp_seq_len(int len, int max_blocks, int page_size, int* err,
+                                             int site, bool report) {
+  const int cap = max_blocks * page_size;
+  if (len > cap) {
+    if (report) record_device_error(err, FA_DEVERR_SEQLEN, site);
+    return cap;
+  }
+  return len;
 }
 
 // ---------------------------------------------------------------- mbarrier
