@@ -9,16 +9,19 @@ autograd) over that batch.  FLOPs are counted on visible (query, key) pairs:
 
 Scaling is weak: with N ranks the global problem is N x that batch, sharded by
 (batch x heads) so every rank owns exactly one B=8 x H=32 shard; no collective runs in
-the timed region (NCCL is used only for the barrier, the max-over-ranks timing and the
-gathered correctness check).  value = N x per-rank FLOPs / max-over-ranks time.
+the timed region.  value = N x per-rank FLOPs / max-over-ranks time.  Every input unit
+(batch row, sequence) is drawn from its own seed, so the check can regenerate it on
+rank 0 independently of the sharding: sampled outputs of every rank are broadcast to
+rank 0 over NCCL and compared there with an fp32 torch reference (`check`).
 
 Also reported in the same line: e2e (same metric through the public API with the
 inputs copied from pinned host memory and out/dq/dk/dv copied back every step), the
 roofline of the dominant kernel (the backward dK/dV kernel, timed live with CUDA
 events on its launch stream), the CPU baseline (the reference's PyTorch attention in
 fp32 on the host cores, on a bounded sample), clocks sampled during the timed region,
-and secondary workloads (the other BASELINE configs: dense fp16 D=64, non-square
-causal, paged GQA prefill, split-KV decode GB/s).
+and secondary workloads at the same N (the other BASELINE configs: dense fp16 D=64,
+non-square causal, paged GQA prefill sharded by sequence, split-KV decode GB/s sharded
+by sequence with balanced token counts; the forward kernel and the whole backward).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
@@ -147,15 +150,69 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- our arm
-def dense_inputs(dev, b, s, h, d, dtype, seed):
-    g = torch.Generator(device=dev).manual_seed(seed)
-    mk = lambda: torch.randn(b, s, h, d, generator=g, device=dev, dtype=torch.float32).to(dtype)
-    return mk(), mk(), mk(), mk()
+# Every input unit of every workload -- a dense batch row, a paged or decode sequence --
+# is drawn from its own seed (SEED_* + its global index), so the rank that owns a unit
+# and rank 0, which regenerates it for the gathered check, produce the same values
+# independently of how the units are sharded.
+SEED_DENSE, SEED_DENSE2, SEED_NONSQ, SEED_PAGED, SEED_DECODE = 1000, 3000, 5000, 7000, 9000
+U_BF16, U_F16 = 2.0 ** -8, 2.0 ** -11  # unit roundoff of the 16-bit input types
+
+
+def reduce_max(dist, dev, *vals):
+    """Element-wise max over ranks of host floats (identity on one GPU)."""
+    if dist is None:
+        return vals
+    t = torch.tensor(vals, device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return tuple(float(x) for x in t)
+
+
+def reduce_sum(dist, dev, *vals):
+    if dist is None:
+        return vals
+    t = torch.tensor(vals, device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return tuple(float(x) for x in t)
+
+
+def timed_ms(dev, dist, steps, fn):
+    """ms per call of fn over `steps` calls, CUDA events on the current stream, barrier +
+    synchronize on both sides, max over ranks."""
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        fn()
+    t1.record()
+    torch.cuda.synchronize(dev)
+    return reduce_max(dist, dev, t0.elapsed_time(t1) / steps)[0]
+
+
+def dense_row(dev, g, sq, skv, h, hk, d, dtype, seed_base):
+    """q [Sq,H,D], k / v [Skv,Hk,D], dO [Sq,H,D] of global batch row g (its own seed)."""
+    gen = torch.Generator(device=dev).manual_seed(seed_base + g)
+    mk = lambda n, hh: torch.randn(n, hh, d, generator=gen, device=dev, dtype=torch.float32).to(dtype)
+    return mk(sq, h), mk(skv, hk), mk(skv, hk), mk(sq, h)
+
+
+def dense_shard(dev, g0, g1, sq, skv, h, hk, d, dtype, seed_base):
+    """Batch rows [g0, g1) of the global problem as BSHD tensors (q, k, v, dO)."""
+    q = torch.empty(g1 - g0, sq, h, d, dtype=dtype, device=dev)
+    do = torch.empty_like(q)
+    k = torch.empty(g1 - g0, skv, hk, d, dtype=dtype, device=dev)
+    v = torch.empty_like(k)
+    for i, g in enumerate(range(g0, g1)):
+        q[i], k[i], v[i], do[i] = dense_row(dev, g, sq, skv, h, hk, d, dtype, seed_base)
+    return q, k, v, do
 
 
 def run_dense_steps(fa, q, k, v, do, causal, n, prof_events=None):
     """n fwd+bwd steps through the public API; optionally arms the dK/dV kernel events."""
     from tilelang_fa_v100 import _ext
+    out = None
     for i in range(n):
         q.grad = k.grad = v.grad = None
         out = fa.tilelang_flash_attn_func(q, k, v, causal=causal)
@@ -165,10 +222,10 @@ def run_dense_steps(fa, q, k, v, do, causal, n, prof_events=None):
     return out
 
 
-def time_dense(fa, dev, b, s, h, d, dtype, causal, steps, warmup, seed, dist=None, profile=False,
-               clk=None):
+def time_dense(fa, dev, q, k, v, do, causal, steps, warmup, dist=None, profile=False, clk=None):
+    """The headline step (fwd + bwd through the API) timed over `steps`; max over ranks.
+    With profile, also the mean dK/dV kernel time from events around its launches."""
     from tilelang_fa_v100 import _ext
-    q, k, v, do = dense_inputs(dev, b, s, h, d, dtype, seed)
     q, k, v = (x.requires_grad_(True) for x in (q, k, v))
     run_dense_steps(fa, q, k, v, do, causal, warmup)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -182,42 +239,144 @@ def time_dense(fa, dev, b, s, h, d, dtype, causal, steps, warmup, seed, dist=Non
     if clk is not None:
         clk.mark_start()
     t0.record()
-    out = run_dense_steps(fa, q, k, v, do, causal, steps, ev)
+    run_dense_steps(fa, q, k, v, do, causal, steps, ev)
     t1.record()
     torch.cuda.synchronize(dev)
     if clk is not None:
         clk.mark_stop()
     launches = _ext.launch_count() - n0
-    if dist is not None:
-        dist.barrier()
     ms = t0.elapsed_time(t1) / steps
-    kern_ms = statistics.mean(a.elapsed_time(b_) for a, b_ in ev) if profile else None
-    return ms, kern_ms, launches, (q, k, v, do, out)
+    kern_ms = statistics.mean(a.elapsed_time(b_) for a, b_ in ev) if profile else 0.0
+    ms, kern_ms = reduce_max(dist, dev, ms, kern_ms)
+    return ms, kern_ms, launches
 
 
-def check_dense(tensors, causal):
-    """Max-abs error of one (batch, head) slice of out against fp32 torch on the GPU."""
-    q, k, v, do, out = tensors
-    torch.backends.cuda.matmul.allow_tf32 = False
-    qs, ks, vs = q[0, :, 0].float(), k[0, :, 0].float(), v[0, :, 0].float()
-    sc = (qs @ ks.T) / math.sqrt(q.shape[-1])
-    if causal:
-        m, n = sc.shape
-        sc = sc.masked_fill(torch.ones(m, n, device=sc.device).tril(n - m) == 0, float("-inf"))
-    ref = torch.softmax(sc, -1) @ vs
-    return float((out.detach()[0, :, 0].float() - ref).abs().max())
+class ErrStats:
+    """Running error statistics of sampled outputs against a reference."""
+
+    def __init__(self):
+        self.d = {}
+
+    def _get(self, name):
+        return self.d.setdefault(name, {"n": 0, "max_abs_err": 0.0, "sum_abs_err": 0.0})
+
+    def north_star(self, name, got, ref):
+        """|got - ref| <= 2e-3 + 1e-2 |ref| elementwise (non-finite refs must match)."""
+        got, ref = got.double(), ref.double()
+        fin = torch.isfinite(ref)
+        same_inf = ~fin & (got == ref)
+        err = torch.where(fin, (got - ref.nan_to_num(0.0)).abs(), torch.zeros_like(got))
+        err = torch.where(fin | same_inf, err, torch.full_like(err, float("inf")))
+        excess = err - (2e-3 + 1e-2 * ref.nan_to_num(0.0, posinf=0.0, neginf=0.0).abs())
+        e = self._get(name)
+        e["n"] += err.numel()
+        e["max_abs_err"] = max(e["max_abs_err"], float(err.max()))
+        e["sum_abs_err"] += float(err[torch.isfinite(err)].sum())
+        e["north_star_fail"] = e.get("north_star_fail", 0) + int((excess > 0).sum())
+        e["north_star_max_excess"] = max(e.get("north_star_max_excess", -1.0), float(excess.max()))
+
+    def grad(self, name, got, ref, u):
+        """Gradients: max-abs error (north-star bar 1e-2) and the error left after the
+        output's own rounding (err - u |ref|)."""
+        got, ref = got.double(), ref.double()
+        err = (got - ref).abs()
+        e = self._get(name)
+        e["n"] += err.numel()
+        e["max_abs_err"] = max(e["max_abs_err"], float(err.max()))
+        e["sum_abs_err"] += float(err.sum())
+        e["gt_1e-2"] = e.get("gt_1e-2", 0) + int((err > 1e-2).sum())
+        e["max_err_beyond_output_rounding"] = max(e.get("max_err_beyond_output_rounding", -1.0),
+                                                  float((err - u * ref.abs()).max()))
+
+    def bound(self, name, got, ref, bnd, atol=1e-4):
+        """|got - ref| <= atol + bnd, the operand-rounding bound."""
+        err = (got.double() - ref.double()).abs()
+        e = self._get(name)
+        e["rounding_bound_fail"] = e.get("rounding_bound_fail", 0) + int((err > atol + bnd.double()).sum())
+        e["rounding_bound_max_ratio"] = max(e.get("rounding_bound_max_ratio", 0.0),
+                                            float((err / (atol + bnd.double())).max()))
+
+    def summary(self):
+        out = {}
+        for k, e in self.d.items():
+            e = dict(e)
+            e["mean_abs_err"] = e.pop("sum_abs_err") / max(1, e["n"])
+            if "north_star_fail" in e:
+                e["north_star_fail_frac"] = e["north_star_fail"] / max(1, e["n"])
+            out[k] = e
+        return out
 
 
-def time_e2e(fa, dev, b, s, h, d, dtype, causal, steps, warmup, seed):
+def _bcast(dist, t, src):
+    if dist is not None:
+        dist.broadcast(t, src=src)
+    return t
+
+
+def check_dense(fa, dev, dist, rank, world, rows, tensors, sq, skv, h, d, dtype, causal, seed_base):
+    """Gathered check of the headline step.  Sampled (batch row, head) slices -- one on
+    every rank plus the first and last of the global problem -- are broadcast from the
+    rank that owns them; rank 0 regenerates that row's inputs from its seed and compares
+    out, lse, dQ, dK, dV with the fp32 torch reference (TF32 off).  Returns the
+    statistics on rank 0 (None elsewhere)."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from slice_ref import slice_ref_2d
+    q, k, v, do = tensors
+    qd, kd, vd = (x.detach().clone().requires_grad_(True) for x in (q, k, v))
+    out, lse, _ = fa.tilelang_flash_attn_func(qd, kd, vd, causal=causal, return_attn_probs=True)
+    out.backward(do)
+    torch.cuda.synchronize(dev)
+    u = U_BF16 if dtype == torch.bfloat16 else U_F16
+    n = world * rows
+    samples = [(0, 0), (n - 1, h - 1)] + [(r * rows + rows // 2, (11 * r + 5) % h) for r in range(world)]
+    samples = list(dict.fromkeys(samples))
+    st = ErrStats()
+    for g, hh in samples:
+        owner = g // rows
+        shapes = [((sq, d), dtype), ((sq,), torch.float32), ((sq, d), dtype), ((skv, d), dtype),
+                  ((skv, d), dtype)]
+        if rank == owner:
+            li = g - rank * rows
+            pack = [out[li, :, hh], lse[li, hh], qd.grad[li, :, hh], kd.grad[li, :, hh],
+                    vd.grad[li, :, hh]]
+            pack = [t.detach().contiguous() for t in pack]
+        else:
+            pack = [torch.empty(s, dtype=dt, device=dev) for s, dt in shapes]
+        pack = [_bcast(dist, t, owner) for t in pack]
+        if rank != 0:
+            continue
+        qg, kg, vg, dog = dense_row(dev, g, sq, skv, h, h, d, dtype, seed_base)
+        o_s, lse_s, dq_s, dk_s, dv_s = pack
+        r = slice_ref_2d(qg[:, hh], kg[:, hh], vg[:, hh], dog[:, hh], o_s, causal, u)
+        st.north_star("out", o_s, r["out"])
+        st.north_star("lse", lse_s, r["lse"])
+        st.bound("out", o_s, r["out"], r["bo"])
+        for nm, got in (("dq", dq_s), ("dk", dk_s), ("dv", dv_s)):
+            st.grad(nm, got, r[nm], u)
+            st.bound(nm, got, r[nm + "_f"], r["b" + nm[1]])
+    del qd, kd, vd, out, lse
+    if rank != 0:
+        return None
+    res = st.summary()
+    res["samples"] = ["batch %d head %d (rank %d)" % (g, hh, g // rows) for g, hh in samples]
+    res["criteria"] = (
+        "fp32 torch on the GPU (TF32 off), inputs regenerated on rank 0 from each row's seed; "
+        "out / lse: north-star |d| <= 2e-3 + 1e-2 |ref| (fail count, fraction, max excess); "
+        "grads: max-abs vs the 1e-2 bar (gt_1e-2) and the error beyond the output's own "
+        "rounding u|ref| (u = %g); rounding_bound_*: |d| <= 1e-4 + u (sum |operand| ...) against "
+        "the reference with D = rowsum(dO * O) from the returned O -- the worst case of rounding "
+        "P, dS and the outputs to %s" % (u, str(dtype).split(".")[-1]))
+    return res
+
+
+def time_e2e(fa, dev, q, k, v, do, causal, steps, warmup):
     """Public API with host buffers.  Every step uploads its q, k, v, dO from pinned host
     memory, runs fwd + bwd and downloads its out, dq, dk, dv into pinned host memory.
     Neighbouring steps overlap the way a training loop that streams its batches does:
     the upload of step k+1 and the download of step k-1 run on two copy streams while
     step k computes (device buffers double-buffered, events order each slot's reuse)."""
-    q, k, v, do = dense_inputs(dev, b, s, h, d, dtype, seed)
-    host_in = [x.cpu().pin_memory() for x in (q, k, v, do)]
-    del q, k, v, do
-    shape, nb = (b, s, h, d), 2
+    host_in = [x.detach().cpu().pin_memory() for x in (q, k, v, do)]
+    shape, dtype, nb = tuple(q.shape), q.dtype, 2
     dev_in = [[torch.empty(shape, dtype=dtype, device=dev) for _ in range(4)] for _ in range(nb)]
     for slot in dev_in:
         for t in slot[:3]:
@@ -302,78 +461,167 @@ def time_e2e(fa, dev, b, s, h, d, dtype, causal, steps, warmup, seed):
         c1.record(main)
         torch.cuda.synchronize(dev)
         link_ms = min(link_ms, c0.elapsed_time(c1))
-    nbytes = b * s * h * d * 2
+    nbytes = q.numel() * q.element_size()
     return ms, 4 * nbytes, 4 * nbytes, link_ms
 
 
-def time_paged(dev, steps, warmup):
-    """16 x 1024 tokens, H 32 / Hkv 8, D 128, page 16, shuffled pages."""
-    from tilelang_fa_v100 import _ext
-    rng = np.random.default_rng(0)
-    g = torch.Generator(device=dev).manual_seed(1)
-    kc = torch.randn(1024, 16, 8, 128, generator=g, device=dev).half()
-    vc = torch.randn(1024, 16, 8, 128, generator=g, device=dev).half()
-    bt = torch.from_numpy(rng.permutation(1024).astype(np.int32).reshape(16, 64)).to(dev)
-    q = torch.randn(16384, 32, 128, generator=g, device=dev).half()
-    qsl = torch.arange(0, 16385, 1024, dtype=torch.int32, device=dev)
-    sl = torch.full((16,), 1024, dtype=torch.int32, device=dev)
-    pkl = torch.zeros(16, dtype=torch.int32, device=dev)
+# ---- paged prefill and decode: sequences with their own seeds
+def seq_inputs(dev, i, q_len, kv_len, h, hkv, d, dtype, seed_base):
+    """q [q_len,H,D] (the sequence's last q_len rows), k / v [kv_len,Hkv,D] of sequence i."""
+    gen = torch.Generator(device=dev).manual_seed(seed_base + i)
+    mk = lambda n, hh: torch.randn(n, hh, d, generator=gen, device=dev, dtype=torch.float32).to(dtype)
+    return mk(q_len, h), mk(kv_len, hkv), mk(kv_len, hkv)
+
+
+def paged_problem(dev, seqs, q_lens, kv_lens, h, hkv, d, page, dtype, seed_base, perm_seed,
+                  max_blocks=None):
+    """The vLLM-layout inputs of the given sequences (global indices): every sequence's
+    pages are scattered over the rank's page pool by a seeded permutation; block-table
+    rows are padded with page 0 up to max_blocks."""
+    pps = [-(-int(n) // page) for n in kv_lens]
+    total = max(1, sum(pps))
+    perm = torch.from_numpy(np.random.default_rng(perm_seed).permutation(total).astype(np.int64))
+    mb = max(pps) if max_blocks is None else max_blocks
+    bt = torch.zeros(len(seqs), mb, dtype=torch.int32)
+    kc = torch.zeros(total, page, hkv, d, dtype=dtype, device=dev)
+    vc = torch.zeros_like(kc)
+    q = torch.empty(int(sum(q_lens)), h, d, dtype=dtype, device=dev)
+    c = t = 0
+    for j, i in enumerate(seqs):
+        pages = perm[c:c + pps[j]]
+        bt[j, :pps[j]] = pages.to(torch.int32)
+        c += pps[j]
+        qi, ki, vi = seq_inputs(dev, i, int(q_lens[j]), pps[j] * page, h, hkv, d, dtype, seed_base)
+        q[t:t + int(q_lens[j])] = qi
+        t += int(q_lens[j])
+        pg = pages.to(dev)
+        kc[pg] = ki.view(pps[j], page, hkv, d)
+        vc[pg] = vi.view(pps[j], page, hkv, d)
+    qsl = torch.tensor(np.concatenate([[0], np.cumsum(q_lens)]), dtype=torch.int32, device=dev)
+    sl = torch.tensor(np.asarray(kv_lens), dtype=torch.int32, device=dev)
+    return q, kc, vc, bt.to(dev), sl, qsl, total
+
+
+PAGED = dict(seqs=16, q_len=1024, kv_len=1024, h=32, hkv=8, d=128, page=16)  # configs[3]
+
+
+def paged_run(dev, dist, rank, world, steps, warmup):
+    """configs[3], weak: every rank runs 16 x 1024-token sequences (global sequences
+    16 r .. 16 r + 15, contiguous); returns aggregate TFLOP/s, ms and the gathered check."""
+    import tilelang_fa_v100 as fa
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from slice_ref import sequence_ref
+    c = PAGED
+    n = c["seqs"]
+    seqs = list(range(rank * n, (rank + 1) * n))
+    q, kc, vc, bt, sl, qsl, _ = paged_problem(dev, seqs, [c["q_len"]] * n, [c["kv_len"]] * n,
+                                              c["h"], c["hkv"], c["d"], c["page"], torch.float16,
+                                              SEED_PAGED, 11 + rank)
+    pkl = torch.zeros(n, dtype=torch.int32, device=dev)
     out = torch.empty_like(q)
-    lse = torch.empty(32, 16384, device=dev)
-    run = lambda: _ext.paged_prefill(q, kc, vc, bt, sl, qsl, pkl, out, lse, 16, 8, 128 ** -0.5,
-                                     True, -1, -1)
+    lse = torch.empty(c["h"], q.shape[0], device=dev)
+    run = lambda: fa.tilelang_paged_forward(q, kc, vc, bt, sl, qsl, pkl, out=out)
     for _ in range(warmup):
         run()
+    ms = timed_ms(dev, dist, steps, run)
+    out, lse = fa.tilelang_paged_forward(q, kc, vc, bt, sl, qsl, pkl, out=out)
     torch.cuda.synchronize(dev)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(steps):
-        run()
-    t1.record()
-    torch.cuda.synchronize(dev)
-    ms = t0.elapsed_time(t1) / steps
-    return ms, 4 * 128 * visible_pairs(16, 32, 1024, 1024, True) / ms / 1e9
+    flops = world * 4.0 * c["d"] * visible_pairs(n, c["h"], c["q_len"], c["kv_len"], True)
+    # gathered check: the first and last sequence of the global batch + one per rank
+    total = world * n
+    samples = list(dict.fromkeys([0, total - 1] + [r * n + (5 * r + 3) % n for r in range(world)]))
+    st = ErrStats()
+    for i in samples:
+        owner = i // n
+        if rank == owner:
+            j = i - owner * n
+            pack = [out[j * c["q_len"]:(j + 1) * c["q_len"]].contiguous(),
+                    lse[:, j * c["q_len"]:(j + 1) * c["q_len"]].contiguous()]
+        else:
+            pack = [torch.empty(c["q_len"], c["h"], c["d"], dtype=torch.float16, device=dev),
+                    torch.empty(c["h"], c["q_len"], device=dev)]
+        pack = [_bcast(dist, t, owner) for t in pack]
+        if rank != 0:
+            continue
+        qi, ki, vi = seq_inputs(dev, i, c["q_len"], c["kv_len"], c["h"], c["hkv"], c["d"],
+                                torch.float16, SEED_PAGED)
+        ro, rl = sequence_ref(qi, ki, vi, c["kv_len"] - c["q_len"], True)
+        st.north_star("out", pack[0], ro)
+        st.north_star("lse", pack[1], rl)
+    del q, kc, vc, out, lse
+    chk = None
+    if rank == 0:
+        chk = st.summary()
+        chk["samples"] = ["sequence %d (rank %d)" % (i, i // n) for i in samples]
+    return flops / ms / 1e9, ms, chk
 
 
-def decode_problem(dev, seed, batch=256, hkv=8, d=128, heads=32):
-    """256 seqs, L ~ U[512, 8192], H 32 / Hkv 8, D 128, page 16, bf16
-    (other head layouts with the same length distribution on request)."""
-    rng = np.random.default_rng(seed)
-    lens = rng.integers(512, 8193, size=batch).astype(np.int32)
-    pps = (lens + 15) // 16
-    total = int(pps.sum())
-    perm = rng.permutation(total).astype(np.int32)
-    bt = np.zeros((batch, 512), np.int32)
-    c = 0
-    for i in range(batch):
-        bt[i, :pps[i]] = perm[c:c + pps[i]]
-        c += pps[i]
-    g = torch.Generator(device=dev).manual_seed(seed + 1)
-    kc = torch.randn(total, 16, hkv, d, generator=g, device=dev).to(torch.bfloat16)
-    vc = torch.randn(total, 16, hkv, d, generator=g, device=dev).to(torch.bfloat16)
-    q = torch.randn(batch, heads, d, generator=g, device=dev).to(torch.bfloat16)
-    nbytes = int(lens.sum()) * hkv * d * 2 * 2 + 2 * batch * heads * d * 2 + total * 4
-    return q, kc, vc, torch.from_numpy(bt).to(dev), torch.from_numpy(lens).to(dev), nbytes
+def decode_lengths(world, batch=256, seed=0):
+    """Global KV lengths of configs[4] (L ~ U[512, 8192]) for world x batch sequences."""
+    return np.random.default_rng(seed).integers(512, 8193, size=world * batch).astype(np.int32)
 
 
-def time_decode(dev, steps, warmup, seed=0, hkv=8, d=128, heads=32):
+def decode_problem(dev, rank, world, batch=256, hkv=8, d=128, heads=32, seed_base=SEED_DECODE):
+    """Rank `rank`'s share of world x batch decode sequences, balanced longest-first by
+    token count (sharding.balance_sequences).  Returns the inputs, the rank's sequence
+    ids and the HBM bytes one decode reads and writes (K/V actually read + q + out +
+    block table)."""
+    from tilelang_fa_v100 import sharding
+    lens = decode_lengths(world, batch)
+    owned = sharding.balance_sequences(lens, world)
+    mine = owned[rank]
+    q, kc, vc, bt, sl, _, total = paged_problem(dev, mine, [1] * len(mine), lens[mine], heads,
+                                                hkv, d, 16, torch.bfloat16, seed_base,
+                                                100 + rank, max_blocks=512)
+    nbytes = int(lens[mine].sum()) * hkv * d * 2 * 2 + 2 * len(mine) * heads * d * 2 + total * 4
+    return q, kc, vc, bt, sl, nbytes, mine, owned, lens
+
+
+def decode_run(dev, dist, rank, world, steps, warmup, hkv=8, d=128, heads=32, check=True):
+    """configs[4] at N GPUs (weak: N x 256 sequences, sharded by sequence with balanced
+    token counts).  Returns aggregate GB/s, ms, the gathered check and the max/mean
+    per-rank token load."""
     import tilelang_fa_v100 as fa
-    q, kc, vc, bt, sl, nbytes = decode_problem(dev, seed, hkv=hkv, d=d, heads=heads)
+    q, kc, vc, bt, sl, nbytes, mine, owned, lens = decode_problem(dev, rank, world, hkv=hkv, d=d,
+                                                                  heads=heads)
     run = lambda: fa.tilelang_decode_forward(q, kc, vc, bt, sl)
     for _ in range(warmup):
         run()
-    torch.cuda.synchronize(dev)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(steps):
-        run()
-    t1.record()
-    torch.cuda.synchronize(dev)
-    ms = t0.elapsed_time(t1) / steps
-    return ms, nbytes / ms / 1e6
+    ms = timed_ms(dev, dist, steps, run)
+    tot_bytes = reduce_sum(dist, dev, float(nbytes))[0]
+    loads = [int(lens[o].sum()) for o in owned]
+    res_chk = None
+    if check:
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        from slice_ref import sequence_ref
+        out = run()
+        torch.cuda.synchronize(dev)
+        samples = list(dict.fromkeys([0, len(lens) - 1] + [o[len(o) // 2] for o in owned]))
+        st = ErrStats()
+        for i in samples:
+            owner = next(r for r, o in enumerate(owned) if i in o)
+            if rank == owner:
+                pack = out[mine.index(i)].contiguous()
+            else:
+                pack = torch.empty(heads, d, dtype=torch.bfloat16, device=dev)
+            pack = _bcast(dist, pack, owner)
+            if rank != 0:
+                continue
+            L = int(lens[i])
+            qi, ki, vi = seq_inputs(dev, i, 1, -(-L // 16) * 16, heads, hkv, d, torch.bfloat16,
+                                    SEED_DECODE)
+            ro, _ = sequence_ref(qi, ki[:L], vi[:L], 0, False)
+            st.north_star("out", pack, ro[0])
+        if rank == 0:
+            res_chk = st.summary()
+            res_chk["samples"] = ["sequence %d (rank %d)" % (i, next(r for r, o in enumerate(owned) if i in o))
+                                  for i in samples]
+    del q, kc, vc
+    balance = {"max_rank_tokens": max(loads), "mean_rank_tokens": sum(loads) / len(loads)}
+    return tot_bytes / ms / 1e6, ms, res_chk, balance
 
 
-def time_kv_write(dev, steps, warmup, tokens=65536, hkv=8, d=128, page=16):
+def time_kv_write(dev, dist, steps, warmup, tokens=65536, hkv=8, d=128, page=16):
     """Paged KV-cache write of one large prefill step: bytes = read key + value and
     write them into the cache (slot_mapping excluded), scattered slots."""
     from tilelang_fa_v100.cache import write_kv_cache
@@ -388,16 +636,35 @@ def time_kv_write(dev, steps, warmup, tokens=65536, hkv=8, d=128, page=16):
     run = lambda: write_kv_cache(key, value, kc, vc, slots)
     for _ in range(warmup):
         run()
-    torch.cuda.synchronize(dev)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(steps):
-        run()
-    t1.record()
-    torch.cuda.synchronize(dev)
-    ms = t0.elapsed_time(t1) / steps
+    ms = timed_ms(dev, dist, steps, run)
     nbytes = 2 * 2 * tokens * hkv * d * 2
     return ms, nbytes / ms / 1e6
+
+
+def kernel_events_ms(dev, dist, kind, fn, reps=5):
+    """Mean duration of one library kernel (events the library records around its
+    launch on the launch stream), max over ranks."""
+    from tilelang_fa_v100 import _ext
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ts = []
+    for _ in range(reps):
+        _ext.profile_next_launch(kind, e0, e1)
+        fn()
+        torch.cuda.synchronize(dev)
+        ts.append(e0.elapsed_time(e1))
+    return reduce_max(dist, dev, statistics.mean(ts))[0]
+
+
+def peak_for_clocks(peaks, clocks):
+    """Burst bf16 peak when the timed region ran at max SM clock with no power cap, the
+    sustained one otherwise (a region long enough to hit the 1000 W cap)."""
+    mhz, mx = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+    burst = (mhz is not None and mx and mhz >= 0.97 * mx
+             and "sw_power_cap" not in (clocks.get("reasons") or []))
+    if burst:
+        return peaks["bf16_tflops"], "bf16_tflops (burst): the timed region ran at %.0f of %.0f MHz with no power cap" % (mhz, mx)
+    return peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]), \
+        "bf16_tflops_sustained: the timed region ran below max clock or under sw_power_cap"
 
 
 def cpu_baseline(budget_s=15.0):
@@ -434,48 +701,39 @@ def run_ours(args):
     torch.cuda.set_device(dev)
     dist = None
     if world > 1:
-        import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     from tilelang_fa_v100 import sharding
+    peaks, src = measured_peaks()
+    hbm = peaks.get("hbm_gbs", 6538.6)
     # Weak scaling: the global batch is world x configs[2]'s batch; rank r owns batch rows
     # [r*B, (r+1)*B) with all heads (a (batch x heads) shard, no data exchange).
     s, h, d, causal = CFG["S"], CFG["H"], CFG["D"], CFG["causal"]
-    b0, b1 = sharding.dense_batch_slice(CFG["B"] * world, world, rank)
-    b = b1 - b0
+    g0, g1 = sharding.dense_batch_slice(CFG["B"] * world, world, rank)
+    b = g1 - g0
     dtype = torch.bfloat16
+    tensors = dense_shard(dev, g0, g1, s, s, h, h, d, dtype, SEED_DENSE)
     with ClockSampler(local) as clk:
-        ms, kern_ms, launches, tensors = time_dense(fa, dev, b, s, h, d, dtype, causal, args.steps,
-                                                    args.warmup, seed=1000 + rank, dist=dist,
-                                                    profile=True, clk=clk)
+        ms, kern_ms, launches = time_dense(fa, dev, *tensors, causal, args.steps, args.warmup,
+                                           dist=dist, profile=True, clk=clk)
     clocks = clk.summary()
-    err = check_dense(tensors, causal)
-    del tensors
-    if dist is not None:
-        t = torch.tensor([ms, err], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)  # max over ranks (time and error)
-        ms, err = float(t[0]), float(t[1])
     fl = step_flops(b, h, s, s, d, causal)
     value = world * fl / ms / 1e9  # TFLOP/s (ms -> s: /1e-3, TFLOP: /1e12)
+    check = check_dense(fa, dev, dist, rank, world, b, tensors, s, s, h, d, dtype, causal,
+                        SEED_DENSE)
     # as many e2e steps as timed steps: the first upload and the last download of a
     # pipelined run are exposed once, so short runs understate the streaming rate
-    e2e_ms, h2d, d2h, link_ms = time_e2e(fa, dev, b, s, h, d, dtype, causal, args.steps, 2,
-                                         seed=1000 + rank)
-    if dist is not None:
-        t = torch.tensor([e2e_ms, link_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms, link_ms = float(t[0]), float(t[1])
-    peaks, src = measured_peaks()
+    e2e_ms, h2d, d2h, link_ms = time_e2e(fa, dev, *tensors, causal, args.steps, 2)
+    e2e_ms, link_ms = reduce_max(dist, dev, e2e_ms, link_ms)
     bwd_fl = 10.0 * d * visible_pairs(b, h, s, s, causal)
     achieved = bwd_fl / kern_ms / 1e9
-    peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+    peak, peak_why = peak_for_clocks(peaks, clocks)
     traffic = ncu_traffic("fa_bwd_dkdv_cfg3")
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic: q/k/v/dO i.i.d. N(0,1) from per-rank seeds (no dataset involved)",
+        "data": "synthetic: q/k/v/dO i.i.d. N(0,1), each batch row from its own seed (no dataset involved)",
         "config": {"workload": WORKLOAD, "global_batch": b * world, "seq_len": s, "heads": h,
                    "head_dim": d, "causal": causal, "parallelism": "dp%d (batch x heads shards)" % world,
                    "l2": "inputs larger than L2 (q/k/v/dO 268 MB each > 126 MB)"},
@@ -492,68 +750,72 @@ def run_ours(args):
         "roofline": {"kernel": "fa_bwd_dkdv_kernel (dense backward dK/dV + fused dQ)",
                      "bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
                      "frac": achieved / peak, "traffic": traffic,
-                     "peak_source": "%s bf16_tflops_sustained (kernel timed inside repeated steps)" % src,
+                     "peak_source": "%s %s" % (src, peak_why),
                      "algorithmic": "10*D FLOP per visible (q,k) pair = %.4g FLOP per launch" % bwd_fl,
                      "kernel_ms": kern_ms},
-        "check": {"max_abs_err_out_vs_fp32": err},
+        "check": check,
     }
-    if not args.no_secondary and world == 1:  # secondary configs: single-GPU runs only
+    if not args.no_secondary:
         sec = {}
-        sms, _, _, tt = time_dense(fa, dev, 4, 2048, 16, 64, torch.float16, True, args.steps, 3,
-                                   seed=7 + rank)
-        del tt
-        sec["cfg2_dense_fp16_B4_S2048_H16_D64"] = {
-            "tflops": step_flops(4, 16, 2048, 2048, 64, True) / sms / 1e9, "ms": sms}
-        # forward-only and backward-only rooflines on the headline shape
-        q, k, v, do = dense_inputs(dev, b, s, h, d, dtype, 5)
-        for _ in range(3):
-            _ext.dense_forward(q, k, v, d ** -0.5, True)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        fts = []
-        for _ in range(5):
-            _ext.profile_next_launch(_ext.PROF_FWD, e0, e1)
-            o, lse = _ext.dense_forward(q, k, v, d ** -0.5, True)
-            torch.cuda.synchronize(dev)
-            fts.append(e0.elapsed_time(e1))
+        burst = peaks["bf16_tflops"]
+        # forward kernel alone and the whole backward (prep + dK/dV + dQ convert) on the
+        # headline shard; each rank times its own, max over ranks
+        q, k, v, do = tensors
+        out, lse = _ext.dense_forward(q, k, v, d ** -0.5, True)
+        fwd_ms = kernel_events_ms(dev, dist, _ext.PROF_FWD,
+                                  lambda: _ext.dense_forward(q, k, v, d ** -0.5, True))
         fwd_fl = 4.0 * d * visible_pairs(b, h, s, s, True)
-        sec["cfg3_forward_kernel"] = {"tflops": fwd_fl / statistics.mean(fts) / 1e9,
-                                      "ms": statistics.mean(fts),
-                                      "frac_of_burst_peak": fwd_fl / statistics.mean(fts) / 1e9 / peaks.get("bf16_tflops", peak)}
-        sec["cfg3_backward_dkdv_kernel"] = {"tflops": achieved, "ms": kern_ms,
-                                            "frac_of_burst_peak": achieved / peaks.get("bf16_tflops", peak)}
-        del q, k, v, do, o, lse
-        # non-square: Sq = 1024, Skv = 4096 needs its own inputs
-        qn, kn, vn, don = dense_inputs(dev, 8, 1024, 32, 128, dtype, 11)
-        kn = torch.randn(8, 4096, 32, 128, device=dev).to(dtype)
-        vn = torch.randn(8, 4096, 32, 128, device=dev).to(dtype)
-        qn, kn, vn = (x.requires_grad_(True) for x in (qn, kn, vn))
-        run_dense_steps(fa, qn, kn, vn, don, True, 3)
-        torch.cuda.synchronize(dev)
-        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0.record()
-        run_dense_steps(fa, qn, kn, vn, don, True, args.steps)
-        t1.record()
-        torch.cuda.synchronize(dev)
-        nms = t0.elapsed_time(t1) / args.steps
+        sec["cfg3_forward_kernel"] = {"tflops": world * fwd_fl / fwd_ms / 1e9, "ms": fwd_ms,
+                                      "frac_of_burst_peak": fwd_fl / fwd_ms / 1e9 / burst}
+        for _ in range(2):
+            _ext.dense_backward(q, k, v, out, do, lse, d ** -0.5, True)
+        bwd_ms = timed_ms(dev, dist, 5, lambda: _ext.dense_backward(q, k, v, out, do, lse,
+                                                                    d ** -0.5, True))
+        sec["cfg3_backward_total"] = {
+            "tflops": world * bwd_fl / bwd_ms / 1e9, "ms": bwd_ms,
+            "frac_of_burst_peak": bwd_fl / bwd_ms / 1e9 / burst,
+            "what": "prep (row dot) + dK/dV (+ fused dQ adds) + dQ convert, event-timed on the "
+                    "stream, 10*D FLOP per visible pair"}
+        sec["cfg3_backward_dkdv_kernel"] = {"tflops": world * achieved, "ms": kern_ms,
+                                            "frac_of_burst_peak": achieved / burst}
+        del q, k, v, do, out, lse, tensors
+        # fp16 D = 64, B = 4 rows per rank
+        t2 = dense_shard(dev, 4 * rank, 4 * rank + 4, 2048, 2048, 16, 16, 64, torch.float16,
+                         SEED_DENSE2)
+        sms, _, _ = time_dense(fa, dev, *t2, True, args.steps, 3, dist=dist)
+        sec["cfg2_dense_fp16_B4_S2048_H16_D64"] = {
+            "tflops": world * step_flops(4, 16, 2048, 2048, 64, True) / sms / 1e9, "ms": sms}
+        del t2
+        # configs[2] non-square variant: Sq = 1024, Skv = 4096, 8 rows per rank
+        tn = dense_shard(dev, g0, g1, 1024, 4096, 32, 32, 128, dtype, SEED_NONSQ)
+        nms, _, _ = time_dense(fa, dev, *tn, True, args.steps, 3, dist=dist)
         sec["cfg3_nonsquare_bf16_Sq1024_Skv4096"] = {
-            "tflops": step_flops(8, 32, 1024, 4096, 128, True) / nms / 1e9, "ms": nms}
-        del qn, kn, vn, don
-        pms, ptf = time_paged(dev, args.steps, 3)
-        sec["cfg4_paged_prefill_fp16"] = {"tflops": ptf, "ms": pms}
-        dms, dgbs = time_decode(dev, args.steps, 3, seed=rank)
+            "tflops": world * step_flops(b, 32, 1024, 4096, 128, True) / nms / 1e9, "ms": nms}
+        del tn
+        ptf, pms, pchk = paged_run(dev, dist, rank, world, args.steps, 3)
+        sec["cfg4_paged_prefill_fp16"] = {"tflops": ptf, "ms": pms,
+                                          "frac_of_burst_peak": ptf / world / burst,
+                                          "sharding": "16 sequences per rank (contiguous)",
+                                          "check": pchk}
+        dgbs, dms, dchk, bal = decode_run(dev, dist, rank, world, args.steps, 3)
         sec["cfg5_decode_bf16_GBps"] = {"gbs": dgbs, "ms": dms,
-                                        "frac_of_hbm": dgbs / peaks.get("hbm_gbs", 6538.6),
-                                        "peak_source": src + " hbm_gbs"}
-        d2ms, d2gbs = time_decode(dev, args.steps, 3, seed=rank, hkv=2, d=256, heads=32)
-        sec["decode_bf16_H32_Hkv2_D256_GBps"] = {
-            "gbs": d2gbs, "ms": d2ms, "frac_of_hbm": d2gbs / peaks.get("hbm_gbs", 6538.6),
-            "note": "the reference's 32/2 D=256 test configuration, cfg5 length distribution"}
-        kms, kgbs = time_kv_write(dev, args.steps, 3)
+                                        "frac_of_hbm": dgbs / world / hbm,
+                                        "peak_source": src + " hbm_gbs",
+                                        "sharding": "256 sequences per rank, balanced longest-first "
+                                                    "by token count", "balance": bal,
+                                        "check": dchk}
+        d2gbs, d2ms, _, _ = decode_run(dev, dist, rank, world, args.steps, 3, hkv=1, d=256,
+                                       heads=8, check=False)
+        sec["decode_bf16_H8_Hkv1_D256_GBps"] = {
+            "gbs": d2gbs, "ms": d2ms, "frac_of_hbm": d2gbs / world / hbm,
+            "note": "the reference's synthetic 8/1 D=256 configuration, configs[4] length "
+                    "distribution"}
+        kms, kgbs = time_kv_write(dev, dist, args.steps, 3)
         sec["kv_cache_write_bf16_65536tok_Hkv8_D128_GBps"] = {
-            "gbs": kgbs, "ms": kms, "frac_of_hbm": kgbs / peaks.get("hbm_gbs", 6538.6)}
+            "gbs": world * kgbs, "ms": kms, "frac_of_hbm": kgbs / hbm}
         line["secondary"] = sec
-        err_code = _ext.read_device_error(clear=True)
-        line["device_error"] = list(err_code)
+        code = _ext.read_device_error(clear=True)
+        line["device_error"] = list(code)
     if rank == 0:
         if world == 1:  # the host-core baseline is reported at N = 1 only
             line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
@@ -609,19 +871,19 @@ def run_profile_case(args):
     import tilelang_fa_v100 as fa
     dev = torch.device("cuda", 0)
     if args.profile_case == "paged":
-        ms, tflops = time_paged(dev, args.steps, args.warmup)
+        tflops, ms, _ = paged_run(dev, None, 0, 1, args.steps, args.warmup)
         print(json.dumps({"profile_case": "paged_cfg4_fp16", "ms": ms, "tflops": tflops}), flush=True)
         return
     if args.profile_case == "decode":
-        q, kc, vc, bt, sl, nbytes = decode_problem(dev, 0, batch=64)
+        q, kc, vc, bt, sl, nbytes, _, _, _ = decode_problem(dev, 0, 1, batch=64)
         for _ in range(args.warmup + args.steps):
             fa.tilelang_decode_forward(q, kc, vc, bt, sl)
         torch.cuda.synchronize(dev)
         print(json.dumps({"profile_case": "decode_B64_bf16", "bytes": nbytes}), flush=True)
         return
-    b, s, h, d = 2, CFG["S"], CFG["H"], CFG["D"]
-    ms, kern_ms, launches, _ = time_dense(fa, dev, b, s, h, d, torch.bfloat16, True, args.steps,
-                                          args.warmup, seed=3, profile=True)
+    s, h, d = CFG["S"], CFG["H"], CFG["D"]
+    t = dense_shard(dev, 0, 2, s, s, h, h, d, torch.bfloat16, SEED_DENSE)
+    ms, kern_ms, launches = time_dense(fa, dev, *t, True, args.steps, args.warmup, profile=True)
     print(json.dumps({"profile_case": "B2_S4096_H32_D128_bf16_causal", "ms_per_step": ms,
                       "dkdv_ms": kern_ms, "launches": launches}), flush=True)
 

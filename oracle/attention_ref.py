@@ -31,6 +31,14 @@ repository's pure-PyTorch attention oracles and the semantics of its kernels:
   are padding.  Pinned by the paged golden vectors: writing a golden sequence's tokens
   through this function reproduces the golden cache.
 
+* rounding bounds (``unit_roundoff`` arguments, ``attention_out_bound``) -- per-element
+  worst cases of what rounding the MMA operands that every FlashAttention kernel rounds
+  to the 16-bit input type (P, dS) and the outputs can change.  The reference rounds
+  the same operands (_kernels_forward.py:162-165, _kernels_backward.py:77).  A kernel
+  inside the bound differs from this fp32 oracle by rounding alone; bf16 tests use it
+  as their bar, since bf16's 8-bit significand puts single rounding errors at the
+  size of the fp16-oriented absolute bars.
+
 Pinning: tests/test_oracle_golden.py checks every function here against golden
 vectors produced by running the reference's own ``pytorch_gqa_ref`` and
 ``make_paged_gqa`` (tests/golden/make_golden.py).
@@ -83,8 +91,23 @@ def attention_ref(q, k, v, causal, scale=None, return_p=False):
     return out.astype(np.float32), lse.astype(np.float32)
 
 
-def attention_bwd_ref(q, k, v, do, causal, scale=None):
-    """Gradients (dq [B,Hq,M,D], dk/dv [B,Hkv,N,D]) of attention_ref w.r.t. q, k, v."""
+def attention_bwd_ref(q, k, v, do, causal, scale=None, o=None, unit_roundoff=None):
+    """Gradients (dq [B,Hq,M,D], dk/dv [B,Hkv,N,D]) of attention_ref w.r.t. q, k, v.
+
+    ``o``: the forward output the backward is given ([B,Hq,M,D]); when passed, the row
+    dot D = rowsum(dO * O) uses it, as the reference backward does with the fp16 output
+    its forward stored (_kernels_backward.py:203).  Without it D uses the exact output
+    (the gradient of the fp32 function).
+
+    ``unit_roundoff`` u (2**-8 for bf16, 2**-11 for fp16): also return per-element
+    bounds (bq, bk, bv) on what rounding the operands that every FlashAttention backward
+    rounds to the input type can change: P before dV = P^T dO (:166), dS before
+    dQ = dS K and dK = dS^T Q (:77, :80, :170), and the three outputs themselves:
+        bv = u (sum_i P_ij |dO_id| + |dV_jd|)
+        bq = u (sum_j |dS_ij| |K_jd| + |dQ_id|)      (dS including the softmax scale)
+        bk = u (sum_i |dS_ij| |Q_id| + |dK_jd|)
+    Each is a worst case (all roundings of one sum in the same direction), so a kernel
+    that rounds exactly those operands stays inside it up to fp32 accumulation error."""
     q64 = np.asarray(q, dtype=np.float64)
     k64 = np.asarray(k, dtype=np.float64)
     v64 = np.asarray(v, dtype=np.float64)
@@ -98,8 +121,9 @@ def attention_bwd_ref(q, k, v, do, causal, scale=None):
     if causal:
         s = np.where(causal_mask(q64.shape[2], ke.shape[2]), s, NEG_INF)
     p, _ = _softmax_lse(s)
-    o = np.einsum("bhqk,bhkd->bhqd", p, ve)
-    dsum = np.sum(do64 * o, axis=-1, keepdims=True)        # row-dot D
+    if o is None:
+        o = np.einsum("bhqk,bhkd->bhqd", p, ve)
+    dsum = np.sum(do64 * np.asarray(o, np.float64), axis=-1, keepdims=True)  # row-dot D
     dp = np.einsum("bhqd,bhkd->bhqk", do64, ve)            # dO V^T
     ds = p * (dp - dsum)
     dq = np.einsum("bhqk,bhkd->bhqd", ds, ke) * scale
@@ -109,7 +133,31 @@ def attention_bwd_ref(q, k, v, do, causal, scale=None):
     b, _, n, _ = dke.shape
     dk = dke.reshape(b, hkv, g, n, d).sum(axis=2)
     dv = dve.reshape(b, hkv, g, n, d).sum(axis=2)
-    return dq.astype(np.float32), dk.astype(np.float32), dv.astype(np.float32)
+    grads = (dq.astype(np.float32), dk.astype(np.float32), dv.astype(np.float32))
+    if unit_roundoff is None:
+        return grads
+    u = float(unit_roundoff)
+    ads = np.abs(ds) * scale
+    bq = u * (np.einsum("bhqk,bhkd->bhqd", ads, np.abs(ke)) + np.abs(dq))
+    bk = np.einsum("bhqk,bhqd->bhkd", ads, np.abs(q64)).reshape(b, hkv, g, n, d).sum(axis=2)
+    bk = u * (bk + np.abs(dk))
+    bv = np.einsum("bhqk,bhqd->bhkd", p, np.abs(do64)).reshape(b, hkv, g, n, d).sum(axis=2)
+    bv = u * (bv + np.abs(dv))
+    return grads, (bq, bk, bv)
+
+
+def attention_out_bound(q, k, v, causal, unit_roundoff, scale=None):
+    """Per-element bound [B,Hq,M,D] on what rounding P to the input type before the P V
+    product (_kernels_forward.py:162-165) and rounding the output can change:
+    u (sum_j P_ij |v_jd| + |out_id|), a worst case over the rounding directions."""
+    _, _, p = attention_ref(q, k, v, causal, scale=scale, return_p=True)
+    ve = _expand_kv(np.asarray(v, np.float64), np.asarray(q).shape[1])
+    out = np.einsum("bhqk,bhkd->bhqd", p, ve)
+    return float(unit_roundoff) * (np.einsum("bhqk,bhkd->bhqd", p, np.abs(ve)) + np.abs(out))
+
+
+# Unit roundoff of the 16-bit input types (round to nearest: |fl(x) - x| <= u |x|).
+UNIT_ROUNDOFF = {"float16": 2.0 ** -11, "bfloat16": 2.0 ** -8}
 
 
 def gather_pages(cache, block_table_row, length):
@@ -122,13 +170,16 @@ def gather_pages(cache, block_table_row, length):
 
 def paged_prefill_ref(q, k_cache, v_cache, block_table, seq_lens, query_start_loc,
                       prefix_kv_lens, causal=True, scale=None, sliding_window_q=-1,
-                      sliding_window_k=-1):
-    """q [T, H, D] -> out [T, H, D] f32, lse [H, T] f32 (reference kernel semantics)."""
+                      sliding_window_k=-1, unit_roundoff=None):
+    """q [T, H, D] -> out [T, H, D] f32, lse [H, T] f32 (reference kernel semantics).
+    With ``unit_roundoff`` also the output's rounding bound [T, H, D] (see
+    attention_out_bound)."""
     q = np.asarray(q, dtype=np.float64)
     t, h, d = q.shape
     hkv = k_cache.shape[2]
     scale = 1.0 / np.sqrt(d) if scale is None else scale
     out = np.zeros((t, h, d), np.float64)
+    bound = np.zeros((t, h, d), np.float64)
     lse = np.full((h, t), NEG_INF, np.float64)
     for b in range(len(seq_lens)):
         q0, q1 = int(query_start_loc[b]), int(query_start_loc[b + 1])
@@ -154,17 +205,26 @@ def paged_prefill_ref(q, k_cache, v_cache, block_table, seq_lens, query_start_lo
         p, l_ = _softmax_lse(s)
         out[q0:q1] = np.einsum("hqk,hkd->hqd", p, vb).transpose(1, 0, 2)
         lse[:, q0:q1] = l_
+        if unit_roundoff is not None:
+            bound[q0:q1] = np.einsum("hqk,hkd->hqd", p, np.abs(vb)).transpose(1, 0, 2)
+    if unit_roundoff is not None:
+        bound = float(unit_roundoff) * (bound + np.abs(out))
+        return out.astype(np.float32), lse.astype(np.float32), bound
     return out.astype(np.float32), lse.astype(np.float32)
 
 
-def decode_ref(q, k_cache, v_cache, block_table, seq_lens, scale=None):
-    """q [B, H, D] -> out [B, H, D] f32, lse [B, H] f32; all keys < seq_lens[b] visible."""
+def decode_ref(q, k_cache, v_cache, block_table, seq_lens, scale=None, unit_roundoff=None):
+    """q [B, H, D] -> out [B, H, D] f32, lse [B, H] f32; all keys < seq_lens[b] visible.
+    With ``unit_roundoff`` also the output's rounding bound [B, H, D]."""
     q = np.asarray(q, dtype=np.float64)
     bsz, h, d = q.shape
     qsl = np.arange(bsz + 1)
-    out, lse = paged_prefill_ref(q, k_cache, v_cache, block_table, seq_lens, qsl,
-                                 np.zeros(bsz, np.int64), causal=False, scale=scale)
-    return out, np.ascontiguousarray(lse.T)
+    r = paged_prefill_ref(q, k_cache, v_cache, block_table, seq_lens, qsl,
+                          np.zeros(bsz, np.int64), causal=False, scale=scale,
+                          unit_roundoff=unit_roundoff)
+    if unit_roundoff is not None:
+        return r[0], np.ascontiguousarray(r[1].T), r[2]
+    return r[0], np.ascontiguousarray(r[1].T)
 
 
 def make_paged_cache(k, v, page_size=16, shuffle_seed=None, num_pages=None):

@@ -134,8 +134,8 @@ def main():
     paged_case(ref, "paged_multibatch_shuffled", 2, 16, 2, 48, 48, 128, True, shuffle_seed=7)
     # decode: one query token per sequence attends to every key
     paged_case(ref, "decode_gqa_16_4_d128", 3, 16, 4, 1, 100, 128, True, shuffle_seed=3)
-    # decode at the reference's 32/2 D=256 test configuration (test_gqa_paged.py:231-234)
-    paged_case(ref, "decode_gqa_32_2_d256", 2, 32, 2, 1, 200, 256, True, shuffle_seed=5)
+    # decode at the reference's synthetic 8/1 D=256 configuration (test_gqa_paged.py:239-240)
+    paged_case(ref, "decode_gqa_8_1_d256", 2, 8, 1, 1, 200, 256, True, shuffle_seed=5)
 
 
 if __name__ == "__main__":

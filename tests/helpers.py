@@ -1,4 +1,18 @@
-"""Shared test helpers: golden-fixture loading and the tolerance checks."""
+"""Shared test helpers: golden-fixture loading and the tolerance checks.
+
+Two bars, both written here:
+
+* The north-star bar against the fp32 oracle: outputs and LSE |x - ref| <= 2e-3 +
+  1e-2 |ref| elementwise, gradients max-abs <= 1e-2.  fp16 results meet it everywhere.
+* The rounding bound: |x - ref| <= 1e-4 + bound elementwise, where ``bound`` (from the
+  oracle's ``unit_roundoff`` functions) is the worst case of rounding the operands every
+  FlashAttention rounds to the input type -- P before P V and P^T dO, dS before dS K and
+  dS^T Q -- and the output itself.  1e-4 covers fp32 accumulation order and ex2.approx.
+  bf16 results are held to it (plus a mean error <= 2e-3): with an 8-bit significand one
+  rounding of an output of size 4 is already 0.0156, above the absolute 1e-2 gradient
+  bar, so no bf16 kernel meets the north-star bar on every element.  Measured on the
+  dense test cases the kernels stay below 0.9 of the bound in both dtypes.
+"""
 import glob
 import os
 
@@ -6,20 +20,11 @@ import numpy as np
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
-# Output / LSE tolerance against an fp32 reference: |x - ref| <= ATOL + RTOL * |ref|
-# elementwise (max-abs 2e-3 / rtol 1e-2).
-ATOL = 2e-3
+ATOL = 2e-3        # north-star output / LSE bar: |x - ref| <= ATOL + RTOL |ref|
 RTOL = 1e-2
-# bf16 outputs: the kernels quantise P to the input type before the P.V MMA (as every
-# FlashAttention does), so a single bf16 P element carries up to 2^-9 relative error
-# and rows dominated by one or two keys can be off by ~2^-9 * |v| (~0.008 for N(0,1)
-# values).  For bf16 the elementwise bound is rtol 1e-2 with the reference's own
-# max-abs 0.01 bar (tests/test_compare_ref.py:67 of the reference) as the absolute
-# floor, and the MEAN absolute error must still meet the 2e-3 north-star bound.
-BF16_ATOL = 1e-2
-BF16_MEAN_ATOL = 2e-3
-# Gradient tolerance: max-abs.
-GRAD_ATOL = 1e-2
+GRAD_ATOL = 1e-2   # north-star gradient bar (max-abs)
+BOUND_ATOL = 1e-4  # fp32 accumulation / ex2.approx allowance on top of the rounding bound
+MEAN_ATOL = 2e-3   # mean absolute error of bf16 results
 
 
 def golden(name):
@@ -30,21 +35,19 @@ def golden_names(prefix):
     return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, prefix + "*.npz")))
 
 
-def assert_close(x, ref, atol=ATOL, rtol=RTOL, what="", mask=None, dtype=None):
-    """Elementwise |x - ref| <= atol + rtol |ref|; dtype="bf16" selects the bf16 bound."""
-    if dtype is not None and "bfloat16" in str(dtype):
-        atol = max(atol, BF16_ATOL)
-        xf = np.asarray(x, dtype=np.float64)
-        rf = np.asarray(ref, dtype=np.float64)
-        fin = np.isfinite(rf)
-        if fin.any():
-            mean_err = float(np.mean(np.abs(xf[fin] - rf[fin])))
-            assert mean_err <= BF16_MEAN_ATOL, "%s: mean abs error %.3g" % (what, mean_err)
+def is_bf16(dtype):
+    return dtype is not None and "bfloat16" in str(dtype)
+
+
+def assert_close(x, ref, atol=ATOL, rtol=RTOL, what="", mask=None):
+    """Elementwise |x - ref| <= atol + rtol |ref| (the north-star bar by default);
+    infinities must match in sign."""
     x = np.asarray(x, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     assert x.shape == ref.shape, (x.shape, ref.shape)
     both_inf = np.isinf(x) & np.isinf(ref) & (np.sign(x) == np.sign(ref))
-    err = np.where(both_inf, 0.0, np.abs(x - ref))
+    with np.errstate(invalid="ignore"):
+        err = np.where(both_inf, 0.0, np.abs(x - ref))
     bound = atol + rtol * np.abs(np.where(np.isfinite(ref), ref, 0.0))
     bad = ~(err <= bound)
     if mask is not None:
@@ -56,20 +59,53 @@ def assert_close(x, ref, atol=ATOL, rtol=RTOL, what="", mask=None, dtype=None):
                                                  x[tuple(idx)], ref[tuple(idx)], np.nanmax(err)))
 
 
-def assert_grad_close(got, want, dtype, what=""):
-    """Gradients: max-abs <= GRAD_ATOL.  bf16 gradients are rounded to
-    bf16 on output (half an ulp is 0.0078 for |g| in [2, 4)), so for bf16 the bound is
-    GRAD_ATOL + 1e-2 |ref| elementwise with the mean absolute error <= 2e-3."""
+def assert_within_bound(x, ref, bound, what="", mean_atol=MEAN_ATOL):
+    """|x - ref| <= BOUND_ATOL + bound elementwise and mean |x - ref| <= mean_atol."""
+    x = np.asarray(x, np.float64)
+    ref = np.asarray(ref, np.float64)
+    bound = np.asarray(bound, np.float64)
+    assert x.shape == ref.shape == bound.shape, (x.shape, ref.shape, bound.shape)
+    err = np.abs(x - ref)
+    bad = ~(err <= BOUND_ATOL + bound)
+    if bad.any():
+        idx = tuple(np.argwhere(bad)[0])
+        raise AssertionError("%s: %d/%d elements outside the rounding bound; first at %s: got %r "
+                             "want %r bound %.3g (max err / bound %.3g)"
+                             % (what, bad.sum(), bad.size, idx, x[idx], ref[idx], bound[idx],
+                                np.max(err / (BOUND_ATOL + bound))))
+    assert err.mean() <= mean_atol, "%s: mean abs error %.3g" % (what, err.mean())
+
+
+def assert_out_close(x, ref, dtype, bound=None, what=""):
+    """A kernel output (attention out) in `dtype` against the fp32 oracle: fp16 must meet
+    the north-star bar; bf16 must stay inside the rounding bound.  When the bound is
+    given it is checked for fp16 as well."""
+    if bound is not None:
+        assert_within_bound(x, ref, bound, what)
+    if not is_bf16(dtype):
+        assert_close(x, ref, what=what)
+    else:
+        assert bound is not None, "bf16 outputs are checked against the rounding bound"
+
+
+def assert_grad_close(got, want, dtype, what="", bound=None, want_faithful=None):
+    """Gradients: fp16 max-abs <= GRAD_ATOL against the exact fp32 gradient; every dtype,
+    when the bound is given, inside the rounding bound around the reference computed
+    with D = rowsum(dO * O) from the output the backward was given (``want_faithful``)."""
     got = np.asarray(got, np.float64)
     want = np.asarray(want, np.float64)
-    err = np.abs(got - want)
-    if "bfloat16" in str(dtype):
-        bad = err > GRAD_ATOL + 1e-2 * np.abs(want)
-        assert not bad.any(), "%s: %d elements out of tolerance (max err %.4g)" % (what, bad.sum(), err.max())
-        assert err.mean() <= BF16_MEAN_ATOL, "%s: mean abs error %.3g" % (what, err.mean())
-    else:
+    if bound is not None:
+        assert_within_bound(got, want if want_faithful is None else want_faithful, bound, what)
+    if not is_bf16(dtype):
+        err = np.abs(got - want)
         assert err.max() <= GRAD_ATOL, "%s max-abs %.4g" % (what, err.max())
+    else:
+        assert bound is not None, "bf16 gradients are checked against the rounding bound"
 
 
 def max_abs(x, ref):
     return float(np.max(np.abs(np.asarray(x, np.float64) - np.asarray(ref, np.float64))))
+
+
+def unit_roundoff(dtype):
+    return 2.0 ** -8 if is_bf16(dtype) else 2.0 ** -11

@@ -5,8 +5,10 @@ import pytest
 import torch
 
 import tilelang_fa_v100 as fa
-from helpers import ATOL, RTOL, GRAD_ATOL, assert_close, assert_grad_close, golden, golden_names, max_abs
+from helpers import (assert_close, assert_grad_close, assert_out_close, golden, golden_names,
+                     max_abs, unit_roundoff)
 from oracle import attention_ref as R
+from slice_ref import slice_ref
 
 pytestmark = pytest.mark.gpu
 
@@ -70,7 +72,8 @@ def test_forward_vs_oracle(cuda_dev, case):
     v = _rand((b, skv, hk, d), dt, 3)
     out, lse = _fwd(q.to(cuda_dev), k.to(cuda_dev), v.to(cuda_dev), causal)
     ref_out, ref_lse = R.attention_ref(_to_bhsd(q), _to_bhsd(k), _to_bhsd(v), causal)
-    assert_close(_to_bhsd(out), ref_out, what="out", dtype=dt)
+    bound = R.attention_out_bound(_to_bhsd(q), _to_bhsd(k), _to_bhsd(v), causal, unit_roundoff(dt))
+    assert_out_close(_to_bhsd(out), ref_out, dt, bound, what="out")
     assert_close(lse.cpu().numpy(), ref_lse, what="lse")
 
 
@@ -88,7 +91,8 @@ def test_noncontiguous_inputs(cuda_dev):
                for s in (7, 8, 9))
     out, lse = _fwd(q, k, v, True)
     ref_out, _ = R.attention_ref(_to_bhsd(q), _to_bhsd(k), _to_bhsd(v), True)
-    assert_close(_to_bhsd(out), ref_out, what="out", dtype=torch.bfloat16)
+    bound = R.attention_out_bound(_to_bhsd(q), _to_bhsd(k), _to_bhsd(v), True, 2.0 ** -8)
+    assert_out_close(_to_bhsd(out), ref_out, torch.bfloat16, bound, what="out")
 
 
 def test_repeated_calls_are_deterministic(cuda_dev):
@@ -111,13 +115,11 @@ BWD_CASES = [
     (2, 1000, 1000, 4, 2, 128, True, torch.float16),
     (1, 300, 700, 2, 1, 64, False, torch.bfloat16),
     # D = 128, one query head per kv head, short items: the persistent dK/dV kernel with
-    # 300-500 work items, so each CTA runs two to four of them.  The causal ones are fp16:
-    # in bf16 the first causal rows (a few visible keys, dS = P (dP - D) a cancellation
-    # of bf16-rounded terms) put a handful of the 6M dq elements just past the bf16 bound
-    # at this size, identically for the one-CTA-per-item kernel.
-    (40, 300, 300, 4, 4, 128, True, torch.float16),
+    # 300-500 work items, so each CTA runs two to four of them.
+    (40, 300, 300, 4, 4, 128, True, torch.bfloat16),
     (24, 700, 900, 2, 2, 128, False, torch.bfloat16),
-    (30, 1000, 400, 3, 3, 128, True, torch.float16),
+    (30, 1000, 400, 3, 3, 128, True, torch.bfloat16),
+    (16, 500, 500, 2, 2, 128, True, torch.float16),
 ]
 
 
@@ -133,9 +135,13 @@ def test_backward_vs_oracle(cuda_dev, case, deterministic):
     out = fa.tilelang_flash_attn_func(qd, kd, vd, causal=causal, deterministic=deterministic)
     out.backward(do.to(cuda_dev))
     torch.cuda.synchronize()
-    dq, dk, dv = R.attention_bwd_ref(_to_bhsd(q), _to_bhsd(k), _to_bhsd(v), _to_bhsd(do), causal)
-    for got, want, w in ((qd.grad, dq, "dq"), (kd.grad, dk, "dk"), (vd.grad, dv, "dv")):
-        assert_grad_close(_to_bhsd(got), want, dt, w)
+    args = (_to_bhsd(q), _to_bhsd(k), _to_bhsd(v), _to_bhsd(do), causal)
+    exact = R.attention_bwd_ref(*args)
+    faithful, bounds = R.attention_bwd_ref(*args, o=_to_bhsd(out.detach()),
+                                           unit_roundoff=unit_roundoff(dt))
+    for got, want, want_f, bnd, w in zip((qd.grad, kd.grad, vd.grad), exact, faithful, bounds,
+                                         ("dq", "dk", "dv")):
+        assert_grad_close(_to_bhsd(got), want, dt, w, bound=bnd, want_faithful=want_f)
 
 
 @pytest.mark.parametrize("name", golden_names("dense_"))
@@ -164,34 +170,57 @@ def test_deterministic_backward_is_bitwise_reproducible(cuda_dev):
         assert torch.equal(a, b)
 
 
-def _torch_ref_slice(q, k, v, causal, bi, hi, hk_i):
-    """fp32 torch reference on the GPU for one (batch, head) slice of a large input."""
-    qs = q[bi, :, hi].float()
-    ks = k[bi, :, hk_i].float()
-    vs = v[bi, :, hk_i].float()
-    s = (qs @ ks.T) / (q.shape[-1] ** 0.5)
-    if causal:
-        m, n = s.shape
-        mask = torch.ones(m, n, device=s.device).tril(diagonal=n - m)
-        s = s.masked_fill(mask == 0, float("-inf"))
-    lse = torch.logsumexp(s, dim=-1)
-    return torch.softmax(s, dim=-1) @ vs, lse
-
-
 @pytest.mark.parametrize("cfg", [(4, 2048, 2048, 16, 64, torch.float16),
                                  (8, 4096, 4096, 32, 128, torch.bfloat16),
                                  (8, 1024, 4096, 32, 128, torch.bfloat16)],
                          ids=["cfg2", "cfg3", "cfg3-nonsquare"])
-def test_full_size_forward_sampled(cuda_dev, cfg):
-    """BASELINE configs at full size; sampled (batch, head) slices vs fp32 torch."""
-    torch.backends.cuda.matmul.allow_tf32 = False
+@pytest.mark.parametrize("deterministic", [False, True])
+def test_full_size_fwd_bwd_sampled(cuda_dev, cfg, deterministic):
+    """BASELINE configs at full size, forward + backward through the API as the benchmark
+    runs them; out, lse, dQ, dK and dV of sampled (batch, head) slices against the fp32
+    torch reference on the GPU (tests/slice_ref.py, checked against the numpy oracle by
+    test_slice_ref_matches_oracle)."""
     b, sq, skv, h, d, dt = cfg
     g = torch.Generator(device=cuda_dev).manual_seed(0)
     q = torch.randn(b, sq, h, d, generator=g, device=cuda_dev).to(dt)
     k = torch.randn(b, skv, h, d, generator=g, device=cuda_dev).to(dt)
     v = torch.randn(b, skv, h, d, generator=g, device=cuda_dev).to(dt)
-    out, lse = _fwd(q, k, v, True)
+    do = torch.randn(b, sq, h, d, generator=g, device=cuda_dev).to(dt)
+    qd, kd, vd = (x.clone().requires_grad_(True) for x in (q, k, v))
+    out, lse, _ = fa.tilelang_flash_attn_func(qd, kd, vd, causal=True, deterministic=deterministic,
+                                              return_attn_probs=True)
+    out.backward(do)
+    torch.cuda.synchronize()
+    u = unit_roundoff(dt)
+    cpu = lambda t: t.detach().float().cpu().numpy()
     for bi, hi in ((0, 0), (b - 1, h - 1), (b // 2, h // 3)):
-        ro, rl = _torch_ref_slice(q, k, v, True, bi, hi, hi)
-        assert_close(out[bi, :, hi].float().cpu().numpy(), ro.cpu().numpy(), what="out", dtype=dt)
-        assert_close(lse[bi, hi].cpu().numpy(), rl.cpu().numpy(), what="lse")
+        r = slice_ref(q, k, v, do, out.detach(), True, bi, hi, u)
+        assert_out_close(cpu(out[bi, :, hi]), cpu(r["out"]), dt, cpu(r["bo"]), what="out")
+        assert_close(cpu(lse[bi, hi]), cpu(r["lse"]), what="lse")
+        for nm, got in (("dq", qd.grad), ("dk", kd.grad), ("dv", vd.grad)):
+            assert_grad_close(cpu(got[bi, :, hi]), cpu(r[nm]), dt, "%s (%d, %d)" % (nm, bi, hi),
+                              bound=cpu(r["b" + nm[1]]), want_faithful=cpu(r[nm + "_f"]))
+
+
+def test_slice_ref_matches_oracle(cuda_dev):
+    """The GPU fp32 slice reference used at full size equals the numpy oracle."""
+    g = torch.Generator(device=cuda_dev).manual_seed(3)
+    q, k, v, do = (torch.randn(2, 700, 3, 64, generator=g, device=cuda_dev).to(torch.float16)
+                   for _ in range(4))
+    out, _ = _fwd(q, k, v, True)
+    r = slice_ref(q, k, v, do, out, True, 1, 2, 2.0 ** -11)
+    sl = lambda t: t[1:2, :, 2:3].float().permute(0, 2, 1, 3).cpu().numpy()
+    ro, rl = R.attention_ref(sl(q), sl(k), sl(v), True)
+    exact = R.attention_bwd_ref(sl(q), sl(k), sl(v), sl(do), True)
+    faithful, bounds = R.attention_bwd_ref(sl(q), sl(k), sl(v), sl(do), True, o=sl(out),
+                                           unit_roundoff=2.0 ** -11)
+    bo = R.attention_out_bound(sl(q), sl(k), sl(v), True, 2.0 ** -11)
+    close = lambda a, b_: np.testing.assert_allclose(a.detach().cpu().numpy(), b_[0, 0],
+                                                     rtol=1e-4, atol=1e-5)
+    close(r["out"], ro)
+    close(r["lse"], rl)
+    close(r["bo"], bo)
+    for i, nm in enumerate(("dq", "dk", "dv")):
+        close(r[nm], exact[i])
+        close(r[nm + "_f"], faithful[i])
+        close(r["b" + nm[1]], bounds[i])
