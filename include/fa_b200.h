@@ -11,8 +11,9 @@
  *   cache  [num_pages, page_size, Hkv, D]          (vLLM paged KV cache)
  *   paged  q/out [num_tokens, H, D], lse [H, num_tokens] fp32
  *   decode q/out [B, H, D]
- * Supported: fp16 and bf16 inputs, H % Hk == 0; head_dim 64/128/256 (dense
- * forward, paged prefill, decode with H / Hkv <= 16), 64/128 (dense backward).
+ * Supported: fp16 and bf16 inputs, H % Hk == 0; head_dim 32/64/96/128/256 (dense
+ * forward and backward; 32 and 96 run the 64 and 128 kernels on zero-filled columns),
+ * 64/128/256 (paged prefill, decode with H / Hkv <= 16).
  * Pointers 16-byte aligned, strides multiples of 8 elements.
  */
 #ifndef FA_B200_H_
@@ -63,7 +64,8 @@ int fa_fwd(const fa_fwd_args_t* args, void* stream);
  * row-dot (:203), the dQ kernel (:10-85) and the dK/dV kernel (:88-176).
  * Gradients are written in the BSHD layout of q/k/v.  Workspace (caller-owned,
  * fa_bwd_workspace_size bytes, 256-byte aligned): the fp32 row-dot [B,H,Sq] and,
- * in atomic mode, the fp32 dQ accumulator [B,H,Sq,D]. */
+ * in atomic mode at head_dim 64/128, the fp32 dQ accumulator [B,H,Sq,D].  At head_dim
+ * 256 both modes run the same atomic-free kernels (bit-reproducible). */
 typedef struct {
   const void* q;
   const void* k;

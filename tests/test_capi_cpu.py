@@ -99,8 +99,9 @@ def test_unsupported_head_dim_rejected_on_host():
     lib = _ext.load()
     a = _ext.FwdArgs(1, 1, 1, 1, 1)
     a.batch, a.seqlen_q, a.seqlen_k, a.num_heads, a.num_heads_k = 1, 8, 8, 2, 2
-    a.head_dim, a.dtype = 96, 0
-    assert lib.fa_fwd(ctypes.byref(a), None) == _ext.FA_ERR_UNSUPPORTED
+    for d in (16, 48, 80, 192, 512):  # dense head dims are 32 / 64 / 96 / 128 / 256
+        a.head_dim, a.dtype = d, 0
+        assert lib.fa_fwd(ctypes.byref(a), None) == _ext.FA_ERR_UNSUPPORTED
     a.head_dim, a.num_heads_k = 64, 3  # H % Hk != 0
     assert lib.fa_fwd(ctypes.byref(a), None) == _ext.FA_ERR_INVALID_ARG
 

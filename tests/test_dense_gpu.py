@@ -61,6 +61,12 @@ FWD_CASES = [
     (1, 4200, 4100, 2, 2, 128, True, torch.float16),    # Sq > Skv
     (1, 2000, 2000, 8, 2, 128, False, torch.float16),   # GQA 4:1, non-causal
     (1, 1700, 1700, 2, 2, 256, False, torch.bfloat16),  # D = 256 non-causal
+    # head_dim 32 / 96 on the 64 / 128 kernels (zero-filled columns, clipped stores)
+    (2, 300, 300, 4, 2, 32, True, torch.bfloat16),
+    (1, 200, 520, 2, 2, 32, False, torch.float16),
+    (1, 1000, 1000, 4, 4, 96, True, torch.float16),
+    (2, 77, 300, 8, 1, 96, True, torch.bfloat16),
+    (1, 2500, 2500, 2, 2, 96, True, torch.bfloat16),   # long items: one-CTA-per-item kernel
 ]
 
 
@@ -120,6 +126,18 @@ BWD_CASES = [
     (24, 700, 900, 2, 2, 128, False, torch.bfloat16),
     (30, 1000, 400, 3, 3, 128, True, torch.bfloat16),
     (16, 500, 500, 2, 2, 128, True, torch.float16),
+    # D = 256: split-D dK / dV kernel + dQ kernel (64-query / 64-key steps)
+    (1, 200, 200, 2, 2, 256, True, torch.bfloat16),
+    (1, 300, 520, 4, 2, 256, False, torch.float16),    # GQA 2:1, non-causal, ragged
+    (2, 130, 90, 2, 2, 256, True, torch.float16),      # Sq > Skv: leading rows fully masked
+    (1, 1000, 1000, 2, 2, 256, True, torch.bfloat16),  # several KV tiles and query steps
+    (3, 64, 300, 8, 1, 256, True, torch.bfloat16),     # MQA 8:1, non-square causal
+    # head_dim 32 / 96 on the 64 / 128 kernels
+    (1, 300, 300, 4, 2, 32, True, torch.bfloat16),
+    (2, 200, 333, 2, 2, 32, False, torch.float16),
+    (1, 700, 700, 2, 2, 96, True, torch.float16),
+    (6, 300, 300, 2, 2, 96, True, torch.bfloat16),     # persistent dK/dV kernel
+    (1, 190, 250, 4, 1, 96, False, torch.bfloat16),
 ]
 
 

@@ -78,6 +78,7 @@ struct BwdCfg {
 
 struct BwdParams {
   int B, Sq, Skv, H, Hk, G, Sq_pad;
+  int d_real;  // the caller's head_dim (32 / 96 run the 64 / 128 kernels)
   int causal;
   int n_t, n_u, n_items;  // KV tiles per (batch, kv head), B * Hk units, n_t * n_u items
   float scale, scale_log2;
@@ -123,6 +124,17 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
     if (globaltimer_ns() - t0 > 200000000ull) return;
 }
 
+// Stores up to 32 16-bit values (four 16-byte units) of a gradient row; units at or past
+// `cols` (the head dims left in the row) are skipped: head_dim 32 / 96 run the 64 / 128
+// kernels, whose extra columns hold zeros that belong to no tensor.
+template <typename T>
+__device__ __forceinline__ void store_units(T* dst, const uint32_t* pk, int cols) {
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+    if (8 * u < cols) d4[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+}
+
 // ---------------------------------------------------------------- 1. preprocess
 // D / 8 lanes per row (16-byte loads), 32 / (D / 8) rows per warp and pass, kPrepPasses
 // passes per warp with every load issued before the arithmetic.  With a dQ accumulator
@@ -137,7 +149,7 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const T* __restrict__ 
                                                           int B, int Sq, int H, int Sq_pad,
                                                           int64_t o_sb, int64_t o_ss, int64_t o_sh,
                                                           int64_t do_sb, int64_t do_ss,
-                                                          int64_t do_sh) {
+                                                          int64_t do_sh, int d_real) {
   constexpr int TPR = D / 8;
   constexpr int RPW = 32 / TPR;
   const int lane = threadIdx.x & 31;
@@ -154,7 +166,7 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const T* __restrict__ 
     const int64_t bh = row / Sq_pad;
     live[ps] = row < rows && i < Sq;
     av[ps] = dv[ps] = make_uint4(0u, 0u, 0u, 0u);
-    if (live[ps]) {
+    if (live[ps] && cl * 8 < d_real) {
       const int h = (int)(bh % H), b = (int)(bh / H);
       av[ps] = __ldcs(reinterpret_cast<const uint4*>(o + b * o_sb + (int64_t)i * o_ss +
                                                      (int64_t)h * o_sh) + cl);
@@ -202,12 +214,13 @@ template <typename T, int D>
 __global__ void __launch_bounds__(256) fa_bwd_dq_convert_kernel(const float* __restrict__ acc,
                                                                 T* dq, int B, int Sq, int H,
                                                                 int Sq_pad, int64_t sb,
-                                                                int64_t ss, int64_t sh) {
+                                                                int64_t ss, int64_t sh,
+                                                                int d_real) {
   const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;  // one thread per 4 elements
-  const int64_t total = (int64_t)B * H * Sq * (D / 4);
+  const int64_t total = (int64_t)B * H * Sq * (d_real / 4);
   if (idx >= total) return;
-  const int c4 = idx % (D / 4);
-  const int64_t row = idx / (D / 4);
+  const int c4 = idx % (d_real / 4);
+  const int64_t row = idx / (d_real / 4);
   const int h = row % H;
   const int64_t bi = row / H;
   const int i = bi % Sq;
@@ -616,13 +629,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           for (int x = 0; x < 16; ++x)
             pk[x] = n_iter > 0 ? Pack2<T>::pack(__uint_as_float(v[2 * x]), __uint_as_float(v[2 * x + 1]))
                                : 0u;
-          if (key_ok) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
-            d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-            d4[2] = make_uint4(pk[8], pk[9], pk[10], pk[11]);
-            d4[3] = make_uint4(pk[12], pk[13], pk[14], pk[15]);
-          }
+          if (key_ok) store_units<T>(dst + c0, pk, p.d_real - (c * (D / 2) + c0));
         }
       }
     }
@@ -1134,13 +1141,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           for (int x = 0; x < 16; ++x)
             pk[x] = n_iter > 0 ? Pack2<T>::pack(__uint_as_float(v[2 * x]), __uint_as_float(v[2 * x + 1]))
                                : 0u;
-          if (key_ok) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
-            d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-            d4[2] = make_uint4(pk[8], pk[9], pk[10], pk[11]);
-            d4[3] = make_uint4(pk[12], pk[13], pk[14], pk[15]);
-          }
+          if (key_ok) store_units<T>(dst + c0, pk, p.d_real - (c * (D / 2) + c0));
         }
       }
     }
@@ -1454,13 +1455,7 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
         for (int x = 0; x < 16; ++x)
           pk[x] = nkv > 0 ? Pack2<T>::pack(__uint_as_float(v[2 * x]), __uint_as_float(v[2 * x + 1])) : 0u;
-        if (q_ok) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
-          d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-          d4[2] = make_uint4(pk[8], pk[9], pk[10], pk[11]);
-          d4[3] = make_uint4(pk[12], pk[13], pk[14], pk[15]);
-        }
+        if (q_ok) store_units<T>(dst + c0, pk, p.d_real - (c * (D / 2) + c0));
       }
     }
   }
@@ -1475,10 +1470,15 @@ __global__ void __launch_bounds__(384, 1)
 // ------------------------------------------------------------------- host side
 static int pad128(int x) { return (x + 127) / 128 * 128; }
 
+// head_dim 32 / 96 run the 64 / 128 kernels (TMA zero-fills the missing columns on
+// load; the prep kernel and the gradient stores stop at the real head_dim).
+static int bwd_kernel_dim(int d) { return d == 32 ? 64 : (d == 96 ? 128 : d); }
+
 size_t bwd_workspace_bytes(const fa_bwd_args_t* a) {
   const size_t rows = (size_t)a->batch * a->num_heads * pad128(a->seqlen_q);
   size_t n = 2 * (rows * 4 + 256);                         // lse2, dsum
-  if (!a->deterministic) n += rows * a->head_dim * 4 + 256;  // dQ accumulator
+  // dQ accumulator (atomic mode at D = 64 / 128; the D = 256 kernels write dQ directly)
+  if (!a->deterministic && a->head_dim != 256) n += rows * bwd_kernel_dim(a->head_dim) * 4 + 256;
   return n + 256;
 }
 
@@ -1507,22 +1507,27 @@ static bool bwd_persistent(const BwdParams& p) {
   return avg_steps <= kBwdPersistMaxSteps;
 }
 
+// Row dot D = rowsum(O * dO), lse * log2 e and (atomic mode) the cleared dQ accumulator.
+template <typename T, int D>
+static int launch_bwd_prep(const fa_bwd_args_t* a, const BwdParams& p, cudaStream_t st) {
+  const int64_t rows = (int64_t)a->batch * a->num_heads * p.Sq_pad;
+  const int64_t rows_per_block = 8 * (32 / (D / 8)) * kPrepPasses;
+  const int blocks = (int)((rows + rows_per_block - 1) / rows_per_block);
+  fa_bwd_prep_kernel<T, D><<<blocks, 256, 0, st>>>(
+      reinterpret_cast<const T*>(a->out), reinterpret_cast<const T*>(a->dout), a->lse,
+      const_cast<float*>(p.lse2), const_cast<float*>(p.dsum), p.dq_acc, a->batch, a->seqlen_q,
+      a->num_heads, p.Sq_pad, a->o_stride[0], a->o_stride[1], a->o_stride[2], a->do_stride[0],
+      a->do_stride[1], a->do_stride[2], p.d_real);
+  FA_CUDA_TRY(cudaGetLastError());
+  count_launch();
+  return FA_OK;
+}
+
 template <typename T, int D>
 static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const CUtensorMap& tk,
                            const CUtensorMap& tv, const CUtensorMap& tdo, BwdParams& p,
                            cudaStream_t st) {
-  {
-    const int64_t rows = (int64_t)a->batch * a->num_heads * p.Sq_pad;
-    const int64_t rows_per_block = 8 * (32 / (D / 8)) * kPrepPasses;
-    const int blocks = (int)((rows + rows_per_block - 1) / rows_per_block);
-    fa_bwd_prep_kernel<T, D><<<blocks, 256, 0, st>>>(
-        reinterpret_cast<const T*>(a->out), reinterpret_cast<const T*>(a->dout), a->lse,
-        const_cast<float*>(p.lse2), const_cast<float*>(p.dsum), p.dq_acc, a->batch, a->seqlen_q,
-        a->num_heads, p.Sq_pad, a->o_stride[0], a->o_stride[1], a->o_stride[2], a->do_stride[0],
-        a->do_stride[1], a->do_stride[2]);
-    FA_CUDA_TRY(cudaGetLastError());
-    count_launch();
-  }
+  if (int s = launch_bwd_prep<T, D>(a, p, st)) return s;
   if (!a->deterministic && bwd_persistent<D>(p)) {
     auto kern = fa_bwd_dkdv_persist_kernel<T, 128, true>;
     static std::atomic<bool> attr[kMaxContexts];
@@ -1539,10 +1544,10 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
     prof_end(FA_PROF_BWD_DKDV, st);
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
-    const int64_t n4 = (int64_t)a->batch * a->num_heads * a->seqlen_q * (D / 4);
+    const int64_t n4 = (int64_t)a->batch * a->num_heads * a->seqlen_q * (p.d_real / 4);
     fa_bwd_dq_convert_kernel<T, D><<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(
         p.dq_acc, reinterpret_cast<T*>(a->dq), a->batch, a->seqlen_q, a->num_heads, p.Sq_pad,
-        a->dq_stride[0], a->dq_stride[1], a->dq_stride[2]);
+        a->dq_stride[0], a->dq_stride[1], a->dq_stride[2], p.d_real);
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
   } else if (!a->deterministic) {
@@ -1561,10 +1566,10 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
     prof_end(FA_PROF_BWD_DKDV, st);
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
-    const int64_t n4 = (int64_t)a->batch * a->num_heads * a->seqlen_q * (D / 4);
+    const int64_t n4 = (int64_t)a->batch * a->num_heads * a->seqlen_q * (p.d_real / 4);
     fa_bwd_dq_convert_kernel<T, D><<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(
         p.dq_acc, reinterpret_cast<T*>(a->dq), a->batch, a->seqlen_q, a->num_heads, p.Sq_pad,
-        a->dq_stride[0], a->dq_stride[1], a->dq_stride[2]);
+        a->dq_stride[0], a->dq_stride[1], a->dq_stride[2], p.d_real);
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
   } else {
@@ -1596,8 +1601,8 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
 static uintptr_t align256(uintptr_t x) { return (x + 255) & ~uintptr_t(255); }
 
 int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st) {
-  const int D = a->head_dim;
-  if (D != 64 && D != 128) return FA_ERR_UNSUPPORTED;
+  const int D = bwd_kernel_dim(a->head_dim);
+  if (D != 64 && D != 128 && D != 256) return FA_ERR_UNSUPPORTED;
   if (a->batch == 0) return FA_OK;
   if (a->seqlen_q == 0 || a->seqlen_k == 0) {
     // Nothing attends: every gradient is zero (outputs are dense BSHD allocations).
@@ -1621,7 +1626,7 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
   const CUtensorMapDataType dt = tmap_dtype(a->dtype);
   CUtensorMap tq, tk, tv, tdo;
   auto enc = [&](CUtensorMap* m, const void* ptr, const int64_t* s, int heads, int seq) {
-    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)heads, (uint64_t)(seq > 0 ? seq : 1),
+    const uint64_t dims[4] = {(uint64_t)a->head_dim, (uint64_t)heads, (uint64_t)(seq > 0 ? seq : 1),
                               (uint64_t)a->batch};
     const uint64_t str[3] = {(uint64_t)s[2] * 2, (uint64_t)s[1] * 2, (uint64_t)s[0] * 2};
     const uint32_t box[4] = {64, 1, 128, 1};
@@ -1640,6 +1645,7 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
   p.Hk = a->num_heads_k;
   p.G = G;
   p.Sq_pad = pad128(a->seqlen_q);
+  p.d_real = a->head_dim;
   p.causal = a->causal;
   p.n_t = (a->seqlen_k + kBwdBN - 1) / kBwdBN;
   p.n_u = a->num_heads_k * a->batch;
@@ -1652,7 +1658,7 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
   w = align256(w + rows * 4);
   p.dsum = reinterpret_cast<const float*>(w);
   w = align256(w + rows * 4);
-  p.dq_acc = a->deterministic ? nullptr : reinterpret_cast<float*>(w);
+  p.dq_acc = (a->deterministic || D == 256) ? nullptr : reinterpret_cast<float*>(w);
   p.dq = a->dq;
   p.dk = a->dk;
   p.dv = a->dv;
@@ -1667,6 +1673,13 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
   p.dv_sh = a->dv_stride[2];
   p.err = err;
   const bool bf16 = a->dtype == FA_DTYPE_BF16;
+  if (D == 256) {
+    // prep (row dot, LSE * log2 e) here, then the two D = 256 kernels of fa_bwd256.cu
+    const int s = bf16 ? launch_bwd_prep<__nv_bfloat16, 256>(a, p, st)
+                       : launch_bwd_prep<__half, 256>(a, p, st);
+    if (s != FA_OK) return s;
+    return launch_bwd_d256(a, p.lse2, p.dsum, p.Sq_pad, err, st);
+  }
   if (D == 64)
     return bf16 ? launch_bwd_impl<__nv_bfloat16, 64>(a, tq, tk, tv, tdo, p, st)
                 : launch_bwd_impl<__half, 64>(a, tq, tk, tv, tdo, p, st);

@@ -228,6 +228,8 @@ CUresult encode_tmap(CUtensorMap* map, CUtensorMapDataType dt, int rank, const v
 }
 
 static bool valid_dtype(int d) { return d == FA_DTYPE_F16 || d == FA_DTYPE_BF16; }
+// Dense head dims: 64 / 128 / 256 natively, 32 / 96 on the 64 / 128 kernels.
+static bool dense_head_dim(int d) { return d == 32 || d == 64 || d == 96 || d == 128 || d == 256; }
 
 }  // namespace fa
 
@@ -283,7 +285,7 @@ int fa_fwd(const fa_fwd_args_t* a, void* stream) {
       a->num_heads_k <= 0 || a->num_heads % a->num_heads_k != 0)
     return FA_ERR_INVALID_ARG;
   if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
-  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256) return FA_ERR_UNSUPPORTED;
+  if (!dense_head_dim(a->head_dim)) return FA_ERR_UNSUPPORTED;
   int* err = nullptr;
   if (int s = device_setup(&err, static_cast<cudaStream_t>(stream))) return s;
   return launch_fwd_dense(a, err, static_cast<cudaStream_t>(stream));
@@ -303,7 +305,7 @@ int fa_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, void* stream) {
       a->num_heads_k <= 0 || a->num_heads % a->num_heads_k != 0)
     return FA_ERR_INVALID_ARG;
   if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
-  if (a->head_dim != 64 && a->head_dim != 128) return FA_ERR_UNSUPPORTED;
+  if (!dense_head_dim(a->head_dim)) return FA_ERR_UNSUPPORTED;
   if (ws_bytes < bwd_workspace_bytes(a) || (bwd_workspace_bytes(a) > 0 && ws == nullptr))
     return FA_ERR_WORKSPACE;
   int* err = nullptr;

@@ -1402,7 +1402,10 @@ static int dispatch_dtype(int dtype, const CUtensorMap& tq, const CUtensorMap& t
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
 int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
-  const int D = a->head_dim;
+  // head_dim 32 and 96 run the 64 / 128 kernels: the tensor maps keep the real head dim
+  // as their inner extent, so TMA loads fill the missing columns with zeros (they add
+  // nothing to Q K^T, and P V writes zeros there) and TMA stores clip them.
+  const int D = (a->head_dim == 32) ? 64 : (a->head_dim == 96 ? 128 : a->head_dim);
   const int G = a->num_heads / a->num_heads_k;
   const int NQ = (D == 256) ? 1 : 2;
   if (G > 128) return FA_ERR_UNSUPPORTED;
@@ -1417,8 +1420,8 @@ int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
   const CUtensorMapDataType dt = tmap_dtype(a->dtype);
   CUtensorMap tq, tk, tv, to;
   {
-    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a->num_heads, (uint64_t)a->seqlen_q,
-                              (uint64_t)a->batch};
+    const uint64_t dims[4] = {(uint64_t)a->head_dim, (uint64_t)a->num_heads,
+                              (uint64_t)a->seqlen_q, (uint64_t)a->batch};
     const uint64_t str[3] = {(uint64_t)a->q_stride[2] * 2, (uint64_t)a->q_stride[1] * 2,
                              (uint64_t)a->q_stride[0] * 2};
     const uint32_t box[4] = {64, (uint32_t)G, (uint32_t)(128 / G), 1};  // TPT tokens x G heads
@@ -1431,7 +1434,7 @@ int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
   const int64_t* kv_str[2] = {a->k_stride, a->v_stride};
   CUtensorMap* kv_map[2] = {&tk, &tv};
   for (int w = 0; w < 2; ++w) {
-    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a->num_heads_k,
+    const uint64_t dims[4] = {(uint64_t)a->head_dim, (uint64_t)a->num_heads_k,
                               (uint64_t)(a->seqlen_k > 0 ? a->seqlen_k : 1), (uint64_t)a->batch};
     const uint64_t str[3] = {(uint64_t)kv_str[w][2] * 2, (uint64_t)kv_str[w][1] * 2,
                              (uint64_t)kv_str[w][0] * 2};

@@ -60,6 +60,9 @@ void prof_end(int kind, cudaStream_t st);
 int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st);
 int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st);
 int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st);
+// Dense backward at head_dim 256 (fa_bwd256.cu) after the prep kernel has written lse2 / dsum.
+int launch_bwd_d256(const fa_bwd_args_t* a, const float* lse2, const float* dsum, int sq_pad,
+                    int* err, cudaStream_t st);
 size_t bwd_workspace_bytes(const fa_bwd_args_t* a);
 int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st);
 size_t decode_workspace_bytes(const fa_decode_args_t* a);

@@ -5,8 +5,8 @@
 // error word and returns false, so a pipeline bug ends the kernel with an error
 // status instead of hanging a shared GPU.
 //
-// No TMA multicast is used anywhere in this library (every load is issued by the
-// CTA that consumes it, from this GPU's own memory).
+// Every TMA load is issued by the CTA that consumes it and reads this GPU's own memory;
+// no load is shared across the CTAs of a cluster.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
