@@ -37,7 +37,7 @@ typedef enum {
   FA_ERR_NOT_SM100 = -7          /* current device is not compute capability 10.x */
 } fa_status_t;
 
-typedef enum { FA_DTYPE_F16 = 0, FA_DTYPE_BF16 = 1 } fa_dtype_t;
+typedef enum { FA_DTYPE_F16 = 0, FA_DTYPE_BF16 = 1, FA_DTYPE_E4M3 = 2 } fa_dtype_t;
 
 /* Dense forward.  Replaces tilelang_forward_lse(...)(q_, k_, v_) at
  * tilelang_fa_v100/interface.py:35-36 (kernel: _kernels_forward.py:94-172), minus
@@ -140,6 +140,13 @@ typedef struct {
   int32_t dtype;
   int32_t num_splits;             /* 0: heuristic from max_blocks and the SM count */
   float softmax_scale;
+  /* KV-cache element type: 0 = the query dtype, FA_DTYPE_E4M3 = fp8 (e4m3) caches
+   * holding key / k_scale and value / v_scale (head_dim 128 or 256); the kernel folds
+   * k_scale into the scores and v_scale into the output.  No counterpart in the
+   * reference (fp16 caches only); the layout of vLLM's fp8 KV cache with per-tensor
+   * scales. */
+  int32_t kv_dtype;
+  float k_scale, v_scale;
 } fa_decode_args_t;
 
 size_t fa_decode_workspace_size(const fa_decode_args_t* args);
@@ -162,7 +169,12 @@ typedef struct {
   int64_t key_stride;             /* elements between consecutive tokens */
   int64_t value_stride;
   int32_t num_tokens, num_kv_heads, head_dim, page_size, num_pages;
-  int32_t dtype;                  /* fa_dtype_t (cache and inputs share it) */
+  int32_t dtype;                  /* fa_dtype_t of key / value (and of the caches when
+                                     cache_dtype is 0) */
+  /* 0: the caches hold `dtype`; FA_DTYPE_E4M3: they hold fp8 e4m3 and the kernel writes
+   * key / k_scale and value / v_scale, rounded to nearest and saturated to +-448. */
+  int32_t cache_dtype;
+  float k_scale, v_scale;
 } fa_kv_write_args_t;
 
 int fa_kv_cache_write(const fa_kv_write_args_t* args, void* stream);

@@ -261,6 +261,22 @@ def kv_cache_write_ref(key, value, k_cache, v_cache, slot_mapping):
         v_cache[slot // page, slot % page] = value[t]
 
 
+def quantize_e4m3(x, scale):
+    """x / scale rounded to nearest even e4m3 and saturated to +-448 (the rounding of
+    cvt.rn.satfinite.e4m3x2.f32), as raw bytes (uint8 array of x's shape).  fp8 caches
+    have no reference counterpart; this restates vLLM's per-tensor-scale fp8 KV cache."""
+    import torch
+    y = np.clip(np.asarray(x, np.float32) / np.float32(scale), -448.0, 448.0)
+    return torch.from_numpy(y).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+
+
+def dequantize_e4m3(raw, scale):
+    """e4m3 bytes (uint8) -> float32 values times scale."""
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(raw)).view(torch.float8_e4m3fn).float().numpy()
+    return t * np.float32(scale)
+
+
 def slots_for(block_table_row, positions, page_size):
     """Slot ids of token positions of one sequence under its block table row."""
     pos = np.asarray(positions)

@@ -25,16 +25,21 @@ namespace fa {
 
 constexpr int kDecChunk = 16;  // tokens per pipeline chunk
 
-template <int D>
+// KV8: the caches hold fp8 e4m3 (one byte per element, 128 elements per 128-byte box
+// row) instead of the query's 16-bit type (64 per box row); half the bytes per chunk,
+// so twice the stages keep as many bytes in flight.
+template <int D, bool KV8 = false>
 struct DecCfg {
-  static constexpr int DH = D / 64;
+  static constexpr int ELEM = KV8 ? 1 : 2;                // cache bytes per element
+  static constexpr int BOX_ELEMS = 128 / ELEM;            // elements per 128-byte box row
+  static constexpr int DH = D / BOX_ELEMS;                // boxes per head row
   static constexpr int WPH = D > 128 ? 2 : 1;             // compute warps per kv head
   static constexpr int DW = D / WPH;                      // output columns per compute warp
   static constexpr int MAXG = D > 128 ? 4 : 8;            // kv heads per CTA
   static constexpr int NTHREADS = 32 + 32 * MAXG * WPH;   // producer warp + compute warps
-  static constexpr int HEAD_BYTES = kDecChunk * D * 2;    // one kv head, one chunk, K or V
+  static constexpr int HEAD_BYTES = kDecChunk * D * ELEM; // one kv head, one chunk, K or V
   static constexpr int STAGE_BYTES_MAX = 2 * MAXG * HEAD_BYTES;
-  static constexpr int STAGES = (D == 64) ? 6 : 3;
+  static constexpr int STAGES = KV8 ? 6 : ((D == 64) ? 6 : 3);
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES_MAX + 256;
   static_assert(SMEM_BYTES <= 232448, "decode smem budget");
 };
@@ -50,7 +55,8 @@ struct DecParams {
   int B, H, Hkv, G, HG;  // HG = kv heads per CTA
   int page_size, num_pages, max_blocks;
   int num_splits, chunks_per_split;
-  float scale_log2, scale;
+  float scale_log2, scale;  // (fp8 caches: times k_scale)
+  float v_scale;            // 1, or the fp8 value cache's scale
   int* err;
 };
 
@@ -88,17 +94,47 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk16) {
   return static_cast<uint32_t>(row * 128 + ((chunk16 ^ (row & 7)) << 4));
 }
 
+// fp8 caches: byte address of element d of row `row` in a chunk of 128-byte-swizzled
+// boxes (128 elements per box row, boxes kDecChunk x 128 bytes apart).
+__device__ __forceinline__ uint32_t swz8(uint32_t base, int row, int d) {
+  return base + (d >> 7) * (kDecChunk * 128) + swz(row, (d & 127) >> 4) + (d & 15);
+}
+__device__ __forceinline__ uint32_t ld_shared_u16(uint32_t addr) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_shared_u8(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+// Two e4m3 values (the first in the low byte) as a 16-bit pair of the MMA's input type.
+// Every e4m3 value is exact in f16 and in bf16, so the conversion loses nothing.
+template <typename T>
+__device__ __forceinline__ uint32_t e4m3x2_to(uint32_t v) {
+  uint32_t h;
+  const uint16_t v16 = static_cast<uint16_t>(v);
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(v16));
+  if constexpr (Pack2<T>::kBf16) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+    return Pack2<T>::pack(f.x, f.y);
+  } else {
+    return h;
+  }
+}
+
 struct DecSmemCtl {
   uint64_t full[8];
   uint64_t empty[8];
   int abort_flag;
 };
 
-template <typename T, int D>
-__global__ void __launch_bounds__(DecCfg<D>::NTHREADS, 1)
+template <typename T, int D, bool KV8>
+__global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
     fa_decode_split_kernel(const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v, const DecParams p) {
-  using Cfg = DecCfg<D>;
+  using Cfg = DecCfg<D, KV8>;
   constexpr int ST = Cfg::STAGES;
   constexpr bool kBf16 = Pack2<T>::kBf16;
   extern __shared__ uint8_t smem_raw[];
@@ -168,7 +204,7 @@ __global__ void __launch_bounds__(DecCfg<D>::NTHREADS, 1)
           for (int hh = 0; hh < HG; ++hh)
             for (int dh = 0; dh < Cfg::DH; ++dh)
               tma_load_4d(dst + (w * HG + hh) * Cfg::HEAD_BYTES + dh * (kDecChunk * 128), tm, fb,
-                          dh * 64, hk0 + hh, in_page, page);
+                          dh * Cfg::BOX_ELEMS, hk0 + hh, in_page, page);
         }
       }
       for (int k = max(0, it - ST); k < it; ++k) {
@@ -222,13 +258,22 @@ __global__ void __launch_bounds__(DecCfg<D>::NTHREADS, 1)
     float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
-      // matrices: (tokens 0-7, d lo), (tokens 0-7, d hi), (tokens 8-15, d lo), (tokens 8-15, d hi)
-      const int mi = lane >> 3;
-      const int row = ((mi >> 1) << 3) + (lane & 7);
-      const int dchunk = (ks & 3) * 2 + (mi & 1);
-      const uint32_t addr = kbase + (ks >> 2) * (kDecChunk * 128) + swz(row, dchunk);
       uint32_t b0, b1, b2, b3;
-      ldsm_x4(addr, b0, b1, b2, b3);
+      if constexpr (KV8) {
+        // B fragments straight from the fp8 rows: token g (+ 8), dims 16 ks + qd (+ 8)
+        const int d = ks * 16 + qd;
+        b0 = e4m3x2_to<T>(ld_shared_u16(swz8(kbase, g, d)));
+        b1 = e4m3x2_to<T>(ld_shared_u16(swz8(kbase, g, d + 8)));
+        b2 = e4m3x2_to<T>(ld_shared_u16(swz8(kbase, g + 8, d)));
+        b3 = e4m3x2_to<T>(ld_shared_u16(swz8(kbase, g + 8, d + 8)));
+      } else {
+        // matrices: (tokens 0-7, d lo), (tokens 0-7, d hi), (tokens 8-15, d lo), (tokens 8-15, d hi)
+        const int mi = lane >> 3;
+        const int row = ((mi >> 1) << 3) + (lane & 7);
+        const int dchunk = (ks & 3) * 2 + (mi & 1);
+        const uint32_t addr = kbase + (ks >> 2) * (kDecChunk * 128) + swz(row, dchunk);
+        ldsm_x4(addr, b0, b1, b2, b3);
+      }
       mma16816<kBf16>(sc[0], qa[ks], b0, b1);
       mma16816<kBf16>(sc[1], qa[ks], b2, b3);
     }
@@ -282,13 +327,26 @@ __global__ void __launch_bounds__(DecCfg<D>::NTHREADS, 1)
 #pragma unroll
     for (int dpl = 0; dpl < DW / 16; ++dpl) {
       const int dp = part * (DW / 16) + dpl;
-      // matrices: (tok 0-7, d 16dp..+7), (tok 8-15, same), (tok 0-7, d +8..+15), (tok 8-15, +8..)
-      const int mi = lane >> 3;
-      const int row = ((mi & 1) << 3) + (lane & 7);
-      const int dchunk = ((dp * 2) & 7) + (mi >> 1);
-      const uint32_t addr = vbase + ((dp * 16) >> 6) * (kDecChunk * 128) + swz(row, dchunk);
       uint32_t b0, b1, b2, b3;
-      ldsm_x4_t(addr, b0, b1, b2, b3);
+      if constexpr (KV8) {
+        // B = V[token][d]: tokens qd, qd + 1 (+ 8) of dim 16 dp + g (+ 8), byte by byte
+        const int d = dp * 16 + g;
+        auto pair = [&](int tok, int dd) {
+          return e4m3x2_to<T>(ld_shared_u8(swz8(vbase, tok, dd)) |
+                              (ld_shared_u8(swz8(vbase, tok + 1, dd)) << 8));
+        };
+        b0 = pair(qd, d);
+        b1 = pair(qd + 8, d);
+        b2 = pair(qd, d + 8);
+        b3 = pair(qd + 8, d + 8);
+      } else {
+        // matrices: (tok 0-7, d 16dp..+7), (tok 8-15, same), (tok 0-7, d +8..+15), (tok 8-15, +8..)
+        const int mi = lane >> 3;
+        const int row = ((mi & 1) << 3) + (lane & 7);
+        const int dchunk = ((dp * 2) & 7) + (mi >> 1);
+        const uint32_t addr = vbase + ((dp * 16) >> 6) * (kDecChunk * 128) + swz(row, dchunk);
+        ldsm_x4_t(addr, b0, b1, b2, b3);
+      }
       mma16816<kBf16>(o[2 * dpl], pa, b0, b1);
       mma16816<kBf16>(o[2 * dpl + 1], pa, b2, b3);
     }
@@ -301,8 +359,8 @@ __global__ void __launch_bounds__(DecCfg<D>::NTHREADS, 1)
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
-  const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+  const float inv0 = l0 > 0.f ? p.v_scale / l0 : 0.f;
+  const float inv1 = l1 > 0.f ? p.v_scale / l1 : 0.f;
   const float lse0 = l0 > 0.f ? m0 * p.scale + logf(l0) : -INFINITY;
   const float lse1 = l1 > 0.f ? m1 * p.scale + logf(l1) : -INFINITY;
   const bool direct = p.num_splits == 1;
@@ -404,11 +462,11 @@ size_t decode_workspace_bytes(const fa_decode_args_t* a) {
   return (n * a->head_dim + n) * sizeof(float) + 256;
 }
 
-template <typename T, int D>
+template <typename T, int D, bool KV8>
 static int launch_decode_impl(const CUtensorMap& tk, const CUtensorMap& tv, const DecParams& p,
                               cudaStream_t st) {
-  using Cfg = DecCfg<D>;
-  auto kern = fa_decode_split_kernel<T, D>;
+  using Cfg = DecCfg<D, KV8>;
+  auto kern = fa_decode_split_kernel<T, D, KV8>;
   static std::atomic<bool> attr_set[kMaxContexts];
   if (int s = smem_attr_once(kern, Cfg::SMEM_BYTES, attr_set)) return s;
   dim3 grid(p.num_splits, p.Hkv / p.HG, p.B);
@@ -438,20 +496,27 @@ int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err
   if (G > 16) return FA_ERR_UNSUPPORTED;
   const int ps = a->page_size;
   if (ps < kDecChunk || (ps & (ps - 1)) != 0) return FA_ERR_UNSUPPORTED;
+  if (a->kv_dtype != 0 && a->kv_dtype != FA_DTYPE_E4M3) return FA_ERR_UNSUPPORTED;
+  const bool kv8 = a->kv_dtype == FA_DTYPE_E4M3;
+  if (kv8 && D == 64) return FA_ERR_UNSUPPORTED;  // fp8 rows of 64 bytes: not built
+  if (kv8 && !(a->k_scale > 0.f && a->v_scale > 0.f && std::isfinite(a->k_scale) &&
+               std::isfinite(a->v_scale)))
+    return FA_ERR_INVALID_ARG;
   if (a->batch == 0) return FA_OK;
   const int splits = decode_num_splits(a);
   if (decode_workspace_bytes(a) > ws_bytes || (splits > 1 && ws == nullptr))
     return FA_ERR_WORKSPACE;
-  const CUtensorMapDataType dt = tmap_dtype(a->dtype);
+  const CUtensorMapDataType dt = kv8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : tmap_dtype(a->dtype);
+  const uint64_t eb = kv8 ? 1 : 2;  // cache bytes per element
   CUtensorMap tk, tv;
   const void* kv_ptr[2] = {a->k_cache, a->v_cache};
   CUtensorMap* kv_map[2] = {&tk, &tv};
   for (int w = 0; w < 2; ++w) {
     const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a->num_kv_heads, (uint64_t)ps,
                               (uint64_t)a->num_pages};
-    const uint64_t str[3] = {(uint64_t)D * 2, (uint64_t)a->num_kv_heads * D * 2,
-                             (uint64_t)ps * a->num_kv_heads * D * 2};
-    const uint32_t box[4] = {64, 1, (uint32_t)kDecChunk, 1};
+    const uint64_t str[3] = {(uint64_t)D * eb, (uint64_t)a->num_kv_heads * D * eb,
+                             (uint64_t)ps * a->num_kv_heads * D * eb};
+    const uint32_t box[4] = {(uint32_t)(128 / eb), 1, (uint32_t)kDecChunk, 1};
     FA_TMAP_TRY(encode_tmap(kv_map[w], dt, 4, kv_ptr[w], dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   DecParams p{};
@@ -470,8 +535,11 @@ int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err
   p.max_blocks = a->max_blocks;
   p.num_splits = splits;
   p.chunks_per_split = chunks_per_split(a, splits);
-  p.scale = a->softmax_scale;
-  p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  // fp8 caches hold key / k_scale: the true scores are k_scale x (q . k8)
+  const float ks = kv8 ? a->k_scale : 1.f;
+  p.scale = a->softmax_scale * ks;
+  p.scale_log2 = a->softmax_scale * ks * 1.4426950408889634f;
+  p.v_scale = kv8 ? a->v_scale : 1.f;
   p.err = err;
   if (splits > 1) {
     const size_t n = (size_t)a->batch * splits * a->num_heads;
@@ -480,14 +548,21 @@ int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err
     p.lse_part = p.o_part + n * D;
   }
   const bool bf16 = a->dtype == FA_DTYPE_BF16;
+  if (kv8) {
+    if (D == 256)
+      return bf16 ? launch_decode_impl<__nv_bfloat16, 256, true>(tk, tv, p, st)
+                  : launch_decode_impl<__half, 256, true>(tk, tv, p, st);
+    return bf16 ? launch_decode_impl<__nv_bfloat16, 128, true>(tk, tv, p, st)
+                : launch_decode_impl<__half, 128, true>(tk, tv, p, st);
+  }
   if (D == 64)
-    return bf16 ? launch_decode_impl<__nv_bfloat16, 64>(tk, tv, p, st)
-                : launch_decode_impl<__half, 64>(tk, tv, p, st);
+    return bf16 ? launch_decode_impl<__nv_bfloat16, 64, false>(tk, tv, p, st)
+                : launch_decode_impl<__half, 64, false>(tk, tv, p, st);
   if (D == 256)
-    return bf16 ? launch_decode_impl<__nv_bfloat16, 256>(tk, tv, p, st)
-                : launch_decode_impl<__half, 256>(tk, tv, p, st);
-  return bf16 ? launch_decode_impl<__nv_bfloat16, 128>(tk, tv, p, st)
-              : launch_decode_impl<__half, 128>(tk, tv, p, st);
+    return bf16 ? launch_decode_impl<__nv_bfloat16, 256, false>(tk, tv, p, st)
+                : launch_decode_impl<__half, 256, false>(tk, tv, p, st);
+  return bf16 ? launch_decode_impl<__nv_bfloat16, 128, false>(tk, tv, p, st)
+              : launch_decode_impl<__half, 128, false>(tk, tv, p, st);
 }
 
 // ------------------------------------------------------------------- no-allocation decode

@@ -27,6 +27,7 @@ FA_ERR_NOT_SM100 = -7
 
 FA_DTYPE_F16 = 0
 FA_DTYPE_BF16 = 1
+FA_DTYPE_E4M3 = 2
 
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -70,14 +71,16 @@ class DecodeArgs(ctypes.Structure):
                 ("seq_lens", _vp), ("out", _vp), ("lse", _vp),
                 ("batch", _i32), ("num_heads", _i32), ("num_kv_heads", _i32), ("head_dim", _i32),
                 ("page_size", _i32), ("num_pages", _i32), ("max_blocks", _i32), ("dtype", _i32),
-                ("num_splits", _i32), ("softmax_scale", _f32)]
+                ("num_splits", _i32), ("softmax_scale", _f32),
+                ("kv_dtype", _i32), ("k_scale", _f32), ("v_scale", _f32)]
 
 
 class KvWriteArgs(ctypes.Structure):
     _fields_ = [("key", _vp), ("value", _vp), ("k_cache", _vp), ("v_cache", _vp),
                 ("slot_mapping", _vp), ("key_stride", _i64), ("value_stride", _i64),
                 ("num_tokens", _i32), ("num_kv_heads", _i32), ("head_dim", _i32),
-                ("page_size", _i32), ("num_pages", _i32), ("dtype", _i32)]
+                ("page_size", _i32), ("num_pages", _i32), ("dtype", _i32),
+                ("cache_dtype", _i32), ("k_scale", _f32), ("v_scale", _f32)]
 
 
 # Exported symbols and their (restype, argtypes); the CPU test checks this list
@@ -273,8 +276,17 @@ def paged_prefill(q, k_cache, v_cache, block_table, seq_lens, query_start_loc, p
     return out, lse
 
 
+def _kv_code(cache, q_dtype):
+    """0 when the cache holds the query dtype, FA_DTYPE_E4M3 for an fp8 (e4m3) cache."""
+    if cache.dtype == q_dtype:
+        return 0
+    if cache.dtype == torch.float8_e4m3fn:
+        return FA_DTYPE_E4M3
+    raise ValueError("cache dtype %s: must be the query dtype or torch.float8_e4m3fn" % cache.dtype)
+
+
 def decode(q, k_cache, v_cache, block_table, seq_lens, page_size, num_kv_heads, softmax_scale,
-           num_splits=0, out=None, lse=None):
+           num_splits=0, out=None, lse=None, k_scale=1.0, v_scale=1.0):
     _require_cuda(q, k_cache, v_cache)
     dev = q.device
     bsz, h, d = q.shape
@@ -283,10 +295,14 @@ def decode(q, k_cache, v_cache, block_table, seq_lens, page_size, num_kv_heads, 
     sl = _i32_on(seq_lens, dev)
     if out is None:
         out = torch.empty_like(q)
+    kv = _kv_code(k_cache, q.dtype)
+    if _kv_code(v_cache, q.dtype) != kv:
+        raise ValueError("k_cache and v_cache dtypes differ")
     a = DecodeArgs(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(),
                    sl.data_ptr(), out.data_ptr(), lse.data_ptr() if lse is not None else None,
                    bsz, h, num_kv_heads, d, page_size, k_cache.shape[0], bt.shape[1],
-                   _dtype_code(q.dtype), int(num_splits), float(softmax_scale))
+                   _dtype_code(q.dtype), int(num_splits), float(softmax_scale),
+                   kv, float(k_scale), float(v_scale))
     lib = load()
     nbytes = int(lib.fa_decode_workspace_size(ctypes.byref(a)))
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
@@ -295,15 +311,17 @@ def decode(q, k_cache, v_cache, block_table, seq_lens, page_size, num_kv_heads, 
     return out
 
 
-def kv_cache_write(key, value, k_cache, v_cache, slot_mapping):
-    """Scatters key/value [num_tokens, Hkv, D] into the paged caches at slot_mapping."""
+def kv_cache_write(key, value, k_cache, v_cache, slot_mapping, k_scale=1.0, v_scale=1.0):
+    """Scatters key/value [num_tokens, Hkv, D] into the paged caches at slot_mapping
+    (quantised to e4m3 with the scales when the caches are torch.float8_e4m3fn)."""
     _require_cuda(key, value, k_cache, v_cache)
     dev = key.device
     n, hkv, d = key.shape
     sm = slot_mapping.to(device=dev, dtype=torch.int64).contiguous()
     a = KvWriteArgs(key.data_ptr(), value.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                     sm.data_ptr(), key.stride(0), value.stride(0), n, hkv, d,
-                    k_cache.shape[1], k_cache.shape[0], _dtype_code(key.dtype))
+                    k_cache.shape[1], k_cache.shape[0], _dtype_code(key.dtype),
+                    _kv_code(k_cache, key.dtype), float(k_scale), float(v_scale))
     with torch.cuda.device(dev):
         check(load().fa_kv_cache_write(ctypes.byref(a), _stream(dev)))
 

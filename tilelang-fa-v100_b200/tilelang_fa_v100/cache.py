@@ -10,14 +10,18 @@ import torch
 from . import _ext
 
 
-def write_kv_cache(key, value, k_cache, v_cache, slot_mapping):
+def write_kv_cache(key, value, k_cache, v_cache, slot_mapping, k_scale=1.0, v_scale=1.0):
     """Copies key[t] and value[t] ([Hkv, D] each) into k_cache / v_cache
     [num_pages, page_size, Hkv, D] at slot slot_mapping[t] = page * page_size + offset.
 
     Negative slots mark padding tokens and are skipped.  key / value may be views with a
     token stride (e.g. slices of a fused QKV projection) but each token's [Hkv, D] block
     must be contiguous.  A slot past the cache is not written and is reported by
-    tilelang_fa_v100._ext.read_device_error() (code 3)."""
+    tilelang_fa_v100._ext.read_device_error() (code 3).
+
+    fp8 caches (torch.float8_e4m3fn): the kernel stores key / k_scale and value / v_scale
+    rounded to nearest and saturated to +-448, the layout tilelang_decode_forward reads
+    with the same scales."""
     if key.dim() != 3 or value.shape != key.shape:
         raise ValueError("key and value must be [num_tokens, num_kv_heads, head_dim] of one shape")
     n, hkv, d = key.shape
@@ -28,10 +32,11 @@ def write_kv_cache(key, value, k_cache, v_cache, slot_mapping):
     for t in (key, value):
         if t.stride(2) != 1 or t.stride(1) != d:
             raise ValueError("each token's [num_kv_heads, head_dim] block must be contiguous")
-    if not (key.dtype == value.dtype == k_cache.dtype == v_cache.dtype):
-        raise ValueError("key, value and caches must share one dtype")
+    if key.dtype != value.dtype or k_cache.dtype != v_cache.dtype or \
+            k_cache.dtype not in (key.dtype, torch.float8_e4m3fn):
+        raise ValueError("key / value share one dtype; the caches hold it or torch.float8_e4m3fn")
     if slot_mapping.dim() != 1 or slot_mapping.shape[0] != n:
         raise ValueError("slot_mapping must be [num_tokens]")
     if n == 0:
         return
-    _ext.kv_cache_write(key, value, k_cache, v_cache, slot_mapping)
+    _ext.kv_cache_write(key, value, k_cache, v_cache, slot_mapping, k_scale, v_scale)

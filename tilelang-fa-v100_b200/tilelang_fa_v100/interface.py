@@ -104,15 +104,16 @@ tilelang_flash_attn_gpu = tilelang_flash_attn_func
 
 def tilelang_decode_forward(q, k_cache, v_cache, block_table, seq_lens,
                             block_size=16, num_kv_heads=None,
-                            softmax_scale=None):
+                            softmax_scale=None, k_scale=1.0, v_scale=1.0):
     """Paged decode forward for vLLM integration.
 
-    Args match the reference FA-V100 decode_fwd API.
+    Args match the reference FA-V100 decode_fwd API; k_scale / v_scale (defaults 1)
+    dequantise torch.float8_e4m3fn caches, which the reference does not accept.
     Returns:
         output: [batch, heads, dim] in the input dtype
     """
     return _decode_forward(
         q, k_cache, v_cache, block_table, seq_lens,
         block_size=block_size, num_kv_heads=num_kv_heads,
-        softmax_scale=softmax_scale,
+        softmax_scale=softmax_scale, k_scale=k_scale, v_scale=v_scale,
     )
