@@ -577,14 +577,28 @@ def decode_problem(dev, rank, world, batch=256, hkv=8, d=128, heads=32, seed_bas
     return q, kc, vc, bt, sl, nbytes, mine, owned, lens
 
 
-def decode_run(dev, dist, rank, world, steps, warmup, hkv=8, d=128, heads=32, check=True):
+FP8_SCALE = 1.0 / 64  # e4m3 cache scale for N(0,1) keys / values: |x| / scale stays < 448
+
+
+def to_e4m3(x):
+    """The fp8 cache a serving engine would hold for x (x / scale, saturated)."""
+    return (x.float() / FP8_SCALE).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+
+
+def decode_run(dev, dist, rank, world, steps, warmup, hkv=8, d=128, heads=32, check=True,
+               fp8=False):
     """configs[4] at N GPUs (weak: N x 256 sequences, sharded by sequence with balanced
-    token counts).  Returns aggregate GB/s, ms, the gathered check and the max/mean
-    per-rank token load."""
+    token counts); fp8: the same sequences in e4m3 caches with per-tensor scales.  Returns
+    aggregate GB/s, ms, the gathered check and the max/mean per-rank token load."""
     import tilelang_fa_v100 as fa
     q, kc, vc, bt, sl, nbytes, mine, owned, lens = decode_problem(dev, rank, world, hkv=hkv, d=d,
                                                                   heads=heads)
-    run = lambda: fa.tilelang_decode_forward(q, kc, vc, bt, sl)
+    kw = {}
+    if fp8:
+        kc, vc = to_e4m3(kc), to_e4m3(vc)
+        kw = dict(k_scale=FP8_SCALE, v_scale=FP8_SCALE)
+        nbytes -= int(lens[mine].sum()) * hkv * d * 2  # one byte per cached element, not two
+    run = lambda: fa.tilelang_decode_forward(q, kc, vc, bt, sl, **kw)
     for _ in range(warmup):
         run()
     ms = timed_ms(dev, dist, steps, run)
@@ -610,6 +624,8 @@ def decode_run(dev, dist, rank, world, steps, warmup, hkv=8, d=128, heads=32, ch
             L = int(lens[i])
             qi, ki, vi = seq_inputs(dev, i, 1, -(-L // 16) * 16, heads, hkv, d, torch.bfloat16,
                                     SEED_DECODE)
+            if fp8:  # the reference attends over the dequantised cache
+                ki, vi = (to_e4m3(x).float() * FP8_SCALE for x in (ki, vi))
             ro, _ = sequence_ref(qi, ki[:L], vi[:L], 0, False)
             st.north_star("out", pack, ro[0])
         if rank == 0:
@@ -804,6 +820,13 @@ def run_ours(args):
                                         "sharding": "256 sequences per rank, balanced longest-first "
                                                     "by token count", "balance": bal,
                                         "check": dchk}
+        f8gbs, f8ms, f8chk, _ = decode_run(dev, dist, rank, world, args.steps, 3, fp8=True)
+        sec["cfg5_decode_fp8kv_GBps"] = {
+            "gbs": f8gbs, "ms": f8ms, "frac_of_hbm": f8gbs / world / hbm,
+            "speedup_vs_bf16_cache": dms / f8ms,
+            "note": "configs[4] sequences with e4m3 K/V caches (per-tensor scale 1/64); bytes "
+                    "count one byte per cached element; checked against the dequantised cache",
+            "check": f8chk}
         d2gbs, d2ms, _, _ = decode_run(dev, dist, rank, world, args.steps, 3, hkv=1, d=256,
                                        heads=8, check=False)
         sec["decode_bf16_H8_Hkv1_D256_GBps"] = {
@@ -881,6 +904,18 @@ def run_profile_case(args):
         torch.cuda.synchronize(dev)
         print(json.dumps({"profile_case": "decode_B64_bf16", "bytes": nbytes}), flush=True)
         return
+    if args.profile_case == "d64":  # configs[1] itself: fp16 [4, 2048, 16, 64] causal
+        t = dense_shard(dev, 0, 4, 2048, 2048, 16, 16, 64, torch.float16, SEED_DENSE2)
+        ms, kern_ms, launches = time_dense(fa, dev, *t, True, args.steps, args.warmup, profile=True)
+        print(json.dumps({"profile_case": "cfg2_B4_S2048_H16_D64_fp16_causal", "ms_per_step": ms,
+                          "dkdv_ms": kern_ms, "launches": launches}), flush=True)
+        return
+    if args.profile_case == "d256":  # head_dim 256: bf16 [2, 4096, 16, 256] causal (67 MB / tensor)
+        t = dense_shard(dev, 0, 2, 4096, 4096, 16, 16, 256, torch.bfloat16, SEED_DENSE)
+        ms, kern_ms, launches = time_dense(fa, dev, *t, True, args.steps, args.warmup, profile=True)
+        print(json.dumps({"profile_case": "B2_S4096_H16_D256_bf16_causal", "ms_per_step": ms,
+                          "dkdv_ms": kern_ms, "launches": launches}), flush=True)
+        return
     s, h, d = CFG["S"], CFG["H"], CFG["D"]
     t = dense_shard(dev, 0, 2, s, s, h, h, d, torch.bfloat16, SEED_DENSE)
     ms, kern_ms, launches = time_dense(fa, dev, *t, True, args.steps, args.warmup, profile=True)
@@ -896,7 +931,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
-    ap.add_argument("--profile-case", choices=["dense", "decode", "paged"], default=None,
+    ap.add_argument("--profile-case", choices=["dense", "decode", "paged", "d64", "d256"], default=None,
                     help="small case for ncu captures (no e2e / CPU / secondary)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
