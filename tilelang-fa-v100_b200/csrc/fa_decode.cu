@@ -99,15 +99,11 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk16) {
 __device__ __forceinline__ uint32_t swz8(uint32_t base, int row, int d) {
   return base + (d >> 7) * (kDecChunk * 128) + swz(row, (d & 127) >> 4) + (d & 15);
 }
-__device__ __forceinline__ uint32_t ld_shared_u16(uint32_t addr) {
-  uint16_t v;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ uint32_t ld_shared_u8(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
+// Bytes (lo, hi) of a 32-bit word picked by a prmt selector, as a 16-bit value.
+__device__ __forceinline__ uint32_t prmt(uint32_t x, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(x), "r"(sel));
+  return r;
 }
 // Two e4m3 values (the first in the low byte) as a 16-bit pair of the MMA's input type.
 // Every e4m3 value is exact in f16 and in bf16, so the conversion loses nothing.
@@ -229,15 +225,20 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
     const T* qb = reinterpret_cast<const T*>(p.q) + ((int64_t)b * p.H + hk * G) * D;
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
-      const int k0 = ks * 16 + qd;
+      // fp8 caches: the K fragments come from ldmatrix over the byte rows, which gives
+      // lane (g, j = lane & 3) dims 4 j .. 4 j + 3 of its 16-dim step; the MMA's k index
+      // 2 j + e then stands for dim 4 j + e and 8 + 2 j + e for dim 4 j + 2 + e, and the
+      // Q fragment takes the same permutation (the sum over k is unchanged).
+      const int k0 = KV8 ? ks * 16 + 2 * qd : ks * 16 + qd;
+      const int k8 = KV8 ? k0 + 2 : k0 + 8;
       auto ld2 = [&](int row, int col) -> uint32_t {
         if (row >= G) return 0u;
         return *reinterpret_cast<const uint32_t*>(qb + (int64_t)row * D + col);
       };
       qa[ks][0] = ld2(g, k0);
       qa[ks][1] = ld2(g + 8, k0);
-      qa[ks][2] = ld2(g, k0 + 8);
-      qa[ks][3] = ld2(g + 8, k0 + 8);
+      qa[ks][2] = ld2(g, k8);
+      qa[ks][3] = ld2(g + 8, k8);
     }
   }
   constexpr int DW = Cfg::DW;
@@ -260,12 +261,26 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
     for (int ks = 0; ks < D / 16; ++ks) {
       uint32_t b0, b1, b2, b3;
       if constexpr (KV8) {
-        // B fragments straight from the fp8 rows: token g (+ 8), dims 16 ks + qd (+ 8)
-        const int d = ks * 16 + qd;
-        b0 = e4m3x2_to<T>(ld_shared_u16(swz8(kbase, g, d)));
-        b1 = e4m3x2_to<T>(ld_shared_u16(swz8(kbase, g, d + 8)));
-        b2 = e4m3x2_to<T>(ld_shared_u16(swz8(kbase, g + 8, d)));
-        b3 = e4m3x2_to<T>(ld_shared_u16(swz8(kbase, g + 8, d + 8)));
+        // Two k steps per ldmatrix x4 over the byte rows (each 8x8 b16 matrix = 8 tokens
+        // x 16 dims): matrices (tokens 0-7, dims 32 kp ..), (8-15, same), (0-7, +16),
+        // (8-15, +16); each lane's word holds 4 consecutive dims of one token.
+        if (ks & 1) continue;  // handled with ks - 1
+        const int mi = lane >> 3;
+        const int tok = ((mi & 1) << 3) + (lane & 7);
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4(swz8(kbase, tok, ks * 16 + (mi >> 1) * 16), r0, r1, r2, r3);
+        const uint32_t w[4] = {r0, r1, r2, r3};
+        uint32_t c[8];
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          c[2 * x] = e4m3x2_to<T>(w[x] & 0xFFFFu);
+          c[2 * x + 1] = e4m3x2_to<T>(w[x] >> 16);
+        }
+        mma16816<kBf16>(sc[0], qa[ks], c[0], c[1]);
+        mma16816<kBf16>(sc[1], qa[ks], c[2], c[3]);
+        mma16816<kBf16>(sc[0], qa[ks + 1], c[4], c[5]);
+        mma16816<kBf16>(sc[1], qa[ks + 1], c[6], c[7]);
+        continue;
       } else {
         // matrices: (tokens 0-7, d lo), (tokens 0-7, d hi), (tokens 8-15, d lo), (tokens 8-15, d hi)
         const int mi = lane >> 3;
@@ -329,16 +344,26 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
       const int dp = part * (DW / 16) + dpl;
       uint32_t b0, b1, b2, b3;
       if constexpr (KV8) {
-        // B = V[token][d]: tokens qd, qd + 1 (+ 8) of dim 16 dp + g (+ 8), byte by byte
-        const int d = dp * 16 + g;
-        auto pair = [&](int tok, int dd) {
-          return e4m3x2_to<T>(ld_shared_u8(swz8(vbase, tok, dd)) |
-                              (ld_shared_u8(swz8(vbase, tok + 1, dd)) << 8));
-        };
-        b0 = pair(qd, d);
-        b1 = pair(qd + 8, d);
-        b2 = pair(qd, d + 8);
-        b3 = pair(qd + 8, d + 8);
+        // ldmatrix.trans over the byte rows, two 16-dim groups per x4: matrices (tokens
+        // 0-7, dims 16 dp ..), (8-15, same), (0-7, dims 16 dp + 16 ..), (8-15, same); lane
+        // (g, j) gets tokens 2 j, 2 j + 1 x dims 2 g, 2 g + 1 of each group.  prmt splits
+        // them into an even-dim and an odd-dim column tile: o[2 dpl] / o[2 dpl + 1] hold,
+        // at n = g, dims 16 dp + 2 g and 16 dp + 2 g + 1.
+        if (dpl & 1) continue;  // handled with dpl - 1
+        const int mi = lane >> 3;
+        const int tok = ((mi & 1) << 3) + (lane & 7);
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4_t(swz8(vbase, tok, dp * 16 + (mi >> 1) * 16), r0, r1, r2, r3);
+        const uint32_t w[4] = {r0, r1, r2, r3};
+#pragma unroll
+        for (int gp = 0; gp < 2; ++gp) {
+          const uint32_t lo = w[2 * gp], hi = w[2 * gp + 1];  // tokens 0-7 / 8-15
+          mma16816<kBf16>(o[2 * (dpl + gp)], pa, e4m3x2_to<T>(prmt(lo, 0x0020)),
+                          e4m3x2_to<T>(prmt(hi, 0x0020)));
+          mma16816<kBf16>(o[2 * (dpl + gp) + 1], pa, e4m3x2_to<T>(prmt(lo, 0x0031)),
+                          e4m3x2_to<T>(prmt(hi, 0x0031)));
+        }
+        continue;
       } else {
         // matrices: (tok 0-7, d 16dp..+7), (tok 8-15, same), (tok 0-7, d +8..+15), (tok 8-15, +8..)
         const int mi = lane >> 3;
@@ -371,7 +396,19 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
     const int h = hk * G + row;
     const float inv = half ? inv1 : inv0;
     const float lse = half ? lse1 : lse0;
-    if (direct) {
+    if (direct && KV8) {
+      // even / odd column tiles: this lane's dims 16 dpl + 2 qd .. + 3
+      T* dst = reinterpret_cast<T*>(p.out) + ((int64_t)b * p.H + h) * D + part * DW;
+#pragma unroll
+      for (int dpl = 0; dpl < DW / 16; ++dpl) {
+        const float* e = o[2 * dpl];
+        const float* od = o[2 * dpl + 1];
+        *reinterpret_cast<uint2*>(dst + dpl * 16 + 2 * qd) =
+            make_uint2(Pack2<T>::pack(e[half * 2] * inv, od[half * 2] * inv),
+                       Pack2<T>::pack(e[half * 2 + 1] * inv, od[half * 2 + 1] * inv));
+      }
+      if (p.lse != nullptr && (lane & 3) == 0 && part == 0) p.lse[(int64_t)b * p.H + h] = lse;
+    } else if (direct) {
       T* dst = reinterpret_cast<T*>(p.out) + ((int64_t)b * p.H + h) * D + part * DW;
 #pragma unroll
       for (int dn = 0; dn < DW / 8; ++dn) {
@@ -381,10 +418,21 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
       if (p.lse != nullptr && (lane & 3) == 0 && part == 0) p.lse[(int64_t)b * p.H + h] = lse;
     } else {
       float* dst = p.o_part + (((int64_t)b * p.num_splits + split) * p.H + h) * D + part * DW;
+      if constexpr (KV8) {
 #pragma unroll
-      for (int dn = 0; dn < DW / 8; ++dn)
-        *reinterpret_cast<float2*>(dst + dn * 8 + qd) =
-            make_float2(o[dn][half * 2] * inv, o[dn][half * 2 + 1] * inv);
+        for (int dpl = 0; dpl < DW / 16; ++dpl) {
+          const float* e = o[2 * dpl];
+          const float* od = o[2 * dpl + 1];
+          *reinterpret_cast<float4*>(dst + dpl * 16 + 2 * qd) =
+              make_float4(e[half * 2] * inv, od[half * 2] * inv, e[half * 2 + 1] * inv,
+                          od[half * 2 + 1] * inv);
+        }
+      } else {
+#pragma unroll
+        for (int dn = 0; dn < DW / 8; ++dn)
+          *reinterpret_cast<float2*>(dst + dn * 8 + qd) =
+              make_float2(o[dn][half * 2] * inv, o[dn][half * 2 + 1] * inv);
+      }
       if ((lane & 3) == 0 && part == 0)
         p.lse_part[((int64_t)b * p.num_splits + split) * p.H + h] = lse;
     }
