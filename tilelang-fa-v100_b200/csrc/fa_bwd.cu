@@ -15,14 +15,14 @@
 //                        dP^T = V dO^T           (SS)      -> TMEM [128,256)
 //                        dV  += P^T dO           (TS, A = P^T from TMEM)
 //                        dK  += dS^T Q           (SS, A = dS^T K-major in smem)
-//                        dQ^T = K^T dS^T         (SS, both MN-major, two 64-query
-//                                                 halves) -> the dP^T columns
+//                        dQ^T = K^T dS^T         (SS, both MN-major) -> the dP^T columns
 //                      and dQ is added to an fp32 accumulator (atomic mode): at D = 128
 //                      each 64-query half is staged in shared memory and added by one
 //                      bulk reduce-add, at D = 64 by per-thread fp32 atomics.  In
-//                      deterministic mode the last GEMM is skipped.
-//                      Issue order per step i: dV(i), S(i+1), dK(i), dQ(i), dP(i+1), so
-//                      S(i+1) overlaps the dS pass of step i.
+//                      deterministic mode the last GEMM is skipped.  All five are
+//                      M = 128, N = 128 (N = D for dV / dK).
+//                      Issue order per step i: dV(i), S(i+1), dQ(i), dK(i), dP(i+1), so
+//                      S(i+1) overlaps the dS pass of step i and the dQ drain overlaps dK(i).
 //   2b. fa_bwd_dkdv_persist  the same pipeline as 2, one CTA per SM looping over the
 //                      work items, for atomic mode at D = 128 with one query head per kv
 //                      head and short items (bwd_persistent on the host).
@@ -99,7 +99,7 @@ struct BwdCtl {
   uint64_t st_full[2];
   uint64_t st_empty[2];
   uint64_t s_full, p_ready, ds_ready, final_done, drain;
-  uint64_t dp_full[2], dq_full[2], dq_free[2];  // per 64-query half
+  uint64_t dp_full, dq_full, dq_free;
   uint64_t do_full[2], do_empty[2];
   uint32_t tmem_base;
   int abort_flag;
@@ -240,19 +240,98 @@ __device__ __forceinline__ void ld_shared_v4f(uint32_t addr, float* v) {
                : "r"(addr));
 }
 
+// cp.async.bulk.wait_group.read 1: at most one committed bulk operation of this thread may
+// still be reading shared memory.
+__device__ __forceinline__ void bulk_wait_group_read_1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
+// One step of the dQ warpgroup (atomic mode): thread = head-dim column dl (TMEM lane of
+// dQ^T, whose 128 columns are the step's queries) moves dQ^T out of TMEM and adds it to
+// the fp32 accumulator rows acc[0, 128).
+// D = 128: all 128 columns go to registers and the TMEM columns are released (dq_free)
+// at once, so dP^T(i+1) never waits for the adds.  The adds are bulk reduce-adds from
+// shared memory (they run in the TMA unit and L2, not as per-thread atomics), in four
+// 32-query pieces of 16 KB through two staging buffers: a piece is written while the
+// previous one is read by its reduce, which keeps the SM's reduce path (~40 GB/s per SM,
+// measured; 64 KB per step) busy.  A warp stores 32 consecutive d of a row: 128
+// contiguous bytes.  The issuer (thread 384) checks that the reduce that last used a
+// buffer has read it before the buffer is written again; named barrier 1 (these 128
+// threads) orders both, and its AND ends the loop for all four warps together when a wait
+// failed in any of them, so none is left at the barrier.
+// D = 64: per-thread atomics, one warp instruction per 128-byte row, the columns released
+// after the second half is in registers.  Returns false after a failed wait.
+template <int D, bool BULK>
+__device__ __forceinline__ bool dq_drain_step(BwdCtl* ctl, uint32_t tq, uint32_t stg, float* acc,
+                                              int dl, bool issuer, uint32_t par,
+                                              volatile int* abort_flag, int* err, int step) {
+  bool w = mbar_wait(smem_u32(&ctl->dq_full), par, abort_flag, err, FA_SITE_BWD_COMPUTE);
+  w = __all_sync(0xffffffffu, w);
+  if constexpr (BULK) {
+    if (!bar_red_and(1, 128, w)) return false;
+    if (issuer) FA_TRACE_EVENT(10, step);
+    tc_fence_after();
+    uint32_t v[128];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) tmem_ld32(tq + 32 * c, v + 32 * c);
+    tmem_wait_ld();
+    tc_fence_before();
+    mbar_arrive(smem_u32(&ctl->dq_free));
+#pragma unroll
+    for (int pc = 0; pc < 4; ++pc) {
+      const uint32_t buf = stg + (pc & 1) * (32 * D * 4);
+      if (issuer) bulk_wait_group_read_1();  // the reduce two pieces back has read `buf`
+      bar_sync_n(1, 128);
+#pragma unroll
+      for (int x = 0; x < 32; ++x)
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(buf + (x * D + dl) * 4), "r"(v[32 * pc + x])
+                     : "memory");
+      fence_async_shared();
+      bar_sync_n(1, 128);
+      if (issuer) {
+        bulk_reduce_add_f32(acc + 32 * pc * D, buf, 32 * D * 4);
+        bulk_commit_group();
+      }
+    }
+    if (issuer) FA_TRACE_EVENT(11, step);
+    return true;
+  } else {
+    if (!w) return false;
+    tc_fence_after();
+    uint32_t v[64];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      tmem_ld32(tq + 64 * hh, v);
+      tmem_ld32(tq + 64 * hh + 32, v + 32);
+      tmem_wait_ld();
+      if (hh == 1) {
+        tc_fence_before();
+        mbar_arrive(smem_u32(&ctl->dq_free));
+      }
+      if (dl < D) {
+        float* a = acc + (int64_t)(64 * hh) * D + dl;
+#pragma unroll
+        for (int x = 0; x < 64; ++x) atomicAdd(a + (int64_t)x * D, __uint_as_float(v[x]));
+      }
+    }
+    return true;
+  }
+}
+
 // 512 threads = 4 warpgroups.  Launch: 128 registers per thread (65,536).  Warpgroup 0
-// (producer, MMA issuer, 2 idle warps) and warpgroup 3 (dQ) drop, the two compute
-// warpgroups rise; the split is sized by ptxas spill reports (none at these values).
+// (producer, MMA issuer, 2 idle warps) drops to 56, the two compute warpgroups rise to
+// 144 and the dQ warpgroup to 168 (it holds a step's 128 dQ^T columns); the split is
+// sized by ptxas spill reports (none at these values) and uses all 65,536.
 constexpr int kBwdThreads = 512;
-constexpr int kBwdRegLow = 104;
-constexpr int kBwdRegDq = 112;
+constexpr int kBwdRegLow = 56;
+constexpr int kBwdRegDq = 168;
 constexpr int kBwdRegHigh = 144;
 static_assert(128 * kBwdRegLow + 256 * kBwdRegHigh + 128 * kBwdRegDq <= 65536,
               "register split exceeds the launch");
 // The persistent kernel's compute warpgroups carry the item loop's state as well: they
-// get 152 registers (ptxas reports 8 bytes of spill there, 120 at 144).
-constexpr int kBwdPRegLow = 104;
-constexpr int kBwdPRegDq = 96;
+// get 152 registers (ptxas reports spills at 144), the dQ warpgroup 152.
+constexpr int kBwdPRegLow = 56;
+constexpr int kBwdPRegDq = 152;
 constexpr int kBwdPRegHigh = 152;
 static_assert(128 * kBwdPRegLow + 256 * kBwdPRegHigh + 128 * kBwdPRegDq <= 65536,
               "register split exceeds the launch");
@@ -307,11 +386,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(smem_u32(&ctl->s_full), 1);
     mbar_init(smem_u32(&ctl->p_ready), 256);
     mbar_init(smem_u32(&ctl->ds_ready), 256);
-    for (int hh = 0; hh < 2; ++hh) {
-      mbar_init(smem_u32(&ctl->dp_full[hh]), 1);
-      mbar_init(smem_u32(&ctl->dq_full[hh]), 1);
-      mbar_init(smem_u32(&ctl->dq_free[hh]), 128);
-    }
+    mbar_init(smem_u32(&ctl->dp_full), 1);
+    mbar_init(smem_u32(&ctl->dq_full), 1);
+    mbar_init(smem_u32(&ctl->dq_free), 128);
     for (int s = 0; s < 2; ++s) {
       mbar_init(smem_u32(&ctl->do_full[s]), 1);
       mbar_init(smem_u32(&ctl->do_empty[s]), 1);
@@ -385,11 +462,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (lane == 0) {
       constexpr bool kBf16 = Pack2<T>::kBf16;
       constexpr uint32_t idS = idesc_f16(128, 128, kBf16, false, false);
-      constexpr uint32_t idS64 = idesc_f16(128, 64, kBf16, false, false);
       constexpr uint32_t idKV = idesc_f16(128, D, kBf16, false, true);
-      // dQ^T half = K^T dS^T (M = 128 head-dim rows; at D = 64 rows 64..127 read the next
-      // 16 KB of shared memory and are ignored), N = 64 queries, both operands MN-major.
-      constexpr uint32_t idQT = idesc_f16(128, 64, kBf16, true, true);
+      // dQ^T = K^T dS^T (M = 128 head-dim rows; at D = 64 rows 64..127 read the next
+      // 16 KB of shared memory and are ignored), N = 128 queries, both operands MN-major.
+      constexpr uint32_t idQT = idesc_f16(128, 128, kBf16, true, true);
       const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 256 + D;
       // Descriptors built once (K-major forms for S^T / dP^T, MN-major for the rest).
       const uint64_t dK_k = sdesc_sw128(sK, 16, 1024), dV_k = sdesc_sw128(sV, 16, 1024);
@@ -402,22 +478,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint64_t dDS_k = sdesc_sw128(sDS, 16, 1024);
       // S^T(i) = K Q(i)^T into [0, 128).
       auto issue_S = [&](int st) {
-        const uint64_t dQk = desc_add(dQ_k0, st * Cfg::TILE);
+        const uint64_t dQk = desc_add(opaque(dQ_k0), st * Cfg::TILE), dKk = opaque(dK_k);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
-          mma_ss(tS, desc_add(dK_k, o), desc_add(dQk, o), idS, kk > 0);
+          mma_ss(tS, desc_add(dKk, o), desc_add(dQk, o), idS, kk > 0);
         }
       };
-      // dP^T(i) = V dO(i)^T for queries [64hh, 64hh + 64) into [128 + 64hh, 192 + 64hh).
-      auto issue_dP = [&](int ds, int hh) {
-        const uint64_t ddOk = desc_add(ddO_k0, ds * Cfg::TILE + hh * 64 * 128);
+      // dP^T(i) = V dO(i)^T into [128, 256).
+      auto issue_dP = [&](int ds) {
+        const uint64_t ddOk = desc_add(opaque(ddO_k0), ds * Cfg::TILE), dVk = opaque(dV_k);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
-          mma_ss(tdP + 64 * hh, desc_add(dV_k, o), desc_add(ddOk, o), idS64, kk > 0);
+          mma_ss(tdP, desc_add(dVk, o), desc_add(ddOk, o), idS, kk > 0);
         }
-        mma_commit(smem_u32(&ctl->dp_full[hh]));
+        mma_commit(smem_u32(&ctl->dp_full));
+      };
+      // dQ^T(i) = K^T dS^T(i) into the dP^T columns, which the dS pass has read.
+      auto issue_dQ = [&]() {
+        const uint64_t dKm = opaque(dK_m), dDSm = opaque(dDS_m);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ss(tdP, desc_add(dKm, kk * 2048), desc_add(dDSm, kk * 2048), idQT, kk > 0);
+        mma_commit(smem_u32(&ctl->dq_full));
       };
       bool ok = mbar_wait(smem_u32(&ctl->kv_full), 0, abort_flag, p.err, FA_SITE_BWD_MMA);
       if (ok && n_iter > 0) {
@@ -429,22 +513,24 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           ok = mbar_wait(smem_u32(&ctl->do_full[0]), 0, abort_flag, p.err, FA_SITE_BWD_MMA);
           if (ok) {
             tc_fence_after();
-            issue_dP(0, 0);
-            issue_dP(0, 1);
+            issue_dP(0);
           }
         }
       }
       // Step i: dV(i) as soon as P^T(i) is in TMEM, then S(i+1) (its columns are free:
       // the tensor pipe runs MMAs in issue order, so dV(i) has read P^T first), then
-      // dK(i) and dQ^T(i) from the dS tile in shared memory, then each half of dP(i+1)
-      // once that half of dQ^T(i) has left TMEM.  The compute warpgroups find S(i+1)
-      // ready when they finish step i.
+      // dQ^T(i) and dK(i) from the dS tile in shared memory, then dP(i+1) once dQ^T(i)
+      // has left TMEM (the dQ warpgroup moves it out while dK(i) runs).  The compute
+      // warpgroups find S(i+1) ready when they finish step i.  Every GEMM is N = 128:
+      // a tcgen05.mma costs about as long at N = 64 as at N = 128 (measured), so halves
+      // would double the tensor time of dP^T and dQ^T.
       for (int i = 0; i < n_iter && ok; ++i) {
         const int s = i & 1;
         const uint32_t par = i & 1;
         const bool has_next = i + 1 < n_iter;
         const int ds = i % Cfg::DO_ST, ds1 = (i + 1) % Cfg::DO_ST;
-        const uint64_t dQm = desc_add(dQ_m0, s * Cfg::TILE), ddOm = desc_add(ddO_m0, ds * Cfg::TILE);
+        const uint64_t dQm = desc_add(opaque(dQ_m0), s * Cfg::TILE);
+        const uint64_t ddOm = desc_add(opaque(ddO_m0), ds * Cfg::TILE);
         // dV += P^T dO   (P^T for q 0..63 in columns 0..31, q 64..127 in 64..95)
         ok = mbar_wait(smem_u32(&ctl->p_ready), par, abort_flag, p.err, FA_SITE_BWD_MMA);
         if (!ok) break;
@@ -460,44 +546,35 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           ok = mbar_wait(smem_u32(&ctl->st_full[s ^ 1]), ((i + 1) >> 1) & 1, abort_flag, p.err,
                          FA_SITE_BWD_MMA);
           if (!ok) break;
+          FA_TRACE_EVENT(2, i);
           tc_fence_after();
           issue_S(s ^ 1);
           mma_commit(smem_u32(&ctl->s_full));
         }
-        // dK += dS^T Q   (A = dS^T, K-major in shared memory; B = Q MN-major)
         ok = mbar_wait(smem_u32(&ctl->ds_ready), par, abort_flag, p.err, FA_SITE_BWD_MMA);
         if (!ok) break;
         FA_TRACE_EVENT(4, i);
         tc_fence_after();
+        if (ATOMIC_DQ) issue_dQ();
+        const uint64_t dDSk = opaque(dDS_k);
+        // dK += dS^T Q   (A = dS^T, K-major in shared memory; B = Q MN-major)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
-          mma_ss(tdK, desc_add(dDS_k, o), desc_add(dQm, kk * 2048), idKV, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        if (ATOMIC_DQ) {
-          // dQ^T = K^T dS^T, one 64-query half at a time, into the dP^T columns.
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              mma_ss(tdP + 64 * hh, desc_add(dK_m, kk * 2048),
-                     desc_add(dDS_m, hh * Cfg::CHUNK + kk * 2048), idQT, kk > 0);
-            mma_commit(smem_u32(&ctl->dq_full[hh]));
-          }
+          mma_ss(tdK, desc_add(dDSk, o), desc_add(dQm, kk * 2048), idKV, (i > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(smem_u32(&ctl->st_empty[s]));
         FA_TRACE_EVENT(5, i);
         if (has_next) {
           ok = mbar_wait(smem_u32(&ctl->do_full[ds1]), ((i + 1) / Cfg::DO_ST) & 1, abort_flag, p.err,
                          FA_SITE_BWD_MMA);
-#pragma unroll
-          for (int hh = 0; hh < 2 && ok; ++hh) {
-            if (ATOMIC_DQ) {
-              ok = mbar_wait(smem_u32(&ctl->dq_free[hh]), par, abort_flag, p.err, FA_SITE_BWD_MMA);
-              if (!ok) break;
-            }
+          FA_TRACE_EVENT(0, i);
+          if (ok && ATOMIC_DQ)
+            ok = mbar_wait(smem_u32(&ctl->dq_free), par, abort_flag, p.err, FA_SITE_BWD_MMA);
+          if (ok) {
+            FA_TRACE_EVENT(1, i);
             tc_fence_after();
-            issue_dP(ds1, hh);
+            issue_dP(ds1);
           }
         }
       }
@@ -567,12 +644,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_arrive(smem_u32(&ctl->p_ready));
       if (threadIdx.x == 128) FA_TRACE_EVENT(7, i);
       // ---- pass B: dS^T = P^T (dP^T - D) * scale, to shared memory (K-major A of dK,
-      // MN-major B of dQ^T).  dP^T(i) was committed after dK(i-1) and dQ^T(i-1), so once
+      // MN-major B of dQ^T).  dP^T(i) was committed after dQ^T(i-1) and dK(i-1), so once
       // dp_full(i) has fired those MMAs have finished reading the previous dS tile.
-      w = mbar_wait(smem_u32(&ctl->dp_full[c]), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+      w = mbar_wait(smem_u32(&ctl->dp_full), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
       ok = __all_sync(0xffffffffu, w);
       if (!ok) break;
       if (threadIdx.x == 128) FA_TRACE_EVENT(8, i);
+      if (threadIdx.x == 256) FA_TRACE_EVENT(13, i);
       tc_fence_after();
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
@@ -601,6 +679,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl->ds_ready));
       if (threadIdx.x == 128) FA_TRACE_EVENT(9, i);
+      if (threadIdx.x == 256) FA_TRACE_EVENT(15, i);
     }
     // ---- dK, dV rows (lane = key row)
     if (ok) {
@@ -634,66 +713,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
   } else {
-    setmaxnreg_dec<kBwdRegDq>();
+    setmaxnreg_inc<kBwdRegDq>();
     if (ATOMIC_DQ) {
     // ============================================================ dQ warpgroup
-    // Thread = head-dim column d (TMEM lane of dQ^T).  Each 64-query half is moved out
-    // of TMEM (its columns are released for the next dP^T half at once) and added to the
-    // fp32 accumulator.  D = 128: the half is written to the staging tile [64 q][D] fp32
-    // in shared memory (a warp stores 32 consecutive d of a row: 128 contiguous bytes)
-    // and added by one bulk reduce-add (the 64 accumulator rows of a half are
-    // contiguous), so the adds run in the TMA unit and L2 instead of as per-thread
-    // atomics (cfg3 backward 3.71 -> 3.39 ms).  Thread 384 issues the reduce and waits
-    // for its read of the staging tile before the tile is written again; named barrier 1
-    // (these 128 threads) orders both, and its AND ends the loop for all four warps
-    // together when a wait fails in any of them, so none is left at the barrier.
-    // D = 64: per-thread atomics, one warp instruction per 128-byte row.
     const int dl = ((warp & 3) << 5) | lane;
-    const bool d_ok = dl < D;
     const bool issuer = threadIdx.x == 384;
     const uint32_t tq = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + 128;
     const uint32_t stg = base + Cfg::OFF_STG;
-    bool ok = true;
-    for (int i = 0; i < n_iter && ok; ++i) {
+    for (int i = 0; i < n_iter; ++i) {
       const int g = i / nqt, qt = t_start + i % nqt, h = hk * p.G + g;
       float* acc = p.dq_acc + (((int64_t)b * p.H + h) * p.Sq_pad + qt * kBwdBM) * D;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        bool w = mbar_wait(smem_u32(&ctl->dq_full[hh]), i & 1, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
-        w = __all_sync(0xffffffffu, w);
-        uint32_t v[64];
-        if (w) {
-          if (issuer) FA_TRACE_EVENT(10 + hh, i);
-          tc_fence_after();
-          tmem_ld32(tq + 64 * hh, v);
-          tmem_ld32(tq + 64 * hh + 32, v + 32);
-          tmem_wait_ld();
-          tc_fence_before();
-          mbar_arrive(smem_u32(&ctl->dq_free[hh]));
-        }
-        if constexpr (Cfg::BULK_DQ) {
-          if (issuer) bulk_wait_group_read();  // the last reduce has read the staging tile
-          ok = bar_red_and(1, 128, w);
-          if (!ok) break;
-#pragma unroll
-          for (int x = 0; x < 64; ++x)
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(stg + (x * D + dl) * 4), "r"(v[x]) : "memory");
-          fence_async_shared();
-          bar_sync_n(1, 128);
-          if (issuer) {
-            bulk_reduce_add_f32(acc + (int64_t)(64 * hh) * D, stg, 64 * D * 4);
-            bulk_commit_group();
-          }
-        } else {
-          ok = w;
-          if (!ok) break;
-          if (d_ok) {
-            float* a = acc + (int64_t)(64 * hh) * D + dl;
-#pragma unroll
-            for (int x = 0; x < 64; ++x) atomicAdd(a + (int64_t)x * D, __uint_as_float(v[x]));
-          }
-        }
-      }
+      if (!dq_drain_step<D, Cfg::BULK_DQ>(ctl, tq, stg, acc, dl, issuer, i & 1, abort_flag, p.err, i))
+        break;
     }
     if (issuer) bulk_wait_group_all();  // the adds complete before the CTA's memory goes
     }
@@ -774,11 +805,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(smem_u32(&ctl->s_full), 1);
     mbar_init(smem_u32(&ctl->p_ready), 256);
     mbar_init(smem_u32(&ctl->ds_ready), 256);
-    for (int hh = 0; hh < 2; ++hh) {
-      mbar_init(smem_u32(&ctl->dp_full[hh]), 1);
-      mbar_init(smem_u32(&ctl->dq_full[hh]), 1);
-      mbar_init(smem_u32(&ctl->dq_free[hh]), 128);
-    }
+    mbar_init(smem_u32(&ctl->dp_full), 1);
+    mbar_init(smem_u32(&ctl->dq_full), 1);
+    mbar_init(smem_u32(&ctl->dq_free), 128);
     for (int s = 0; s < 2; ++s) {
       mbar_init(smem_u32(&ctl->do_full[s]), 1);
       mbar_init(smem_u32(&ctl->do_empty[s]), 1);
@@ -869,11 +898,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (lane == 0) {
       constexpr bool kBf16 = Pack2<T>::kBf16;
       constexpr uint32_t idS = idesc_f16(128, 128, kBf16, false, false);
-      constexpr uint32_t idS64 = idesc_f16(128, 64, kBf16, false, false);
       constexpr uint32_t idKV = idesc_f16(128, D, kBf16, false, true);
-      // dQ^T half = K^T dS^T (M = 128 head-dim rows; at D = 64 rows 64..127 read the next
-      // 16 KB of shared memory and are ignored), N = 64 queries, both operands MN-major.
-      constexpr uint32_t idQT = idesc_f16(128, 64, kBf16, true, true);
+      // dQ^T = K^T dS^T (M = 128 head-dim rows; at D = 64 rows 64..127 read the next
+      // 16 KB of shared memory and are ignored), N = 128 queries, both operands MN-major.
+      constexpr uint32_t idQT = idesc_f16(128, 128, kBf16, true, true);
       const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 256 + D;
       // Descriptors built once (K-major forms for S^T / dP^T, MN-major for the rest).
       const uint64_t dK_k = sdesc_sw128(sK, 16, 1024), dV_k = sdesc_sw128(sV, 16, 1024);
@@ -886,30 +914,38 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint64_t dDS_k = sdesc_sw128(sDS, 16, 1024);
       // S^T(i) = K Q(i)^T into [0, 128).
       auto issue_S = [&](int st) {
-        const uint64_t dQk = desc_add(dQ_k0, st * Cfg::TILE);
+        const uint64_t dQk = desc_add(opaque(dQ_k0), st * Cfg::TILE), dKk = opaque(dK_k);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
-          mma_ss(tS, desc_add(dK_k, o), desc_add(dQk, o), idS, kk > 0);
+          mma_ss(tS, desc_add(dKk, o), desc_add(dQk, o), idS, kk > 0);
         }
       };
-      // dP^T(i) = V dO(i)^T for queries [64hh, 64hh + 64) into [128 + 64hh, 192 + 64hh).
-      auto issue_dP = [&](int ds, int hh) {
-        const uint64_t ddOk = desc_add(ddO_k0, ds * Cfg::TILE + hh * 64 * 128);
+      // dP^T(i) = V dO(i)^T into [128, 256).
+      auto issue_dP = [&](int ds) {
+        const uint64_t ddOk = desc_add(opaque(ddO_k0), ds * Cfg::TILE), dVk = opaque(dV_k);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
-          mma_ss(tdP + 64 * hh, desc_add(dV_k, o), desc_add(ddOk, o), idS64, kk > 0);
+          mma_ss(tdP, desc_add(dVk, o), desc_add(ddOk, o), idS, kk > 0);
         }
-        mma_commit(smem_u32(&ctl->dp_full[hh]));
+        mma_commit(smem_u32(&ctl->dp_full));
       };
-      // Per item: wait for its K / V, issue S and dP^T of its first step (the first dP^T
-      // half waits until the dQ warpgroup has moved the last step's dQ^T half out of
-      // those columns), then the steps.  Step g: dV(g) as soon as P^T(g) is in TMEM, then
-      // S(g+1) (its columns are free: the tensor pipe runs MMAs in issue order, so dV(g)
-      // has read P^T first), then dK(g) and dQ^T(g) from the dS tile in shared memory,
-      // then each half of dP(g+1) once that half of dQ^T(g) has left TMEM.  The compute
-      // warpgroups find S(g+1) ready when they finish step g.  After the item's last step:
+      // dQ^T(i) = K^T dS^T(i) into the dP^T columns, which the dS pass has read.
+      auto issue_dQ = [&]() {
+        const uint64_t dKm = opaque(dK_m), dDSm = opaque(dDS_m);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ss(tdP, desc_add(dKm, kk * 2048), desc_add(dDSm, kk * 2048), idQT, kk > 0);
+        mma_commit(smem_u32(&ctl->dq_full));
+      };
+      // Per item: wait for its K / V, issue S and dP^T of its first step (dP^T waits
+      // until the dQ warpgroup has moved the last step's dQ^T out of those columns), then
+      // the steps.  Step g: dV(g) as soon as P^T(g) is in TMEM, then S(g+1) (its columns
+      // are free: the tensor pipe runs MMAs in issue order, so dV(g) has read P^T first),
+      // then dQ^T(g) and dK(g) from the dS tile in shared memory, then dP(g+1) once
+      // dQ^T(g) has left TMEM.  The compute warpgroups find S(g+1) ready when they finish
+      // step g.  After the item's last step:
       // final_done (its dK / dV are complete in TMEM) and kv_empty (K / V are free).  The
       // next item's first dV / dK overwrite the accumulators only after its p_ready /
       // ds_ready, which the compute warpgroups give after they have read dK / dV out.
@@ -927,15 +963,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         mma_commit(smem_u32(&ctl->s_full));
         ok = mbar_wait(smem_u32(&ctl->do_full[gi % Cfg::DO_ST]), (gi / Cfg::DO_ST) & 1, abort_flag,
                        p.err, FA_SITE_BWD_MMA);
-#pragma unroll
-        for (int hh = 0; hh < 2 && ok; ++hh) {
-          if (ATOMIC_DQ && gi > 0) {
-            ok = mbar_wait(smem_u32(&ctl->dq_free[hh]), (gi - 1) & 1, abort_flag, p.err,
-                           FA_SITE_BWD_MMA);
-            if (!ok) break;
-          }
+        if (ok && ATOMIC_DQ && gi > 0)
+          ok = mbar_wait(smem_u32(&ctl->dq_free), (gi - 1) & 1, abort_flag, p.err, FA_SITE_BWD_MMA);
+        if (ok) {
           tc_fence_after();
-          issue_dP(gi % Cfg::DO_ST, hh);
+          issue_dP(gi % Cfg::DO_ST);
         }
         for (int i = 0; i < n_iter && ok; ++i) {
           const int g = gi + i;
@@ -943,7 +975,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const uint32_t par = g & 1;
           const bool has_next = i + 1 < n_iter;
           const int ds = g % Cfg::DO_ST, ds1 = (g + 1) % Cfg::DO_ST;
-          const uint64_t dQm = desc_add(dQ_m0, s * Cfg::TILE), ddOm = desc_add(ddO_m0, ds * Cfg::TILE);
+          const uint64_t dQm = desc_add(opaque(dQ_m0), s * Cfg::TILE);
+          const uint64_t ddOm = desc_add(opaque(ddO_m0), ds * Cfg::TILE);
           // dV += P^T dO   (P^T for q 0..63 in columns 0..31, q 64..127 in 64..95)
           ok = mbar_wait(smem_u32(&ctl->p_ready), par, abort_flag, p.err, FA_SITE_BWD_MMA);
           if (!ok) break;
@@ -963,40 +996,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             issue_S(s ^ 1);
             mma_commit(smem_u32(&ctl->s_full));
           }
-          // dK += dS^T Q   (A = dS^T, K-major in shared memory; B = Q MN-major)
           ok = mbar_wait(smem_u32(&ctl->ds_ready), par, abort_flag, p.err, FA_SITE_BWD_MMA);
           if (!ok) break;
           FA_TRACE_EVENT(4, g);
           tc_fence_after();
+          if (ATOMIC_DQ) issue_dQ();
+          const uint64_t dDSk = opaque(dDS_k);
+          // dK += dS^T Q   (A = dS^T, K-major in shared memory; B = Q MN-major)
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t o = (kk >> 2) * Cfg::CHUNK + (kk & 3) * 32;
-            mma_ss(tdK, desc_add(dDS_k, o), desc_add(dQm, kk * 2048), idKV, (i > 0 || kk > 0) ? 1u : 0u);
-          }
-          if (ATOMIC_DQ) {
-            // dQ^T = K^T dS^T, one 64-query half at a time, into the dP^T columns.
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-#pragma unroll
-              for (int kk = 0; kk < 8; ++kk)
-                mma_ss(tdP + 64 * hh, desc_add(dK_m, kk * 2048),
-                       desc_add(dDS_m, hh * Cfg::CHUNK + kk * 2048), idQT, kk > 0);
-              mma_commit(smem_u32(&ctl->dq_full[hh]));
-            }
+            mma_ss(tdK, desc_add(dDSk, o), desc_add(dQm, kk * 2048), idKV, (i > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(smem_u32(&ctl->st_empty[s]));
           FA_TRACE_EVENT(5, g);
           if (has_next) {
             ok = mbar_wait(smem_u32(&ctl->do_full[ds1]), ((g + 1) / Cfg::DO_ST) & 1, abort_flag,
                            p.err, FA_SITE_BWD_MMA);
-#pragma unroll
-            for (int hh = 0; hh < 2 && ok; ++hh) {
-              if (ATOMIC_DQ) {
-                ok = mbar_wait(smem_u32(&ctl->dq_free[hh]), par, abort_flag, p.err, FA_SITE_BWD_MMA);
-                if (!ok) break;
-              }
+            if (ok && ATOMIC_DQ)
+              ok = mbar_wait(smem_u32(&ctl->dq_free), par, abort_flag, p.err, FA_SITE_BWD_MMA);
+            if (ok) {
               tc_fence_after();
-              issue_dP(ds1, hh);
+              issue_dP(ds1);
             }
           }
         }
@@ -1075,9 +1096,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_arrive(smem_u32(&ctl->p_ready));
       if (threadIdx.x == 128) FA_TRACE_EVENT(7, g);
       // ---- pass B: dS^T = P^T (dP^T - D) * scale, to shared memory (K-major A of dK,
-      // MN-major B of dQ^T).  dP^T(i) was committed after dK(i-1) and dQ^T(i-1), so once
+      // MN-major B of dQ^T).  dP^T(i) was committed after dQ^T(i-1) and dK(i-1), so once
       // dp_full(i) has fired those MMAs have finished reading the previous dS tile.
-      w = mbar_wait(smem_u32(&ctl->dp_full[c]), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
+      w = mbar_wait(smem_u32(&ctl->dp_full), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
       ok = __all_sync(0xffffffffu, w);
       if (!ok) break;
       if (threadIdx.x == 128) FA_TRACE_EVENT(8, g);
@@ -1152,72 +1173,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     }
   } else {
-    setmaxnreg_dec<kBwdPRegDq>();
+    setmaxnreg_inc<kBwdPRegDq>();
     if (ATOMIC_DQ) {
     // ============================================================ dQ warpgroup
-    // Thread = head-dim column d (TMEM lane of dQ^T).  Each 64-query half is moved out
-    // of TMEM (its columns are released for the next dP^T half at once) and added to the
-    // fp32 accumulator.  D = 128: the half is written to the staging tile [64 q][D] fp32
-    // in shared memory (a warp stores 32 consecutive d of a row: 128 contiguous bytes)
-    // and added by one bulk reduce-add (the 64 accumulator rows of a half are
-    // contiguous), so the adds run in the TMA unit and L2 instead of as per-thread
-    // atomics (cfg3 backward 3.71 -> 3.39 ms).  Thread 384 issues the reduce and waits
-    // for its read of the staging tile before the tile is written again; named barrier 1
-    // (these 128 threads) orders both, and its AND ends the loop for all four warps
-    // together when a wait fails in any of them, so none is left at the barrier.
-    // D = 64: per-thread atomics, one warp instruction per 128-byte row.
     const int dl = ((warp & 3) << 5) | lane;
-    const bool d_ok = dl < D;
     const bool issuer = threadIdx.x == 384;
     const uint32_t tq = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + 128;
     const uint32_t stg = base + Cfg::OFF_STG;
     bool ok = true;
     int gi = 0;
     for (int L = blockIdx.x; L < p.n_items && ok; L += gridDim.x) {
-    const BwdItem it = bwd_item(p, L);
-    for (int i = 0; i < it.n_iter && ok; ++i) {
-      const int gs = gi + i;
-      const int g = i / it.nqt, qt = it.t_start + i % it.nqt, h = it.hk * p.G + g;
-      float* acc = p.dq_acc + (((int64_t)it.b * p.H + h) * p.Sq_pad + qt * kBwdBM) * D;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        bool w = mbar_wait(smem_u32(&ctl->dq_full[hh]), gs & 1, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
-        w = __all_sync(0xffffffffu, w);
-        uint32_t v[64];
-        if (w) {
-          if (issuer) FA_TRACE_EVENT(10 + hh, gs);
-          tc_fence_after();
-          tmem_ld32(tq + 64 * hh, v);
-          tmem_ld32(tq + 64 * hh + 32, v + 32);
-          tmem_wait_ld();
-          tc_fence_before();
-          mbar_arrive(smem_u32(&ctl->dq_free[hh]));
-        }
-        if constexpr (Cfg::BULK_DQ) {
-          if (issuer) bulk_wait_group_read();  // the last reduce has read the staging tile
-          ok = bar_red_and(1, 128, w);
-          if (!ok) break;
-#pragma unroll
-          for (int x = 0; x < 64; ++x)
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(stg + (x * D + dl) * 4), "r"(v[x]) : "memory");
-          fence_async_shared();
-          bar_sync_n(1, 128);
-          if (issuer) {
-            bulk_reduce_add_f32(acc + (int64_t)(64 * hh) * D, stg, 64 * D * 4);
-            bulk_commit_group();
-          }
-        } else {
-          ok = w;
-          if (!ok) break;
-          if (d_ok) {
-            float* a = acc + (int64_t)(64 * hh) * D + dl;
-#pragma unroll
-            for (int x = 0; x < 64; ++x) atomicAdd(a + (int64_t)x * D, __uint_as_float(v[x]));
-          }
-        }
+      const BwdItem it = bwd_item(p, L);
+      for (int i = 0; i < it.n_iter && ok; ++i) {
+        const int gs = gi + i;
+        const int g = i / it.nqt, qt = it.t_start + i % it.nqt, h = it.hk * p.G + g;
+        float* acc = p.dq_acc + (((int64_t)it.b * p.H + h) * p.Sq_pad + qt * kBwdBM) * D;
+        ok = dq_drain_step<D, Cfg::BULK_DQ>(ctl, tq, stg, acc, dl, issuer, gs & 1, abort_flag,
+                                            p.err, gs);
       }
-    }
-    gi += it.n_iter;
+      gi += it.n_iter;
     }
     if (issuer) bulk_wait_group_all();  // the adds complete before the CTA's memory goes
     }

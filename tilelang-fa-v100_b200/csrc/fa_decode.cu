@@ -259,7 +259,6 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
     float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
-      uint32_t b0, b1, b2, b3;
       if constexpr (KV8) {
         // Two k steps per ldmatrix x4 over the byte rows (each 8x8 b16 matrix = 8 tokens
         // x 16 dims): matrices (tokens 0-7, dims 32 kp ..), (8-15, same), (0-7, +16),
@@ -280,17 +279,17 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
         mma16816<kBf16>(sc[1], qa[ks], c[2], c[3]);
         mma16816<kBf16>(sc[0], qa[ks + 1], c[4], c[5]);
         mma16816<kBf16>(sc[1], qa[ks + 1], c[6], c[7]);
-        continue;
       } else {
         // matrices: (tokens 0-7, d lo), (tokens 0-7, d hi), (tokens 8-15, d lo), (tokens 8-15, d hi)
         const int mi = lane >> 3;
         const int row = ((mi >> 1) << 3) + (lane & 7);
         const int dchunk = (ks & 3) * 2 + (mi & 1);
         const uint32_t addr = kbase + (ks >> 2) * (kDecChunk * 128) + swz(row, dchunk);
+        uint32_t b0, b1, b2, b3;
         ldsm_x4(addr, b0, b1, b2, b3);
+        mma16816<kBf16>(sc[0], qa[ks], b0, b1);
+        mma16816<kBf16>(sc[1], qa[ks], b2, b3);
       }
-      mma16816<kBf16>(sc[0], qa[ks], b0, b1);
-      mma16816<kBf16>(sc[1], qa[ks], b2, b3);
     }
     const int tok0 = (c_begin + it) * kDecChunk;
     if (tok0 + kDecChunk > L) {
@@ -342,7 +341,6 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
 #pragma unroll
     for (int dpl = 0; dpl < DW / 16; ++dpl) {
       const int dp = part * (DW / 16) + dpl;
-      uint32_t b0, b1, b2, b3;
       if constexpr (KV8) {
         // ldmatrix.trans over the byte rows, two 16-dim groups per x4: matrices (tokens
         // 0-7, dims 16 dp ..), (8-15, same), (0-7, dims 16 dp + 16 ..), (8-15, same); lane
@@ -363,17 +361,17 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
           mma16816<kBf16>(o[2 * (dpl + gp) + 1], pa, e4m3x2_to<T>(prmt(lo, 0x0031)),
                           e4m3x2_to<T>(prmt(hi, 0x0031)));
         }
-        continue;
       } else {
         // matrices: (tok 0-7, d 16dp..+7), (tok 8-15, same), (tok 0-7, d +8..+15), (tok 8-15, +8..)
         const int mi = lane >> 3;
         const int row = ((mi & 1) << 3) + (lane & 7);
         const int dchunk = ((dp * 2) & 7) + (mi >> 1);
         const uint32_t addr = vbase + ((dp * 16) >> 6) * (kDecChunk * 128) + swz(row, dchunk);
+        uint32_t b0, b1, b2, b3;
         ldsm_x4_t(addr, b0, b1, b2, b3);
+        mma16816<kBf16>(o[2 * dpl], pa, b0, b1);
+        mma16816<kBf16>(o[2 * dpl + 1], pa, b2, b3);
       }
-      mma16816<kBf16>(o[2 * dpl], pa, b0, b1);
-      mma16816<kBf16>(o[2 * dpl + 1], pa, b2, b3);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&ctl->empty[s]));

@@ -255,6 +255,13 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
+// The value of x, opaque to the compiler at this point: a descriptor laundered inside a
+// loop is not hoisted (with everything derived from it) out of the loop, which keeps the
+// MMA issuer's unrolled descriptor sets from occupying registers across the whole loop.
+__device__ __forceinline__ uint64_t opaque(uint64_t x) {
+  asm volatile("" : "+l"(x));
+  return x;
+}
 // Descriptor of a sub-tile `byte_off` bytes past the one `d` describes (the start
 // address field holds addr >> 4 in its low 14 bits; shared addresses stay < 256 KB).
 __device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t byte_off) {
@@ -339,7 +346,7 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool a
 // %globaltimer at named phases of the first FA_TRACE_CTAS CTAs so the pipeline's
 // per-phase latencies can be read back with fa_debug_trace_read().
 #ifdef FA_TRACE
-constexpr int FA_TRACE_CTAS = 2, FA_TRACE_EVENTS = 16, FA_TRACE_ITERS = 64;
+constexpr int FA_TRACE_CTAS = 2, FA_TRACE_EVENTS = 24, FA_TRACE_ITERS = 64;
 // One copy per translation unit (no relocatable device code); the unit that traces
 // also exports the reader.
 static __device__ unsigned long long g_fa_trace[FA_TRACE_CTAS][FA_TRACE_EVENTS][FA_TRACE_ITERS];
