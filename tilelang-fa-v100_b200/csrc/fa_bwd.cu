@@ -291,6 +291,7 @@ __device__ __forceinline__ bool dq_drain_step(BwdCtl* ctl, uint32_t tq, uint32_t
       if (issuer) {
         bulk_reduce_add_f32(acc + 32 * pc * D, buf, 32 * D * 4);
         bulk_commit_group();
+        FA_TRACE_EVENT(16 + pc, step);
       }
     }
     if (issuer) FA_TRACE_EVENT(11, step);
@@ -607,32 +608,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       ok = __all_sync(0xffffffffu, w);
       if (!ok) break;
       if (threadIdx.x == 128) FA_TRACE_EVENT(6, i);
+      if (threadIdx.x == 128) FA_TRACE_CYCLES(20, i);
       tc_fence_after();
       // ---- pass A: P^T = exp2(S^T * scale*log2e - lse*log2e), masked; 32 columns at a time
       const int qbase = q0 + 64 * c;
       const bool full = key_ok && (!p.causal || key <= qbase + off);
+      // Both 32-column halves of S^T are requested before the one wait, so a single TMEM
+      // load latency is exposed per pass.
       float pv[64];
+      {
+        uint32_t sv[64];
+        tmem_ld32(tS + 64 * c, sv);
+        tmem_ld32(tS + 64 * c + 32, sv + 32);
 #pragma unroll
-      for (int ch = 0; ch < 2; ++ch) {
-        uint32_t sv[32];
-        tmem_ld32(tS + 64 * c + 32 * ch, sv);
-        float lv[32];
+        for (int ch = 0; ch < 2; ++ch) {
+          float lv[32];
 #pragma unroll
-        for (int m = 0; m < 8; ++m) ld_shared_v4f(lse_a + (32 * ch + 4 * m) * 4, lv + 4 * m);
-        tmem_wait_ld();
-        if (full) {
+          for (int m = 0; m < 8; ++m) ld_shared_v4f(lse_a + (32 * ch + 4 * m) * 4, lv + 4 * m);
+          if (ch == 0) tmem_wait_ld();
+          if (full) {
 #pragma unroll
-          for (int x = 0; x < 32; ++x)
-            pv[32 * ch + x] = ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lv[x]));
-        } else {
+            for (int x = 0; x < 32; ++x)
+              pv[32 * ch + x] = ex2_approx(fmaf(__uint_as_float(sv[32 * ch + x]), c2, -lv[x]));
+          } else {
 #pragma unroll
-          for (int x = 0; x < 32; ++x) {
-            const bool vis = key_ok && key <= qbase + 32 * ch + x + off;
-            pv[32 * ch + x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lv[x])) : 0.f;
+            for (int x = 0; x < 32; ++x) {
+              const bool vis = key_ok && key <= qbase + 32 * ch + x + off;
+              pv[32 * ch + x] =
+                  vis ? ex2_approx(fmaf(__uint_as_float(sv[32 * ch + x]), c2, -lv[x])) : 0.f;
+            }
           }
         }
       }
       if (threadIdx.x == 128) FA_TRACE_EVENT(14, i);
+      if (threadIdx.x == 128) FA_TRACE_CYCLES(21, i);
       {
         uint32_t pk[32];
 #pragma unroll
@@ -1063,24 +1072,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // ---- pass A: P^T = exp2(S^T * scale*log2e - lse*log2e), masked; 32 columns at a time
       const int qbase = q0 + 64 * c;
       const bool full = key_ok && (!p.causal || key <= qbase + off);
+      // Both 32-column halves of S^T are requested before the one wait, so a single TMEM
+      // load latency is exposed per pass.
       float pv[64];
+      {
+        uint32_t sv[64];
+        tmem_ld32(tS + 64 * c, sv);
+        tmem_ld32(tS + 64 * c + 32, sv + 32);
 #pragma unroll
-      for (int ch = 0; ch < 2; ++ch) {
-        uint32_t sv[32];
-        tmem_ld32(tS + 64 * c + 32 * ch, sv);
-        float lv[32];
+        for (int ch = 0; ch < 2; ++ch) {
+          float lv[32];
 #pragma unroll
-        for (int m = 0; m < 8; ++m) ld_shared_v4f(lse_a + (32 * ch + 4 * m) * 4, lv + 4 * m);
-        tmem_wait_ld();
-        if (full) {
+          for (int m = 0; m < 8; ++m) ld_shared_v4f(lse_a + (32 * ch + 4 * m) * 4, lv + 4 * m);
+          if (ch == 0) tmem_wait_ld();
+          if (full) {
 #pragma unroll
-          for (int x = 0; x < 32; ++x)
-            pv[32 * ch + x] = ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lv[x]));
-        } else {
+            for (int x = 0; x < 32; ++x)
+              pv[32 * ch + x] = ex2_approx(fmaf(__uint_as_float(sv[32 * ch + x]), c2, -lv[x]));
+          } else {
 #pragma unroll
-          for (int x = 0; x < 32; ++x) {
-            const bool vis = key_ok && key <= qbase + 32 * ch + x + off;
-            pv[32 * ch + x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lv[x])) : 0.f;
+            for (int x = 0; x < 32; ++x) {
+              const bool vis = key_ok && key <= qbase + 32 * ch + x + off;
+              pv[32 * ch + x] =
+                  vis ? ex2_approx(fmaf(__uint_as_float(sv[32 * ch + x]), c2, -lv[x])) : 0.f;
+            }
           }
         }
       }

@@ -3,11 +3,11 @@
 // (tilelang_flash_attn_func, reference kernel _kernels_forward.py:94-172) and the paged
 // vLLM-cache path (tilelang_paged_forward, reference kernel _kernels_paged.py:193-344).
 // Two schedules of the same per-item pipeline, chosen per launch (fwd_persistent):
-//   fa_fwd_kernel          one CTA per work item (dense D = 128 / 256 with long items)
+//   fa_fwd_kernel          one CTA per work item (dense D = 256 non-causal with long items)
 //   fa_fwd_persist_kernel  one CTA per SM claiming work items in the same order, the
 //                          next item's Q load and first S overlapping the current
-//                          item's tail (paged prefill, dense D = 64, short dense items,
-//                          dense D = 256 causal)
+//                          item's tail (paged prefill, dense D = 64 and 128, short dense
+//                          items, dense D = 256 causal)
 //
 // CTA work item: NQ Q tiles of 128 rows for one kv head.  A row is a (token, head)
 // pair: the G = H / Hk query heads that share a kv head are packed into the rows
@@ -41,6 +41,14 @@ namespace fa {
 constexpr int kFwdBM = 128;  // rows per Q tile = TMEM lanes
 constexpr int kFwdBN = 128;  // keys per KV tile
 constexpr int kFwdOrderGroup = 8;  // (batch, kv head) units ordered together (dense)
+// Two-tile CTAs (384 threads, 168 registers a thread at launch): the producer / MMA
+// warpgroup drops to 56 registers and the two softmax warpgroups rise to 224, enough for
+// a row's 128 S values at once.  The issuer's descriptors are laundered per use (opaque)
+// so the MMA warp fits 56; ptxas reports no spills at these values.
+constexpr int kFwdRegLow = 56;
+constexpr int kFwdRegHigh = 224;
+static_assert(128 * kFwdRegLow + 256 * kFwdRegHigh <= 384 * 168,
+              "forward register split exceeds the launch");
 
 // Dense work order over n_t q blocks x n_u (batch, kv head) units: linear index L walks
 // groups of kFwdOrderGroup units and, inside a group, the q block ranks across all its
@@ -214,6 +222,8 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
   const int b = ctl->b, tok0 = ctl->tok0, q_len = ctl->q_len, kv_len = ctl->kv_len;
   const int off = ctl->off, tok_base = ctl->tok_base, j0 = ctl->j0, nkv = ctl->nkv;
 
+  if (warp < 4) {
+    if (NQ == 2) setmaxnreg_dec<kFwdRegLow>();
   if (warp == 0) {
     // ============================================================ TMA producer
     // Dense: lane 0 issues every copy.  Paged: lane r fetches the page id of box r of the
@@ -304,8 +314,8 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
       // S_t = Q_t K^T over D in steps of 16 (K-major, 128-byte swizzle: step = +32 B
       // inside a 64-column chunk, next chunk at +16 KB).
       auto issue_S = [&](int t, int slot) {
-        const uint64_t qa = desc_add(q_desc0, t * Cfg::TILE_BYTES);
-        const uint64_t ka = desc_add(k_desc0, slot * Cfg::TILE_BYTES);
+        const uint64_t qa = desc_add(opaque(q_desc0), t * Cfg::TILE_BYTES);
+        const uint64_t ka = desc_add(opaque(k_desc0), slot * Cfg::TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK_BYTES + (kk & 3) * 32;
@@ -316,7 +326,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
       // rows = +2 KB, 64-column chunks of D at +16 KB = LBO).  P's 16-bit pairs: 16 keys
       // = 8 TMEM columns.
       auto issue_PV = [&](int t, int slot, bool acc, int hf) {
-        const uint64_t va = desc_add(v_desc0, slot * Cfg::TILE_BYTES);
+        const uint64_t va = desc_add(opaque(v_desc0), slot * Cfg::TILE_BYTES);
 #pragma unroll
         for (int k4 = 0; k4 < kFwdBN / 32; ++k4) {
           const int kk = hf * (kFwdBN / 32) + k4;
@@ -384,7 +394,9 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
       mma_commit(smem_u32(&ctl->drain));
       mbar_wait_drain(smem_u32(&ctl->drain), 0);
     }
-  } else if (warp >= 4) {
+  }
+  } else {
+    if (NQ == 2) setmaxnreg_inc<kFwdRegHigh>();
     // ============================================================ softmax / epilogue
     const int t = (warp - 4) >> 2;
     const int r = ((warp & 3) << 5) | lane;
@@ -735,7 +747,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
   using Cfg = FwdPersistCfg<D, NQ>;
   constexpr int ST = Cfg::STAGES;
   constexpr int QB = Cfg::QB;
-  constexpr bool kReloadS = NQ == 2;  // S values re-read from TMEM to stay within 168 registers
+  constexpr bool kReloadS = false;  // true: S values re-read from TMEM (for a tighter register budget)
   // Release P_t in two halves (PV over the first 64 keys overlaps the second half's
   // exponentials).  Measured faster for dense D >= 128; for D = 64 (cheap PV) and the
   // paged path the extra barrier costs more than the overlap gains.
@@ -787,6 +799,8 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
 
+  if (warp < 4) {
+    if (NQ == 2) setmaxnreg_dec<kFwdRegLow>();
   if (warp == 0) {
     // ============================================================ scheduler + TMA producer
     // Lane 0 claims and publishes each work item.  Dense: lane 0 issues every copy.
@@ -915,8 +929,8 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
       // S_t = Q_t K^T over D in steps of 16 (K-major, 128-byte swizzle: step = +32 B
       // inside a 64-column chunk, next chunk at +16 KB).
       auto issue_S = [&](int t, int slot) {
-        const uint64_t qa = desc_add(q_desc0, qoff + t * Cfg::TILE_BYTES);
-        const uint64_t ka = desc_add(k_desc0, slot * Cfg::TILE_BYTES);
+        const uint64_t qa = desc_add(opaque(q_desc0), qoff + t * Cfg::TILE_BYTES);
+        const uint64_t ka = desc_add(opaque(k_desc0), slot * Cfg::TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t o = (kk >> 2) * Cfg::CHUNK_BYTES + (kk & 3) * 32;
@@ -927,7 +941,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
       // rows = +2 KB, 64-column chunks of D at +16 KB = LBO).  P's 16-bit pairs: 16 keys
       // = 8 TMEM columns.
       auto issue_PV = [&](int t, int slot, bool acc, int hf) {
-        const uint64_t va = desc_add(v_desc0, slot * Cfg::TILE_BYTES);
+        const uint64_t va = desc_add(opaque(v_desc0), slot * Cfg::TILE_BYTES);
 #pragma unroll
         for (int k4 = 0; k4 < kFwdBN / 32; ++k4) {
           const int kk = hf * (kFwdBN / 32) + k4;
@@ -1025,7 +1039,9 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
       mma_commit(smem_u32(&ctl->drain));
       mbar_wait_drain(smem_u32(&ctl->drain), 0);
     }
-  } else if (warp >= 4) {
+  }
+  } else {
+    if (NQ == 2) setmaxnreg_inc<kFwdRegHigh>();
     // ============================================================ softmax / epilogue
     const int t = (warp - 4) >> 2;
     const int r = ((warp & 3) << 5) | lane;
@@ -1319,14 +1335,15 @@ static int* fwd_sched_counter(cudaStream_t st) {
   return c;
 }
 // Which schedule serves a launch.  The persistent kernel hides each work item's set-up
-// (Q load, first S, epilogue) behind the previous item, which pays when items are short;
-// the one-CTA-per-item kernel runs each KV step faster at D = 128 (there the persistent
-// kernel's two-tile softmax needs two-pass S loads to fit 168 registers and its larger
-// code misses the instruction cache more).  Measured (bf16, TFLOP/s, direct -> persistent):
-// D = 128 causal S = 512 238 -> 338, 1024 404 -> 496, 2048 620 -> 662, 4096 855 -> 777;
-// non-causal S = 1024 946 -> 959, 4096 1195 -> 1127; D = 256 causal S = 4096 860 -> 945,
-// non-causal 1112 -> 1103.  Hence: paged and D = 64 always persistent; dense D = 128 / 256
-// persistent when a work item averages at most 12 KV tiles, and D = 256 causal always.
+// (Q load, first S, epilogue) behind the previous item.  With the register split
+// (softmax warpgroups at 224 registers, a row's 128 S values loaded once) its KV steps
+// are as fast as the one-CTA-per-item kernel's, so it serves every D = 128 launch.
+// Measured (bf16, TFLOP/s, one-CTA-per-item -> persistent, same process): D = 128 causal
+// S = 4096 849 -> 940-978, S = 2048 (B 16) 750-789 -> 747-765, GQA 32/8 883-896 ->
+// 997-1017, fp16 causal 758-815 -> 883-937, non-causal S = 4096 1047-1168 -> 1040-1166;
+// D = 256 non-causal S = 4096 1006-1056 -> 975-1040 (earlier, without the split: causal
+// 860 -> 945).  Hence: paged, D = 64 and D = 128 always persistent; D = 256 causal always,
+// non-causal when a work item averages at most 12 KV tiles.
 constexpr int kFwdPersistMaxTiles = 12;
 template <int D, bool PAGED>
 constexpr bool fwd_may_persist() { return true; }
@@ -1334,7 +1351,7 @@ template <int D, bool PAGED>
 constexpr bool fwd_may_direct() { return !PAGED && D != 64; }
 template <int D, bool PAGED>
 static bool fwd_persistent(bool causal, int kv_len) {
-  if (!fwd_may_direct<D, PAGED>()) return true;
+  if (!fwd_may_direct<D, PAGED>() || D == 128) return true;
   const int tiles = (kv_len + kFwdBN - 1) / kFwdBN;
   const int avg_tiles = causal ? (tiles + 1) / 2 : tiles;  // per work item
   if (D == 256 && causal) return true;

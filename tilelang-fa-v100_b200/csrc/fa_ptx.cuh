@@ -356,7 +356,17 @@ static __device__ unsigned long long g_fa_trace[FA_TRACE_CTAS][FA_TRACE_EVENTS][
     if (cta_ < (unsigned)FA_TRACE_CTAS && (it) < FA_TRACE_ITERS)                            \
       g_fa_trace[cta_][(ev)][(it)] = ::fa::globaltimer_ns();                                \
   } while (0)
+// Same slots, SM clock cycles instead of nanoseconds (for the achieved clock rate).
+#define FA_TRACE_CYCLES(ev, it)                                                             \
+  do {                                                                                      \
+    const unsigned cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);   \
+    if (cta_ < (unsigned)FA_TRACE_CTAS && (it) < FA_TRACE_ITERS)                            \
+      g_fa_trace[cta_][(ev)][(it)] = clock64();                                             \
+  } while (0)
 #else
+#define FA_TRACE_CYCLES(ev, it) \
+  do {                          \
+  } while (0)
 #define FA_TRACE_EVENT(ev, it) \
   do {                         \
   } while (0)
