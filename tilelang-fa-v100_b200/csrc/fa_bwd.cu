@@ -625,7 +625,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           float lv[32];
 #pragma unroll
           for (int m = 0; m < 8; ++m) ld_shared_v4f(lse_a + (32 * ch + 4 * m) * 4, lv + 4 * m);
-          if (ch == 0) tmem_wait_ld();
+          if (ch == 0) {
+            tmem_wait_ld();
+            if (threadIdx.x == 128) FA_TRACE_CYCLES(22, i);
+          }
           if (full) {
 #pragma unroll
             for (int x = 0; x < 32; ++x)
