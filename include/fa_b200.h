@@ -56,6 +56,12 @@ typedef struct {
   int32_t dtype;          /* fa_dtype_t */
   int32_t causal;         /* bottom-right aligned: key j visible to row i iff j <= i + Skv - Sq */
   float softmax_scale;
+  /* Sliding window (FA2 window_size = (left, right) as window_q = left + 1,
+   * window_k = right + 1; <= 0: unbounded on that side, so a zero-filled struct has
+   * none): key j visible to row i iff i + Skv - Sq - window_q < j (window_q > 0) and
+   * j < i + Skv - Sq + window_k (window_k > 0), on top of the causal bound.  No reference
+   * counterpart: the reference accepts window_size and ignores it. */
+  int32_t window_q, window_k;
 } fa_fwd_args_t;
 
 int fa_fwd(const fa_fwd_args_t* args, void* stream);
@@ -90,6 +96,7 @@ typedef struct {
   int32_t deterministic;  /* 1: dQ by a separate per-Q-tile kernel (bit-reproducible);
                              0: dQ by fp32 atomics from the dK/dV kernel */
   float softmax_scale;
+  int32_t window_q, window_k; /* as in fa_fwd_args_t; must match the forward's */
 } fa_bwd_args_t;
 
 size_t fa_bwd_workspace_size(const fa_bwd_args_t* args);

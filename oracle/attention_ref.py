@@ -13,6 +13,9 @@ repository's pure-PyTorch attention oracles and the semantics of its kernels:
   ``tril(ones(M, N), diagonal=N-M)`` (:41-43), softmax (:44), P V (:45).  The LSE
   is the natural-log ``m * scale + ln(l)`` the kernels write
   (_kernels_forward.py:170).
+* ``visible_mask`` -- that causal mask combined with FA2's dense sliding window
+  (window_size = (left, right), bottom-right aligned), which the reference accepts and
+  ignores (interface.py:33); the default (-1, -1) leaves the reference's mask.
 * ``attention_bwd_ref`` -- gradients of the same function, i.e. what the reference
   backward computes (_kernels_backward.py): D = rowsum(dO * O) (:203),
   dP = dO V^T (:55), dS = P * (dP - D) (:72-74), dQ = scale dS K (:80),
@@ -69,12 +72,34 @@ def causal_mask(m, n):
     return j <= i + (n - m)
 
 
+def visible_mask(m, n, causal, window=(-1, -1)):
+    """Key visibility [m, n] of a dense call, or None when every key is visible: the
+    causal mask above and FA2's sliding window ``window_size = (left, right)``, bottom-right
+    aligned like it -- key j visible to query i iff i + n - m - left <= j (left >= 0) and
+    j <= i + n - m + right (right >= 0).  The window has no reference counterpart (the
+    reference accepts window_size and ignores it, interface.py:33); with the default
+    (-1, -1) this is the reference's mask."""
+    left, right = (-1, -1) if window is None else (int(window[0]), int(window[1]))
+    if not causal and left < 0 and right < 0:
+        return None
+    a = np.arange(m)[:, None] + (n - m)
+    j = np.arange(n)[None, :]
+    vis = np.ones((m, n), dtype=bool)
+    if causal:
+        vis &= j <= a
+    if left >= 0:
+        vis &= j >= a - left
+    if right >= 0:
+        vis &= j <= a + right
+    return vis
+
+
 def _expand_kv(x, hq):
     hkv = x.shape[1]
     return np.repeat(x, hq // hkv, axis=1)
 
 
-def attention_ref(q, k, v, causal, scale=None, return_p=False):
+def attention_ref(q, k, v, causal, scale=None, return_p=False, window=(-1, -1)):
     """q [B, Hq, M, D], k/v [B, Hkv, N, D] -> out [B, Hq, M, D] f32, lse [B, Hq, M] f32."""
     q = np.asarray(q, dtype=np.float64)
     k = _expand_kv(np.asarray(k, dtype=np.float64), q.shape[1])
@@ -82,8 +107,9 @@ def attention_ref(q, k, v, causal, scale=None, return_p=False):
     d = q.shape[-1]
     scale = 1.0 / np.sqrt(d) if scale is None else scale
     s = np.einsum("bhqd,bhkd->bhqk", q, k) * scale
-    if causal:
-        s = np.where(causal_mask(q.shape[2], k.shape[2]), s, NEG_INF)
+    vis = visible_mask(q.shape[2], k.shape[2], causal, window)
+    if vis is not None:
+        s = np.where(vis, s, NEG_INF)
     p, lse = _softmax_lse(s)
     out = np.einsum("bhqk,bhkd->bhqd", p, v)
     if return_p:
@@ -91,7 +117,8 @@ def attention_ref(q, k, v, causal, scale=None, return_p=False):
     return out.astype(np.float32), lse.astype(np.float32)
 
 
-def attention_bwd_ref(q, k, v, do, causal, scale=None, o=None, unit_roundoff=None):
+def attention_bwd_ref(q, k, v, do, causal, scale=None, o=None, unit_roundoff=None,
+                      window=(-1, -1)):
     """Gradients (dq [B,Hq,M,D], dk/dv [B,Hkv,N,D]) of attention_ref w.r.t. q, k, v.
 
     ``o``: the forward output the backward is given ([B,Hq,M,D]); when passed, the row
@@ -118,8 +145,9 @@ def attention_bwd_ref(q, k, v, do, causal, scale=None, o=None, unit_roundoff=Non
     ke = _expand_kv(k64, hq)
     ve = _expand_kv(v64, hq)
     s = np.einsum("bhqd,bhkd->bhqk", q64, ke) * scale
-    if causal:
-        s = np.where(causal_mask(q64.shape[2], ke.shape[2]), s, NEG_INF)
+    vis = visible_mask(q64.shape[2], ke.shape[2], causal, window)
+    if vis is not None:
+        s = np.where(vis, s, NEG_INF)
     p, _ = _softmax_lse(s)
     if o is None:
         o = np.einsum("bhqk,bhkd->bhqd", p, ve)
@@ -146,11 +174,11 @@ def attention_bwd_ref(q, k, v, do, causal, scale=None, o=None, unit_roundoff=Non
     return grads, (bq, bk, bv)
 
 
-def attention_out_bound(q, k, v, causal, unit_roundoff, scale=None):
+def attention_out_bound(q, k, v, causal, unit_roundoff, scale=None, window=(-1, -1)):
     """Per-element bound [B,Hq,M,D] on what rounding P to the input type before the P V
     product (_kernels_forward.py:162-165) and rounding the output can change:
     u (sum_j P_ij |v_jd| + |out_id|), a worst case over the rounding directions."""
-    _, _, p = attention_ref(q, k, v, causal, scale=scale, return_p=True)
+    _, _, p = attention_ref(q, k, v, causal, scale=scale, return_p=True, window=window)
     ve = _expand_kv(np.asarray(v, np.float64), np.asarray(q).shape[1])
     out = np.einsum("bhqk,bhkd->bhqd", p, ve)
     return float(unit_roundoff) * (np.einsum("bhqk,bhkd->bhqd", p, np.abs(ve)) + np.abs(out))

@@ -80,6 +80,7 @@ struct BwdParams {
   int B, Sq, Skv, H, Hk, G, Sq_pad;
   int d_real;  // the caller's head_dim (32 / 96 run the 64 / 128 kernels)
   int causal;
+  int swq, swk;  // sliding window (dense_visible in fa_internal.h; <= 0: off)
   int n_t, n_u, n_items;  // KV tiles per (batch, kv head), B * Hk units, n_t * n_u items
   float scale, scale_log2;
   const float* lse2;  // [B, H, Sq_pad] lse * log2(e); +inf for padded / empty rows
@@ -337,7 +338,7 @@ constexpr int kBwdPRegHigh = 152;
 static_assert(128 * kBwdPRegLow + 256 * kBwdPRegHigh + 128 * kBwdPRegDq <= 65536,
               "register split exceeds the launch");
 
-template <typename T, int D, bool ATOMIC_DQ>
+template <typename T, int D, bool ATOMIC_DQ, bool WIN>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
@@ -372,9 +373,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int hk = unit % gridDim.y, b = unit / gridDim.y;
   const int k0 = nblk * kBwdBN;
   const int off = p.Skv - p.Sq;
-  const int nqt_all = (p.Sq + kBwdBM - 1) / kBwdBM;
-  const int t_start = p.causal ? min(nqt_all, max(0, k0 - off) / kBwdBM) : 0;
-  const int nqt = nqt_all - t_start;
+  int t_start, t_end;  // query tiles that see this CTA's keys (causal bound and window)
+  dense_q_tiles(k0, kBwdBN, kBwdBM, p.Sq, off, p.causal, WIN ? p.swq : 0, WIN ? p.swk : 0,
+                t_start, t_end);
+  const int nqt = t_end - t_start;
   const int n_iter = p.G * nqt;
 
   if (threadIdx.x == 0) {
@@ -612,7 +614,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_after();
       // ---- pass A: P^T = exp2(S^T * scale*log2e - lse*log2e), masked; 32 columns at a time
       const int qbase = q0 + 64 * c;
-      const bool full = key_ok && (!p.causal || key <= qbase + off);
+      // Every one of the 64 query columns sees this key (row): the first and last
+      // columns bound the causal and window conditions.  WIN (a sliding window) is a
+      // kernel variant, so launches without one run the causal-only masks.
+      const bool full = WIN ? key_ok && dense_visible(key, qbase, off, p.causal, 0, p.swk) &&
+                                  dense_visible(key, qbase + 63, off, 0, p.swq, 0)
+                            : key_ok && (!p.causal || key <= qbase + off);
       // Both 32-column halves of S^T are requested before the one wait, so a single TMEM
       // load latency is exposed per pass.
       float pv[64];
@@ -633,6 +640,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
             for (int x = 0; x < 32; ++x)
               pv[32 * ch + x] = ex2_approx(fmaf(__uint_as_float(sv[32 * ch + x]), c2, -lv[x]));
+          } else if constexpr (WIN) {
+#pragma unroll
+            for (int x = 0; x < 32; ++x) {
+              const bool vis =
+                  key_ok && dense_visible(key, qbase + 32 * ch + x, off, p.causal, p.swq, p.swk);
+              pv[32 * ch + x] =
+                  vis ? ex2_approx(fmaf(__uint_as_float(sv[32 * ch + x]), c2, -lv[x])) : 0.f;
+            }
           } else {
 #pragma unroll
             for (int x = 0; x < 32; ++x) {
@@ -772,6 +787,8 @@ __device__ __forceinline__ BwdItem bwd_item(const BwdParams& p, int L) {
   it.hk = unit % p.Hk;
   it.b = unit / p.Hk;
   it.k0 = (within / gcount) * kBwdBN;
+  // The persistent kernel serves launches without a sliding window only (bwd_persistent):
+  // query tiles from the first one the causal bound lets see these keys.
   const int nqt_all = (p.Sq + kBwdBM - 1) / kBwdBM;
   it.t_start = p.causal ? min(nqt_all, max(0, it.k0 - (p.Skv - p.Sq)) / kBwdBM) : 0;
   it.nqt = nqt_all - it.t_start;
@@ -1074,6 +1091,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_after();
       // ---- pass A: P^T = exp2(S^T * scale*log2e - lse*log2e), masked; 32 columns at a time
       const int qbase = q0 + 64 * c;
+      // Every one of the 64 query columns sees this key (row).  Windowed launches run the
+      // one-CTA-per-item kernel (bwd_persistent), so only the causal bound applies here.
       const bool full = key_ok && (!p.causal || key <= qbase + off);
       // Both 32-column halves of S^T are requested before the one wait, so a single TMEM
       // load latency is exposed per pass.
@@ -1248,7 +1267,7 @@ struct DqCtl {
   int abort_flag;
 };
 
-template <typename T, int D>
+template <typename T, int D, bool WIN>
 __global__ void __launch_bounds__(384, 1)
     fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
@@ -1271,11 +1290,12 @@ __global__ void __launch_bounds__(384, 1)
   const int qt = p.causal ? (gridDim.x - 1 - blockIdx.x) : blockIdx.x;
   const int q0 = qt * kBwdBM;
   const int off = p.Skv - p.Sq;
-  int nkv = (p.Skv + kBwdBN - 1) / kBwdBN;
-  if (p.causal) {
-    const int max_key = min(q0 + kBwdBM, p.Sq) - 1 + off;
-    nkv = min(nkv, max_key >= 0 ? max_key / kBwdBN + 1 : 0);
-  }
+  // KV tiles j0 .. j0 + nkv - 1 hold the keys this Q tile sees (causal bound and window);
+  // the loops below count j from 0 (pipeline index) and read tile j0 + j.
+  int j0, j1;
+  dense_k_tiles(q0, kBwdBM, kBwdBN, p.Sq, p.Skv, off, p.causal, WIN ? p.swq : 0, WIN ? p.swk : 0,
+                j0, j1);
+  const int nkv = j1 - j0;
 
   if (threadIdx.x == 0) {
     ctl->abort_flag = 0;
@@ -1319,8 +1339,9 @@ __global__ void __launch_bounds__(384, 1)
         mbar_arrive_expect_tx(fb, 2 * Cfg::TILE);
         const uint32_t dk = base + Cfg::OFF_KV + s * 2 * Cfg::TILE;
         for (int dh = 0; dh < Cfg::DH; ++dh) {
-          tma_load_4d(dk + dh * Cfg::CHUNK, &tm_k, fb, dh * 64, hk, j * kBwdBN, b);
-          tma_load_4d(dk + Cfg::TILE + dh * Cfg::CHUNK, &tm_v, fb, dh * 64, hk, j * kBwdBN, b);
+          tma_load_4d(dk + dh * Cfg::CHUNK, &tm_k, fb, dh * 64, hk, (j0 + j) * kBwdBN, b);
+          tma_load_4d(dk + Cfg::TILE + dh * Cfg::CHUNK, &tm_v, fb, dh * 64, hk,
+                      (j0 + j) * kBwdBN, b);
         }
       }
       drain_wait(qb, 0);
@@ -1393,12 +1414,22 @@ __global__ void __launch_bounds__(384, 1)
         tmem_ld32(tmem + lane_off + 64 * c, sv);
         tmem_ld32(tmem + lane_off + 64 * c + 32, sv + 32);
         tmem_wait_ld();
-        const int kb = j * kBwdBN + 64 * c;
+        const int kb = (j0 + j) * kBwdBN + 64 * c;
+        if constexpr (WIN) {
 #pragma unroll
-        for (int x = 0; x < 64; ++x) {
-          const int key = kb + x;
-          const bool vis = q_ok && key < p.Skv && (!p.causal || key <= qi + off);
-          pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lse2)) : 0.f;
+          for (int x = 0; x < 64; ++x) {
+            const int key = kb + x;
+            const bool vis =
+                q_ok && key < p.Skv && dense_visible(key, qi, off, p.causal, p.swq, p.swk);
+            pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lse2)) : 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int x = 0; x < 64; ++x) {
+            const int key = kb + x;
+            const bool vis = q_ok && key < p.Skv && (!p.causal || key <= qi + off);
+            pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lse2)) : 0.f;
+          }
         }
       }
       w = mbar_wait(smem_u32(&ctl->dp_full), j & 1, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
@@ -1493,7 +1524,7 @@ constexpr int kBwdPRegTotal = 128 * kBwdPRegLow + 256 * kBwdPRegHigh + 128 * kBw
 constexpr int kBwdPersistMaxSteps = 8;
 template <int D>
 static bool bwd_persistent(const BwdParams& p) {
-  if (D != 128 || p.G != 1) return false;
+  if (D != 128 || p.G != 1 || p.swq > 0 || p.swk > 0) return false;
   const int nqt_all = (p.Sq + kBwdBM - 1) / kBwdBM;
   const int avg_steps = p.causal ? (nqt_all + 1) / 2 : nqt_all;
   return avg_steps <= kBwdPersistMaxSteps;
@@ -1515,12 +1546,14 @@ static int launch_bwd_prep(const fa_bwd_args_t* a, const BwdParams& p, cudaStrea
   return FA_OK;
 }
 
-template <typename T, int D>
+// WIN: the launch has a sliding window (kernel variants with the window masks; the
+// persistent kernel has none and serves launches without one).
+template <typename T, int D, bool WIN>
 static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const CUtensorMap& tk,
                            const CUtensorMap& tv, const CUtensorMap& tdo, BwdParams& p,
                            cudaStream_t st) {
   if (int s = launch_bwd_prep<T, D>(a, p, st)) return s;
-  if (!a->deterministic && bwd_persistent<D>(p)) {
+  if (!WIN && !a->deterministic && bwd_persistent<D>(p)) {
     auto kern = fa_bwd_dkdv_persist_kernel<T, 128, true>;
     static std::atomic<bool> attr[kMaxContexts];
     const int slot = call_context_slot();
@@ -1543,7 +1576,7 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
   } else if (!a->deterministic) {
-    auto kern = fa_bwd_dkdv_kernel<T, D, true>;
+    auto kern = fa_bwd_dkdv_kernel<T, D, true, WIN>;
     static std::atomic<bool> attr[kMaxContexts];
     const int slot = call_context_slot();
     if (slot < 0 || slot >= kMaxContexts) return FA_ERR_CUDA;
@@ -1565,8 +1598,8 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
   } else {
-    auto kern = fa_bwd_dkdv_kernel<T, D, false>;
-    auto kq = fa_bwd_dq_kernel<T, D>;
+    auto kern = fa_bwd_dkdv_kernel<T, D, false, WIN>;
+    auto kq = fa_bwd_dq_kernel<T, D, WIN>;
     static std::atomic<bool> attr[kMaxContexts];
     const int slot = call_context_slot();
     if (slot < 0 || slot >= kMaxContexts) return FA_ERR_CUDA;
@@ -1639,6 +1672,8 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
   p.Sq_pad = pad128(a->seqlen_q);
   p.d_real = a->head_dim;
   p.causal = a->causal;
+  p.swq = a->window_q > 0 ? a->window_q : 0;
+  p.swk = a->window_k > 0 ? a->window_k : 0;
   p.n_t = (a->seqlen_k + kBwdBN - 1) / kBwdBN;
   p.n_u = a->num_heads_k * a->batch;
   p.n_items = p.n_t * p.n_u;
@@ -1665,6 +1700,7 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
   p.dv_sh = a->dv_stride[2];
   p.err = err;
   const bool bf16 = a->dtype == FA_DTYPE_BF16;
+  const bool win = p.swq > 0 || p.swk > 0;
   if (D == 256) {
     // prep (row dot, LSE * log2 e) here, then the two D = 256 kernels of fa_bwd256.cu
     const int s = bf16 ? launch_bwd_prep<__nv_bfloat16, 256>(a, p, st)
@@ -1673,10 +1709,14 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
     return launch_bwd_d256(a, p.lse2, p.dsum, p.Sq_pad, err, st);
   }
   if (D == 64)
-    return bf16 ? launch_bwd_impl<__nv_bfloat16, 64>(a, tq, tk, tv, tdo, p, st)
-                : launch_bwd_impl<__half, 64>(a, tq, tk, tv, tdo, p, st);
-  return bf16 ? launch_bwd_impl<__nv_bfloat16, 128>(a, tq, tk, tv, tdo, p, st)
-              : launch_bwd_impl<__half, 128>(a, tq, tk, tv, tdo, p, st);
+    return win ? (bf16 ? launch_bwd_impl<__nv_bfloat16, 64, true>(a, tq, tk, tv, tdo, p, st)
+                       : launch_bwd_impl<__half, 64, true>(a, tq, tk, tv, tdo, p, st))
+               : (bf16 ? launch_bwd_impl<__nv_bfloat16, 64, false>(a, tq, tk, tv, tdo, p, st)
+                       : launch_bwd_impl<__half, 64, false>(a, tq, tk, tv, tdo, p, st));
+  return win ? (bf16 ? launch_bwd_impl<__nv_bfloat16, 128, true>(a, tq, tk, tv, tdo, p, st)
+                     : launch_bwd_impl<__half, 128, true>(a, tq, tk, tv, tdo, p, st))
+             : (bf16 ? launch_bwd_impl<__nv_bfloat16, 128, false>(a, tq, tk, tv, tdo, p, st)
+                     : launch_bwd_impl<__half, 128, false>(a, tq, tk, tv, tdo, p, st));
 }
 
 }  // namespace fa

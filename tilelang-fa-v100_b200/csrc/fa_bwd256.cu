@@ -43,6 +43,7 @@ constexpr int kB2Chunk64 = 64 * 128;    // 64 rows x 64 dims
 
 struct B2Params {
   int B, Sq, Skv, H, Hk, G, Sq_pad, causal;
+  int swq, swk;  // sliding window (dense_visible in fa_internal.h; <= 0: off)
   float scale, scale_log2;
   const float* lse2;  // [B, H, Sq_pad] lse * log2(e), +inf for padded / empty rows
   const float* dsum;  // [B, H, Sq_pad] rowsum(O * dO)
@@ -125,7 +126,7 @@ struct B2KvCtl {
 };
 static_assert(sizeof(B2KvCtl) <= 256, "dK/dV (D = 256) control block");
 
-template <typename T>
+template <typename T, bool WIN>
 __global__ void __launch_bounds__(kB2Threads, 1)
     fa_bwd_dkdv_d256_kernel(const __grid_constant__ CUtensorMap tm_q,   // box 64 rows
                             const __grid_constant__ CUtensorMap tm_k,   // box 128 rows
@@ -148,9 +149,10 @@ __global__ void __launch_bounds__(kB2Threads, 1)
   const int k0 = (blockIdx.x >> 1) * kB2Keys;    // first key (heaviest tiles first when causal)
   const int hk = blockIdx.y, b = blockIdx.z;
   const int off = p.Skv - p.Sq;                  // causal: key j visible to query i iff j <= i + off
-  const int nqs_all = (p.Sq + kB2QStep - 1) / kB2QStep;
-  const int s_start = p.causal ? min(nqs_all, max(0, k0 - off) / kB2QStep) : 0;
-  const int nqs = nqs_all - s_start;
+  int s_start, s_end;  // query steps that see this CTA's keys (causal bound and window)
+  dense_q_tiles(k0, kB2Keys, kB2QStep, p.Sq, off, p.causal, WIN ? p.swq : 0, WIN ? p.swk : 0,
+                s_start, s_end);
+  const int nqs = s_end - s_start;
   const int n_iter = p.G * nqs;
 
   if (threadIdx.x == 0) {
@@ -337,11 +339,22 @@ __global__ void __launch_bounds__(kB2Threads, 1)
         for (int m = 0; m < 8; ++m)
           b2_ld_shared_v4f(base + Cfg::OFF_LSE + s * 256 + (32 * c + 4 * m) * 4, lv + 4 * m);
         tmem_wait_ld();
-        const bool full = key_ok && (!p.causal || key <= qbase + off);
+        if constexpr (WIN) {
+          const bool full = key_ok && dense_visible(key, qbase, off, p.causal, 0, p.swk) &&
+                            dense_visible(key, qbase + 31, off, 0, p.swq, 0);
 #pragma unroll
-        for (int x = 0; x < 32; ++x) {
-          const bool vis = full || (key_ok && key <= qbase + x + off);
-          pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lv[x])) : 0.f;
+          for (int x = 0; x < 32; ++x) {
+            const bool vis =
+                full || (key_ok && dense_visible(key, qbase + x, off, p.causal, p.swq, p.swk));
+            pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lv[x])) : 0.f;
+          }
+        } else {
+          const bool full = key_ok && (!p.causal || key <= qbase + off);
+#pragma unroll
+          for (int x = 0; x < 32; ++x) {
+            const bool vis = full || (key_ok && key <= qbase + x + off);
+            pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lv[x])) : 0.f;
+          }
         }
         uint32_t pk[16];
 #pragma unroll
@@ -421,7 +434,7 @@ struct B2DqCtl {
 };
 static_assert(sizeof(B2DqCtl) <= 256, "dQ (D = 256) control block");
 
-template <typename T>
+template <typename T, bool WIN>
 __global__ void __launch_bounds__(kB2Threads, 1)
     fa_bwd_dq_d256_kernel(const __grid_constant__ CUtensorMap tm_q,   // box 128 rows
                           const __grid_constant__ CUtensorMap tm_k,   // box 64 rows
@@ -444,11 +457,12 @@ __global__ void __launch_bounds__(kB2Threads, 1)
   const int qt = p.causal ? (gridDim.x - 1 - blockIdx.x) : blockIdx.x;  // heaviest first
   const int q0 = qt * kB2Rows;
   const int off = p.Skv - p.Sq;
-  int nks = (p.Skv + kB2KStep - 1) / kB2KStep;
-  if (p.causal) {
-    const int max_key = min(q0 + kB2Rows, p.Sq) - 1 + off;
-    nks = min(nks, max_key >= 0 ? max_key / kB2KStep + 1 : 0);
-  }
+  // Key steps j0 .. j0 + nks - 1 hold the keys this Q tile sees (causal bound and window);
+  // the loops below count j from 0 (pipeline index) and read step j0 + j.
+  int j0, j1;
+  dense_k_tiles(q0, kB2Rows, kB2KStep, p.Sq, p.Skv, off, p.causal, WIN ? p.swq : 0,
+                WIN ? p.swk : 0, j0, j1);
+  const int nks = j1 - j0;
 
   if (threadIdx.x == 0) {
     ctl->abort_flag = 0;
@@ -500,14 +514,15 @@ __global__ void __launch_bounds__(kB2Threads, 1)
         const uint32_t kb = smem_u32(&ctl->k_full[s]);
         mbar_arrive_expect_tx(kb, 4 * kB2Chunk64);
         for (int c = 0; c < 4; ++c)
-          tma_load_4d(sK + (s * 4 + c) * kB2Chunk64, &tm_k, kb, c * 64, hk, j * kB2KStep, b);
+          tma_load_4d(sK + (s * 4 + c) * kB2Chunk64, &tm_k, kb, c * 64, hk, (j0 + j) * kB2KStep,
+                      b);
         jk = j + 1;
         ok = mbar_wait(smem_u32(&ctl->v_empty), (j & 1) ^ 1, abort_flag, p.err, FA_SITE_BWD_PRODUCER);
         if (!ok) break;
         const uint32_t vb = smem_u32(&ctl->v_full);
         mbar_arrive_expect_tx(vb, 4 * kB2Chunk64);
         for (int c = 0; c < 4; ++c)
-          tma_load_4d(sV + c * kB2Chunk64, &tm_v, vb, c * 64, hk, j * kB2KStep, b);
+          tma_load_4d(sV + c * kB2Chunk64, &tm_v, vb, c * 64, hk, (j0 + j) * kB2KStep, b);
         jv = j + 1;
       }
       b2_drain_wait(qb, 0);
@@ -583,12 +598,22 @@ __global__ void __launch_bounds__(kB2Threads, 1)
         uint32_t sv[32];
         tmem_ld32(tS + 32 * c, sv);
         tmem_wait_ld();
-        const int kb = j * kB2KStep + 32 * c;
+        const int kb = (j0 + j) * kB2KStep + 32 * c;
+        if constexpr (WIN) {
 #pragma unroll
-        for (int x = 0; x < 32; ++x) {
-          const int key = kb + x;
-          const bool vis = q_ok && key < p.Skv && (!p.causal || key <= qi + off);
-          pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lse2)) : 0.f;
+          for (int x = 0; x < 32; ++x) {
+            const int key = kb + x;
+            const bool vis =
+                q_ok && key < p.Skv && dense_visible(key, qi, off, p.causal, p.swq, p.swk);
+            pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lse2)) : 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int x = 0; x < 32; ++x) {
+            const int key = kb + x;
+            const bool vis = q_ok && key < p.Skv && (!p.causal || key <= qi + off);
+            pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lse2)) : 0.f;
+          }
         }
       }
       w = mbar_wait(smem_u32(&ctl->dp_full), j & 1, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
@@ -632,7 +657,7 @@ __global__ void __launch_bounds__(kB2Threads, 1)
 }
 
 // ------------------------------------------------------------------- host side
-template <typename T>
+template <typename T, bool WIN>
 static int launch_bwd_d256_impl(const fa_bwd_args_t* a, const B2Params& p, cudaStream_t st) {
   const CUtensorMapDataType dt = tmap_dtype(a->dtype);
   auto enc = [&](CUtensorMap* m, const void* ptr, const int64_t* s, int heads, int seq, int rows) {
@@ -650,8 +675,8 @@ static int launch_bwd_d256_impl(const fa_bwd_args_t* a, const B2Params& p, cudaS
   FA_TMAP_TRY(enc(&tdo128, a->dout, a->do_stride, a->num_heads, a->seqlen_q, 128));
   FA_TMAP_TRY(enc(&tk64, a->k, a->k_stride, a->num_heads_k, a->seqlen_k, 64));
   FA_TMAP_TRY(enc(&tv64, a->v, a->v_stride, a->num_heads_k, a->seqlen_k, 64));
-  auto kkv = fa_bwd_dkdv_d256_kernel<T>;
-  auto kq = fa_bwd_dq_d256_kernel<T>;
+  auto kkv = fa_bwd_dkdv_d256_kernel<T, WIN>;
+  auto kq = fa_bwd_dq_d256_kernel<T, WIN>;
   static std::atomic<bool> attr_kv[kMaxContexts], attr_q[kMaxContexts];
   if (int s = smem_attr_once(kkv, B2KvCfg::SMEM_BYTES, attr_kv)) return s;
   if (int s = smem_attr_once(kq, B2DqCfg::SMEM_BYTES, attr_q)) return s;
@@ -679,6 +704,8 @@ int launch_bwd_d256(const fa_bwd_args_t* a, const float* lse2, const float* dsum
   p.G = a->num_heads / a->num_heads_k;
   p.Sq_pad = sq_pad;
   p.causal = a->causal;
+  p.swq = a->window_q > 0 ? a->window_q : 0;
+  p.swk = a->window_k > 0 ? a->window_k : 0;
   p.scale = a->softmax_scale;
   p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
   p.lse2 = lse2;
@@ -696,8 +723,12 @@ int launch_bwd_d256(const fa_bwd_args_t* a, const float* lse2, const float* dsum
   p.dv_ss = a->dv_stride[1];
   p.dv_sh = a->dv_stride[2];
   p.err = err;
-  return a->dtype == FA_DTYPE_BF16 ? launch_bwd_d256_impl<__nv_bfloat16>(a, p, st)
-                                   : launch_bwd_d256_impl<__half>(a, p, st);
+  const bool bf16 = a->dtype == FA_DTYPE_BF16;
+  if (p.swq > 0 || p.swk > 0)
+    return bf16 ? launch_bwd_d256_impl<__nv_bfloat16, true>(a, p, st)
+                : launch_bwd_d256_impl<__half, true>(a, p, st);
+  return bf16 ? launch_bwd_d256_impl<__nv_bfloat16, false>(a, p, st)
+              : launch_bwd_d256_impl<__half, false>(a, p, st);
 }
 
 }  // namespace fa

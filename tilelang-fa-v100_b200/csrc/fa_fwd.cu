@@ -63,6 +63,37 @@ __device__ __forceinline__ void fwd_dense_order(int L, int n_t, int n_u, int& x,
   unit = gbase + within % gcount;
 }
 
+// Sliding window: dense launches take FA2's window_size, bottom-right aligned like the
+// causal mask (anchor = row's token + Skv - Sq); paged launches the reference's paged
+// window, anchored on the row's token and honoured only with causal
+// (_kernels_paged.py:275-294).  Key j is visible iff anchor - swq < j (swq > 0) and
+// j < anchor + swk (swk > 0).
+template <bool PAGED>
+__device__ __forceinline__ bool fwd_window_on(const FwdParams& p) {
+  return (PAGED ? p.causal != 0 : true) && (p.swq > 0 || p.swk > 0);
+}
+// KV tiles [j0, j1) that the rows of tokens [tok0, tok0 + TPB) of a work item can see:
+// keys below kv_len, the causal bound and the sliding window.
+template <bool PAGED>
+__device__ __forceinline__ void fwd_kv_range(const FwdParams& p, int tok0, int TPB, int q_len,
+                                             int kv_len, int off, int& j0, int& j1) {
+  j0 = 0;
+  j1 = (kv_len + kFwdBN - 1) / kFwdBN;
+  const int last_lt = min(tok0 + TPB, q_len) - 1;
+  if (p.causal) {
+    const int max_key = last_lt + off;
+    j1 = min(j1, max_key >= 0 ? max_key / kFwdBN + 1 : 0);
+  }
+  if (fwd_window_on<PAGED>(p)) {
+    const int a0 = PAGED ? tok0 : tok0 + off, a1 = PAGED ? last_lt : last_lt + off;
+    if (p.swq > 0) j0 = max(0, a0 - p.swq + 1) / kFwdBN;
+    if (p.swk > 0) {
+      const int max_key = a1 + p.swk - 1;
+      j1 = min(j1, max_key >= 0 ? max_key / kFwdBN + 1 : 0);
+    }
+  }
+}
+
 template <int D, int NQ>
 struct FwdCfg {
   static constexpr int DH = D / 64;                       // 128-byte column chunks
@@ -174,13 +205,8 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
       tok_base = 0;
     }
     const int tok0 = tile * TPB;
-    int j0 = 0, j1 = (kv_len + kFwdBN - 1) / kFwdBN;
-    if (valid && p.causal) {
-      const int last_lt = min(tok0 + TPB, q_len) - 1;
-      const int max_key = last_lt + off;
-      j1 = min(j1, max_key >= 0 ? max_key / kFwdBN + 1 : 0);
-      if (PAGED && p.swq > 0) j0 = max(0, tok0 - p.swq + 1) / kFwdBN;
-    }
+    int j0 = 0, j1 = 0;
+    if (valid) fwd_kv_range<PAGED>(p, tok0, TPB, q_len, kv_len, off, j0, j1);
     ctl->b = b;
     ctl->tok0 = tok0;
     ctl->q_len = q_len;
@@ -408,7 +434,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
     const int h = hk * G + (r - tr * G);     // query head
     const bool row_valid = tr < TPT && lt < q_len;
     const int limit = lt + off;              // causal: key <= limit
-    const bool window = PAGED && p.causal && (p.swq > 0 || p.swk > 0);
+    const bool window = fwd_window_on<PAGED>(p);
     const float c2 = p.scale_log2;
     const float NEG_INF = -INFINITY;
     float m_run = NEG_INF, m_ref = NEG_INF, l = 0.f;
@@ -440,12 +466,11 @@ __global__ void __launch_bounds__(FwdCfg<D, NQ>::NTHREADS, 1)
         for (int c = 0; c < 128; ++c) {
           const int key = key0 + c;
           bool vis = key < kv_len;
-          if (p.causal) {
-            vis = vis && key <= limit;
-            if (window) {
-              if (p.swq > 0) vis = vis && (lt < key + p.swq);
-              if (p.swk > 0) vis = vis && (key < lt + p.swk);
-            }
+          if (p.causal) vis = vis && key <= limit;
+          if (window) {
+            const int wa = PAGED ? lt : lt + off;  // window anchor
+            if (p.swq > 0) vis = vis && (wa < key + p.swq);
+            if (p.swk > 0) vis = vis && (key < wa + p.swk);
           }
           if (!vis) s[c] = __float_as_uint(NEG_INF);
         }
@@ -723,13 +748,8 @@ __device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it, int lane
     it.tok_base = 0;
   }
   it.tok0 = tile * TPB;
-  int j0 = 0, j1 = (it.kv_len + kFwdBN - 1) / kFwdBN;
-  if (p.causal) {
-    const int last_lt = min(it.tok0 + TPB, it.q_len) - 1;
-    const int max_key = last_lt + it.off;
-    j1 = min(j1, max_key >= 0 ? max_key / kFwdBN + 1 : 0);
-    if (PAGED && p.swq > 0) j0 = max(0, it.tok0 - p.swq + 1) / kFwdBN;
-  }
+  int j0 = 0, j1 = 0;
+  fwd_kv_range<PAGED>(p, it.tok0, TPB, it.q_len, it.kv_len, it.off, j0, j1);
   it.j0 = j0;
   it.nkv = max(0, j1 - j0);
   it.live = 1;
@@ -1051,7 +1071,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
     const int tr = r / G;                    // token of this row inside the tile
     const float c2 = p.scale_log2;
     const float NEG_INF = -INFINITY;
-    const bool window = PAGED && p.causal && (p.swq > 0 || p.swk > 0);
+    const bool window = fwd_window_on<PAGED>(p);
     bool ok = true;
     int gj = 0, n_staged = 0;
     if (NQ == 2 && t == 1) mbar_arrive(smem_u32(&ctl->exp_turn[0]));  // tile 0 goes first
@@ -1075,16 +1095,16 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
         if (!ok) break;
         tc_fence_after();
         // Visible keys of this row form one range [lo, hi): key < kv_len; causal: key <=
-        // lt + off; sliding window (paged, causal): lt - swq < key and key < lt + swk.
+        // lt + off; sliding window: anchor - swq < key and key < anchor + swk, anchor = lt
+        // (paged, with causal) or lt + off (dense).
         const int key0 = j * kFwdBN;
         const int lt = itp->tok0 + t * TPT + tr;  // token index within the sequence / chunk
         int lo = 0, hi = itp->kv_len;
-        if (p.causal) {
-          hi = min(hi, lt + itp->off + 1);
-          if (window) {
-            if (p.swq > 0) lo = lt - p.swq + 1;
-            if (p.swk > 0) hi = min(hi, lt + p.swk);
-          }
+        if (p.causal) hi = min(hi, lt + itp->off + 1);
+        if (window) {
+          const int wa = PAGED ? lt : lt + itp->off;
+          if (p.swq > 0) lo = max(lo, wa - p.swq + 1);
+          if (p.swk > 0) hi = min(hi, wa + p.swk);
         }
         const int clo = lo - key0, chi = hi - key0;  // visible columns [clo, chi)
         const bool masked = clo > 0 || chi < kFwdBN;
@@ -1465,6 +1485,8 @@ int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
   p.Hk = a->num_heads_k;
   p.G = G;
   p.causal = a->causal;
+  p.swq = a->window_q > 0 ? a->window_q : 0;
+  p.swk = a->window_k > 0 ? a->window_k : 0;
   p.scale = a->softmax_scale;
   p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
   p.out = a->out;

@@ -33,6 +33,42 @@ struct FwdParams {
   int* err;
 };
 
+// Dense visibility (forward and backward): key j is visible to query row i iff, with the
+// anchor a = i + Skv - Sq (bottom-right alignment), j <= a when causal, a - swq < j when
+// swq > 0 and j < a + swk when swk > 0 (FA2 window_size (left, right) as swq = left + 1,
+// swk = right + 1; <= 0: unbounded on that side).
+__host__ __device__ __forceinline__ bool dense_visible(int key, int qi, int off, int causal,
+                                                      int swq, int swk) {
+  const int a = qi + off;
+  return (!causal || key <= a) && (swq <= 0 || a - swq < key) && (swk <= 0 || key < a + swk);
+}
+// Query tiles [t0, t1) (bm rows each, Sq rows in all) holding a row that sees a key of
+// [k0, k0 + bn).
+__host__ __device__ __forceinline__ void dense_q_tiles(int k0, int bn, int bm, int Sq, int off,
+                                                      int causal, int swq, int swk, int& t0,
+                                                      int& t1) {
+  const int nq = (Sq + bm - 1) / bm;
+  int lo = 0, hi = Sq - 1;
+  if (causal) lo = max(lo, k0 - off);
+  if (swk > 0) lo = max(lo, k0 - off - swk + 1);
+  if (swq > 0) hi = min(hi, k0 + bn - 2 - off + swq);
+  t0 = min(nq, lo / bm);
+  t1 = hi < lo ? t0 : min(nq, hi / bm + 1);
+}
+// Key tiles [j0, j1) (bn keys each, Skv keys in all) holding a key that a row of
+// [q0, q0 + bm) sees.
+__host__ __device__ __forceinline__ void dense_k_tiles(int q0, int bm, int bn, int Sq, int Skv,
+                                                      int off, int causal, int swq, int swk,
+                                                      int& j0, int& j1) {
+  const int q1 = min(q0 + bm, Sq) - 1;
+  int lo = 0, hi = Skv - 1;
+  if (causal) hi = min(hi, q1 + off);
+  if (swk > 0) hi = min(hi, q1 + off + swk - 1);
+  if (swq > 0) lo = max(lo, q0 + off - swq + 1);
+  j0 = min(lo / bn, (Skv + bn - 1) / bn);
+  j1 = hi < lo ? j0 : hi / bn + 1;
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 CUresult encode_tmap(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
                      const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,

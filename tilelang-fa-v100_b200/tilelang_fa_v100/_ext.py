@@ -41,7 +41,7 @@ class FwdArgs(ctypes.Structure):
                 ("o_stride", _i64 * 3),
                 ("batch", _i32), ("seqlen_q", _i32), ("seqlen_k", _i32), ("num_heads", _i32),
                 ("num_heads_k", _i32), ("head_dim", _i32), ("dtype", _i32), ("causal", _i32),
-                ("softmax_scale", _f32)]
+                ("softmax_scale", _f32), ("window_q", _i32), ("window_k", _i32)]
 
 
 class BwdArgs(ctypes.Structure):
@@ -52,7 +52,8 @@ class BwdArgs(ctypes.Structure):
                 ("dk_stride", _i64 * 3), ("dv_stride", _i64 * 3),
                 ("batch", _i32), ("seqlen_q", _i32), ("seqlen_k", _i32), ("num_heads", _i32),
                 ("num_heads_k", _i32), ("head_dim", _i32), ("dtype", _i32), ("causal", _i32),
-                ("deterministic", _i32), ("softmax_scale", _f32)]
+                ("deterministic", _i32), ("softmax_scale", _f32), ("window_q", _i32),
+                ("window_k", _i32)]
 
 
 class PagedArgs(ctypes.Structure):
@@ -200,7 +201,13 @@ def _bshd(t):
     return t
 
 
-def dense_forward(q, k, v, softmax_scale, causal):
+def window_fields(window_size):
+    """FA2 window_size (left, right), -1 = unbounded, as the C-ABI's (window_q, window_k)."""
+    left, right = (int(window_size[0]), int(window_size[1])) if window_size is not None else (-1, -1)
+    return (left + 1 if left >= 0 else 0), (right + 1 if right >= 0 else 0)
+
+
+def dense_forward(q, k, v, softmax_scale, causal, window_size=(-1, -1)):
     """out [B,Sq,H,D] and lse [B,H,Sq] fp32 for BSHD q/k/v."""
     _require_cuda(q, k, v)
     if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
@@ -217,13 +224,14 @@ def dense_forward(q, k, v, softmax_scale, causal):
     a = FwdArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr(),
                 _strides3(q), _strides3(k), _strides3(v), _strides3(out),
                 b, sq, skv, h, hk, d, _dtype_code(q.dtype), 1 if causal else 0,
-                float(softmax_scale))
+                float(softmax_scale), *window_fields(window_size))
     with torch.cuda.device(q.device):
         check(load().fa_fwd(ctypes.byref(a), _stream(q.device)))
     return out, lse
 
 
-def dense_backward(q, k, v, out, dout, lse, softmax_scale, causal, deterministic=False):
+def dense_backward(q, k, v, out, dout, lse, softmax_scale, causal, deterministic=False,
+                   window_size=(-1, -1)):
     """dq, dk, dv (BSHD, q/k/v dtype) for the forward that produced out / lse."""
     _require_cuda(q, k, v, out, dout, lse)
     b, sq, h, d = q.shape
@@ -239,7 +247,7 @@ def dense_backward(q, k, v, out, dout, lse, softmax_scale, causal, deterministic
                 _strides3(q), _strides3(k), _strides3(v), _strides3(out), _strides3(dout),
                 _strides3(dq), _strides3(dk), _strides3(dv),
                 b, sq, skv, h, hk, d, _dtype_code(q.dtype), 1 if causal else 0,
-                1 if deterministic else 0, float(softmax_scale))
+                1 if deterministic else 0, float(softmax_scale), *window_fields(window_size))
     lib = load()
     nbytes = int(lib.fa_bwd_workspace_size(ctypes.byref(a)))
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)

@@ -36,11 +36,15 @@ class FlashAttnTileLangVFunc(torch.autograd.Function):
             raise NotImplementedError("softcap not supported")
 
         scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
-        # window_size is accepted and ignored, as in the reference (interface.py:33).
-        out, lse = _ext.dense_forward(q, k, v, scale, causal)
+        # window_size is honoured (FA2 semantics, bottom-right aligned; (-1, -1) = none).
+        # The reference accepts it and ignores it (interface.py:33): with the default the
+        # two agree.
+        window = tuple(window_size) if window_size is not None else (-1, -1)
+        out, lse = _ext.dense_forward(q, k, v, scale, causal, window)
 
         ctx.save_for_backward(q, k, v, out, lse)
         ctx.causal = causal
+        ctx.window = window
         ctx.softmax_scale = scale
         ctx.deterministic = bool(deterministic)
 
@@ -52,7 +56,7 @@ class FlashAttnTileLangVFunc(torch.autograd.Function):
     def backward(ctx, dout, *args):
         q, k, v, out, lse = ctx.saved_tensors
         dq, dk, dv = _ext.dense_backward(q, k, v, out, dout, lse, ctx.softmax_scale,
-                                         ctx.causal, ctx.deterministic)
+                                         ctx.causal, ctx.deterministic, ctx.window)
         return dq, dk, dv, None, None, None, None, None, None, None, None, None
 
 
