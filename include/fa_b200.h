@@ -13,7 +13,7 @@
  *   decode q/out [B, H, D]
  * Supported: fp16 and bf16 inputs, H % Hk == 0; head_dim 32/64/96/128/256 (dense
  * forward and backward; 32 and 96 run the 64 and 128 kernels on zero-filled columns),
- * 64/128/256 (paged prefill, decode with H / Hkv <= 16).
+ * 64/128/256/512 (paged prefill), 64/128/256 (decode with H / Hkv <= 16).
  * Pointers 16-byte aligned, strides multiples of 8 elements.
  */
 #ifndef FA_B200_H_
@@ -62,6 +62,11 @@ typedef struct {
    * j < i + Skv - Sq + window_k (window_k > 0), on top of the causal bound.  No reference
    * counterpart: the reference accepts window_size and ignores it. */
   int32_t window_q, window_k;
+  /* FA2 softcap: each score becomes softcap * tanh(softmax_scale * q.k / softcap) and
+   * the softmax runs on those with unit scale; lse is their log-sum-exp.  0: off (a
+   * zero-filled struct has none); otherwise finite and > 0 (FA_ERR_INVALID_ARG if not).
+   * The reference raises NotImplementedError for softcap != 0 (interface.py:29-30). */
+  float softcap;
 } fa_fwd_args_t;
 
 int fa_fwd(const fa_fwd_args_t* args, void* stream);
@@ -97,6 +102,7 @@ typedef struct {
                              0: dQ by fp32 atomics from the dK/dV kernel */
   float softmax_scale;
   int32_t window_q, window_k; /* as in fa_fwd_args_t; must match the forward's */
+  float softcap;              /* as in fa_fwd_args_t; must match the forward's */
 } fa_bwd_args_t;
 
 size_t fa_bwd_workspace_size(const fa_bwd_args_t* args);

@@ -16,6 +16,10 @@ repository's pure-PyTorch attention oracles and the semantics of its kernels:
 * ``visible_mask`` -- that causal mask combined with FA2's dense sliding window
   (window_size = (left, right), bottom-right aligned), which the reference accepts and
   ignores (interface.py:33); the default (-1, -1) leaves the reference's mask.
+* ``softcap`` arguments -- FA2's score softcapping, scores = c tanh(scale q k^T / c)
+  with a unit-scale softmax on top (its backward multiplies dS by 1 - tanh^2).  The
+  reference raises NotImplementedError for softcap != 0 (interface.py:29-30); 0 leaves
+  the reference's function.
 * ``attention_bwd_ref`` -- gradients of the same function, i.e. what the reference
   backward computes (_kernels_backward.py): D = rowsum(dO * O) (:203),
   dP = dO V^T (:55), dS = P * (dP - D) (:72-74), dQ = scale dS K (:80),
@@ -99,14 +103,24 @@ def _expand_kv(x, hq):
     return np.repeat(x, hq // hkv, axis=1)
 
 
-def attention_ref(q, k, v, causal, scale=None, return_p=False, window=(-1, -1)):
+def _scores(q, k, scale, softcap):
+    """scale q k^T, softcapped to c tanh(. / c) when softcap = c > 0; also returns the
+    factor d(capped)/d(scaled) = 1 - tanh^2 (1 without softcap)."""
+    s = np.einsum("bhqd,bhkd->bhqk", q, k) * scale
+    if softcap is None or softcap <= 0:
+        return s, 1.0
+    t = np.tanh(s / softcap)
+    return softcap * t, 1.0 - t * t
+
+
+def attention_ref(q, k, v, causal, scale=None, return_p=False, window=(-1, -1), softcap=0.0):
     """q [B, Hq, M, D], k/v [B, Hkv, N, D] -> out [B, Hq, M, D] f32, lse [B, Hq, M] f32."""
     q = np.asarray(q, dtype=np.float64)
     k = _expand_kv(np.asarray(k, dtype=np.float64), q.shape[1])
     v = _expand_kv(np.asarray(v, dtype=np.float64), q.shape[1])
     d = q.shape[-1]
     scale = 1.0 / np.sqrt(d) if scale is None else scale
-    s = np.einsum("bhqd,bhkd->bhqk", q, k) * scale
+    s, _ = _scores(q, k, scale, softcap)
     vis = visible_mask(q.shape[2], k.shape[2], causal, window)
     if vis is not None:
         s = np.where(vis, s, NEG_INF)
@@ -118,7 +132,7 @@ def attention_ref(q, k, v, causal, scale=None, return_p=False, window=(-1, -1)):
 
 
 def attention_bwd_ref(q, k, v, do, causal, scale=None, o=None, unit_roundoff=None,
-                      window=(-1, -1)):
+                      window=(-1, -1), softcap=0.0):
     """Gradients (dq [B,Hq,M,D], dk/dv [B,Hkv,N,D]) of attention_ref w.r.t. q, k, v.
 
     ``o``: the forward output the backward is given ([B,Hq,M,D]); when passed, the row
@@ -144,7 +158,7 @@ def attention_bwd_ref(q, k, v, do, causal, scale=None, o=None, unit_roundoff=Non
     scale = 1.0 / np.sqrt(d) if scale is None else scale
     ke = _expand_kv(k64, hq)
     ve = _expand_kv(v64, hq)
-    s = np.einsum("bhqd,bhkd->bhqk", q64, ke) * scale
+    s, dcap = _scores(q64, ke, scale, softcap)
     vis = visible_mask(q64.shape[2], ke.shape[2], causal, window)
     if vis is not None:
         s = np.where(vis, s, NEG_INF)
@@ -153,7 +167,7 @@ def attention_bwd_ref(q, k, v, do, causal, scale=None, o=None, unit_roundoff=Non
         o = np.einsum("bhqk,bhkd->bhqd", p, ve)
     dsum = np.sum(do64 * np.asarray(o, np.float64), axis=-1, keepdims=True)  # row-dot D
     dp = np.einsum("bhqd,bhkd->bhqk", do64, ve)            # dO V^T
-    ds = p * (dp - dsum)
+    ds = p * (dp - dsum) * dcap
     dq = np.einsum("bhqk,bhkd->bhqd", ds, ke) * scale
     dke = np.einsum("bhqk,bhqd->bhkd", ds, q64) * scale
     dve = np.einsum("bhqk,bhqd->bhkd", p, do64)
@@ -174,11 +188,13 @@ def attention_bwd_ref(q, k, v, do, causal, scale=None, o=None, unit_roundoff=Non
     return grads, (bq, bk, bv)
 
 
-def attention_out_bound(q, k, v, causal, unit_roundoff, scale=None, window=(-1, -1)):
+def attention_out_bound(q, k, v, causal, unit_roundoff, scale=None, window=(-1, -1),
+                        softcap=0.0):
     """Per-element bound [B,Hq,M,D] on what rounding P to the input type before the P V
     product (_kernels_forward.py:162-165) and rounding the output can change:
     u (sum_j P_ij |v_jd| + |out_id|), a worst case over the rounding directions."""
-    _, _, p = attention_ref(q, k, v, causal, scale=scale, return_p=True, window=window)
+    _, _, p = attention_ref(q, k, v, causal, scale=scale, return_p=True, window=window,
+                            softcap=softcap)
     ve = _expand_kv(np.asarray(v, np.float64), np.asarray(q).shape[1])
     out = np.einsum("bhqk,bhkd->bhqd", p, ve)
     return float(unit_roundoff) * (np.einsum("bhqk,bhkd->bhqd", p, np.abs(ve)) + np.abs(out))

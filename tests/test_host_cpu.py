@@ -20,12 +20,19 @@ def test_exports_match_reference_api():
 
 
 @pytest.mark.parametrize("kw,msg", [(dict(dropout_p=0.1), "dropout"),
-                                    (dict(alibi_slopes=torch.ones(2)), "alibi"),
-                                    (dict(softcap=1.0), "softcap")])
+                                    (dict(alibi_slopes=torch.ones(2)), "alibi")])
 def test_unsupported_features_raise_like_reference(kw, msg):
     q, k, v = _qkv()
     with pytest.raises(NotImplementedError, match=msg):
         fa.tilelang_flash_attn_func(q, k, v, **kw)
+
+
+def test_softcap_is_accepted_and_still_needs_cuda():
+    # softcap is honoured (the reference raises NotImplementedError for it): the call gets
+    # past the guards and is refused only for its CPU tensors.
+    q, k, v = _qkv()
+    with pytest.raises(ValueError, match="CUDA"):
+        fa.tilelang_flash_attn_func(q, k, v, softcap=30.0)
 
 
 def test_cpu_tensors_are_rejected_not_computed():

@@ -81,6 +81,9 @@ struct BwdParams {
   int d_real;  // the caller's head_dim (32 / 96 run the 64 / 128 kernels)
   int causal;
   int swq, swk;  // sliding window (dense_visible in fa_internal.h; <= 0: off)
+  // softcap (0: off): sc_a = softcap / scale, sc_k = 2 log2(e) / sc_a (softcap_score),
+  // sc_ia = 1 / sc_a, sc_t = 1 / (log2(e) softcap) (tanh of a score from its P)
+  float sc_a, sc_k, sc_ia, sc_t;
   int n_t, n_u, n_items;  // KV tiles per (batch, kv head), B * Hk units, n_t * n_u items
   float scale, scale_log2;
   const float* lse2;  // [B, H, Sq_pad] lse * log2(e); +inf for padded / empty rows
@@ -338,7 +341,7 @@ constexpr int kBwdPRegHigh = 152;
 static_assert(128 * kBwdPRegLow + 256 * kBwdPRegHigh + 128 * kBwdPRegDq <= 65536,
               "register split exceeds the launch");
 
-template <typename T, int D, bool ATOMIC_DQ, bool WIN>
+template <typename T, int D, bool ATOMIC_DQ, bool EXT>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
@@ -374,7 +377,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int k0 = nblk * kBwdBN;
   const int off = p.Skv - p.Sq;
   int t_start, t_end;  // query tiles that see this CTA's keys (causal bound and window)
-  dense_q_tiles(k0, kBwdBN, kBwdBM, p.Sq, off, p.causal, WIN ? p.swq : 0, WIN ? p.swk : 0,
+  dense_q_tiles(k0, kBwdBN, kBwdBM, p.Sq, off, p.causal, EXT ? p.swq : 0, EXT ? p.swk : 0,
                 t_start, t_end);
   const int nqt = t_end - t_start;
   const int n_iter = p.G * nqt;
@@ -615,9 +618,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // ---- pass A: P^T = exp2(S^T * scale*log2e - lse*log2e), masked; 32 columns at a time
       const int qbase = q0 + 64 * c;
       // Every one of the 64 query columns sees this key (row): the first and last
-      // columns bound the causal and window conditions.  WIN (a sliding window) is a
-      // kernel variant, so launches without one run the causal-only masks.
-      const bool full = WIN ? key_ok && dense_visible(key, qbase, off, p.causal, 0, p.swk) &&
+      // columns bound the causal and window conditions.  EXT (a sliding window or a
+      // softcap) is a kernel variant, so launches without either run the causal-only
+      // masks and raw scores.
+      const bool full = EXT ? key_ok && dense_visible(key, qbase, off, p.causal, 0, p.swk) &&
                                   dense_visible(key, qbase + 63, off, 0, p.swq, 0)
                             : key_ok && (!p.causal || key <= qbase + off);
       // Both 32-column halves of S^T are requested before the one wait, so a single TMEM
@@ -636,11 +640,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             tmem_wait_ld();
             if (threadIdx.x == 128) FA_TRACE_CYCLES(22, i);
           }
+          if constexpr (EXT) {
+            if (p.sc_a != 0.f) {
+#pragma unroll
+              for (int x = 0; x < 32; ++x)
+                sv[32 * ch + x] = __float_as_uint(
+                    softcap_score(__uint_as_float(sv[32 * ch + x]), p.sc_a, p.sc_k));
+            }
+          }
           if (full) {
 #pragma unroll
             for (int x = 0; x < 32; ++x)
               pv[32 * ch + x] = ex2_approx(fmaf(__uint_as_float(sv[32 * ch + x]), c2, -lv[x]));
-          } else if constexpr (WIN) {
+          } else if constexpr (EXT) {
 #pragma unroll
             for (int x = 0; x < 32; ++x) {
               const bool vis =
@@ -670,6 +682,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl->p_ready));
       if (threadIdx.x == 128) FA_TRACE_EVENT(7, i);
+      if constexpr (EXT) {
+        // softcap: dS picks up d(capped)/d(scaled) = 1 - tanh^2.  P^T is in TMEM for dV
+        // already, so pv now takes P (1 - tanh^2), tanh recovered from P and the LSE while
+        // dP^T is computed.
+        if (p.sc_a != 0.f) {
+#pragma unroll
+          for (int ch = 0; ch < 2; ++ch) {
+            float lv[32];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) ld_shared_v4f(lse_a + (32 * ch + 4 * m) * 4, lv + 4 * m);
+#pragma unroll
+            for (int x = 0; x < 32; ++x)
+              pv[32 * ch + x] = softcap_grad_p(pv[32 * ch + x], lv[x], p.sc_t);
+          }
+        }
+      }
       // ---- pass B: dS^T = P^T (dP^T - D) * scale, to shared memory (K-major A of dK,
       // MN-major B of dQ^T).  dP^T(i) was committed after dQ^T(i-1) and dK(i-1), so once
       // dp_full(i) has fired those MMAs have finished reading the previous dS tile.
@@ -787,7 +815,8 @@ __device__ __forceinline__ BwdItem bwd_item(const BwdParams& p, int L) {
   it.hk = unit % p.Hk;
   it.b = unit / p.Hk;
   it.k0 = (within / gcount) * kBwdBN;
-  // The persistent kernel serves launches without a sliding window only (bwd_persistent):
+  // The persistent kernel serves launches without a sliding window or softcap only
+  // (bwd_persistent):
   // query tiles from the first one the causal bound lets see these keys.
   const int nqt_all = (p.Sq + kBwdBM - 1) / kBwdBM;
   it.t_start = p.causal ? min(nqt_all, max(0, it.k0 - (p.Skv - p.Sq)) / kBwdBM) : 0;
@@ -1267,7 +1296,7 @@ struct DqCtl {
   int abort_flag;
 };
 
-template <typename T, int D, bool WIN>
+template <typename T, int D, bool EXT>
 __global__ void __launch_bounds__(384, 1)
     fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
@@ -1293,7 +1322,7 @@ __global__ void __launch_bounds__(384, 1)
   // KV tiles j0 .. j0 + nkv - 1 hold the keys this Q tile sees (causal bound and window);
   // the loops below count j from 0 (pipeline index) and read tile j0 + j.
   int j0, j1;
-  dense_k_tiles(q0, kBwdBM, kBwdBN, p.Sq, p.Skv, off, p.causal, WIN ? p.swq : 0, WIN ? p.swk : 0,
+  dense_k_tiles(q0, kBwdBM, kBwdBN, p.Sq, p.Skv, off, p.causal, EXT ? p.swq : 0, EXT ? p.swk : 0,
                 j0, j1);
   const int nkv = j1 - j0;
 
@@ -1415,13 +1444,21 @@ __global__ void __launch_bounds__(384, 1)
         tmem_ld32(tmem + lane_off + 64 * c + 32, sv + 32);
         tmem_wait_ld();
         const int kb = (j0 + j) * kBwdBN + 64 * c;
-        if constexpr (WIN) {
+        if constexpr (EXT) {
+          // softcap: pv takes P (1 - tanh^2), the factor dS picks up from the cap
+          const bool capped = p.sc_a != 0.f;
 #pragma unroll
           for (int x = 0; x < 64; ++x) {
             const int key = kb + x;
             const bool vis =
                 q_ok && key < p.Skv && dense_visible(key, qi, off, p.causal, p.swq, p.swk);
-            pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lse2)) : 0.f;
+            float sx = __uint_as_float(sv[x]), g = 1.f;
+            if (capped) {
+              sx = softcap_score(sx, p.sc_a, p.sc_k);
+              const float t = sx * p.sc_ia;
+              g = fmaf(-t, t, 1.f);
+            }
+            pv[x] = vis ? ex2_approx(fmaf(sx, c2, -lse2)) * g : 0.f;
           }
         } else {
 #pragma unroll
@@ -1524,7 +1561,7 @@ constexpr int kBwdPRegTotal = 128 * kBwdPRegLow + 256 * kBwdPRegHigh + 128 * kBw
 constexpr int kBwdPersistMaxSteps = 8;
 template <int D>
 static bool bwd_persistent(const BwdParams& p) {
-  if (D != 128 || p.G != 1 || p.swq > 0 || p.swk > 0) return false;
+  if (D != 128 || p.G != 1 || p.swq > 0 || p.swk > 0 || p.sc_a != 0.f) return false;
   const int nqt_all = (p.Sq + kBwdBM - 1) / kBwdBM;
   const int avg_steps = p.causal ? (nqt_all + 1) / 2 : nqt_all;
   return avg_steps <= kBwdPersistMaxSteps;
@@ -1546,14 +1583,15 @@ static int launch_bwd_prep(const fa_bwd_args_t* a, const BwdParams& p, cudaStrea
   return FA_OK;
 }
 
-// WIN: the launch has a sliding window (kernel variants with the window masks; the
-// persistent kernel has none and serves launches without one).
-template <typename T, int D, bool WIN>
+// EXT: the launch has a sliding window or a softcap (kernel variants with the window
+// masks and the softcap transforms; the persistent kernel has neither and serves the
+// launches without them).
+template <typename T, int D, bool EXT>
 static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const CUtensorMap& tk,
                            const CUtensorMap& tv, const CUtensorMap& tdo, BwdParams& p,
                            cudaStream_t st) {
   if (int s = launch_bwd_prep<T, D>(a, p, st)) return s;
-  if (!WIN && !a->deterministic && bwd_persistent<D>(p)) {
+  if (!EXT && !a->deterministic && bwd_persistent<D>(p)) {
     auto kern = fa_bwd_dkdv_persist_kernel<T, 128, true>;
     static std::atomic<bool> attr[kMaxContexts];
     const int slot = call_context_slot();
@@ -1576,7 +1614,7 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
   } else if (!a->deterministic) {
-    auto kern = fa_bwd_dkdv_kernel<T, D, true, WIN>;
+    auto kern = fa_bwd_dkdv_kernel<T, D, true, EXT>;
     static std::atomic<bool> attr[kMaxContexts];
     const int slot = call_context_slot();
     if (slot < 0 || slot >= kMaxContexts) return FA_ERR_CUDA;
@@ -1598,8 +1636,8 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
   } else {
-    auto kern = fa_bwd_dkdv_kernel<T, D, false, WIN>;
-    auto kq = fa_bwd_dq_kernel<T, D, WIN>;
+    auto kern = fa_bwd_dkdv_kernel<T, D, false, EXT>;
+    auto kq = fa_bwd_dq_kernel<T, D, EXT>;
     static std::atomic<bool> attr[kMaxContexts];
     const int slot = call_context_slot();
     if (slot < 0 || slot >= kMaxContexts) return FA_ERR_CUDA;
@@ -1679,6 +1717,12 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
   p.n_items = p.n_t * p.n_u;
   p.scale = a->softmax_scale;
   p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  if (a->softcap > 0.f) {
+    p.sc_a = a->softcap / a->softmax_scale;
+    p.sc_k = 2.f * 1.4426950408889634f / p.sc_a;
+    p.sc_ia = a->softmax_scale / a->softcap;
+    p.sc_t = 1.f / (1.4426950408889634f * a->softcap);
+  }
   const size_t rows = (size_t)a->batch * a->num_heads * p.Sq_pad;
   uintptr_t w = align256(reinterpret_cast<uintptr_t>(ws));
   p.lse2 = reinterpret_cast<const float*>(w);
@@ -1700,7 +1744,7 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
   p.dv_sh = a->dv_stride[2];
   p.err = err;
   const bool bf16 = a->dtype == FA_DTYPE_BF16;
-  const bool win = p.swq > 0 || p.swk > 0;
+  const bool ext = p.swq > 0 || p.swk > 0 || p.sc_a != 0.f;
   if (D == 256) {
     // prep (row dot, LSE * log2 e) here, then the two D = 256 kernels of fa_bwd256.cu
     const int s = bf16 ? launch_bwd_prep<__nv_bfloat16, 256>(a, p, st)
@@ -1709,11 +1753,11 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
     return launch_bwd_d256(a, p.lse2, p.dsum, p.Sq_pad, err, st);
   }
   if (D == 64)
-    return win ? (bf16 ? launch_bwd_impl<__nv_bfloat16, 64, true>(a, tq, tk, tv, tdo, p, st)
+    return ext ? (bf16 ? launch_bwd_impl<__nv_bfloat16, 64, true>(a, tq, tk, tv, tdo, p, st)
                        : launch_bwd_impl<__half, 64, true>(a, tq, tk, tv, tdo, p, st))
                : (bf16 ? launch_bwd_impl<__nv_bfloat16, 64, false>(a, tq, tk, tv, tdo, p, st)
                        : launch_bwd_impl<__half, 64, false>(a, tq, tk, tv, tdo, p, st));
-  return win ? (bf16 ? launch_bwd_impl<__nv_bfloat16, 128, true>(a, tq, tk, tv, tdo, p, st)
+  return ext ? (bf16 ? launch_bwd_impl<__nv_bfloat16, 128, true>(a, tq, tk, tv, tdo, p, st)
                      : launch_bwd_impl<__half, 128, true>(a, tq, tk, tv, tdo, p, st))
              : (bf16 ? launch_bwd_impl<__nv_bfloat16, 128, false>(a, tq, tk, tv, tdo, p, st)
                      : launch_bwd_impl<__half, 128, false>(a, tq, tk, tv, tdo, p, st));

@@ -45,6 +45,8 @@ struct B2Params {
   int B, Sq, Skv, H, Hk, G, Sq_pad, causal;
   int swq, swk;  // sliding window (dense_visible in fa_internal.h; <= 0: off)
   float scale, scale_log2;
+  // softcap (0: off): as in the D = 64 / 128 backward's parameters
+  float sc_a, sc_k, sc_ia, sc_t;
   const float* lse2;  // [B, H, Sq_pad] lse * log2(e), +inf for padded / empty rows
   const float* dsum;  // [B, H, Sq_pad] rowsum(O * dO)
   void* dq;
@@ -126,7 +128,7 @@ struct B2KvCtl {
 };
 static_assert(sizeof(B2KvCtl) <= 256, "dK/dV (D = 256) control block");
 
-template <typename T, bool WIN>
+template <typename T, bool EXT>
 __global__ void __launch_bounds__(kB2Threads, 1)
     fa_bwd_dkdv_d256_kernel(const __grid_constant__ CUtensorMap tm_q,   // box 64 rows
                             const __grid_constant__ CUtensorMap tm_k,   // box 128 rows
@@ -150,7 +152,7 @@ __global__ void __launch_bounds__(kB2Threads, 1)
   const int hk = blockIdx.y, b = blockIdx.z;
   const int off = p.Skv - p.Sq;                  // causal: key j visible to query i iff j <= i + off
   int s_start, s_end;  // query steps that see this CTA's keys (causal bound and window)
-  dense_q_tiles(k0, kB2Keys, kB2QStep, p.Sq, off, p.causal, WIN ? p.swq : 0, WIN ? p.swk : 0,
+  dense_q_tiles(k0, kB2Keys, kB2QStep, p.Sq, off, p.causal, EXT ? p.swq : 0, EXT ? p.swk : 0,
                 s_start, s_end);
   const int nqs = s_end - s_start;
   const int n_iter = p.G * nqs;
@@ -339,7 +341,12 @@ __global__ void __launch_bounds__(kB2Threads, 1)
         for (int m = 0; m < 8; ++m)
           b2_ld_shared_v4f(base + Cfg::OFF_LSE + s * 256 + (32 * c + 4 * m) * 4, lv + 4 * m);
         tmem_wait_ld();
-        if constexpr (WIN) {
+        if constexpr (EXT) {
+          if (p.sc_a != 0.f) {
+#pragma unroll
+            for (int x = 0; x < 32; ++x)
+              sv[x] = __float_as_uint(softcap_score(__uint_as_float(sv[x]), p.sc_a, p.sc_k));
+          }
           const bool full = key_ok && dense_visible(key, qbase, off, p.causal, 0, p.swk) &&
                             dense_visible(key, qbase + 31, off, 0, p.swq, 0);
 #pragma unroll
@@ -364,6 +371,17 @@ __global__ void __launch_bounds__(kB2Threads, 1)
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl->p_ready));
+      if constexpr (EXT) {
+        // softcap: pv takes P (1 - tanh^2) (tanh from P and the LSE) now that P^T is in TMEM
+        if (p.sc_a != 0.f) {
+          float lv[32];
+#pragma unroll
+          for (int m = 0; m < 8; ++m)
+            b2_ld_shared_v4f(base + Cfg::OFF_LSE + s * 256 + (32 * c + 4 * m) * 4, lv + 4 * m);
+#pragma unroll
+          for (int x = 0; x < 32; ++x) pv[x] = softcap_grad_p(pv[x], lv[x], p.sc_t);
+        }
+      }
       // ---- pass B: dS^T = P^T (dP^T - D) * scale, packed over its own dP^T columns
       w = mbar_wait(smem_u32(&ctl->dp_full), par, abort_flag, p.err, FA_SITE_BWD_COMPUTE);
       ok = __all_sync(0xffffffffu, w);
@@ -434,7 +452,7 @@ struct B2DqCtl {
 };
 static_assert(sizeof(B2DqCtl) <= 256, "dQ (D = 256) control block");
 
-template <typename T, bool WIN>
+template <typename T, bool EXT>
 __global__ void __launch_bounds__(kB2Threads, 1)
     fa_bwd_dq_d256_kernel(const __grid_constant__ CUtensorMap tm_q,   // box 128 rows
                           const __grid_constant__ CUtensorMap tm_k,   // box 64 rows
@@ -460,8 +478,8 @@ __global__ void __launch_bounds__(kB2Threads, 1)
   // Key steps j0 .. j0 + nks - 1 hold the keys this Q tile sees (causal bound and window);
   // the loops below count j from 0 (pipeline index) and read step j0 + j.
   int j0, j1;
-  dense_k_tiles(q0, kB2Rows, kB2KStep, p.Sq, p.Skv, off, p.causal, WIN ? p.swq : 0,
-                WIN ? p.swk : 0, j0, j1);
+  dense_k_tiles(q0, kB2Rows, kB2KStep, p.Sq, p.Skv, off, p.causal, EXT ? p.swq : 0,
+                EXT ? p.swk : 0, j0, j1);
   const int nks = j1 - j0;
 
   if (threadIdx.x == 0) {
@@ -599,13 +617,21 @@ __global__ void __launch_bounds__(kB2Threads, 1)
         tmem_ld32(tS + 32 * c, sv);
         tmem_wait_ld();
         const int kb = (j0 + j) * kB2KStep + 32 * c;
-        if constexpr (WIN) {
+        if constexpr (EXT) {
+          // softcap: pv takes P (1 - tanh^2), the factor dS picks up from the cap
+          const bool capped = p.sc_a != 0.f;
 #pragma unroll
           for (int x = 0; x < 32; ++x) {
             const int key = kb + x;
             const bool vis =
                 q_ok && key < p.Skv && dense_visible(key, qi, off, p.causal, p.swq, p.swk);
-            pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lse2)) : 0.f;
+            float sx = __uint_as_float(sv[x]), g = 1.f;
+            if (capped) {
+              sx = softcap_score(sx, p.sc_a, p.sc_k);
+              const float t = sx * p.sc_ia;
+              g = fmaf(-t, t, 1.f);
+            }
+            pv[x] = vis ? ex2_approx(fmaf(sx, c2, -lse2)) * g : 0.f;
           }
         } else {
 #pragma unroll
@@ -657,7 +683,7 @@ __global__ void __launch_bounds__(kB2Threads, 1)
 }
 
 // ------------------------------------------------------------------- host side
-template <typename T, bool WIN>
+template <typename T, bool EXT>
 static int launch_bwd_d256_impl(const fa_bwd_args_t* a, const B2Params& p, cudaStream_t st) {
   const CUtensorMapDataType dt = tmap_dtype(a->dtype);
   auto enc = [&](CUtensorMap* m, const void* ptr, const int64_t* s, int heads, int seq, int rows) {
@@ -675,8 +701,8 @@ static int launch_bwd_d256_impl(const fa_bwd_args_t* a, const B2Params& p, cudaS
   FA_TMAP_TRY(enc(&tdo128, a->dout, a->do_stride, a->num_heads, a->seqlen_q, 128));
   FA_TMAP_TRY(enc(&tk64, a->k, a->k_stride, a->num_heads_k, a->seqlen_k, 64));
   FA_TMAP_TRY(enc(&tv64, a->v, a->v_stride, a->num_heads_k, a->seqlen_k, 64));
-  auto kkv = fa_bwd_dkdv_d256_kernel<T, WIN>;
-  auto kq = fa_bwd_dq_d256_kernel<T, WIN>;
+  auto kkv = fa_bwd_dkdv_d256_kernel<T, EXT>;
+  auto kq = fa_bwd_dq_d256_kernel<T, EXT>;
   static std::atomic<bool> attr_kv[kMaxContexts], attr_q[kMaxContexts];
   if (int s = smem_attr_once(kkv, B2KvCfg::SMEM_BYTES, attr_kv)) return s;
   if (int s = smem_attr_once(kq, B2DqCfg::SMEM_BYTES, attr_q)) return s;
@@ -708,6 +734,12 @@ int launch_bwd_d256(const fa_bwd_args_t* a, const float* lse2, const float* dsum
   p.swk = a->window_k > 0 ? a->window_k : 0;
   p.scale = a->softmax_scale;
   p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  if (a->softcap > 0.f) {
+    p.sc_a = a->softcap / a->softmax_scale;
+    p.sc_k = 2.f * 1.4426950408889634f / p.sc_a;
+    p.sc_ia = a->softmax_scale / a->softcap;
+    p.sc_t = 1.f / (1.4426950408889634f * a->softcap);
+  }
   p.lse2 = lse2;
   p.dsum = dsum;
   p.dq = a->dq;
@@ -724,7 +756,7 @@ int launch_bwd_d256(const fa_bwd_args_t* a, const float* lse2, const float* dsum
   p.dv_sh = a->dv_stride[2];
   p.err = err;
   const bool bf16 = a->dtype == FA_DTYPE_BF16;
-  if (p.swq > 0 || p.swk > 0)
+  if (p.swq > 0 || p.swk > 0 || p.sc_a != 0.f)
     return bf16 ? launch_bwd_d256_impl<__nv_bfloat16, true>(a, p, st)
                 : launch_bwd_d256_impl<__half, true>(a, p, st);
   return bf16 ? launch_bwd_d256_impl<__nv_bfloat16, false>(a, p, st)

@@ -2,6 +2,7 @@
 // encoding and dispatch to the kernel launchers.  Nothing here allocates device
 // memory; outputs and workspaces are owned by the caller.
 #include <atomic>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -277,6 +278,12 @@ int fa_read_device_error(int32_t* code, int32_t* site, int32_t* block, int32_t c
   return FA_OK;
 }
 
+// softcap: 0 (off) or a finite positive cap with a positive softmax scale.
+static bool valid_softcap(float cap, float scale) {
+  if (cap == 0.f) return true;
+  return std::isfinite(cap) && cap > 0.f && std::isfinite(scale) && scale > 0.f;
+}
+
 int fa_fwd(const fa_fwd_args_t* a, void* stream) {
   if (a == nullptr || a->q == nullptr || a->k == nullptr || a->v == nullptr ||
       a->out == nullptr || a->lse == nullptr)
@@ -286,6 +293,7 @@ int fa_fwd(const fa_fwd_args_t* a, void* stream) {
     return FA_ERR_INVALID_ARG;
   if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
   if (!dense_head_dim(a->head_dim)) return FA_ERR_UNSUPPORTED;
+  if (!valid_softcap(a->softcap, a->softmax_scale)) return FA_ERR_INVALID_ARG;
   int* err = nullptr;
   if (int s = device_setup(&err, static_cast<cudaStream_t>(stream))) return s;
   return launch_fwd_dense(a, err, static_cast<cudaStream_t>(stream));
@@ -306,6 +314,7 @@ int fa_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, void* stream) {
     return FA_ERR_INVALID_ARG;
   if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
   if (!dense_head_dim(a->head_dim)) return FA_ERR_UNSUPPORTED;
+  if (!valid_softcap(a->softcap, a->softmax_scale)) return FA_ERR_INVALID_ARG;
   if (ws_bytes < bwd_workspace_bytes(a) || (bwd_workspace_bytes(a) > 0 && ws == nullptr))
     return FA_ERR_WORKSPACE;
   int* err = nullptr;
@@ -322,7 +331,8 @@ int fa_paged_prefill(const fa_paged_args_t* a, void* stream) {
       a->num_heads % a->num_kv_heads != 0 || a->num_pages <= 0 || a->max_blocks <= 0)
     return FA_ERR_INVALID_ARG;
   if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
-  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256) return FA_ERR_UNSUPPORTED;
+  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256 && a->head_dim != 512)
+    return FA_ERR_UNSUPPORTED;
   int* err = nullptr;
   if (int s = device_setup(&err, static_cast<cudaStream_t>(stream))) return s;
   return launch_paged_prefill(a, err, static_cast<cudaStream_t>(stream));

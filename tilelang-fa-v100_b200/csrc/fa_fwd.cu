@@ -39,7 +39,6 @@
 namespace fa {
 
 constexpr int kFwdBM = 128;  // rows per Q tile = TMEM lanes
-constexpr int kFwdBN = 128;  // keys per KV tile
 constexpr int kFwdOrderGroup = 8;  // (batch, kv head) units ordered together (dense)
 // Two-tile CTAs (384 threads, 168 registers a thread at launch): the producer / MMA
 // warpgroup drops to 56 registers and the two softmax warpgroups rise to 224, enough for
@@ -63,37 +62,18 @@ __device__ __forceinline__ void fwd_dense_order(int L, int n_t, int n_u, int& x,
   unit = gbase + within % gcount;
 }
 
-// Sliding window: dense launches take FA2's window_size, bottom-right aligned like the
-// causal mask (anchor = row's token + Skv - Sq); paged launches the reference's paged
-// window, anchored on the row's token and honoured only with causal
-// (_kernels_paged.py:275-294).  Key j is visible iff anchor - swq < j (swq > 0) and
-// j < anchor + swk (swk > 0).
-template <bool PAGED>
-__device__ __forceinline__ bool fwd_window_on(const FwdParams& p) {
-  return (PAGED ? p.causal != 0 : true) && (p.swq > 0 || p.swk > 0);
+// FA2 softcap (dense launches only; the paged API has none): each score becomes
+// softcap_score(s) before the mask, the row max and the exponentials, so the running max,
+// the rescale test and LSE = m * scale + ln l all work on the capped scores.  Only the
+// persistent kernel has it, as its CAP variant: launches without a softcap run kernels
+// without the code (as a runtime branch it cost those launches 4-12 %).
+// Caps n consecutive scores held as raw bits in v.
+template <int N>
+__device__ __forceinline__ void fwd_softcap(uint32_t* v, const FwdParams& p) {
+  const float a = p.sc_a, k = p.sc_k;
+#pragma unroll
+  for (int c = 0; c < N; ++c) v[c] = __float_as_uint(softcap_score(__uint_as_float(v[c]), a, k));
 }
-// KV tiles [j0, j1) that the rows of tokens [tok0, tok0 + TPB) of a work item can see:
-// keys below kv_len, the causal bound and the sliding window.
-template <bool PAGED>
-__device__ __forceinline__ void fwd_kv_range(const FwdParams& p, int tok0, int TPB, int q_len,
-                                             int kv_len, int off, int& j0, int& j1) {
-  j0 = 0;
-  j1 = (kv_len + kFwdBN - 1) / kFwdBN;
-  const int last_lt = min(tok0 + TPB, q_len) - 1;
-  if (p.causal) {
-    const int max_key = last_lt + off;
-    j1 = min(j1, max_key >= 0 ? max_key / kFwdBN + 1 : 0);
-  }
-  if (fwd_window_on<PAGED>(p)) {
-    const int a0 = PAGED ? tok0 : tok0 + off, a1 = PAGED ? last_lt : last_lt + off;
-    if (p.swq > 0) j0 = max(0, a0 - p.swq + 1) / kFwdBN;
-    if (p.swk > 0) {
-      const int max_key = a1 + p.swk - 1;
-      j1 = min(j1, max_key >= 0 ? max_key / kFwdBN + 1 : 0);
-    }
-  }
-}
-
 template <int D, int NQ>
 struct FwdCfg {
   static constexpr int DH = D / 64;                       // 128-byte column chunks
@@ -759,7 +739,7 @@ __device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it, int lane
 // Persistent: one CTA per SM claims work items from a device counter (p.sched) in list
 // order, so the claim order matches a one-CTA-per-item launch while the next item's
 // loads and first S overlap the current item's tail.
-template <typename T, int D, int NQ, bool PAGED>
+template <typename T, int D, int NQ, bool PAGED, bool CAP>
 __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
     fa_fwd_persist_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -1072,6 +1052,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
     const float c2 = p.scale_log2;
     const float NEG_INF = -INFINITY;
     const bool window = fwd_window_on<PAGED>(p);
+    constexpr bool capped = CAP;  // softcap variant (dense only)
     bool ok = true;
     int gj = 0, n_staged = 0;
     if (NQ == 2 && t == 1) mbar_arrive(smem_u32(&ctl->exp_turn[0]));  // tile 0 goes first
@@ -1136,11 +1117,13 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
         tmem_ld32(tS + 64, s_hi);
         tmem_ld32(tS + 96, s_hi + 32);
         tmem_wait_ld();
+        if constexpr (capped) fwd_softcap<64>(s_hi, p);
         if (masked) mask64(s_hi, 64);
         const float mx_hi = max64(s_hi);
         tmem_ld32(tS + 0, s);
         tmem_ld32(tS + 32, s + 32);
         tmem_wait_ld();
+        if constexpr (capped) fwd_softcap<64>(s, p);
         if (masked) mask64(s, 0);
         const float mx = fmaxf(mx_hi, max64(s));
         const float m_new = fmaxf(m_run, mx);
@@ -1200,6 +1183,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
         }
         if (kReloadS) {
           tmem_wait_ld();
+          if constexpr (capped) fwd_softcap<64>(s_hi, p);
           if (masked) mask64(s_hi, 64);
         }
         {
@@ -1378,11 +1362,11 @@ static bool fwd_persistent(bool causal, int kv_len) {
   return avg_tiles <= kFwdPersistMaxTiles;
 }
 
-template <typename T, int D, int NQ, bool PAGED>
+template <typename T, int D, int NQ, bool PAGED, bool CAP>
 static int launch_fwd_persist(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                               const CUtensorMap& to, const FwdParams& p, int kind, cudaStream_t st) {
   using Cfg = FwdPersistCfg<D, NQ>;
-  auto kern = fa_fwd_persist_kernel<T, D, NQ, PAGED>;
+  auto kern = fa_fwd_persist_kernel<T, D, NQ, PAGED, CAP>;
   static std::atomic<bool> attr_set[kMaxContexts];
   if (int s = smem_attr_once(kern, Cfg::SMEM_BYTES, attr_set)) return s;
   FwdParams q = p;
@@ -1415,9 +1399,12 @@ static int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const C
                            const CUtensorMap& to, const FwdParams& p, cudaStream_t st) {
   const int kind = PAGED ? FA_PROF_PAGED : FA_PROF_FWD;
   int s = FA_OK;
-  if (fwd_persistent<D, PAGED>(p.causal != 0, p.Skv)) {
+  if (!PAGED && p.sc_a != 0.f) {
+    // softcap: the persistent kernel's CAP variant serves every shape
+    if constexpr (!PAGED) s = launch_fwd_persist<T, D, NQ, false, true>(tq, tk, tv, to, p, kind, st);
+  } else if (fwd_persistent<D, PAGED>(p.causal != 0, p.Skv)) {
     if constexpr (fwd_may_persist<D, PAGED>())
-      s = launch_fwd_persist<T, D, NQ, PAGED>(tq, tk, tv, to, p, kind, st);
+      s = launch_fwd_persist<T, D, NQ, PAGED, false>(tq, tk, tv, to, p, kind, st);
   } else {
     if constexpr (fwd_may_direct<D, PAGED>())
       s = launch_fwd_direct<T, D, NQ, PAGED>(tq, tk, tv, to, p, kind, st);
@@ -1489,6 +1476,10 @@ int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
   p.swk = a->window_k > 0 ? a->window_k : 0;
   p.scale = a->softmax_scale;
   p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  if (a->softcap > 0.f) {
+    p.sc_a = a->softcap / a->softmax_scale;
+    p.sc_k = 2.f * 1.4426950408889634f / p.sc_a;
+  }
   p.out = a->out;
   p.lse = a->lse;
   p.o_sb = a->o_stride[0];
@@ -1518,6 +1509,7 @@ int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st) {
   if (a->num_tokens == 0 || a->num_seqs == 0) return FA_OK;
   if (!aligned16(a->q) || !aligned16(a->k_cache) || !aligned16(a->v_cache) || !aligned16(a->out))
     return FA_ERR_ALIGNMENT;
+  if (D == 512) return launch_paged512(a, err, st);  // half-width work items (fa_paged512.cu)
   const CUtensorMapDataType dt = tmap_dtype(a->dtype);
   CUtensorMap tq, tk, tv, to;
   {

@@ -27,6 +27,8 @@ struct FwdParams {
   const int32_t* pkl;
   int num_seqs, max_blocks, page_size, num_pages;
   int swq, swk;
+  // softcap (dense only): sc_a = softcap / scale (0: off), sc_k = 2 log2(e) / sc_a
+  float sc_a, sc_k;
   // persistent scheduling: the work list is nbx q-block slots x kv heads (x batch, dense)
   int nbx, n_items;
   int* sched;  // device counter of claimed work-list entries (zeroed before the launch)
@@ -69,6 +71,39 @@ __host__ __device__ __forceinline__ void dense_k_tiles(int q0, int bm, int bn, i
   j1 = hi < lo ? j0 : hi / bn + 1;
 }
 
+constexpr int kFwdBN = 128;  // keys per forward KV tile
+
+// Sliding window: dense launches take FA2's window_size, bottom-right aligned like the
+// causal mask (anchor = row's token + Skv - Sq); paged launches the reference's paged
+// window, anchored on the row's token and honoured only with causal
+// (_kernels_paged.py:275-294).  Key j is visible iff anchor - swq < j (swq > 0) and
+// j < anchor + swk (swk > 0).
+template <bool PAGED>
+__device__ __forceinline__ bool fwd_window_on(const FwdParams& p) {
+  return (PAGED ? p.causal != 0 : true) && (p.swq > 0 || p.swk > 0);
+}
+// KV tiles [j0, j1) that the rows of tokens [tok0, tok0 + TPB) of a work item can see:
+// keys below kv_len, the causal bound and the sliding window.
+template <bool PAGED>
+__device__ __forceinline__ void fwd_kv_range(const FwdParams& p, int tok0, int TPB, int q_len,
+                                             int kv_len, int off, int& j0, int& j1) {
+  j0 = 0;
+  j1 = (kv_len + kFwdBN - 1) / kFwdBN;
+  const int last_lt = min(tok0 + TPB, q_len) - 1;
+  if (p.causal) {
+    const int max_key = last_lt + off;
+    j1 = min(j1, max_key >= 0 ? max_key / kFwdBN + 1 : 0);
+  }
+  if (fwd_window_on<PAGED>(p)) {
+    const int a0 = PAGED ? tok0 : tok0 + off, a1 = PAGED ? last_lt : last_lt + off;
+    if (p.swq > 0) j0 = max(0, a0 - p.swq + 1) / kFwdBN;
+    if (p.swk > 0) {
+      const int max_key = a1 + p.swk - 1;
+      j1 = min(j1, max_key >= 0 ? max_key / kFwdBN + 1 : 0);
+    }
+  }
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 CUresult encode_tmap(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
                      const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
@@ -95,6 +130,8 @@ void prof_end(int kind, cudaStream_t st);
 
 int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st);
 int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st);
+// Paged prefill at head_dim 512 (fa_paged512.cu); called by launch_paged_prefill.
+int launch_paged512(const fa_paged_args_t* a, int* err, cudaStream_t st);
 int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st);
 // Dense backward at head_dim 256 (fa_bwd256.cu) after the prep kernel has written lse2 / dsum.
 int launch_bwd_d256(const fa_bwd_args_t* a, const float* lse2, const float* dsum, int sq_pad,

@@ -396,6 +396,33 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+__device__ __forceinline__ float lg2_approx(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// Softcapped score in raw-score units (FA2 softcap c, softmax scale sc):
+// a * tanh(s / a) with a = c / sc, so that scale * result = c * tanh(scale * s / c) and the
+// softmax around it is unchanged.  From tanh(u) = 1 - 2 / (1 + e^(2u)) with e^(2u) =
+// 2^(k s), k = 2 log2(e) / a: one exponential, one reciprocal.  Saturates to +-a (e^(2u)
+// overflowing to +inf gives a reciprocal of 0).  The absolute error is a few units of
+// 2^-23 * a (ex2 and rcp are both within about 2 ulp); for small |u| the result is a
+// difference near 0 with the same absolute error, which is what the softmax sees.
+__device__ __forceinline__ float softcap_score(float s, float a, float k) {
+  return fmaf(-2.f * a, rcp_approx(1.f + ex2_approx(s * k)), a);
+}
+// P * (1 - tanh^2) for a softcapped score, from P alone: the capped score times
+// scale * log2(e) is lg2(P) + lse2, so tanh = (lg2(P) + lse2) * t_k with
+// t_k = 1 / (log2(e) * softcap).  P = 0 (masked or underflowed) gives 0.
+__device__ __forceinline__ float softcap_grad_p(float pv, float lse2, float t_k) {
+  const float t = (lg2_approx(pv) + lse2) * t_k;
+  return pv > 0.f ? pv * fmaf(-t, t, 1.f) : 0.f;
+}
 template <typename T>
 struct Pack2;
 template <>

@@ -41,7 +41,8 @@ class FwdArgs(ctypes.Structure):
                 ("o_stride", _i64 * 3),
                 ("batch", _i32), ("seqlen_q", _i32), ("seqlen_k", _i32), ("num_heads", _i32),
                 ("num_heads_k", _i32), ("head_dim", _i32), ("dtype", _i32), ("causal", _i32),
-                ("softmax_scale", _f32), ("window_q", _i32), ("window_k", _i32)]
+                ("softmax_scale", _f32), ("window_q", _i32), ("window_k", _i32),
+                ("softcap", _f32)]
 
 
 class BwdArgs(ctypes.Structure):
@@ -53,7 +54,7 @@ class BwdArgs(ctypes.Structure):
                 ("batch", _i32), ("seqlen_q", _i32), ("seqlen_k", _i32), ("num_heads", _i32),
                 ("num_heads_k", _i32), ("head_dim", _i32), ("dtype", _i32), ("causal", _i32),
                 ("deterministic", _i32), ("softmax_scale", _f32), ("window_q", _i32),
-                ("window_k", _i32)]
+                ("window_k", _i32), ("softcap", _f32)]
 
 
 class PagedArgs(ctypes.Structure):
@@ -207,7 +208,7 @@ def window_fields(window_size):
     return (left + 1 if left >= 0 else 0), (right + 1 if right >= 0 else 0)
 
 
-def dense_forward(q, k, v, softmax_scale, causal, window_size=(-1, -1)):
+def dense_forward(q, k, v, softmax_scale, causal, window_size=(-1, -1), softcap=0.0):
     """out [B,Sq,H,D] and lse [B,H,Sq] fp32 for BSHD q/k/v."""
     _require_cuda(q, k, v)
     if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
@@ -224,14 +225,14 @@ def dense_forward(q, k, v, softmax_scale, causal, window_size=(-1, -1)):
     a = FwdArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr(),
                 _strides3(q), _strides3(k), _strides3(v), _strides3(out),
                 b, sq, skv, h, hk, d, _dtype_code(q.dtype), 1 if causal else 0,
-                float(softmax_scale), *window_fields(window_size))
+                float(softmax_scale), *window_fields(window_size), float(softcap))
     with torch.cuda.device(q.device):
         check(load().fa_fwd(ctypes.byref(a), _stream(q.device)))
     return out, lse
 
 
 def dense_backward(q, k, v, out, dout, lse, softmax_scale, causal, deterministic=False,
-                   window_size=(-1, -1)):
+                   window_size=(-1, -1), softcap=0.0):
     """dq, dk, dv (BSHD, q/k/v dtype) for the forward that produced out / lse."""
     _require_cuda(q, k, v, out, dout, lse)
     b, sq, h, d = q.shape
@@ -247,7 +248,8 @@ def dense_backward(q, k, v, out, dout, lse, softmax_scale, causal, deterministic
                 _strides3(q), _strides3(k), _strides3(v), _strides3(out), _strides3(dout),
                 _strides3(dq), _strides3(dk), _strides3(dv),
                 b, sq, skv, h, hk, d, _dtype_code(q.dtype), 1 if causal else 0,
-                1 if deterministic else 0, float(softmax_scale), *window_fields(window_size))
+                1 if deterministic else 0, float(softmax_scale), *window_fields(window_size),
+                float(softcap))
     lib = load()
     nbytes = int(lib.fa_bwd_workspace_size(ctypes.byref(a)))
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)

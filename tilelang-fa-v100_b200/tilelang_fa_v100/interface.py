@@ -11,6 +11,8 @@ are gone, and gradients come back as contiguous BSHD tensors (the reference retu
 permuted views of the same values, interface.py:53-55).  ``softmax_scale`` is
 honoured (the reference kernels hard-code 1/sqrt(D), _kernels_forward.py:96; equal
 for the default).  ``deterministic=True`` selects the dQ kernel without atomics.
+``window_size`` and ``softcap`` follow FA2 (the reference ignores the first and rejects
+the second, interface.py:29-33; with their defaults the results agree).
 """
 import math
 
@@ -32,19 +34,22 @@ class FlashAttnTileLangVFunc(torch.autograd.Function):
             raise NotImplementedError("dropout not supported")
         if alibi_slopes is not None:
             raise NotImplementedError("alibi not supported")
-        if softcap != 0.0:
-            raise NotImplementedError("softcap not supported")
 
         scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
         # window_size is honoured (FA2 semantics, bottom-right aligned; (-1, -1) = none).
         # The reference accepts it and ignores it (interface.py:33): with the default the
         # two agree.
         window = tuple(window_size) if window_size is not None else (-1, -1)
-        out, lse = _ext.dense_forward(q, k, v, scale, causal, window)
+        # softcap is honoured (FA2 semantics: score = softcap * tanh(scale * q.k / softcap),
+        # > 0 enables it, lse is over the capped scores).  The reference raises
+        # NotImplementedError for softcap != 0 (interface.py:29-30).
+        cap = float(softcap) if softcap > 0 else 0.0
+        out, lse = _ext.dense_forward(q, k, v, scale, causal, window, cap)
 
         ctx.save_for_backward(q, k, v, out, lse)
         ctx.causal = causal
         ctx.window = window
+        ctx.softcap = cap
         ctx.softmax_scale = scale
         ctx.deterministic = bool(deterministic)
 
@@ -56,7 +61,8 @@ class FlashAttnTileLangVFunc(torch.autograd.Function):
     def backward(ctx, dout, *args):
         q, k, v, out, lse = ctx.saved_tensors
         dq, dk, dv = _ext.dense_backward(q, k, v, out, dout, lse, ctx.softmax_scale,
-                                         ctx.causal, ctx.deterministic, ctx.window)
+                                         ctx.causal, ctx.deterministic, ctx.window,
+                                         ctx.softcap)
         return dq, dk, dv, None, None, None, None, None, None, None, None, None
 
 
@@ -70,6 +76,8 @@ def tilelang_flash_attn_func(q, k, v, dropout_p=0.0, softmax_scale=None,
         q: [B, M, H, D]; k, v: [B, N, Hk, D] (FA2 layout, H % Hk == 0), fp16 or bf16
         causal: bottom-right aligned causal mask (key j visible to row i iff j <= i + N - M)
         softmax_scale: (default: 1/sqrt(D))
+        window_size: FA2 (left, right) sliding window, -1 = unbounded on that side
+        softcap: > 0: scores become softcap * tanh(scale * q.k / softcap) (FA2 softcapping)
         deterministic: compute dQ without atomics (bit-reproducible backward)
         return_attn_probs: return (out, lse, None) instead of just out
 
