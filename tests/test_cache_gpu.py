@@ -104,10 +104,11 @@ def _step_case(rng, ctx, new, h, hkv, d, page, dt):
     return [cast(x) for x in (q, k, v, kc, vc)], bt, np.array(lens, np.int32), slots
 
 
-@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
-def test_backend_mixed_decode_and_chunked_prefill(cuda_dev, dt):
+@pytest.mark.parametrize("dt,h,hkv,d", [(torch.bfloat16, 32, 8, 128), (torch.float16, 32, 8, 128),
+                                        (torch.bfloat16, 8, 2, 512)])
+def test_backend_mixed_decode_and_chunked_prefill(cuda_dev, dt, h, hkv, d):
     rng = np.random.default_rng(11)
-    h, hkv, d, page = 32, 8, 128, 16
+    page = 16
     ctx = [100, 1000, 17, 0, 250]   # cached tokens per sequence
     new = [1, 1, 1, 300, 64]        # three decodes first, then a prefill and a chunked prefill
     (q, k, v, kc, vc), bt, sl, slots = _step_case(rng, ctx, new, h, hkv, d, page, dt)

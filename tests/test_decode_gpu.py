@@ -67,6 +67,9 @@ DECODE_CASES = [
     ([300, 1, 0], 8, 1, 256, 16, torch.float16, 3),       # D = 256 MQA 8:1, explicit splits
     ([17, 4096], 16, 4, 256, 32, torch.bfloat16, 1),      # D = 256, 4 kv heads per CTA, direct
     ([2000], 8, 8, 256, 64, torch.float16, 0),            # D = 256 MHA, 8 kv heads in 2 CTAs
+    ([64, 129, 1000, 3000], 16, 4, 512, 16, torch.bfloat16, 0),  # D = 512 (paged prefill's
+    ([300, 1, 0], 8, 1, 512, 32, torch.float16, 3),       # companion), explicit splits, MQA
+    ([17, 2000], 4, 4, 512, 16, torch.bfloat16, 1),       # D = 512 MHA, direct
 ]
 
 

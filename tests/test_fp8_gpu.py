@@ -44,6 +44,7 @@ DECODE_FP8_CASES = [
     ([33, 700, 0], 16, 2, 128, 32, torch.bfloat16, 3),
     ([64, 129, 1000, 3000], 8, 1, 256, 16, torch.bfloat16, 0),
     ([300, 2000], 16, 4, 256, 64, torch.float16, 2),
+    ([100, 1500], 8, 2, 512, 16, torch.bfloat16, 0),
 ]
 
 

@@ -9,7 +9,7 @@
 //     16-token chunks of one sequence; splits run in parallel across SMs.
 //   * warp 0 lane 0 streams chunks with TMA (one 16-row x 128-byte box per kv head
 //     and 64-column half) into a STAGES-deep ring of 128-byte-swizzled slots.
-//   * one compute warp per kv head (two at D = 256, each accumulating half of the
+//   * one compute warp per kv head (D / 128 above D = 128, each accumulating 128 of the
 //     output columns): the G = H/Hkv query heads of the group are the rows of an
 //     m16n8k16 MMA, so one read of K/V serves the whole group.
 //   * per split: partial O (normalised) and LSE in an fp32 workspace; a second
@@ -33,14 +33,25 @@ struct DecCfg {
   static constexpr int ELEM = KV8 ? 1 : 2;                // cache bytes per element
   static constexpr int BOX_ELEMS = 128 / ELEM;            // elements per 128-byte box row
   static constexpr int DH = D / BOX_ELEMS;                // boxes per head row
-  static constexpr int WPH = D > 128 ? 2 : 1;             // compute warps per kv head
+  // compute warps per kv head: one up to D = 128, then one per 128 output columns
+  static constexpr int WPH = D > 128 ? D / 128 : 1;
   static constexpr int DW = D / WPH;                      // output columns per compute warp
-  static constexpr int MAXG = D > 128 ? 4 : 8;            // kv heads per CTA
+  // kv heads per CTA.  D = 512: one, so the CTA's 160 threads may hold the 128 registers
+  // of Q fragments next to the 64 of their O columns (each warp forms the whole S).
+  static constexpr int MAXG = D > 256 ? 1 : (D > 128 ? 4 : 8);
   static constexpr int NTHREADS = 32 + 32 * MAXG * WPH;   // producer warp + compute warps
   static constexpr int HEAD_BYTES = kDecChunk * D * ELEM; // one kv head, one chunk, K or V
   static constexpr int STAGE_BYTES_MAX = 2 * MAXG * HEAD_BYTES;
-  static constexpr int STAGES = KV8 ? 6 : ((D == 64) ? 6 : 3);
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES_MAX + 256;
+  // D = 512 runs one CTA per SM (registers), so its ring is deeper.
+  static constexpr int STAGES = D == 512 ? (KV8 ? 8 : 6) : (KV8 ? 6 : ((D == 64) ? 6 : 3));
+  static_assert(STAGES <= 8, "decode ring: DecSmemCtl holds 8 stages");
+  // Above D = 128 the WPH warps of a kv head each form the partial S over their own
+  // D / WPH dims and exchange it through shared memory (double buffered per chunk):
+  // 16 rows x 16 tokens fp32 per warp.
+  static constexpr int KS = (WPH > 1 ? DW : D) / 16;      // S k-steps per compute warp
+  static constexpr int XCH_BYTES_PER_HEAD = WPH > 1 ? 2 * WPH * 32 * 8 * 4 : 0;
+  static constexpr int SMEM_BYTES =
+      1024 + STAGES * STAGE_BYTES_MAX + 256 + MAXG * XCH_BYTES_PER_HEAD;
   static_assert(SMEM_BYTES <= 232448, "decode smem budget");
 };
 
@@ -212,19 +223,23 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
     return;
   }
   const int hh = (warp - 1) / Cfg::WPH;    // kv head of this compute warp
-  const int part = (warp - 1) % Cfg::WPH;  // output-column half (D = 256)
+  const int part = (warp - 1) % Cfg::WPH;  // 128-column part of the output (D > 128)
   if (hh >= HG) return;
   const int hk = hk0 + hh;
   const int G = p.G;
   const int g = lane >> 2;       // MMA row group (row g and g + 8)
   const int qd = (lane & 3) * 2;  // column pair inside an 8-wide n tile
 
-  // Q fragment (A operand, rows = query heads of the group, zero beyond G).
-  uint32_t qa[D / 16][4];
+  // Q fragment (A operand, rows = query heads of the group, zero beyond G) of this warp's
+  // S k-steps: all of D up to D = 128, else its own D / WPH dims.
+  constexpr int KS = Cfg::KS;
+  const int ks0 = Cfg::WPH > 1 ? part * KS : 0;
+  uint32_t qa[KS][4];
   {
     const T* qb = reinterpret_cast<const T*>(p.q) + ((int64_t)b * p.H + hk * G) * D;
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
+    for (int i = 0; i < KS; ++i) {
+      const int ks = ks0 + i;
       // fp8 caches: the K fragments come from ldmatrix over the byte rows, which gives
       // lane (g, j = lane & 3) dims 4 j .. 4 j + 3 of its 16-dim step; the MMA's k index
       // 2 j + e then stands for dim 4 j + e and 8 + 2 j + e for dim 4 j + 2 + e, and the
@@ -235,10 +250,10 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
         if (row >= G) return 0u;
         return *reinterpret_cast<const uint32_t*>(qb + (int64_t)row * D + col);
       };
-      qa[ks][0] = ld2(g, k0);
-      qa[ks][1] = ld2(g + 8, k0);
-      qa[ks][2] = ld2(g, k8);
-      qa[ks][3] = ld2(g + 8, k8);
+      qa[i][0] = ld2(g, k0);
+      qa[i][1] = ld2(g + 8, k0);
+      qa[i][2] = ld2(g, k8);
+      qa[i][3] = ld2(g + 8, k8);
     }
   }
   constexpr int DW = Cfg::DW;
@@ -248,22 +263,30 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   const float c2 = p.scale_log2;
 
+  // Partial-S exchange slots of this kv head: [2 chunk parities][WPH warps][32 lanes][8].
+  float* const xch = reinterpret_cast<float*>(base_ptr + ST * stage_bytes + 256) +
+                     hh * (Cfg::XCH_BYTES_PER_HEAD / 4);
   for (int it = 0; it < nchunks; ++it) {
     const int s = it % ST;
     const bool w_ok =
         mbar_wait(smem_u32(&ctl->full[s]), (it / ST) & 1, abort_flag, p.err, FA_SITE_DEC_COMPUTE);
-    if (!__all_sync(0xffffffffu, w_ok)) break;
+    // One warp per kv head decides alone; the warps of a head that share S decide together
+    // at the exchange barrier below (a barrier some of them skipped would never open).
+    if constexpr (Cfg::WPH == 1) {
+      if (!__all_sync(0xffffffffu, w_ok)) break;
+    }
     const uint32_t kbase = base + s * stage_bytes + hh * Cfg::HEAD_BYTES;
     const uint32_t vbase = base + s * stage_bytes + (HG + hh) * Cfg::HEAD_BYTES;
-    // S[16 rows x 16 tokens] = Q K^T
+    // S[16 rows x 16 tokens] = Q K^T over this warp's k-steps
     float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
+    for (int i = 0; i < KS; ++i) {
+      const int ks = ks0 + i;
       if constexpr (KV8) {
         // Two k steps per ldmatrix x4 over the byte rows (each 8x8 b16 matrix = 8 tokens
         // x 16 dims): matrices (tokens 0-7, dims 32 kp ..), (8-15, same), (0-7, +16),
         // (8-15, +16); each lane's word holds 4 consecutive dims of one token.
-        if (ks & 1) continue;  // handled with ks - 1
+        if (i & 1) continue;  // handled with i - 1 (ks0 is even)
         const int mi = lane >> 3;
         const int tok = ((mi & 1) << 3) + (lane & 7);
         uint32_t r0, r1, r2, r3;
@@ -275,10 +298,10 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
           c[2 * x] = e4m3x2_to<T>(w[x] & 0xFFFFu);
           c[2 * x + 1] = e4m3x2_to<T>(w[x] >> 16);
         }
-        mma16816<kBf16>(sc[0], qa[ks], c[0], c[1]);
-        mma16816<kBf16>(sc[1], qa[ks], c[2], c[3]);
-        mma16816<kBf16>(sc[0], qa[ks + 1], c[4], c[5]);
-        mma16816<kBf16>(sc[1], qa[ks + 1], c[6], c[7]);
+        mma16816<kBf16>(sc[0], qa[i], c[0], c[1]);
+        mma16816<kBf16>(sc[1], qa[i], c[2], c[3]);
+        mma16816<kBf16>(sc[0], qa[i + 1], c[4], c[5]);
+        mma16816<kBf16>(sc[1], qa[i + 1], c[6], c[7]);
       } else {
         // matrices: (tokens 0-7, d lo), (tokens 0-7, d hi), (tokens 8-15, d lo), (tokens 8-15, d hi)
         const int mi = lane >> 3;
@@ -287,8 +310,31 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
         const uint32_t addr = kbase + (ks >> 2) * (kDecChunk * 128) + swz(row, dchunk);
         uint32_t b0, b1, b2, b3;
         ldsm_x4(addr, b0, b1, b2, b3);
-        mma16816<kBf16>(sc[0], qa[ks], b0, b1);
-        mma16816<kBf16>(sc[1], qa[ks], b2, b3);
+        mma16816<kBf16>(sc[0], qa[i], b0, b1);
+        mma16816<kBf16>(sc[1], qa[i], b2, b3);
+      }
+    }
+    if constexpr (Cfg::WPH > 1) {
+      // S = the sum of the WPH partials, added in warp order by every warp of the head
+      // so all of them hold the same S (and the same P).  Double buffered by chunk
+      // parity: a slot is rewritten two chunks later, after every warp has passed the
+      // next chunk's barrier and so finished reading it.
+      float* slot = xch + (it & 1) * (Cfg::WPH * 256);
+      float4* mine = reinterpret_cast<float4*>(slot + (part * 32 + lane) * 8);
+      mine[0] = make_float4(sc[0][0], sc[0][1], sc[0][2], sc[0][3]);
+      mine[1] = make_float4(sc[1][0], sc[1][1], sc[1][2], sc[1][3]);
+      if (!bar_red_and(1 + hh, 32 * Cfg::WPH, w_ok)) break;
+#pragma unroll
+      for (int w = 0; w < Cfg::WPH; ++w) {
+        const float4* x = reinterpret_cast<const float4*>(slot + (w * 32 + lane) * 8);
+        const float4 a = x[0], c = x[1];
+        if (w == 0) {
+          sc[0][0] = a.x; sc[0][1] = a.y; sc[0][2] = a.z; sc[0][3] = a.w;
+          sc[1][0] = c.x; sc[1][1] = c.y; sc[1][2] = c.z; sc[1][3] = c.w;
+        } else {
+          sc[0][0] += a.x; sc[0][1] += a.y; sc[0][2] += a.z; sc[0][3] += a.w;
+          sc[1][0] += c.x; sc[1][1] += c.y; sc[1][2] += c.z; sc[1][3] += c.w;
+        }
       }
     }
     const int tok0 = (c_begin + it) * kDecChunk;
@@ -518,7 +564,8 @@ static int launch_decode_impl(const CUtensorMap& tk, const CUtensorMap& tv, cons
   dim3 grid(p.num_splits, p.Hkv / p.HG, p.B);
   // Shared memory for the actual group: small groups (few kv heads) fit several CTAs
   // per SM, which keeps enough K/V bytes in flight.
-  const int smem = 1024 + Cfg::STAGES * 2 * p.HG * Cfg::HEAD_BYTES + 256;
+  const int smem =
+      1024 + Cfg::STAGES * 2 * p.HG * Cfg::HEAD_BYTES + 256 + p.HG * Cfg::XCH_BYTES_PER_HEAD;
   prof_begin(FA_PROF_DECODE, st);
   kern<<<grid, 32 + 32 * p.HG * Cfg::WPH, smem, st>>>(tk, tv, p);
   prof_end(FA_PROF_DECODE, st);
@@ -537,7 +584,7 @@ static int launch_decode_impl(const CUtensorMap& tk, const CUtensorMap& tv, cons
 int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err,
                   cudaStream_t st) {
   const int D = a->head_dim;
-  if (D != 64 && D != 128 && D != 256) return FA_ERR_UNSUPPORTED;
+  if (D != 64 && D != 128 && D != 256 && D != 512) return FA_ERR_UNSUPPORTED;
   const int G = a->num_heads / a->num_kv_heads;
   if (G > 16) return FA_ERR_UNSUPPORTED;
   const int ps = a->page_size;
@@ -575,7 +622,9 @@ int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err
   p.H = a->num_heads;
   p.Hkv = a->num_kv_heads;
   p.G = G;
-  p.HG = dec_group(a->num_kv_heads, D > 128 ? DecCfg<256>::MAXG : DecCfg<128>::MAXG);
+  p.HG = dec_group(a->num_kv_heads, D > 256   ? DecCfg<512>::MAXG
+                                     : D > 128 ? DecCfg<256>::MAXG
+                                               : DecCfg<128>::MAXG);
   p.page_size = ps;
   p.num_pages = a->num_pages;
   p.max_blocks = a->max_blocks;
@@ -595,6 +644,9 @@ int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err
   }
   const bool bf16 = a->dtype == FA_DTYPE_BF16;
   if (kv8) {
+    if (D == 512)
+      return bf16 ? launch_decode_impl<__nv_bfloat16, 512, true>(tk, tv, p, st)
+                  : launch_decode_impl<__half, 512, true>(tk, tv, p, st);
     if (D == 256)
       return bf16 ? launch_decode_impl<__nv_bfloat16, 256, true>(tk, tv, p, st)
                   : launch_decode_impl<__half, 256, true>(tk, tv, p, st);
@@ -604,6 +656,9 @@ int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err
   if (D == 64)
     return bf16 ? launch_decode_impl<__nv_bfloat16, 64, false>(tk, tv, p, st)
                 : launch_decode_impl<__half, 64, false>(tk, tv, p, st);
+  if (D == 512)
+    return bf16 ? launch_decode_impl<__nv_bfloat16, 512, false>(tk, tv, p, st)
+                : launch_decode_impl<__half, 512, false>(tk, tv, p, st);
   if (D == 256)
     return bf16 ? launch_decode_impl<__nv_bfloat16, 256, false>(tk, tv, p, st)
                 : launch_decode_impl<__half, 256, false>(tk, tv, p, st);
