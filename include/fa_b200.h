@@ -13,7 +13,7 @@
  *   decode q/out [B, H, D]
  * Supported: fp16 and bf16 inputs, H % Hk == 0; head_dim 32/64/96/128/256 (dense
  * forward and backward; 32 and 96 run the 64 and 128 kernels on zero-filled columns),
- * 64/128/256/512 (paged prefill), 64/128/256 (decode with H / Hkv <= 16).
+ * 64/128/256/512 (paged prefill; decode with H / Hkv <= 16).
  * Pointers 16-byte aligned, strides multiples of 8 elements.
  */
 #ifndef FA_B200_H_
@@ -154,7 +154,7 @@ typedef struct {
   int32_t num_splits;             /* 0: heuristic from max_blocks and the SM count */
   float softmax_scale;
   /* KV-cache element type: 0 = the query dtype, FA_DTYPE_E4M3 = fp8 (e4m3) caches
-   * holding key / k_scale and value / v_scale (head_dim 128 or 256); the kernel folds
+   * holding key / k_scale and value / v_scale (head_dim 128, 256 or 512); the kernel folds
    * k_scale into the scores and v_scale into the output.  No counterpart in the
    * reference (fp16 caches only); the layout of vLLM's fp8 KV cache with per-tensor
    * scales. */

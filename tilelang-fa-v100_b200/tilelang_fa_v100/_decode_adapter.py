@@ -6,7 +6,7 @@ the kernel use 1/sqrt(dim), _kernels_paged.py:396; equal for the default).
 
 Beyond the reference (fp16 caches only): the caches may be torch.float8_e4m3fn holding
 key / k_scale and value / v_scale (vLLM's fp8 KV cache with per-tensor scales, head_dim
-128 or 256); ``k_scale`` / ``v_scale`` default to 1.
+128, 256 or 512); ``k_scale`` / ``v_scale`` default to 1.
 """
 import math
 
