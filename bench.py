@@ -503,19 +503,22 @@ def paged_problem(dev, seqs, q_lens, kv_lens, h, hkv, d, page, dtype, seed_base,
 
 
 PAGED = dict(seqs=16, q_len=1024, kv_len=1024, h=32, hkv=8, d=128, page=16)  # configs[3]
+# head_dim 512 paged prefill (the reference's _BEST_CONFIGS[512] entry), configs[3]'s
+# sequence shape with 16 query / 4 kv heads
+PAGED512 = dict(seqs=16, q_len=1024, kv_len=1024, h=16, hkv=4, d=512, page=16)
 
 
-def paged_run(dev, dist, rank, world, steps, warmup):
-    """configs[3], weak: every rank runs 16 x 1024-token sequences (global sequences
-    16 r .. 16 r + 15, contiguous); returns aggregate TFLOP/s, ms and the gathered check."""
+def paged_run(dev, dist, rank, world, steps, warmup, c=PAGED, dtype=torch.float16):
+    """configs[3] (or `c`), weak: every rank runs 16 x 1024-token sequences (global
+    sequences 16 r .. 16 r + 15, contiguous); returns aggregate TFLOP/s, ms and the
+    gathered check."""
     import tilelang_fa_v100 as fa
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     from slice_ref import sequence_ref
-    c = PAGED
     n = c["seqs"]
     seqs = list(range(rank * n, (rank + 1) * n))
     q, kc, vc, bt, sl, qsl, _ = paged_problem(dev, seqs, [c["q_len"]] * n, [c["kv_len"]] * n,
-                                              c["h"], c["hkv"], c["d"], c["page"], torch.float16,
+                                              c["h"], c["hkv"], c["d"], c["page"], dtype,
                                               SEED_PAGED, 11 + rank)
     pkl = torch.zeros(n, dtype=torch.int32, device=dev)
     out = torch.empty_like(q)
@@ -538,13 +541,13 @@ def paged_run(dev, dist, rank, world, steps, warmup):
             pack = [out[j * c["q_len"]:(j + 1) * c["q_len"]].contiguous(),
                     lse[:, j * c["q_len"]:(j + 1) * c["q_len"]].contiguous()]
         else:
-            pack = [torch.empty(c["q_len"], c["h"], c["d"], dtype=torch.float16, device=dev),
+            pack = [torch.empty(c["q_len"], c["h"], c["d"], dtype=dtype, device=dev),
                     torch.empty(c["h"], c["q_len"], device=dev)]
         pack = [_bcast(dist, t, owner) for t in pack]
         if rank != 0:
             continue
         qi, ki, vi = seq_inputs(dev, i, c["q_len"], c["kv_len"], c["h"], c["hkv"], c["d"],
-                                torch.float16, SEED_PAGED)
+                                dtype, SEED_PAGED)
         ro, rl = sequence_ref(qi, ki, vi, c["kv_len"] - c["q_len"], True)
         st.north_star("out", pack[0], ro)
         st.north_star("lse", pack[1], rl)
@@ -827,6 +830,17 @@ def run_ours(args):
             "note": "configs[4] sequences with e4m3 K/V caches (per-tensor scale 1/64); bytes "
                     "count one byte per cached element; checked against the dequantised cache",
             "check": f8chk}
+        p5tf, p5ms, p5chk = paged_run(dev, dist, rank, world, args.steps, 3, c=PAGED512)
+        sec["paged_prefill_fp16_D512_16x1024_H16_Hkv4"] = {
+            "tflops": p5tf, "ms": p5ms, "frac_of_burst_peak": p5tf / world / burst,
+            "note": "useful FLOPs (4*D per visible pair); each q block computes S twice "
+                    "(half-width output items), so executed tensor work is 1.5x",
+            "check": p5chk}
+        d5gbs, d5ms, _, _ = decode_run(dev, dist, rank, world, args.steps, 3, hkv=4, d=512,
+                                       heads=16, check=False)
+        sec["decode_bf16_H16_Hkv4_D512_GBps"] = {
+            "gbs": d5gbs, "ms": d5ms, "frac_of_hbm": d5gbs / world / hbm,
+            "note": "configs[4] length distribution, head_dim 512"}
         d2gbs, d2ms, _, _ = decode_run(dev, dist, rank, world, args.steps, 3, hkv=1, d=256,
                                        heads=8, check=False)
         sec["decode_bf16_H8_Hkv1_D256_GBps"] = {
