@@ -108,6 +108,73 @@ typedef struct {
 size_t fa_bwd_workspace_size(const fa_bwd_args_t* args);
 int fa_bwd(const fa_bwd_args_t* args, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Dense variable-length ("varlen") forward: FA2's flash_attn_varlen_func over packed
+ * sequences.  No reference counterpart (the reference's dense API takes equal-length
+ * batches).  Sequence b owns query rows [cu_seqlens_q[b], cu_seqlens_q[b + 1]) of q / out
+ * and key rows [cu_seqlens_k[b], cu_seqlens_k[b + 1]) of k / v; causal and the window
+ * are bottom-right aligned per sequence (key j visible to row i iff j <= i + Lk - Lq),
+ * exactly as a dense call on that sequence alone.  lse is [H, total_q] (FA2's varlen
+ * layout).  head_dim 64 / 128 / 256. */
+typedef struct {
+  const void* q;              /* [total_q, H, D]  */
+  const void* k;              /* [total_k, Hk, D] */
+  const void* v;              /* [total_k, Hk, D] */
+  void* out;                  /* [total_q, H, D]  */
+  float* lse;                 /* [H, total_q] (required) */
+  const int32_t* cu_seqlens_q; /* [batch + 1], device, non-decreasing, cu[0] = 0 */
+  const int32_t* cu_seqlens_k; /* [batch + 1], device */
+  int64_t q_stride[2];        /* token, head strides in elements */
+  int64_t k_stride[2];
+  int64_t v_stride[2];
+  int64_t o_stride[2];
+  int32_t batch, total_q, total_k, max_seqlen_q, max_seqlen_k;
+  int32_t num_heads, num_heads_k, head_dim;
+  int32_t dtype;
+  int32_t causal;
+  float softmax_scale;
+  int32_t window_q, window_k; /* as in fa_fwd_args_t */
+  float softcap;              /* as in fa_fwd_args_t */
+} fa_varlen_fwd_args_t;
+
+int fa_varlen_fwd(const fa_varlen_fwd_args_t* args, void* stream);
+
+/* Dense varlen backward (FA2's varlen backward): gradients in the packed layouts of
+ * q / k / v.  max_seqlen_q / max_seqlen_k must bound every sequence (they size the
+ * grids and the workspace); workspace as fa_bwd's for batch x max_seqlen_q rows. */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* out;
+  const void* dout;           /* [total_q, H, D] */
+  const float* lse;           /* [H, total_q] from fa_varlen_fwd */
+  void* dq;                   /* [total_q, H, D] */
+  void* dk;                   /* [total_k, Hk, D] */
+  void* dv;
+  const int32_t* cu_seqlens_q;
+  const int32_t* cu_seqlens_k;
+  int64_t q_stride[2];
+  int64_t k_stride[2];
+  int64_t v_stride[2];
+  int64_t o_stride[2];
+  int64_t do_stride[2];
+  int64_t dq_stride[2];
+  int64_t dk_stride[2];
+  int64_t dv_stride[2];
+  int32_t batch, total_q, total_k, max_seqlen_q, max_seqlen_k;
+  int32_t num_heads, num_heads_k, head_dim;
+  int32_t dtype;
+  int32_t causal;
+  int32_t deterministic;
+  float softmax_scale;
+  int32_t window_q, window_k;
+  float softcap;
+} fa_varlen_bwd_args_t;
+
+size_t fa_varlen_bwd_workspace_size(const fa_varlen_bwd_args_t* args);
+int fa_varlen_bwd(const fa_varlen_bwd_args_t* args, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
 /* Paged (vLLM-layout) prefill / chunked prefill forward.  Replaces
  * get_paged_kernel(...)(q, k_cache, v_cache, block_table, seq_lens,
  * query_start_loc, prefix_kv_lens, num_tokens, sm_scale) at

@@ -58,6 +58,8 @@ int main(void) {
 
 @pytest.mark.parametrize("cname,cls", [("fa_fwd_args_t", _ext.FwdArgs),
                                        ("fa_bwd_args_t", _ext.BwdArgs),
+                                       ("fa_varlen_fwd_args_t", _ext.VarlenFwdArgs),
+                                       ("fa_varlen_bwd_args_t", _ext.VarlenBwdArgs),
                                        ("fa_paged_args_t", _ext.PagedArgs),
                                        ("fa_decode_args_t", _ext.DecodeArgs),
                                        ("fa_kv_write_args_t", _ext.KvWriteArgs)])
@@ -115,3 +117,31 @@ def test_decode_workspace_size_is_host_computed():
     assert n > 256 * 32 * 128 * 4  # several splits of fp32 partial outputs
     d.num_splits = 1
     assert lib.fa_decode_workspace_size(ctypes.byref(d)) == 0
+
+
+def test_varlen_entry_points_validate_on_host():
+    lib = _ext.load()
+    assert lib.fa_varlen_fwd(None, None) == _ext.FA_ERR_INVALID_ARG
+    a = _ext.VarlenFwdArgs()
+    assert lib.fa_varlen_fwd(ctypes.byref(a), None) == _ext.FA_ERR_INVALID_ARG  # null tensors
+    a.q = a.k = a.v = a.out = a.lse = a.cu_seqlens_q = a.cu_seqlens_k = 16
+    a.batch, a.total_q, a.total_k, a.max_seqlen_q, a.max_seqlen_k = 2, 10, 12, 6, 7
+    a.num_heads, a.num_heads_k, a.dtype = 4, 2, 1
+    for d in (32, 96, 512):  # varlen head dims are 64 / 128 / 256
+        a.head_dim = d
+        assert lib.fa_varlen_fwd(ctypes.byref(a), None) == _ext.FA_ERR_UNSUPPORTED
+    a.head_dim, a.num_heads_k = 64, 3  # H % Hk != 0
+    assert lib.fa_varlen_fwd(ctypes.byref(a), None) == _ext.FA_ERR_INVALID_ARG
+    a.num_heads_k, a.softmax_scale, a.softcap = 2, 0.125, -1.0
+    assert lib.fa_varlen_fwd(ctypes.byref(a), None) == _ext.FA_ERR_INVALID_ARG
+    a.softcap = 0.0
+    a.q_stride[0], a.q_stride[1] = 4 * 64 + 4, 64  # token stride not a multiple of 8
+    assert lib.fa_varlen_fwd(ctypes.byref(a), None) == _ext.FA_ERR_ALIGNMENT
+    b = _ext.VarlenBwdArgs()
+    assert lib.fa_varlen_bwd(ctypes.byref(b), None, 0, None) == _ext.FA_ERR_INVALID_ARG
+    # workspace: the dense backward's for batch x max_seqlen_q rows
+    b.batch, b.total_q, b.total_k, b.max_seqlen_q, b.max_seqlen_k = 3, 300, 400, 200, 250
+    b.num_heads, b.num_heads_k, b.head_dim = 4, 2, 128
+    d = _ext.BwdArgs()
+    d.batch, d.seqlen_q, d.seqlen_k, d.num_heads, d.num_heads_k, d.head_dim = 3, 200, 250, 4, 2, 128
+    assert lib.fa_varlen_bwd_workspace_size(ctypes.byref(b)) == lib.fa_bwd_workspace_size(ctypes.byref(d))

@@ -84,6 +84,12 @@ struct BwdParams {
   // softcap (0: off): sc_a = softcap / scale, sc_k = 2 log2(e) / sc_a (softcap_score),
   // sc_ia = 1 / sc_a, sc_t = 1 / (log2(e) softcap) (tanh of a score from its P)
   float sc_a, sc_k, sc_ia, sc_t;
+  // varlen (packed sequences, EXT kernels only): sequence b's query rows are [cu_q[b],
+  // cu_q[b + 1]) and key rows [cu_k[b], cu_k[b + 1]) of [total, heads, D] tensors; B, Sq
+  // and Skv are then the batch and the longest lengths (grids, padded lse2 / dsum / dQ
+  // accumulator rows).  Null for dense launches.
+  const int32_t* cu_q;
+  const int32_t* cu_k;
   int n_t, n_u, n_items;  // KV tiles per (batch, kv head), B * Hk units, n_t * n_u items
   float scale, scale_log2;
   const float* lse2;  // [B, H, Sq_pad] lse * log2(e); +inf for padded / empty rows
@@ -153,7 +159,9 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const T* __restrict__ 
                                                           int B, int Sq, int H, int Sq_pad,
                                                           int64_t o_sb, int64_t o_ss, int64_t o_sh,
                                                           int64_t do_sb, int64_t do_ss,
-                                                          int64_t do_sh, int d_real) {
+                                                          int64_t do_sh, int d_real,
+                                                          const int32_t* __restrict__ cu_q,
+                                                          int total_q) {
   constexpr int TPR = D / 8;
   constexpr int RPW = 32 / TPR;
   const int lane = threadIdx.x & 31;
@@ -168,13 +176,16 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const T* __restrict__ 
     const int64_t row = row0 + ps * RPW + sub;
     const int i = (int)(row % Sq_pad);
     const int64_t bh = row / Sq_pad;
-    live[ps] = row < rows && i < Sq;
+    const int h = (int)(bh % H), b = (int)(bh / H);
+    // varlen: row i of sequence b is packed row cu_q[b] + i (batch strides are 0)
+    const int q_len = (cu_q != nullptr && row < rows) ? min(cu_q[b + 1] - cu_q[b], Sq) : Sq;
+    const int64_t tok = (cu_q != nullptr && row < rows) ? (int64_t)cu_q[b] + i : i;
+    live[ps] = row < rows && i < q_len;
     av[ps] = dv[ps] = make_uint4(0u, 0u, 0u, 0u);
     if (live[ps] && cl * 8 < d_real) {
-      const int h = (int)(bh % H), b = (int)(bh / H);
-      av[ps] = __ldcs(reinterpret_cast<const uint4*>(o + b * o_sb + (int64_t)i * o_ss +
+      av[ps] = __ldcs(reinterpret_cast<const uint4*>(o + b * o_sb + tok * o_ss +
                                                      (int64_t)h * o_sh) + cl);
-      dv[ps] = __ldcs(reinterpret_cast<const uint4*>(dout + b * do_sb + (int64_t)i * do_ss +
+      dv[ps] = __ldcs(reinterpret_cast<const uint4*>(dout + b * do_sb + tok * do_ss +
                                                      (int64_t)h * do_sh) + cl);
     }
   }
@@ -198,7 +209,10 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const T* __restrict__ 
         if (live[ps]) {
           const int i = (int)(row % Sq_pad);
           const int64_t bh = row / Sq_pad;
-          const float L = lse[bh * Sq + i];
+          // lse: dense [B, H, Sq]; varlen [H, total_q] (FA2's varlen layout)
+          const float L = cu_q != nullptr
+                              ? lse[(bh % H) * (int64_t)total_q + cu_q[bh / H] + i]
+                              : lse[bh * Sq + i];
           l2 = (L == -INFINITY) ? INFINITY : L * 1.4426950408889634f;
         }
         lse2[row] = l2;
@@ -219,7 +233,8 @@ __global__ void __launch_bounds__(256) fa_bwd_dq_convert_kernel(const float* __r
                                                                 T* dq, int B, int Sq, int H,
                                                                 int Sq_pad, int64_t sb,
                                                                 int64_t ss, int64_t sh,
-                                                                int d_real) {
+                                                                int d_real,
+                                                                const int32_t* __restrict__ cu_q) {
   const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;  // one thread per 4 elements
   const int64_t total = (int64_t)B * H * Sq * (d_real / 4);
   if (idx >= total) return;
@@ -229,12 +244,18 @@ __global__ void __launch_bounds__(256) fa_bwd_dq_convert_kernel(const float* __r
   const int64_t bi = row / H;
   const int i = bi % Sq;
   const int b = bi / Sq;
+  // varlen: Sq is the longest sequence; rows past this one's end hold nothing
+  int64_t tok = i;
+  if (cu_q != nullptr) {
+    if (i >= cu_q[b + 1] - cu_q[b]) return;
+    tok = (int64_t)cu_q[b] + i;
+  }
   const float4 v =
       *reinterpret_cast<const float4*>(acc + (((int64_t)b * H + h) * Sq_pad + i) * D + c4 * 4);
   uint2 pk;
   pk.x = Pack2<T>::pack(v.x, v.y);
   pk.y = Pack2<T>::pack(v.z, v.w);
-  *reinterpret_cast<uint2*>(dq + b * sb + (int64_t)i * ss + (int64_t)h * sh + c4 * 4) = pk;
+  *reinterpret_cast<uint2*>(dq + b * sb + tok * ss + (int64_t)h * sh + c4 * 4) = pk;
 }
 
 // ---------------------------------------------------------------- 2. dK / dV (+ dQ atomics)
@@ -375,9 +396,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int unit = gbase + within % gcount;
   const int hk = unit % gridDim.y, b = unit / gridDim.y;
   const int k0 = nblk * kBwdBN;
-  const int off = p.Skv - p.Sq;
+  const BwdSeq sq = bwd_seq<EXT>(p, b);
+  // varlen: the grid spans the longest sequence; tiles past this one's keys have no work
+  // (uniform, before any barrier or TMEM is set up)
+  if (EXT && k0 >= sq.Skv) return;
+  const int off = sq.Skv - sq.Sq;
   int t_start, t_end;  // query tiles that see this CTA's keys (causal bound and window)
-  dense_q_tiles(k0, kBwdBN, kBwdBM, p.Sq, off, p.causal, EXT ? p.swq : 0, EXT ? p.swk : 0,
+  dense_q_tiles(k0, kBwdBN, kBwdBM, sq.Sq, off, p.causal, EXT ? p.swq : 0, EXT ? p.swk : 0,
                 t_start, t_end);
   const int nqt = t_end - t_start;
   const int n_iter = p.G * nqt;
@@ -425,8 +450,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t kvb = smem_u32(&ctl->kv_full);
       mbar_arrive_expect_tx(kvb, 2 * Cfg::TILE);
       for (int dh = 0; dh < Cfg::DH; ++dh) {
-        tma_load_4d(sK + dh * Cfg::CHUNK, &tm_k, kvb, dh * 64, hk, k0, b);
-        tma_load_4d(sV + dh * Cfg::CHUNK, &tm_v, kvb, dh * 64, hk, k0, b);
+        tma_load_4d(sK + dh * Cfg::CHUNK, &tm_k, kvb, dh * 64, hk, sq.kr + k0, sq.tb);
+        tma_load_4d(sV + dh * Cfg::CHUNK, &tm_v, kvb, dh * 64, hk, sq.kr + k0, sq.tb);
       }
       int i = 0, n_do = 0;
       for (; i < n_iter; ++i) {
@@ -440,7 +465,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         mbar_arrive_expect_tx(fb, Cfg::TILE + 1024);
         const uint32_t sQ = base + Cfg::OFF_Q + s * Cfg::TILE;
         for (int dh = 0; dh < Cfg::DH; ++dh)
-          tma_load_4d(sQ + dh * Cfg::CHUNK, &tm_q, fb, dh * 64, h, qt * kBwdBM, b);
+          tma_load_4d(sQ + dh * Cfg::CHUNK, &tm_q, fb, dh * 64, h, sq.qr + qt * kBwdBM, sq.tb);
         const int64_t row0 = ((int64_t)b * p.H + h) * p.Sq_pad + qt * kBwdBM;
         bulk_load(base + Cfg::OFF_LSE + s * 512, p.lse2 + row0, 512, fb);
         bulk_load(base + Cfg::OFF_DI + s * 512, p.dsum + row0, 512, fb);
@@ -455,7 +480,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         mbar_arrive_expect_tx(db, Cfg::TILE);
         for (int dh = 0; dh < Cfg::DH; ++dh)
           tma_load_4d(base + Cfg::OFF_DO + ds * Cfg::TILE + dh * Cfg::CHUNK, &tm_do, db, dh * 64,
-                      h, qt * kBwdBM, b);
+                      h, sq.qr + qt * kBwdBM, sq.tb);
         n_do = i + 1;
       }
       drain_wait(kvb, 0);
@@ -597,7 +622,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_off, tdP = tmem + lane_off + 128;
     const int key = k0 + j;
-    const bool key_ok = key < p.Skv;
+    const bool key_ok = key < sq.Skv;
     const float c2 = p.scale_log2;
     bool ok = true;
     for (int i = 0; i < n_iter; ++i) {
@@ -743,9 +768,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     if (ok) {
       tc_fence_after();
-      T* dkr = reinterpret_cast<T*>(p.dk) + (int64_t)b * p.dk_sb + (int64_t)key * p.dk_ss +
+      T* dkr = reinterpret_cast<T*>(p.dk) + (int64_t)b * p.dk_sb + (int64_t)(sq.kr + key) * p.dk_ss +
                (int64_t)hk * p.dk_sh + c * (D / 2);
-      T* dvr = reinterpret_cast<T*>(p.dv) + (int64_t)b * p.dv_sb + (int64_t)key * p.dv_ss +
+      T* dvr = reinterpret_cast<T*>(p.dv) + (int64_t)b * p.dv_sb + (int64_t)(sq.kr + key) * p.dv_ss +
                (int64_t)hk * p.dv_sh + c * (D / 2);
 #pragma unroll
       for (int w2 = 0; w2 < 2; ++w2) {
@@ -1318,12 +1343,16 @@ __global__ void __launch_bounds__(384, 1)
   const int h = blockIdx.y, b = blockIdx.z, hk = h / p.G;
   const int qt = p.causal ? (gridDim.x - 1 - blockIdx.x) : blockIdx.x;
   const int q0 = qt * kBwdBM;
-  const int off = p.Skv - p.Sq;
+  const BwdSeq sq = bwd_seq<EXT>(p, b);
+  // varlen: the grid spans the longest sequence; tiles past this one's rows have no work
+  // (uniform, before any barrier or TMEM is set up)
+  if (EXT && q0 >= sq.Sq) return;
+  const int off = sq.Skv - sq.Sq;
   // KV tiles j0 .. j0 + nkv - 1 hold the keys this Q tile sees (causal bound and window);
   // the loops below count j from 0 (pipeline index) and read tile j0 + j.
   int j0, j1;
-  dense_k_tiles(q0, kBwdBM, kBwdBN, p.Sq, p.Skv, off, p.causal, EXT ? p.swq : 0, EXT ? p.swk : 0,
-                j0, j1);
+  dense_k_tiles(q0, kBwdBM, kBwdBN, sq.Sq, sq.Skv, off, p.causal, EXT ? p.swq : 0,
+                EXT ? p.swk : 0, j0, j1);
   const int nkv = j1 - j0;
 
   if (threadIdx.x == 0) {
@@ -1355,8 +1384,8 @@ __global__ void __launch_bounds__(384, 1)
       const uint32_t qb = smem_u32(&ctl->q_full);
       mbar_arrive_expect_tx(qb, 2 * Cfg::TILE);
       for (int dh = 0; dh < Cfg::DH; ++dh) {
-        tma_load_4d(sQ + dh * Cfg::CHUNK, &tm_q, qb, dh * 64, h, q0, b);
-        tma_load_4d(sdO + dh * Cfg::CHUNK, &tm_do, qb, dh * 64, h, q0, b);
+        tma_load_4d(sQ + dh * Cfg::CHUNK, &tm_q, qb, dh * 64, h, sq.qr + q0, sq.tb);
+        tma_load_4d(sdO + dh * Cfg::CHUNK, &tm_do, qb, dh * 64, h, sq.qr + q0, sq.tb);
       }
       int j = 0;
       for (; j < nkv; ++j) {
@@ -1368,9 +1397,10 @@ __global__ void __launch_bounds__(384, 1)
         mbar_arrive_expect_tx(fb, 2 * Cfg::TILE);
         const uint32_t dk = base + Cfg::OFF_KV + s * 2 * Cfg::TILE;
         for (int dh = 0; dh < Cfg::DH; ++dh) {
-          tma_load_4d(dk + dh * Cfg::CHUNK, &tm_k, fb, dh * 64, hk, (j0 + j) * kBwdBN, b);
+          tma_load_4d(dk + dh * Cfg::CHUNK, &tm_k, fb, dh * 64, hk, sq.kr + (j0 + j) * kBwdBN,
+                      sq.tb);
           tma_load_4d(dk + Cfg::TILE + dh * Cfg::CHUNK, &tm_v, fb, dh * 64, hk,
-                      (j0 + j) * kBwdBN, b);
+                      sq.kr + (j0 + j) * kBwdBN, sq.tb);
         }
       }
       drain_wait(qb, 0);
@@ -1426,7 +1456,7 @@ __global__ void __launch_bounds__(384, 1)
     const int r = ((warp & 3) << 5) | lane;  // query row
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int qi = q0 + r;
-    const bool q_ok = qi < p.Sq;
+    const bool q_ok = qi < sq.Sq;
     const int64_t row = ((int64_t)b * p.H + h) * p.Sq_pad + qi;
     const float lse2 = p.lse2[row];  // padded rows hold +inf -> P = 0
     const float di = p.dsum[row];
@@ -1451,7 +1481,7 @@ __global__ void __launch_bounds__(384, 1)
           for (int x = 0; x < 64; ++x) {
             const int key = kb + x;
             const bool vis =
-                q_ok && key < p.Skv && dense_visible(key, qi, off, p.causal, p.swq, p.swk);
+                q_ok && key < sq.Skv && dense_visible(key, qi, off, p.causal, p.swq, p.swk);
             float sx = __uint_as_float(sv[x]), g = 1.f;
             if (capped) {
               sx = softcap_score(sx, p.sc_a, p.sc_k);
@@ -1464,7 +1494,7 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int x = 0; x < 64; ++x) {
             const int key = kb + x;
-            const bool vis = q_ok && key < p.Skv && (!p.causal || key <= qi + off);
+            const bool vis = q_ok && key < sq.Skv && (!p.causal || key <= qi + off);
             pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lse2)) : 0.f;
           }
         }
@@ -1502,7 +1532,7 @@ __global__ void __launch_bounds__(384, 1)
     }
     if (ok) {
       tc_fence_after();
-      T* dst = reinterpret_cast<T*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)qi * p.dq_ss +
+      T* dst = reinterpret_cast<T*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)(sq.qr + qi) * p.dq_ss +
                (int64_t)h * p.dq_sh + c * (D / 2);
 #pragma unroll
       for (int c0 = 0; c0 < D / 2; c0 += 32) {
@@ -1534,8 +1564,9 @@ static int pad128(int x) { return (x + 127) / 128 * 128; }
 // load; the prep kernel and the gradient stores stop at the real head_dim).
 static int bwd_kernel_dim(int d) { return d == 32 ? 64 : (d == 96 ? 128 : d); }
 
-size_t bwd_workspace_bytes(const fa_bwd_args_t* a) {
-  const size_t rows = (size_t)a->batch * a->num_heads * pad128(a->seqlen_q);
+size_t bwd_workspace_bytes(const fa_bwd_args_t* a, const BwdVarlen* vl) {
+  const size_t rows = (size_t)(vl ? vl->batch : a->batch) * a->num_heads *
+                      pad128(vl ? vl->max_q : a->seqlen_q);
   size_t n = 2 * (rows * 4 + 256);                         // lse2, dsum
   // dQ accumulator (atomic mode at D = 64 / 128; the D = 256 kernels write dQ directly)
   if (!a->deterministic && a->head_dim != 256) n += rows * bwd_kernel_dim(a->head_dim) * 4 + 256;
@@ -1570,14 +1601,18 @@ static bool bwd_persistent(const BwdParams& p) {
 // Row dot D = rowsum(O * dO), lse * log2 e and (atomic mode) the cleared dQ accumulator.
 template <typename T, int D>
 static int launch_bwd_prep(const fa_bwd_args_t* a, const BwdParams& p, cudaStream_t st) {
-  const int64_t rows = (int64_t)a->batch * a->num_heads * p.Sq_pad;
+  const int64_t rows = (int64_t)p.B * a->num_heads * p.Sq_pad;
   const int64_t rows_per_block = 8 * (32 / (D / 8)) * kPrepPasses;
   const int blocks = (int)((rows + rows_per_block - 1) / rows_per_block);
+  // varlen: `a` describes the packed tensors as one batch entry of total_q rows (its
+  // seqlen_q); rows are found through cu_q, so the batch strides drop out
+  const bool vl = p.cu_q != nullptr;
   fa_bwd_prep_kernel<T, D><<<blocks, 256, 0, st>>>(
       reinterpret_cast<const T*>(a->out), reinterpret_cast<const T*>(a->dout), a->lse,
-      const_cast<float*>(p.lse2), const_cast<float*>(p.dsum), p.dq_acc, a->batch, a->seqlen_q,
-      a->num_heads, p.Sq_pad, a->o_stride[0], a->o_stride[1], a->o_stride[2], a->do_stride[0],
-      a->do_stride[1], a->do_stride[2], p.d_real);
+      const_cast<float*>(p.lse2), const_cast<float*>(p.dsum), p.dq_acc, p.B, p.Sq,
+      a->num_heads, p.Sq_pad, vl ? 0 : a->o_stride[0], a->o_stride[1], a->o_stride[2],
+      vl ? 0 : a->do_stride[0], a->do_stride[1], a->do_stride[2], p.d_real, p.cu_q,
+      a->seqlen_q);
   FA_CUDA_TRY(cudaGetLastError());
   count_launch();
   return FA_OK;
@@ -1607,10 +1642,10 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
     prof_end(FA_PROF_BWD_DKDV, st);
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
-    const int64_t n4 = (int64_t)a->batch * a->num_heads * a->seqlen_q * (p.d_real / 4);
+    const int64_t n4 = (int64_t)p.B * a->num_heads * p.Sq * (p.d_real / 4);
     fa_bwd_dq_convert_kernel<T, D><<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(
-        p.dq_acc, reinterpret_cast<T*>(a->dq), a->batch, a->seqlen_q, a->num_heads, p.Sq_pad,
-        a->dq_stride[0], a->dq_stride[1], a->dq_stride[2], p.d_real);
+        p.dq_acc, reinterpret_cast<T*>(a->dq), p.B, p.Sq, a->num_heads, p.Sq_pad, p.dq_sb,
+        p.dq_ss, p.dq_sh, p.d_real, p.cu_q);
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
   } else if (!a->deterministic) {
@@ -1623,16 +1658,16 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
       if (int s = set_smem(kern, BwdCfg<D>::SMEM_BYTES)) return s;
       attr[slot].store(true, std::memory_order_release);
     }
-    dim3 grid((a->seqlen_k + kBwdBN - 1) / kBwdBN, a->num_heads_k, a->batch);
+    dim3 grid((p.Skv + kBwdBN - 1) / kBwdBN, a->num_heads_k, p.B);
     prof_begin(FA_PROF_BWD_DKDV, st);
     kern<<<grid, kBwdThreads, BwdCfg<D>::SMEM_BYTES, st>>>(tq, tk, tv, tdo, p);
     prof_end(FA_PROF_BWD_DKDV, st);
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
-    const int64_t n4 = (int64_t)a->batch * a->num_heads * a->seqlen_q * (p.d_real / 4);
+    const int64_t n4 = (int64_t)p.B * a->num_heads * p.Sq * (p.d_real / 4);
     fa_bwd_dq_convert_kernel<T, D><<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(
-        p.dq_acc, reinterpret_cast<T*>(a->dq), a->batch, a->seqlen_q, a->num_heads, p.Sq_pad,
-        a->dq_stride[0], a->dq_stride[1], a->dq_stride[2], p.d_real);
+        p.dq_acc, reinterpret_cast<T*>(a->dq), p.B, p.Sq, a->num_heads, p.Sq_pad, p.dq_sb,
+        p.dq_ss, p.dq_sh, p.d_real, p.cu_q);
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
   } else {
@@ -1647,13 +1682,13 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
       if (int s = set_smem(kq, DqCfg<D>::SMEM_BYTES)) return s;
       attr[slot].store(true, std::memory_order_release);
     }
-    dim3 grid((a->seqlen_k + kBwdBN - 1) / kBwdBN, a->num_heads_k, a->batch);
+    dim3 grid((p.Skv + kBwdBN - 1) / kBwdBN, a->num_heads_k, p.B);
     prof_begin(FA_PROF_BWD_DKDV, st);
     kern<<<grid, kBwdThreads, BwdCfg<D>::SMEM_BYTES, st>>>(tq, tk, tv, tdo, p);
     prof_end(FA_PROF_BWD_DKDV, st);
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
-    dim3 gq((a->seqlen_q + kBwdBM - 1) / kBwdBM, a->num_heads, a->batch);
+    dim3 gq((p.Sq + kBwdBM - 1) / kBwdBM, a->num_heads, p.B);
     kq<<<gq, 384, DqCfg<D>::SMEM_BYTES, st>>>(tq, tk, tv, tdo, p);
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
@@ -1663,7 +1698,8 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
 
 static uintptr_t align256(uintptr_t x) { return (x + 255) & ~uintptr_t(255); }
 
-int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st) {
+int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st,
+               const BwdVarlen* vl) {
   const int D = bwd_kernel_dim(a->head_dim);
   if (D != 64 && D != 128 && D != 256) return FA_ERR_UNSUPPORTED;
   if (a->batch == 0) return FA_OK;
@@ -1701,19 +1737,23 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
   FA_TMAP_TRY(enc(&tv, a->v, a->v_stride, a->num_heads_k, a->seqlen_k));
 
   BwdParams p{};
-  p.B = a->batch;
-  p.Sq = a->seqlen_q;
-  p.Skv = a->seqlen_k;
+  p.B = vl ? vl->batch : a->batch;
+  p.Sq = vl ? vl->max_q : a->seqlen_q;
+  p.Skv = vl ? vl->max_k : a->seqlen_k;
+  if (vl) {
+    p.cu_q = vl->cu_q;
+    p.cu_k = vl->cu_k;
+  }
   p.H = a->num_heads;
   p.Hk = a->num_heads_k;
   p.G = G;
-  p.Sq_pad = pad128(a->seqlen_q);
+  p.Sq_pad = pad128(p.Sq);
   p.d_real = a->head_dim;
   p.causal = a->causal;
   p.swq = a->window_q > 0 ? a->window_q : 0;
   p.swk = a->window_k > 0 ? a->window_k : 0;
-  p.n_t = (a->seqlen_k + kBwdBN - 1) / kBwdBN;
-  p.n_u = a->num_heads_k * a->batch;
+  p.n_t = (p.Skv + kBwdBN - 1) / kBwdBN;
+  p.n_u = a->num_heads_k * p.B;
   p.n_items = p.n_t * p.n_u;
   p.scale = a->softmax_scale;
   p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
@@ -1723,7 +1763,7 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
     p.sc_ia = a->softmax_scale / a->softcap;
     p.sc_t = 1.f / (1.4426950408889634f * a->softcap);
   }
-  const size_t rows = (size_t)a->batch * a->num_heads * p.Sq_pad;
+  const size_t rows = (size_t)p.B * a->num_heads * p.Sq_pad;
   uintptr_t w = align256(reinterpret_cast<uintptr_t>(ws));
   p.lse2 = reinterpret_cast<const float*>(w);
   w = align256(w + rows * 4);
@@ -1733,24 +1773,25 @@ int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cuda
   p.dq = a->dq;
   p.dk = a->dk;
   p.dv = a->dv;
-  p.dq_sb = a->dq_stride[0];
+  // varlen: rows are addressed through the packed offsets, so the batch strides drop out
+  p.dq_sb = vl ? 0 : a->dq_stride[0];
   p.dq_ss = a->dq_stride[1];
   p.dq_sh = a->dq_stride[2];
-  p.dk_sb = a->dk_stride[0];
+  p.dk_sb = vl ? 0 : a->dk_stride[0];
   p.dk_ss = a->dk_stride[1];
   p.dk_sh = a->dk_stride[2];
-  p.dv_sb = a->dv_stride[0];
+  p.dv_sb = vl ? 0 : a->dv_stride[0];
   p.dv_ss = a->dv_stride[1];
   p.dv_sh = a->dv_stride[2];
   p.err = err;
   const bool bf16 = a->dtype == FA_DTYPE_BF16;
-  const bool ext = p.swq > 0 || p.swk > 0 || p.sc_a != 0.f;
+  const bool ext = p.swq > 0 || p.swk > 0 || p.sc_a != 0.f || vl != nullptr;
   if (D == 256) {
     // prep (row dot, LSE * log2 e) here, then the two D = 256 kernels of fa_bwd256.cu
     const int s = bf16 ? launch_bwd_prep<__nv_bfloat16, 256>(a, p, st)
                        : launch_bwd_prep<__half, 256>(a, p, st);
     if (s != FA_OK) return s;
-    return launch_bwd_d256(a, p.lse2, p.dsum, p.Sq_pad, err, st);
+    return launch_bwd_d256(a, p.lse2, p.dsum, p.Sq_pad, err, st, vl);
   }
   if (D == 64)
     return ext ? (bf16 ? launch_bwd_impl<__nv_bfloat16, 64, true>(a, tq, tk, tv, tdo, p, st)

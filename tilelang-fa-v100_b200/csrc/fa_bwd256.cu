@@ -47,6 +47,10 @@ struct B2Params {
   float scale, scale_log2;
   // softcap (0: off): as in the D = 64 / 128 backward's parameters
   float sc_a, sc_k, sc_ia, sc_t;
+  // varlen (EXT kernels): packed-row offsets of the sequences, as in the D = 64 / 128
+  // backward's parameters; null for dense
+  const int32_t* cu_q;
+  const int32_t* cu_k;
   const float* lse2;  // [B, H, Sq_pad] lse * log2(e), +inf for padded / empty rows
   const float* dsum;  // [B, H, Sq_pad] rowsum(O * dO)
   void* dq;
@@ -150,9 +154,11 @@ __global__ void __launch_bounds__(kB2Threads, 1)
   const int dh = blockIdx.x & 1;                 // half of the head dimension
   const int k0 = (blockIdx.x >> 1) * kB2Keys;    // first key (heaviest tiles first when causal)
   const int hk = blockIdx.y, b = blockIdx.z;
-  const int off = p.Skv - p.Sq;                  // causal: key j visible to query i iff j <= i + off
+  const BwdSeq sq = bwd_seq<EXT>(p, b);
+  if (EXT && k0 >= sq.Skv) return;  // varlen: past this sequence's keys (uniform, no setup yet)
+  const int off = sq.Skv - sq.Sq;                // causal: key j visible to query i iff j <= i + off
   int s_start, s_end;  // query steps that see this CTA's keys (causal bound and window)
-  dense_q_tiles(k0, kB2Keys, kB2QStep, p.Sq, off, p.causal, EXT ? p.swq : 0, EXT ? p.swk : 0,
+  dense_q_tiles(k0, kB2Keys, kB2QStep, sq.Sq, off, p.causal, EXT ? p.swq : 0, EXT ? p.swk : 0,
                 s_start, s_end);
   const int nqs = s_end - s_start;
   const int n_iter = p.G * nqs;
@@ -195,8 +201,8 @@ __global__ void __launch_bounds__(kB2Threads, 1)
       const uint32_t kvb = smem_u32(&ctl->kv_full);
       mbar_arrive_expect_tx(kvb, 8 * kB2Chunk128);
       for (int c = 0; c < 4; ++c) {
-        tma_load_4d(sK + c * kB2Chunk128, &tm_k, kvb, c * 64, hk, k0, b);
-        tma_load_4d(sV + c * kB2Chunk128, &tm_v, kvb, c * 64, hk, k0, b);
+        tma_load_4d(sK + c * kB2Chunk128, &tm_k, kvb, c * 64, hk, sq.kr + k0, sq.tb);
+        tma_load_4d(sV + c * kB2Chunk128, &tm_v, kvb, c * 64, hk, sq.kr + k0, sq.tb);
       }
       int i = 0, n_do = 0;
       for (; i < n_iter; ++i) {
@@ -208,7 +214,7 @@ __global__ void __launch_bounds__(kB2Threads, 1)
         const uint32_t fb = smem_u32(&ctl->q_full[s]);
         mbar_arrive_expect_tx(fb, 4 * kB2Chunk64 + 2 * 256);
         for (int c = 0; c < 4; ++c)
-          tma_load_4d(sQ + (s * 4 + c) * kB2Chunk64, &tm_q, fb, c * 64, h, q0, b);
+          tma_load_4d(sQ + (s * 4 + c) * kB2Chunk64, &tm_q, fb, c * 64, h, sq.qr + q0, sq.tb);
         const int64_t row0 = ((int64_t)b * p.H + h) * p.Sq_pad + q0;
         b2_bulk_load(base + Cfg::OFF_LSE + s * 256, p.lse2 + row0, 256, fb);
         b2_bulk_load(base + Cfg::OFF_DI + s * 256, p.dsum + row0, 256, fb);
@@ -221,7 +227,7 @@ __global__ void __launch_bounds__(kB2Threads, 1)
         const uint32_t db = smem_u32(&ctl->do_full);
         mbar_arrive_expect_tx(db, 4 * kB2Chunk64);
         for (int c = 0; c < 4; ++c)
-          tma_load_4d(sdO + c * kB2Chunk64, &tm_do, db, c * 64, h, q0, b);
+          tma_load_4d(sdO + c * kB2Chunk64, &tm_do, db, c * 64, h, sq.qr + q0, sq.tb);
         n_do = i + 1;
       }
       b2_drain_wait(kvb, 0);
@@ -318,7 +324,7 @@ __global__ void __launch_bounds__(kB2Threads, 1)
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_off, tdP = tmem + lane_off + 64;
     const int key = k0 + j;
-    const bool key_ok = key < p.Skv;
+    const bool key_ok = key < sq.Skv;
     const float c2 = p.scale_log2;
     bool ok = true;
     for (int i = 0; i < n_iter; ++i) {
@@ -415,9 +421,9 @@ __global__ void __launch_bounds__(kB2Threads, 1)
     if (ok) {
       tc_fence_after();
       const int d0 = 128 * dh + 64 * c;  // this warpgroup's 64 dims of the CTA's half
-      T* dvr = reinterpret_cast<T*>(p.dv) + (int64_t)b * p.dv_sb + (int64_t)key * p.dv_ss +
+      T* dvr = reinterpret_cast<T*>(p.dv) + (int64_t)b * p.dv_sb + (int64_t)(sq.kr + key) * p.dv_ss +
                (int64_t)hk * p.dv_sh + d0;
-      T* dkr = reinterpret_cast<T*>(p.dk) + (int64_t)b * p.dk_sb + (int64_t)key * p.dk_ss +
+      T* dkr = reinterpret_cast<T*>(p.dk) + (int64_t)b * p.dk_sb + (int64_t)(sq.kr + key) * p.dk_ss +
                (int64_t)hk * p.dk_sh + d0;
       b2_store_row64<T>(tmem + lane_off + 128 + 64 * c, dvr, key_ok, n_iter > 0);
       b2_store_row64<T>(tmem + lane_off + 256 + 64 * c, dkr, key_ok, n_iter > 0);
@@ -474,11 +480,13 @@ __global__ void __launch_bounds__(kB2Threads, 1)
   const int h = blockIdx.y, b = blockIdx.z, hk = h / p.G;
   const int qt = p.causal ? (gridDim.x - 1 - blockIdx.x) : blockIdx.x;  // heaviest first
   const int q0 = qt * kB2Rows;
-  const int off = p.Skv - p.Sq;
+  const BwdSeq sq = bwd_seq<EXT>(p, b);
+  if (EXT && q0 >= sq.Sq) return;  // varlen: past this sequence's rows (uniform, no setup yet)
+  const int off = sq.Skv - sq.Sq;
   // Key steps j0 .. j0 + nks - 1 hold the keys this Q tile sees (causal bound and window);
   // the loops below count j from 0 (pipeline index) and read step j0 + j.
   int j0, j1;
-  dense_k_tiles(q0, kB2Rows, kB2KStep, p.Sq, p.Skv, off, p.causal, EXT ? p.swq : 0,
+  dense_k_tiles(q0, kB2Rows, kB2KStep, sq.Sq, sq.Skv, off, p.causal, EXT ? p.swq : 0,
                 EXT ? p.swk : 0, j0, j1);
   const int nks = j1 - j0;
 
@@ -519,8 +527,8 @@ __global__ void __launch_bounds__(kB2Threads, 1)
       const uint32_t qb = smem_u32(&ctl->q_full);
       mbar_arrive_expect_tx(qb, 8 * kB2Chunk128);
       for (int c = 0; c < 4; ++c) {
-        tma_load_4d(sQ + c * kB2Chunk128, &tm_q, qb, c * 64, h, q0, b);
-        tma_load_4d(sdO + c * kB2Chunk128, &tm_do, qb, c * 64, h, q0, b);
+        tma_load_4d(sQ + c * kB2Chunk128, &tm_q, qb, c * 64, h, sq.qr + q0, sq.tb);
+        tma_load_4d(sdO + c * kB2Chunk128, &tm_do, qb, c * 64, h, sq.qr + q0, sq.tb);
       }
       int jk = 0, jv = 0;
       bool ok = true;
@@ -532,15 +540,16 @@ __global__ void __launch_bounds__(kB2Threads, 1)
         const uint32_t kb = smem_u32(&ctl->k_full[s]);
         mbar_arrive_expect_tx(kb, 4 * kB2Chunk64);
         for (int c = 0; c < 4; ++c)
-          tma_load_4d(sK + (s * 4 + c) * kB2Chunk64, &tm_k, kb, c * 64, hk, (j0 + j) * kB2KStep,
-                      b);
+          tma_load_4d(sK + (s * 4 + c) * kB2Chunk64, &tm_k, kb, c * 64, hk,
+                      sq.kr + (j0 + j) * kB2KStep, sq.tb);
         jk = j + 1;
         ok = mbar_wait(smem_u32(&ctl->v_empty), (j & 1) ^ 1, abort_flag, p.err, FA_SITE_BWD_PRODUCER);
         if (!ok) break;
         const uint32_t vb = smem_u32(&ctl->v_full);
         mbar_arrive_expect_tx(vb, 4 * kB2Chunk64);
         for (int c = 0; c < 4; ++c)
-          tma_load_4d(sV + c * kB2Chunk64, &tm_v, vb, c * 64, hk, (j0 + j) * kB2KStep, b);
+          tma_load_4d(sV + c * kB2Chunk64, &tm_v, vb, c * 64, hk, sq.kr + (j0 + j) * kB2KStep,
+                      sq.tb);
         jv = j + 1;
       }
       b2_drain_wait(qb, 0);
@@ -600,7 +609,7 @@ __global__ void __launch_bounds__(kB2Threads, 1)
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_off, tdP = tmem + lane_off + 64;
     const int qi = q0 + r;
-    const bool q_ok = qi < p.Sq;
+    const bool q_ok = qi < sq.Sq;
     const int64_t row = ((int64_t)b * p.H + h) * p.Sq_pad + qi;
     const float lse2 = p.lse2[row];  // padded / empty rows hold +inf -> P = 0
     const float di = p.dsum[row];
@@ -624,7 +633,7 @@ __global__ void __launch_bounds__(kB2Threads, 1)
           for (int x = 0; x < 32; ++x) {
             const int key = kb + x;
             const bool vis =
-                q_ok && key < p.Skv && dense_visible(key, qi, off, p.causal, p.swq, p.swk);
+                q_ok && key < sq.Skv && dense_visible(key, qi, off, p.causal, p.swq, p.swk);
             float sx = __uint_as_float(sv[x]), g = 1.f;
             if (capped) {
               sx = softcap_score(sx, p.sc_a, p.sc_k);
@@ -637,7 +646,7 @@ __global__ void __launch_bounds__(kB2Threads, 1)
 #pragma unroll
           for (int x = 0; x < 32; ++x) {
             const int key = kb + x;
-            const bool vis = q_ok && key < p.Skv && (!p.causal || key <= qi + off);
+            const bool vis = q_ok && key < sq.Skv && (!p.causal || key <= qi + off);
             pv[x] = vis ? ex2_approx(fmaf(__uint_as_float(sv[x]), c2, -lse2)) : 0.f;
           }
         }
@@ -668,7 +677,7 @@ __global__ void __launch_bounds__(kB2Threads, 1)
     }
     if (ok) {
       tc_fence_after();
-      T* dst = reinterpret_cast<T*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)qi * p.dq_ss +
+      T* dst = reinterpret_cast<T*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)(sq.qr + qi) * p.dq_ss +
                (int64_t)h * p.dq_sh + 128 * c;
       b2_store_row64<T>(tmem + lane_off + 128 + 128 * c, dst, q_ok, nks > 0);
       b2_store_row64<T>(tmem + lane_off + 128 + 128 * c + 64, dst + 64, q_ok, nks > 0);
@@ -706,13 +715,13 @@ static int launch_bwd_d256_impl(const fa_bwd_args_t* a, const B2Params& p, cudaS
   static std::atomic<bool> attr_kv[kMaxContexts], attr_q[kMaxContexts];
   if (int s = smem_attr_once(kkv, B2KvCfg::SMEM_BYTES, attr_kv)) return s;
   if (int s = smem_attr_once(kq, B2DqCfg::SMEM_BYTES, attr_q)) return s;
-  const dim3 gkv(2 * ((a->seqlen_k + kB2Keys - 1) / kB2Keys), a->num_heads_k, a->batch);
+  const dim3 gkv(2 * ((p.Skv + kB2Keys - 1) / kB2Keys), a->num_heads_k, p.B);
   prof_begin(FA_PROF_BWD_DKDV, st);
   kkv<<<gkv, kB2Threads, B2KvCfg::SMEM_BYTES, st>>>(tq64, tk128, tv128, tdo64, p);
   prof_end(FA_PROF_BWD_DKDV, st);
   FA_CUDA_TRY(cudaGetLastError());
   count_launch();
-  const dim3 gq((a->seqlen_q + kB2Rows - 1) / kB2Rows, a->num_heads, a->batch);
+  const dim3 gq((p.Sq + kB2Rows - 1) / kB2Rows, a->num_heads, p.B);
   kq<<<gq, kB2Threads, B2DqCfg::SMEM_BYTES, st>>>(tq128, tk64, tv64, tdo128, p);
   FA_CUDA_TRY(cudaGetLastError());
   count_launch();
@@ -720,11 +729,15 @@ static int launch_bwd_d256_impl(const fa_bwd_args_t* a, const B2Params& p, cudaS
 }
 
 int launch_bwd_d256(const fa_bwd_args_t* a, const float* lse2, const float* dsum, int sq_pad,
-                    int* err, cudaStream_t st) {
+                    int* err, cudaStream_t st, const BwdVarlen* vl) {
   B2Params p{};
-  p.B = a->batch;
-  p.Sq = a->seqlen_q;
-  p.Skv = a->seqlen_k;
+  p.B = vl ? vl->batch : a->batch;
+  p.Sq = vl ? vl->max_q : a->seqlen_q;
+  p.Skv = vl ? vl->max_k : a->seqlen_k;
+  if (vl) {
+    p.cu_q = vl->cu_q;
+    p.cu_k = vl->cu_k;
+  }
   p.H = a->num_heads;
   p.Hk = a->num_heads_k;
   p.G = a->num_heads / a->num_heads_k;
@@ -745,18 +758,18 @@ int launch_bwd_d256(const fa_bwd_args_t* a, const float* lse2, const float* dsum
   p.dq = a->dq;
   p.dk = a->dk;
   p.dv = a->dv;
-  p.dq_sb = a->dq_stride[0];
+  p.dq_sb = vl ? 0 : a->dq_stride[0];  // varlen: rows through the packed offsets
   p.dq_ss = a->dq_stride[1];
   p.dq_sh = a->dq_stride[2];
-  p.dk_sb = a->dk_stride[0];
+  p.dk_sb = vl ? 0 : a->dk_stride[0];
   p.dk_ss = a->dk_stride[1];
   p.dk_sh = a->dk_stride[2];
-  p.dv_sb = a->dv_stride[0];
+  p.dv_sb = vl ? 0 : a->dv_stride[0];
   p.dv_ss = a->dv_stride[1];
   p.dv_sh = a->dv_stride[2];
   p.err = err;
   const bool bf16 = a->dtype == FA_DTYPE_BF16;
-  if (p.swq > 0 || p.swk > 0 || p.sc_a != 0.f)
+  if (p.swq > 0 || p.swk > 0 || p.sc_a != 0.f || vl != nullptr)
     return bf16 ? launch_bwd_d256_impl<__nv_bfloat16, true>(a, p, st)
                 : launch_bwd_d256_impl<__half, true>(a, p, st);
   return bf16 ? launch_bwd_d256_impl<__nv_bfloat16, false>(a, p, st)

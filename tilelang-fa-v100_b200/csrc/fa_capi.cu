@@ -322,6 +322,114 @@ int fa_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, void* stream) {
   return launch_bwd(a, ws, ws_bytes, err, static_cast<cudaStream_t>(stream));
 }
 
+// ---- dense varlen: the packed tensors as one batch entry of total rows + the offsets
+static bool varlen_dims_ok(int batch, int total_q, int total_k, int max_q, int max_k, int h,
+                           int hk) {
+  return batch >= 0 && total_q >= 0 && total_k >= 0 && max_q >= 0 && max_k >= 0 && h > 0 &&
+         hk > 0 && h % hk == 0;
+}
+static bool strides8(const int64_t* s) { return s[0] % 8 == 0 && s[1] % 8 == 0; }
+// Batch stride of the one-entry view: past the last row (only its alignment is checked).
+static void one_entry(int64_t dst[3], const int64_t src[2], int rows) {
+  dst[0] = src[0] * (rows > 0 ? rows : 1);
+  dst[1] = src[0];
+  dst[2] = src[1];
+}
+
+int fa_varlen_fwd(const fa_varlen_fwd_args_t* a, void* stream) {
+  if (a == nullptr || a->q == nullptr || a->k == nullptr || a->v == nullptr ||
+      a->out == nullptr || a->lse == nullptr || a->cu_seqlens_q == nullptr ||
+      a->cu_seqlens_k == nullptr)
+    return FA_ERR_INVALID_ARG;
+  if (!varlen_dims_ok(a->batch, a->total_q, a->total_k, a->max_seqlen_q, a->max_seqlen_k,
+                      a->num_heads, a->num_heads_k))
+    return FA_ERR_INVALID_ARG;
+  if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
+  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256) return FA_ERR_UNSUPPORTED;
+  if (!valid_softcap(a->softcap, a->softmax_scale)) return FA_ERR_INVALID_ARG;
+  if (!strides8(a->q_stride) || !strides8(a->k_stride) || !strides8(a->v_stride) ||
+      !strides8(a->o_stride))
+    return FA_ERR_ALIGNMENT;
+  int* err = nullptr;
+  if (int s = device_setup(&err, static_cast<cudaStream_t>(stream))) return s;
+  return launch_varlen_fwd(a, err, static_cast<cudaStream_t>(stream));
+}
+
+// The dense backward's argument block for the packed tensors (one batch entry of total_q
+// / total_k rows) and the varlen description that goes with it.
+static void varlen_as_dense(const fa_varlen_bwd_args_t* a, fa_bwd_args_t* d, BwdVarlen* vl) {
+  memset(d, 0, sizeof(*d));
+  d->q = a->q;
+  d->k = a->k;
+  d->v = a->v;
+  d->out = a->out;
+  d->dout = a->dout;
+  d->lse = a->lse;
+  d->dq = a->dq;
+  d->dk = a->dk;
+  d->dv = a->dv;
+  one_entry(d->q_stride, a->q_stride, a->total_q);
+  one_entry(d->k_stride, a->k_stride, a->total_k);
+  one_entry(d->v_stride, a->v_stride, a->total_k);
+  one_entry(d->o_stride, a->o_stride, a->total_q);
+  one_entry(d->do_stride, a->do_stride, a->total_q);
+  one_entry(d->dq_stride, a->dq_stride, a->total_q);
+  one_entry(d->dk_stride, a->dk_stride, a->total_k);
+  one_entry(d->dv_stride, a->dv_stride, a->total_k);
+  d->batch = 1;
+  d->seqlen_q = a->total_q;
+  d->seqlen_k = a->total_k;
+  d->num_heads = a->num_heads;
+  d->num_heads_k = a->num_heads_k;
+  d->head_dim = a->head_dim;
+  d->dtype = a->dtype;
+  d->causal = a->causal;
+  d->deterministic = a->deterministic;
+  d->softmax_scale = a->softmax_scale;
+  d->window_q = a->window_q;
+  d->window_k = a->window_k;
+  d->softcap = a->softcap;
+  vl->cu_q = a->cu_seqlens_q;
+  vl->cu_k = a->cu_seqlens_k;
+  vl->batch = a->batch;
+  vl->max_q = a->max_seqlen_q;
+  vl->max_k = a->max_seqlen_k;
+}
+
+size_t fa_varlen_bwd_workspace_size(const fa_varlen_bwd_args_t* a) {
+  if (a == nullptr) return 0;
+  fa_bwd_args_t d;
+  BwdVarlen vl;
+  varlen_as_dense(a, &d, &vl);
+  return bwd_workspace_bytes(&d, &vl);
+}
+
+int fa_varlen_bwd(const fa_varlen_bwd_args_t* a, void* ws, size_t ws_bytes, void* stream) {
+  if (a == nullptr || a->q == nullptr || a->k == nullptr || a->v == nullptr ||
+      a->out == nullptr || a->dout == nullptr || a->lse == nullptr || a->dq == nullptr ||
+      a->dk == nullptr || a->dv == nullptr || a->cu_seqlens_q == nullptr ||
+      a->cu_seqlens_k == nullptr)
+    return FA_ERR_INVALID_ARG;
+  if (!varlen_dims_ok(a->batch, a->total_q, a->total_k, a->max_seqlen_q, a->max_seqlen_k,
+                      a->num_heads, a->num_heads_k))
+    return FA_ERR_INVALID_ARG;
+  if (!valid_dtype(a->dtype)) return FA_ERR_UNSUPPORTED;
+  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256) return FA_ERR_UNSUPPORTED;
+  if (!valid_softcap(a->softcap, a->softmax_scale)) return FA_ERR_INVALID_ARG;
+  const int64_t* strs[8] = {a->q_stride, a->k_stride, a->v_stride, a->o_stride,
+                            a->do_stride, a->dq_stride, a->dk_stride, a->dv_stride};
+  for (const int64_t* s : strs)
+    if (!strides8(s)) return FA_ERR_ALIGNMENT;
+  fa_bwd_args_t d;
+  BwdVarlen vl;
+  varlen_as_dense(a, &d, &vl);
+  if (a->batch == 0) return FA_OK;
+  if (ws_bytes < bwd_workspace_bytes(&d, &vl) || ws == nullptr) return FA_ERR_WORKSPACE;
+  int* err = nullptr;
+  if (int s = device_setup(&err, static_cast<cudaStream_t>(stream))) return s;
+  return launch_bwd(&d, ws, ws_bytes, err, static_cast<cudaStream_t>(stream), &vl);
+}
+
 int fa_paged_prefill(const fa_paged_args_t* a, void* stream) {
   if (a == nullptr || a->q == nullptr || a->k_cache == nullptr || a->v_cache == nullptr ||
       a->block_table == nullptr || a->seq_lens == nullptr || a->query_start_loc == nullptr ||

@@ -648,6 +648,7 @@ struct FwdPersistCfg {
 struct FwdItem {
   int live;  // 0: the work list is exhausted
   int b, hk, tok0, q_len, kv_len, off, tok_base, j0, nkv;
+  int kv_row0;  // varlen: the sequence's first row of the packed K / V
 };
 
 struct FwdPersistCtl {
@@ -715,9 +716,17 @@ __device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it, int lane
     it.b = s;
     tile = x - cum;
     it.q_len = p.qsl[s + 1] - p.qsl[s];
-    it.kv_len = clamp_seq_len(p.seq_lens[s], p.max_blocks, p.page_size, p.err,
-                              FA_SITE_PAGED_SEQLEN, lane == 0);
-    it.off = p.pkl[s];
+    if (p.cu_k != nullptr) {
+      // varlen: packed K / V rows, bottom-right alignment of the sequence's own lengths
+      it.kv_row0 = p.cu_k[s];
+      it.kv_len = p.cu_k[s + 1] - it.kv_row0;
+      it.off = it.kv_len - it.q_len;
+    } else {
+      it.kv_row0 = 0;
+      it.kv_len = clamp_seq_len(p.seq_lens[s], p.max_blocks, p.page_size, p.err,
+                                FA_SITE_PAGED_SEQLEN, lane == 0);
+      it.off = p.pkl[s];
+    }
     it.tok_base = p.qsl[s];
   } else {
     it.b = unit / p.Hk;
@@ -726,6 +735,7 @@ __device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it, int lane
     it.kv_len = p.Skv;
     it.off = p.Skv - p.Sq;
     it.tok_base = 0;
+    it.kv_row0 = 0;
   }
   it.tok0 = tile * TPB;
   int j0 = 0, j1 = 0;
@@ -861,23 +871,24 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
       }
       ok = __shfl_sync(0xffffffffu, okl, 0) != 0;
       if (!ok) break;
+      const bool linear = !PAGED || p.cu_k != nullptr;  // dense / varlen: 128-row K/V boxes
       const int n_valid_pages =
-          PAGED ? min((item.kv_len + p.page_size - 1) / p.page_size, p.max_blocks) : 0;
+          linear ? 0 : min((item.kv_len + p.page_size - 1) / p.page_size, p.max_blocks);
       // Page id of box `lane` of KV tile j; pages past the sequence are fetched out of
       // range (page id num_pages), which TMA fills with zeros.
       auto page_of = [&](int j) -> int {
         int pg = p.num_pages;
-        if (PAGED && lane < boxes) {
+        if (!linear && lane < boxes) {
           const int lp = (j * kFwdBN + lane * box_rows) / p.page_size;
           if (lp < n_valid_pages) pg = p.block_table[(int64_t)b * p.max_blocks + lp];
         }
         return pg;
       };
-      int pg_next = (PAGED && nkv > 0) ? page_of(j0) : 0;
+      int pg_next = (!linear && nkv > 0) ? page_of(j0) : 0;
       for (int jj = 0; jj < nkv && ok; ++jj) {
         const int j = j0 + jj;
         const int pg_cur = pg_next;
-        if (PAGED && jj + 1 < nkv) pg_next = page_of(j + 1);
+        if (!linear && jj + 1 < nkv) pg_next = page_of(j + 1);
         for (int w = 0; w < 2 && ok; ++w, ++it) {
           const int s = it % ST;
           const uint32_t ph = (it / ST) & 1;
@@ -891,7 +902,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
           const CUtensorMap* tm = (w == 0) ? &tm_k : &tm_v;
           const uint32_t dst = sKV + s * Cfg::TILE_BYTES;
           if (lane == 0) mbar_arrive_expect_tx(fb, Cfg::TILE_BYTES);
-          if constexpr (PAGED) {
+          if (!linear) {
             __syncwarp();
             if (lane < boxes) {
               const int in_page = (j * kFwdBN + lane * box_rows) % p.page_size;
@@ -900,9 +911,12 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
                             in_page, pg_cur);
             }
           } else {
+            // dense: batch b's rows; varlen: rows from the sequence's first packed row
+            // (rows past it belong to the next sequence or lie past the tensor: masked)
             if (lane == 0)
               for (int dh = 0; dh < Cfg::DH; ++dh)
-                tma_load_4d(dst + dh * Cfg::CHUNK_BYTES, tm, fb, dh * 64, hk, j * kFwdBN, b);
+                tma_load_4d(dst + dh * Cfg::CHUNK_BYTES, tm, fb, dh * 64, hk,
+                            item.kv_row0 + j * kFwdBN, PAGED ? 0 : b);
           }
         }
       }
@@ -1052,7 +1066,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
     const float c2 = p.scale_log2;
     const float NEG_INF = -INFINITY;
     const bool window = fwd_window_on<PAGED>(p);
-    constexpr bool capped = CAP;  // softcap variant (dense only)
+    constexpr bool capped = CAP;  // softcap variant (dense and varlen)
     bool ok = true;
     int gj = 0, n_staged = 0;
     if (NQ == 2 && t == 1) mbar_arrive(smem_u32(&ctl->exp_turn[0]));  // tile 0 goes first
@@ -1083,7 +1097,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
         int lo = 0, hi = itp->kv_len;
         if (p.causal) hi = min(hi, lt + itp->off + 1);
         if (window) {
-          const int wa = PAGED ? lt : lt + itp->off;
+          const int wa = fwd_paged_window<PAGED>(p) ? lt : lt + itp->off;
           if (p.swq > 0) lo = max(lo, wa - p.swq + 1);
           if (p.swk > 0) hi = min(hi, wa + p.swk);
         }
@@ -1399,9 +1413,9 @@ static int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const C
                            const CUtensorMap& to, const FwdParams& p, cudaStream_t st) {
   const int kind = PAGED ? FA_PROF_PAGED : FA_PROF_FWD;
   int s = FA_OK;
-  if (!PAGED && p.sc_a != 0.f) {
-    // softcap: the persistent kernel's CAP variant serves every shape
-    if constexpr (!PAGED) s = launch_fwd_persist<T, D, NQ, false, true>(tq, tk, tv, to, p, kind, st);
+  if (p.sc_a != 0.f) {
+    // softcap (dense, varlen): the persistent kernel's CAP variant serves every shape
+    s = launch_fwd_persist<T, D, NQ, PAGED, true>(tq, tk, tv, to, p, kind, st);
   } else if (fwd_persistent<D, PAGED>(p.causal != 0, p.Skv)) {
     if constexpr (fwd_may_persist<D, PAGED>())
       s = launch_fwd_persist<T, D, NQ, PAGED, false>(tq, tk, tv, to, p, kind, st);
@@ -1559,6 +1573,67 @@ int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st) {
   // Sum over sequences of ceil(q_len / TPB) <= num_tokens / TPB + num_seqs.
   p.nbx = a->num_tokens / TPB + a->num_seqs;
   p.n_items = p.nbx * a->num_kv_heads;
+  switch (D) {
+    case 64: return dispatch_dtype<64, 2, true>(a->dtype, tq, tk, to, tv, p, st);
+    case 128: return dispatch_dtype<128, 2, true>(a->dtype, tq, tk, to, tv, p, st);
+    case 256: return dispatch_dtype<256, 1, true>(a->dtype, tq, tk, to, tv, p, st);
+    default: return FA_ERR_UNSUPPORTED;
+  }
+}
+
+// Dense varlen: packed sequences run through the paged pipeline (one work list over the
+// sequences' q blocks, GQA rows packed per kv head, LSE [H, total_q]) with K / V read as
+// 128-row boxes from each sequence's first packed row instead of through a block table,
+// and FA2's window anchor.
+int launch_varlen_fwd(const fa_varlen_fwd_args_t* a, int* err, cudaStream_t st) {
+  const int D = a->head_dim;
+  const int G = a->num_heads / a->num_heads_k;
+  const int NQ = (D == 256) ? 1 : 2;
+  if (G > 128) return FA_ERR_UNSUPPORTED;
+  if (a->total_q == 0 || a->batch == 0) return FA_OK;
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out))
+    return FA_ERR_ALIGNMENT;
+  const CUtensorMapDataType dt = tmap_dtype(a->dtype);
+  CUtensorMap tq, tk, tv, to;
+  auto rows_map = [&](CUtensorMap* m, const void* ptr, const int64_t* str2, int heads, int rows,
+                      uint32_t box_h, uint32_t box_r) {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)heads, (uint64_t)(rows > 0 ? rows : 1), 1};
+    const uint64_t str[3] = {(uint64_t)str2[1] * 2, (uint64_t)str2[0] * 2,
+                             (uint64_t)str2[0] * 2 * (uint64_t)(rows > 0 ? rows : 1)};
+    const uint32_t box[4] = {64, box_h, box_r, 1};
+    return encode_tmap(m, dt, 4, ptr, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  };
+  FA_TMAP_TRY(rows_map(&tq, a->q, a->q_stride, a->num_heads, a->total_q, G, 128 / G));
+  FA_TMAP_TRY(rows_map(&to, a->out, a->o_stride, a->num_heads, a->total_q, G, 128 / G));
+  FA_TMAP_TRY(rows_map(&tk, a->k, a->k_stride, a->num_heads_k, a->total_k, 1, kFwdBN));
+  FA_TMAP_TRY(rows_map(&tv, a->v, a->v_stride, a->num_heads_k, a->total_k, 1, kFwdBN));
+  FwdParams p{};
+  p.H = a->num_heads;
+  p.Hk = a->num_heads_k;
+  p.G = G;
+  p.causal = a->causal;
+  p.scale = a->softmax_scale;
+  p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  if (a->softcap > 0.f) {
+    p.sc_a = a->softcap / a->softmax_scale;
+    p.sc_k = 2.f * 1.4426950408889634f / p.sc_a;
+  }
+  p.out = a->out;
+  p.lse = a->lse;
+  p.o_st = a->o_stride[0];
+  p.o_sh = a->o_stride[1];
+  p.lse_sh = a->total_q;
+  p.qsl = a->cu_seqlens_q;
+  p.cu_k = a->cu_seqlens_k;
+  p.num_seqs = a->batch;
+  p.page_size = kFwdBN;  // unused by varlen loads; keeps the page-box arithmetic defined
+  p.swq = a->window_q > 0 ? a->window_q : 0;
+  p.swk = a->window_k > 0 ? a->window_k : 0;
+  p.err = err;
+  const int TPB = NQ * (128 / G);
+  // Sum over sequences of ceil(q_len / TPB) <= total_q / TPB + batch.
+  p.nbx = a->total_q / TPB + a->batch;
+  p.n_items = p.nbx * a->num_heads_k;
   switch (D) {
     case 64: return dispatch_dtype<64, 2, true>(a->dtype, tq, tk, to, tv, p, st);
     case 128: return dispatch_dtype<128, 2, true>(a->dtype, tq, tk, to, tv, p, st);

@@ -26,6 +26,9 @@ struct FwdParams {
   const int32_t* qsl;
   const int32_t* pkl;
   int num_seqs, max_blocks, page_size, num_pages;
+  // varlen (dense packed sequences through the paged pipeline): sequence b's K / V rows
+  // are [cu_k[b], cu_k[b + 1]) of [total_k, Hk, D] tensors; null for paged and dense
+  const int32_t* cu_k;
   int swq, swk;
   // softcap (dense only): sc_a = softcap / scale (0: off), sc_k = 2 log2(e) / sc_a
   float sc_a, sc_k;
@@ -71,16 +74,40 @@ __host__ __device__ __forceinline__ void dense_k_tiles(int q0, int bm, int bn, i
   j1 = hi < lo ? j0 : hi / bn + 1;
 }
 
+// Lengths and packed-row offsets of batch entry b: dense launches use the call's Sq / Skv
+// and TMA batch coordinate b; varlen launches (EXT kernels) the sequence's own lengths,
+// its first packed rows and batch coordinate 0.  A varlen length is capped at the call's
+// longest (Sq / Skv = max_seqlen_q / _k), which sizes the grids and the padded per-row
+// workspace: a sequence longer than its max_seqlen loses its excess rows, it never reads
+// or writes past the workspace.
+struct BwdSeq {
+  int Sq, Skv;  // query / key rows of this batch entry
+  int qr, kr;   // first packed query / key row (0 for dense)
+  int tb;       // TMA batch coordinate
+};
+template <bool EXT, typename Params>
+__device__ __forceinline__ BwdSeq bwd_seq(const Params& p, int b) {
+  if (EXT && p.cu_q != nullptr) {
+    const int qr = p.cu_q[b], kr = p.cu_k[b];
+    return {min(p.cu_q[b + 1] - qr, p.Sq), min(p.cu_k[b + 1] - kr, p.Skv), qr, kr, 0};
+  }
+  return {p.Sq, p.Skv, 0, 0, b};
+}
+
 constexpr int kFwdBN = 128;  // keys per forward KV tile
 
-// Sliding window: dense launches take FA2's window_size, bottom-right aligned like the
-// causal mask (anchor = row's token + Skv - Sq); paged launches the reference's paged
-// window, anchored on the row's token and honoured only with causal
+// Sliding window: dense and varlen launches take FA2's window_size, bottom-right aligned
+// like the causal mask (anchor = row's token + Skv - Sq); paged launches the reference's
+// paged window, anchored on the row's token and honoured only with causal
 // (_kernels_paged.py:275-294).  Key j is visible iff anchor - swq < j (swq > 0) and
 // j < anchor + swk (swk > 0).
 template <bool PAGED>
+__device__ __forceinline__ bool fwd_paged_window(const FwdParams& p) {
+  return PAGED && p.cu_k == nullptr;
+}
+template <bool PAGED>
 __device__ __forceinline__ bool fwd_window_on(const FwdParams& p) {
-  return (PAGED ? p.causal != 0 : true) && (p.swq > 0 || p.swk > 0);
+  return (fwd_paged_window<PAGED>(p) ? p.causal != 0 : true) && (p.swq > 0 || p.swk > 0);
 }
 // KV tiles [j0, j1) that the rows of tokens [tok0, tok0 + TPB) of a work item can see:
 // keys below kv_len, the causal bound and the sliding window.
@@ -95,7 +122,8 @@ __device__ __forceinline__ void fwd_kv_range(const FwdParams& p, int tok0, int T
     j1 = min(j1, max_key >= 0 ? max_key / kFwdBN + 1 : 0);
   }
   if (fwd_window_on<PAGED>(p)) {
-    const int a0 = PAGED ? tok0 : tok0 + off, a1 = PAGED ? last_lt : last_lt + off;
+    const bool pw = fwd_paged_window<PAGED>(p);
+    const int a0 = pw ? tok0 : tok0 + off, a1 = pw ? last_lt : last_lt + off;
     if (p.swq > 0) j0 = max(0, a0 - p.swq + 1) / kFwdBN;
     if (p.swk > 0) {
       const int max_key = a1 + p.swk - 1;
@@ -130,13 +158,22 @@ void prof_end(int kind, cudaStream_t st);
 
 int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st);
 int launch_paged_prefill(const fa_paged_args_t* a, int* err, cudaStream_t st);
+int launch_varlen_fwd(const fa_varlen_fwd_args_t* a, int* err, cudaStream_t st);
 // Paged prefill at head_dim 512 (fa_paged512.cu); called by launch_paged_prefill.
 int launch_paged512(const fa_paged_args_t* a, int* err, cudaStream_t st);
-int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st);
+// Varlen backward: `a` describes the packed tensors as one batch entry of total_q / total_k
+// rows; this adds the sequences' row offsets and the longest lengths.
+struct BwdVarlen {
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  int batch, max_q, max_k;
+};
+int launch_bwd(const fa_bwd_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st,
+               const BwdVarlen* vl = nullptr);
 // Dense backward at head_dim 256 (fa_bwd256.cu) after the prep kernel has written lse2 / dsum.
 int launch_bwd_d256(const fa_bwd_args_t* a, const float* lse2, const float* dsum, int sq_pad,
-                    int* err, cudaStream_t st);
-size_t bwd_workspace_bytes(const fa_bwd_args_t* a);
+                    int* err, cudaStream_t st, const BwdVarlen* vl = nullptr);
+size_t bwd_workspace_bytes(const fa_bwd_args_t* a, const BwdVarlen* vl = nullptr);
 int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err, cudaStream_t st);
 size_t decode_workspace_bytes(const fa_decode_args_t* a);
 int launch_decode_noalloc(const fa_decode_args_t* a, int* err, cudaStream_t st);

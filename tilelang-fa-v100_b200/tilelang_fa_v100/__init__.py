@@ -11,6 +11,9 @@ from .interface import (
     tilelang_paged_forward,
     tilelang_decode_forward,
 )
+# FA2's packed variable-length entry; an addition beyond the reference's four exports,
+# so it is importable by name but left out of __all__ (which mirrors the reference's).
+from .interface import tilelang_flash_attn_varlen_func
 
 __version__ = "1.0.0"
 __all__ = [

@@ -57,6 +57,31 @@ class BwdArgs(ctypes.Structure):
                 ("window_k", _i32), ("softcap", _f32)]
 
 
+class VarlenFwdArgs(ctypes.Structure):
+    _fields_ = [("q", _vp), ("k", _vp), ("v", _vp), ("out", _vp), ("lse", _vp),
+                ("cu_seqlens_q", _vp), ("cu_seqlens_k", _vp),
+                ("q_stride", _i64 * 2), ("k_stride", _i64 * 2), ("v_stride", _i64 * 2),
+                ("o_stride", _i64 * 2),
+                ("batch", _i32), ("total_q", _i32), ("total_k", _i32), ("max_seqlen_q", _i32),
+                ("max_seqlen_k", _i32), ("num_heads", _i32), ("num_heads_k", _i32),
+                ("head_dim", _i32), ("dtype", _i32), ("causal", _i32), ("softmax_scale", _f32),
+                ("window_q", _i32), ("window_k", _i32), ("softcap", _f32)]
+
+
+class VarlenBwdArgs(ctypes.Structure):
+    _fields_ = [("q", _vp), ("k", _vp), ("v", _vp), ("out", _vp), ("dout", _vp), ("lse", _vp),
+                ("dq", _vp), ("dk", _vp), ("dv", _vp),
+                ("cu_seqlens_q", _vp), ("cu_seqlens_k", _vp),
+                ("q_stride", _i64 * 2), ("k_stride", _i64 * 2), ("v_stride", _i64 * 2),
+                ("o_stride", _i64 * 2), ("do_stride", _i64 * 2), ("dq_stride", _i64 * 2),
+                ("dk_stride", _i64 * 2), ("dv_stride", _i64 * 2),
+                ("batch", _i32), ("total_q", _i32), ("total_k", _i32), ("max_seqlen_q", _i32),
+                ("max_seqlen_k", _i32), ("num_heads", _i32), ("num_heads_k", _i32),
+                ("head_dim", _i32), ("dtype", _i32), ("causal", _i32), ("deterministic", _i32),
+                ("softmax_scale", _f32), ("window_q", _i32), ("window_k", _i32),
+                ("softcap", _f32)]
+
+
 class PagedArgs(ctypes.Structure):
     _fields_ = [("q", _vp), ("k_cache", _vp), ("v_cache", _vp), ("block_table", _vp),
                 ("seq_lens", _vp), ("query_start_loc", _vp), ("prefix_kv_lens", _vp),
@@ -91,6 +116,9 @@ SIGNATURES = {
     "fa_fwd": (_i32, [ctypes.POINTER(FwdArgs), _vp]),
     "fa_bwd_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(BwdArgs)]),
     "fa_bwd": (_i32, [ctypes.POINTER(BwdArgs), _vp, ctypes.c_size_t, _vp]),
+    "fa_varlen_fwd": (_i32, [ctypes.POINTER(VarlenFwdArgs), _vp]),
+    "fa_varlen_bwd_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(VarlenBwdArgs)]),
+    "fa_varlen_bwd": (_i32, [ctypes.POINTER(VarlenBwdArgs), _vp, ctypes.c_size_t, _vp]),
     "fa_paged_prefill": (_i32, [ctypes.POINTER(PagedArgs), _vp]),
     "fa_decode_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(DecodeArgs)]),
     "fa_decode": (_i32, [ctypes.POINTER(DecodeArgs), _vp, ctypes.c_size_t, _vp]),
@@ -256,6 +284,77 @@ def dense_backward(q, k, v, out, dout, lse, softmax_scale, causal, deterministic
     with torch.cuda.device(q.device):
         check(lib.fa_bwd(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), nbytes,
                          _stream(q.device)))
+    return dq, dk, dv
+
+
+def _tokens_heads(t, what):
+    """[total, heads, D] with a contiguous last dim; (token, head) strides in elements."""
+    if t.dim() != 3:
+        raise ValueError("%s must be [total_tokens, heads, head_dim]" % what)
+    if t.stride(-1) != 1 or t.stride(0) % 8 or t.stride(1) % 8:
+        t = t.contiguous()
+    return t
+
+
+def _cu(t, dev, n):
+    t = t.to(device=dev, dtype=torch.int32).contiguous()
+    if t.dim() != 1 or t.numel() != n:
+        raise ValueError("cu_seqlens must be [batch + 1]")
+    return t
+
+
+def varlen_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
+                   softmax_scale, causal, window_size=(-1, -1), softcap=0.0):
+    """out [total_q, H, D] and lse [H, total_q] fp32 for packed sequences (FA2 varlen)."""
+    _require_cuda(q, k, v)
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError("q, k, v dtypes differ")
+    q, k, v = _tokens_heads(q, "q"), _tokens_heads(k, "k"), _tokens_heads(v, "v")
+    if tuple(v.shape) != tuple(k.shape) or k.shape[2] != q.shape[2]:
+        raise ValueError("k/v shape %s incompatible with q %s" % (tuple(k.shape), tuple(q.shape)))
+    batch = cu_seqlens_q.numel() - 1
+    cq, ck = _cu(cu_seqlens_q, q.device, batch + 1), _cu(cu_seqlens_k, q.device, batch + 1)
+    tq, h, d = q.shape
+    tk, hk = k.shape[0], k.shape[1]
+    out = torch.empty((tq, h, d), dtype=q.dtype, device=q.device)
+    lse = torch.empty((h, tq), dtype=torch.float32, device=q.device)
+    st2 = lambda t: (_i64 * 2)(t.stride(0), t.stride(1))
+    a = VarlenFwdArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr(),
+                      cq.data_ptr(), ck.data_ptr(), st2(q), st2(k), st2(v), st2(out),
+                      batch, tq, tk, int(max_seqlen_q), int(max_seqlen_k), h, hk, d,
+                      _dtype_code(q.dtype), 1 if causal else 0, float(softmax_scale),
+                      *window_fields(window_size), float(softcap))
+    with torch.cuda.device(q.device):
+        check(load().fa_varlen_fwd(ctypes.byref(a), _stream(q.device)))
+    return out, lse
+
+
+def varlen_backward(q, k, v, out, dout, lse, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+                    max_seqlen_k, softmax_scale, causal, deterministic=False,
+                    window_size=(-1, -1), softcap=0.0):
+    """dq, dk, dv in the packed layouts of q / k / v."""
+    _require_cuda(q, k, v, out, dout, lse)
+    q, k, v, out = (_tokens_heads(t, w) for t, w in ((q, "q"), (k, "k"), (v, "v"), (out, "out")))
+    dout = _tokens_heads(dout.to(q.dtype), "dout")
+    lse = lse.contiguous()
+    batch = cu_seqlens_q.numel() - 1
+    cq, ck = _cu(cu_seqlens_q, q.device, batch + 1), _cu(cu_seqlens_k, q.device, batch + 1)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    st2 = lambda t: (_i64 * 2)(t.stride(0), t.stride(1))
+    tq, h, d = q.shape
+    a = VarlenBwdArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dout.data_ptr(),
+                      lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                      cq.data_ptr(), ck.data_ptr(), st2(q), st2(k), st2(v), st2(out), st2(dout),
+                      st2(dq), st2(dk), st2(dv), batch, tq, k.shape[0], int(max_seqlen_q),
+                      int(max_seqlen_k), h, k.shape[1], d, _dtype_code(q.dtype),
+                      1 if causal else 0, 1 if deterministic else 0, float(softmax_scale),
+                      *window_fields(window_size), float(softcap))
+    lib = load()
+    nbytes = int(lib.fa_varlen_bwd_workspace_size(ctypes.byref(a)))
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
+    with torch.cuda.device(q.device):
+        check(lib.fa_varlen_bwd(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), nbytes,
+                                _stream(q.device)))
     return dq, dk, dv
 
 

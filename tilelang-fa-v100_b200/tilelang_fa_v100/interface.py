@@ -129,3 +129,61 @@ def tilelang_decode_forward(q, k_cache, v_cache, block_table, seq_lens,
         block_size=block_size, num_kv_heads=num_kv_heads,
         softmax_scale=softmax_scale, k_scale=k_scale, v_scale=v_scale,
     )
+
+
+class FlashAttnVarlenFunc(torch.autograd.Function):
+    """Autograd function for packed variable-length sequences (FA2's varlen path)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
+                dropout_p, softmax_scale, causal, window_size, softcap, alibi_slopes,
+                deterministic, return_softmax):
+        if dropout_p != 0.0:
+            raise NotImplementedError("dropout not supported")
+        if alibi_slopes is not None:
+            raise NotImplementedError("alibi not supported")
+        scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q.shape[-1])
+        window = tuple(window_size) if window_size is not None else (-1, -1)
+        cap = float(softcap) if softcap > 0 else 0.0
+        out, lse = _ext.varlen_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+                                       max_seqlen_k, scale, causal, window, cap)
+        ctx.save_for_backward(q, k, v, out, lse, cu_seqlens_q, cu_seqlens_k)
+        ctx.max_seqlen = (int(max_seqlen_q), int(max_seqlen_k))
+        ctx.causal, ctx.window, ctx.softcap, ctx.softmax_scale = causal, window, cap, scale
+        ctx.deterministic = bool(deterministic)
+        if return_softmax:
+            return out, lse, None
+        return out
+
+    @staticmethod
+    def backward(ctx, dout, *args):
+        q, k, v, out, lse, cu_q, cu_k = ctx.saved_tensors
+        dq, dk, dv = _ext.varlen_backward(q, k, v, out, dout, lse, cu_q, cu_k, *ctx.max_seqlen,
+                                          ctx.softmax_scale, ctx.causal, ctx.deterministic,
+                                          ctx.window, ctx.softcap)
+        return (dq, dk, dv) + (None,) * 12
+
+
+def tilelang_flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+                                    max_seqlen_k, dropout_p=0.0, softmax_scale=None,
+                                    causal=False, window_size=(-1, -1), softcap=0.0,
+                                    alibi_slopes=None, deterministic=False,
+                                    return_attn_probs=False):
+    """FA2-compatible ``flash_attn_varlen_func`` over packed sequences (no reference
+    counterpart: the reference's dense API takes equal-length batches).
+
+    Args:
+        q: [total_q, H, D]; k, v: [total_k, Hk, D] (H % Hk == 0), fp16 or bf16, D 64/128/256
+        cu_seqlens_q / cu_seqlens_k: [batch + 1] int32 offsets of each sequence's rows
+        max_seqlen_q / max_seqlen_k: upper bounds of the sequences' lengths
+        causal, window_size, softcap: as tilelang_flash_attn_func, per sequence
+            (bottom-right aligned on that sequence's own lengths)
+
+    Returns:
+        out: [total_q, H, D], or (out, lse [H, total_q] fp32, None)
+    """
+    return FlashAttnVarlenFunc.apply(
+        q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, dropout_p,
+        softmax_scale, causal, window_size, softcap, alibi_slopes, deterministic,
+        return_attn_probs,
+    )
