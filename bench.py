@@ -904,12 +904,18 @@ def run_profile_case(args):
     """Small cases for ncu captures.  dense: B=2 of configs[2] (q/k/v/dO 67 MB each,
     268 MB together > the 126 MB L2), fwd+bwd steps.  decode: 64 sequences of
     configs[4] (L ~ U[512, 8192], ~1.1 GB of K/V pages), decode steps.  paged: configs[3]
-    itself (q 134 MB > L2, K/V pages 34 MB), paged prefill steps."""
+    itself (q 134 MB > L2, K/V pages 34 MB), paged prefill steps.  paged512: the head_dim
+    512 paged workload (q 268 MB, K/V pages 134 MB)."""
     import tilelang_fa_v100 as fa
     dev = torch.device("cuda", 0)
     if args.profile_case == "paged":
         tflops, ms, _ = paged_run(dev, None, 0, 1, args.steps, args.warmup)
         print(json.dumps({"profile_case": "paged_cfg4_fp16", "ms": ms, "tflops": tflops}), flush=True)
+        return
+    if args.profile_case == "paged512":  # the head_dim 512 secondary line's workload
+        tflops, ms, _ = paged_run(dev, None, 0, 1, args.steps, args.warmup, c=PAGED512)
+        print(json.dumps({"profile_case": "paged_D512_16x1024_H16_Hkv4_fp16", "ms": ms,
+                          "tflops": tflops}), flush=True)
         return
     if args.profile_case == "decode":
         q, kc, vc, bt, sl, nbytes, _, _, _ = decode_problem(dev, 0, 1, batch=64)
@@ -945,7 +951,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
-    ap.add_argument("--profile-case", choices=["dense", "decode", "paged", "d64", "d256"], default=None,
+    ap.add_argument("--profile-case", choices=["dense", "decode", "paged", "paged512", "d64", "d256"], default=None,
                     help="small case for ncu captures (no e2e / CPU / secondary)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":

@@ -151,7 +151,7 @@ __device__ __forceinline__ void store_units(T* dst, const uint32_t* pk, int cols
 // (atomic mode) the same kernel clears its rows, so no separate memset is needed.
 constexpr int kPrepPasses = 4;
 
-template <typename T, int D>
+template <typename T, int D, bool VARLEN>
 __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const T* __restrict__ o,
                                                           const T* __restrict__ dout,
                                                           const float* __restrict__ lse,
@@ -176,13 +176,19 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const T* __restrict__ 
     const int64_t row = row0 + ps * RPW + sub;
     const int i = (int)(row % Sq_pad);
     const int64_t bh = row / Sq_pad;
-    const int h = (int)(bh % H), b = (int)(bh / H);
-    // varlen: row i of sequence b is packed row cu_q[b] + i (batch strides are 0)
-    const int q_len = (cu_q != nullptr && row < rows) ? min(cu_q[b + 1] - cu_q[b], Sq) : Sq;
-    const int64_t tok = (cu_q != nullptr && row < rows) ? (int64_t)cu_q[b] + i : i;
-    live[ps] = row < rows && i < q_len;
+    live[ps] = row < rows && i < Sq;
+    int64_t tok = i;
+    if constexpr (VARLEN) {
+      // row i of sequence b is packed row cu_q[b] + i (the batch strides are 0)
+      if (row < rows) {
+        const int b = (int)(bh / H);
+        live[ps] = i < min(cu_q[b + 1] - cu_q[b], Sq);
+        tok = (int64_t)cu_q[b] + i;
+      }
+    }
     av[ps] = dv[ps] = make_uint4(0u, 0u, 0u, 0u);
     if (live[ps] && cl * 8 < d_real) {
+      const int h = (int)(bh % H), b = (int)(bh / H);
       av[ps] = __ldcs(reinterpret_cast<const uint4*>(o + b * o_sb + tok * o_ss +
                                                      (int64_t)h * o_sh) + cl);
       dv[ps] = __ldcs(reinterpret_cast<const uint4*>(dout + b * do_sb + tok * do_ss +
@@ -210,9 +216,8 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const T* __restrict__ 
           const int i = (int)(row % Sq_pad);
           const int64_t bh = row / Sq_pad;
           // lse: dense [B, H, Sq]; varlen [H, total_q] (FA2's varlen layout)
-          const float L = cu_q != nullptr
-                              ? lse[(bh % H) * (int64_t)total_q + cu_q[bh / H] + i]
-                              : lse[bh * Sq + i];
+          const float L = VARLEN ? lse[(bh % H) * (int64_t)total_q + cu_q[bh / H] + i]
+                                 : lse[bh * Sq + i];
           l2 = (L == -INFINITY) ? INFINITY : L * 1.4426950408889634f;
         }
         lse2[row] = l2;
@@ -228,7 +233,7 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const T* __restrict__ 
 }
 
 // ---------------------------------------------------------------- 4. dQ convert
-template <typename T, int D>
+template <typename T, int D, bool VARLEN>
 __global__ void __launch_bounds__(256) fa_bwd_dq_convert_kernel(const float* __restrict__ acc,
                                                                 T* dq, int B, int Sq, int H,
                                                                 int Sq_pad, int64_t sb,
@@ -246,7 +251,7 @@ __global__ void __launch_bounds__(256) fa_bwd_dq_convert_kernel(const float* __r
   const int b = bi / Sq;
   // varlen: Sq is the longest sequence; rows past this one's end hold nothing
   int64_t tok = i;
-  if (cu_q != nullptr) {
+  if constexpr (VARLEN) {
     if (i >= cu_q[b + 1] - cu_q[b]) return;
     tok = (int64_t)cu_q[b] + i;
   }
@@ -1607,7 +1612,8 @@ static int launch_bwd_prep(const fa_bwd_args_t* a, const BwdParams& p, cudaStrea
   // varlen: `a` describes the packed tensors as one batch entry of total_q rows (its
   // seqlen_q); rows are found through cu_q, so the batch strides drop out
   const bool vl = p.cu_q != nullptr;
-  fa_bwd_prep_kernel<T, D><<<blocks, 256, 0, st>>>(
+  auto kern = vl ? fa_bwd_prep_kernel<T, D, true> : fa_bwd_prep_kernel<T, D, false>;
+  kern<<<blocks, 256, 0, st>>>(
       reinterpret_cast<const T*>(a->out), reinterpret_cast<const T*>(a->dout), a->lse,
       const_cast<float*>(p.lse2), const_cast<float*>(p.dsum), p.dq_acc, p.B, p.Sq,
       a->num_heads, p.Sq_pad, vl ? 0 : a->o_stride[0], a->o_stride[1], a->o_stride[2],
@@ -1643,7 +1649,9 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
     const int64_t n4 = (int64_t)p.B * a->num_heads * p.Sq * (p.d_real / 4);
-    fa_bwd_dq_convert_kernel<T, D><<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(
+    auto conv = p.cu_q != nullptr ? fa_bwd_dq_convert_kernel<T, D, true>
+                                  : fa_bwd_dq_convert_kernel<T, D, false>;
+    conv<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(
         p.dq_acc, reinterpret_cast<T*>(a->dq), p.B, p.Sq, a->num_heads, p.Sq_pad, p.dq_sb,
         p.dq_ss, p.dq_sh, p.d_real, p.cu_q);
     FA_CUDA_TRY(cudaGetLastError());
@@ -1665,7 +1673,9 @@ static int launch_bwd_impl(const fa_bwd_args_t* a, const CUtensorMap& tq, const 
     FA_CUDA_TRY(cudaGetLastError());
     count_launch();
     const int64_t n4 = (int64_t)p.B * a->num_heads * p.Sq * (p.d_real / 4);
-    fa_bwd_dq_convert_kernel<T, D><<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(
+    auto conv = p.cu_q != nullptr ? fa_bwd_dq_convert_kernel<T, D, true>
+                                  : fa_bwd_dq_convert_kernel<T, D, false>;
+    conv<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(
         p.dq_acc, reinterpret_cast<T*>(a->dq), p.B, p.Sq, a->num_heads, p.Sq_pad, p.dq_sb,
         p.dq_ss, p.dq_sh, p.d_real, p.cu_q);
     FA_CUDA_TRY(cudaGetLastError());

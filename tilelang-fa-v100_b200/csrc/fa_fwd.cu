@@ -676,7 +676,7 @@ struct FwdPersistCtl {
 // slots per kv head, the tail empty).  Returns false for an empty slot.  Called by all 32
 // lanes of a warp (the paged scan over sequences takes 32 of them per step); the result is
 // the same in every lane.
-template <int NQ, bool PAGED>
+template <int NQ, bool PAGED, bool VARLEN>
 __device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it, int lane) {
   const int TPB = NQ * (kFwdBM / p.G);
   int x = L % p.nbx;
@@ -716,7 +716,7 @@ __device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it, int lane
     it.b = s;
     tile = x - cum;
     it.q_len = p.qsl[s + 1] - p.qsl[s];
-    if (p.cu_k != nullptr) {
+    if constexpr (VARLEN) {
       // varlen: packed K / V rows, bottom-right alignment of the sequence's own lengths
       it.kv_row0 = p.cu_k[s];
       it.kv_len = p.cu_k[s + 1] - it.kv_row0;
@@ -739,7 +739,7 @@ __device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it, int lane
   }
   it.tok0 = tile * TPB;
   int j0 = 0, j1 = 0;
-  fwd_kv_range<PAGED>(p, it.tok0, TPB, it.q_len, it.kv_len, it.off, j0, j1);
+  fwd_kv_range<PAGED, VARLEN>(p, it.tok0, TPB, it.q_len, it.kv_len, it.off, j0, j1);
   it.j0 = j0;
   it.nkv = max(0, j1 - j0);
   it.live = 1;
@@ -749,7 +749,7 @@ __device__ bool fwd_decode_item(int L, const FwdParams& p, FwdItem& it, int lane
 // Persistent: one CTA per SM claims work items from a device counter (p.sched) in list
 // order, so the claim order matches a one-CTA-per-item launch while the next item's
 // loads and first S overlap the current item's tail.
-template <typename T, int D, int NQ, bool PAGED, bool CAP>
+template <typename T, int D, int NQ, bool PAGED, bool CAP, bool VARLEN>
 __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
     fa_fwd_persist_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -841,7 +841,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
           if (lane == 0) L = atomicAdd(p.sched, 1);
           L = __shfl_sync(0xffffffffu, L, 0);
           if (L >= p.n_items) break;
-          if (fwd_decode_item<NQ, PAGED>(L, p, item, lane)) break;
+          if (fwd_decode_item<NQ, PAGED, VARLEN>(L, p, item, lane)) break;
         }
       }
       if (lane == 0) {
@@ -871,7 +871,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
       }
       ok = __shfl_sync(0xffffffffu, okl, 0) != 0;
       if (!ok) break;
-      const bool linear = !PAGED || p.cu_k != nullptr;  // dense / varlen: 128-row K/V boxes
+      constexpr bool linear = !PAGED || VARLEN;  // dense / varlen: 128-row K/V boxes
       const int n_valid_pages =
           linear ? 0 : min((item.kv_len + p.page_size - 1) / p.page_size, p.max_blocks);
       // Page id of box `lane` of KV tile j; pages past the sequence are fetched out of
@@ -902,7 +902,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
           const CUtensorMap* tm = (w == 0) ? &tm_k : &tm_v;
           const uint32_t dst = sKV + s * Cfg::TILE_BYTES;
           if (lane == 0) mbar_arrive_expect_tx(fb, Cfg::TILE_BYTES);
-          if (!linear) {
+          if constexpr (!linear) {
             __syncwarp();
             if (lane < boxes) {
               const int in_page = (j * kFwdBN + lane * box_rows) % p.page_size;
@@ -1065,7 +1065,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
     const int tr = r / G;                    // token of this row inside the tile
     const float c2 = p.scale_log2;
     const float NEG_INF = -INFINITY;
-    const bool window = fwd_window_on<PAGED>(p);
+    const bool window = fwd_window_on<PAGED, VARLEN>(p);
     constexpr bool capped = CAP;  // softcap variant (dense and varlen)
     bool ok = true;
     int gj = 0, n_staged = 0;
@@ -1097,7 +1097,7 @@ __global__ void __launch_bounds__(FwdPersistCfg<D, NQ>::NTHREADS, 1)
         int lo = 0, hi = itp->kv_len;
         if (p.causal) hi = min(hi, lt + itp->off + 1);
         if (window) {
-          const int wa = fwd_paged_window<PAGED>(p) ? lt : lt + itp->off;
+          const int wa = fwd_paged_window<PAGED, VARLEN>() ? lt : lt + itp->off;
           if (p.swq > 0) lo = max(lo, wa - p.swq + 1);
           if (p.swk > 0) hi = min(hi, wa + p.swk);
         }
@@ -1376,11 +1376,11 @@ static bool fwd_persistent(bool causal, int kv_len) {
   return avg_tiles <= kFwdPersistMaxTiles;
 }
 
-template <typename T, int D, int NQ, bool PAGED, bool CAP>
+template <typename T, int D, int NQ, bool PAGED, bool CAP, bool VARLEN = false>
 static int launch_fwd_persist(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                               const CUtensorMap& to, const FwdParams& p, int kind, cudaStream_t st) {
   using Cfg = FwdPersistCfg<D, NQ>;
-  auto kern = fa_fwd_persist_kernel<T, D, NQ, PAGED, CAP>;
+  auto kern = fa_fwd_persist_kernel<T, D, NQ, PAGED, CAP, VARLEN>;
   static std::atomic<bool> attr_set[kMaxContexts];
   if (int s = smem_attr_once(kern, Cfg::SMEM_BYTES, attr_set)) return s;
   FwdParams q = p;
@@ -1413,9 +1413,9 @@ static int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const C
                            const CUtensorMap& to, const FwdParams& p, cudaStream_t st) {
   const int kind = PAGED ? FA_PROF_PAGED : FA_PROF_FWD;
   int s = FA_OK;
-  if (p.sc_a != 0.f) {
-    // softcap (dense, varlen): the persistent kernel's CAP variant serves every shape
-    s = launch_fwd_persist<T, D, NQ, PAGED, true>(tq, tk, tv, to, p, kind, st);
+  if (!PAGED && p.sc_a != 0.f) {
+    // dense softcap: the persistent kernel's CAP variant serves every shape
+    if constexpr (!PAGED) s = launch_fwd_persist<T, D, NQ, false, true>(tq, tk, tv, to, p, kind, st);
   } else if (fwd_persistent<D, PAGED>(p.causal != 0, p.Skv)) {
     if constexpr (fwd_may_persist<D, PAGED>())
       s = launch_fwd_persist<T, D, NQ, PAGED, false>(tq, tk, tv, to, p, kind, st);
@@ -1438,6 +1438,25 @@ static int dispatch_dtype(int dtype, const CUtensorMap& tq, const CUtensorMap& t
 }
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+// Varlen launches: the persistent kernel's VARLEN variant (with CAP for a softcap).
+template <int D, int NQ>
+static int dispatch_varlen(int dtype, const CUtensorMap& tq, const CUtensorMap& tk,
+                           const CUtensorMap& to, const CUtensorMap& tv, const FwdParams& p,
+                           cudaStream_t st) {
+  const bool bf16 = dtype == FA_DTYPE_BF16, cap = p.sc_a != 0.f;
+  int s;
+  if (bf16)
+    s = cap ? launch_fwd_persist<__nv_bfloat16, D, NQ, true, true, true>(tq, tk, tv, to, p, FA_PROF_FWD, st)
+            : launch_fwd_persist<__nv_bfloat16, D, NQ, true, false, true>(tq, tk, tv, to, p, FA_PROF_FWD, st);
+  else
+    s = cap ? launch_fwd_persist<__half, D, NQ, true, true, true>(tq, tk, tv, to, p, FA_PROF_FWD, st)
+            : launch_fwd_persist<__half, D, NQ, true, false, true>(tq, tk, tv, to, p, FA_PROF_FWD, st);
+  if (s != FA_OK) return s;
+  FA_CUDA_TRY(cudaGetLastError());
+  count_launch();
+  return FA_OK;
+}
 
 int launch_fwd_dense(const fa_fwd_args_t* a, int* err, cudaStream_t st) {
   // head_dim 32 and 96 run the 64 / 128 kernels: the tensor maps keep the real head dim
@@ -1635,9 +1654,9 @@ int launch_varlen_fwd(const fa_varlen_fwd_args_t* a, int* err, cudaStream_t st) 
   p.nbx = a->total_q / TPB + a->batch;
   p.n_items = p.nbx * a->num_heads_k;
   switch (D) {
-    case 64: return dispatch_dtype<64, 2, true>(a->dtype, tq, tk, to, tv, p, st);
-    case 128: return dispatch_dtype<128, 2, true>(a->dtype, tq, tk, to, tv, p, st);
-    case 256: return dispatch_dtype<256, 1, true>(a->dtype, tq, tk, to, tv, p, st);
+    case 64: return dispatch_varlen<64, 2>(a->dtype, tq, tk, to, tv, p, st);
+    case 128: return dispatch_varlen<128, 2>(a->dtype, tq, tk, to, tv, p, st);
+    case 256: return dispatch_varlen<256, 1>(a->dtype, tq, tk, to, tv, p, st);
     default: return FA_ERR_UNSUPPORTED;
   }
 }

@@ -101,17 +101,19 @@ constexpr int kFwdBN = 128;  // keys per forward KV tile
 // paged window, anchored on the row's token and honoured only with causal
 // (_kernels_paged.py:275-294).  Key j is visible iff anchor - swq < j (swq > 0) and
 // j < anchor + swk (swk > 0).
-template <bool PAGED>
-__device__ __forceinline__ bool fwd_paged_window(const FwdParams& p) {
-  return PAGED && p.cu_k == nullptr;
+// VARLEN: a varlen launch of the paged pipeline (compile-time, so paged launches keep
+// their code unchanged).
+template <bool PAGED, bool VARLEN = false>
+__device__ __forceinline__ constexpr bool fwd_paged_window() {
+  return PAGED && !VARLEN;
 }
-template <bool PAGED>
+template <bool PAGED, bool VARLEN = false>
 __device__ __forceinline__ bool fwd_window_on(const FwdParams& p) {
-  return (fwd_paged_window<PAGED>(p) ? p.causal != 0 : true) && (p.swq > 0 || p.swk > 0);
+  return (fwd_paged_window<PAGED, VARLEN>() ? p.causal != 0 : true) && (p.swq > 0 || p.swk > 0);
 }
 // KV tiles [j0, j1) that the rows of tokens [tok0, tok0 + TPB) of a work item can see:
 // keys below kv_len, the causal bound and the sliding window.
-template <bool PAGED>
+template <bool PAGED, bool VARLEN = false>
 __device__ __forceinline__ void fwd_kv_range(const FwdParams& p, int tok0, int TPB, int q_len,
                                              int kv_len, int off, int& j0, int& j1) {
   j0 = 0;
@@ -121,8 +123,8 @@ __device__ __forceinline__ void fwd_kv_range(const FwdParams& p, int tok0, int T
     const int max_key = last_lt + off;
     j1 = min(j1, max_key >= 0 ? max_key / kFwdBN + 1 : 0);
   }
-  if (fwd_window_on<PAGED>(p)) {
-    const bool pw = fwd_paged_window<PAGED>(p);
+  if (fwd_window_on<PAGED, VARLEN>(p)) {
+    constexpr bool pw = fwd_paged_window<PAGED, VARLEN>();
     const int a0 = pw ? tok0 : tok0 + off, a1 = pw ? last_lt : last_lt + off;
     if (p.swq > 0) j0 = max(0, a0 - p.swq + 1) / kFwdBN;
     if (p.swk > 0) {
