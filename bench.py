@@ -155,6 +155,7 @@ class ClockSampler:
 # and rank 0, which regenerates it for the gathered check, produce the same values
 # independently of how the units are sharded.
 SEED_DENSE, SEED_DENSE2, SEED_NONSQ, SEED_PAGED, SEED_DECODE = 1000, 3000, 5000, 7000, 9000
+SEED_VARLEN = 11000
 U_BF16, U_F16 = 2.0 ** -8, 2.0 ** -11  # unit roundoff of the 16-bit input types
 
 
@@ -559,6 +560,58 @@ def paged_run(dev, dist, rank, world, steps, warmup, c=PAGED, dtype=torch.float1
     return flops / ms / 1e9, ms, chk
 
 
+VARLEN = dict(seqs=16, lo=256, hi=4096, h=32, d=128)  # packed mixed-length batch per rank
+
+
+def varlen_run(dev, dist, rank, world, steps, warmup):
+    """Dense varlen (FA2 flash_attn_varlen_func), weak: every rank packs 16 causal
+    sequences of L ~ U[256, 4096] tokens (global sequences 16 r .. 16 r + 15, each from
+    its own seed), bf16, 32 heads, D 128; a step is the forward and the backward through
+    the C ABI.  Returns aggregate TFLOP/s (14 D per visible pair of every rank's
+    sequences over the slowest rank's time), ms, rank 0's check of one head of its first
+    and last sequence against the fp32 reference, and rank 0's lengths."""
+    from tilelang_fa_v100 import _ext
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from slice_ref import slice_ref_2d
+    c = VARLEN
+    n, h, d = c["seqs"], c["h"], c["d"]
+    lens = np.random.default_rng(SEED_VARLEN).integers(c["lo"], c["hi"] + 1, size=world * n)
+    mine = [int(x) for x in lens[rank * n:(rank + 1) * n]]
+    rows = [dense_row(dev, rank * n + i, L, L, h, h, d, torch.bfloat16, SEED_VARLEN)
+            for i, L in enumerate(mine)]
+    q, k, v, do = (torch.cat([r[j] for r in rows]) for j in range(4))
+    del rows
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(mine)]), dtype=torch.int32, device=dev)
+    mx, sc = max(mine), d ** -0.5
+    state = {}
+
+    def step():
+        o, lse = _ext.varlen_forward(q, k, v, cu, cu, mx, mx, sc, True)
+        state["g"] = _ext.varlen_backward(q, k, v, o, do, lse, cu, cu, mx, mx, sc, True)
+        state["o"] = o
+    for _ in range(warmup):
+        step()
+    ms = timed_ms(dev, dist, steps, step)
+    pairs = h * sum(int(L) * (int(L) + 1) // 2 for L in lens)  # every rank's sequences
+    chk = None
+    if rank == 0:
+        st = ErrStats()
+        o, (dq, dk, dv) = state["o"], state["g"]
+        for i in (0, n - 1):
+            a, b_ = int(cu[i]), int(cu[i + 1])
+            r = slice_ref_2d(q[a:b_, 0], k[a:b_, 0], v[a:b_, 0], do[a:b_, 0], o[a:b_, 0], True,
+                             2.0 ** -8)
+            st.north_star("out", o[a:b_, 0], r["out"])
+            st.bound("out", o[a:b_, 0], r["out"], r["bo"])
+            for nm, g_, bn in (("dq", dq, "bq"), ("dk", dk, "bk"), ("dv", dv, "bv")):
+                st.grad(nm, g_[a:b_, 0], r[nm + "_f"], 2.0 ** -8)
+                st.bound(nm, g_[a:b_, 0], r[nm + "_f"], r[bn])
+        chk = st.summary()
+        chk["samples"] = ["sequence %d head 0 (L %d)" % (i, mine[i]) for i in (0, n - 1)]
+    del q, k, v, do, state
+    return 14.0 * d * pairs / ms / 1e9, ms, chk, mine
+
+
 def decode_lengths(world, batch=256, seed=0):
     """Global KV lengths of configs[4] (L ~ U[512, 8192]) for world x batch sequences."""
     return np.random.default_rng(seed).integers(512, 8193, size=world * batch).astype(np.int32)
@@ -847,6 +900,13 @@ def run_ours(args):
             "gbs": d2gbs, "ms": d2ms, "frac_of_hbm": d2gbs / world / hbm,
             "note": "the reference's synthetic 8/1 D=256 configuration, configs[4] length "
                     "distribution"}
+        vtf, vms, vchk, vlens = varlen_run(dev, dist, rank, world, args.steps, 3)
+        sec["varlen_fwd_bwd_bf16_16seq_U256_4096_H32_D128_causal"] = {
+            "tflops": vtf, "ms": vms, "frac_of_burst_peak": vtf / world / burst,
+            "note": "dense varlen (FA2 flash_attn_varlen_func): forward + backward of a packed "
+                    "mixed-length batch per rank through the C ABI; 14*D FLOP per visible "
+                    "pair; ranks draw their own lengths, so their work differs",
+            "tokens_rank0": int(sum(vlens)), "check": vchk}
         kms, kgbs = time_kv_write(dev, dist, args.steps, 3)
         sec["kv_cache_write_bf16_65536tok_Hkv8_D128_GBps"] = {
             "gbs": world * kgbs, "ms": kms, "frac_of_hbm": kgbs / hbm}

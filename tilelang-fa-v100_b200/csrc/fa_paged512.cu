@@ -90,7 +90,10 @@ __global__ void __launch_bounds__(kP5Threads, 1)
   const int G = p.G;
   const int TPT = 128 / G;  // tokens per Q tile (rows TPT * G .. 127 unused when G does not divide 128)
   const int hk = blockIdx.y;
-  const int half = blockIdx.z;  // output columns [256 half, 256 half + 256)
+  // The two output halves of a q block are adjacent in launch order (blockIdx.x & 1), so
+  // the second one reads Q and the K/V pages from L2.
+  const int half = blockIdx.x & 1;  // output columns [256 half, 256 half + 256)
+  const int qblk = blockIdx.x >> 1;
 
   // ---------------------------------------------------------------- work item
   if (threadIdx.x == 0) {
@@ -99,9 +102,9 @@ __global__ void __launch_bounds__(kP5Threads, 1)
     for (int s = 0, cum = 0; s < p.num_seqs; ++s) {
       const int ql = p.qsl[s + 1] - p.qsl[s];
       const int nb = ql > 0 ? (ql + TPT - 1) / TPT : 0;
-      if (static_cast<int>(blockIdx.x) < cum + nb) {
+      if (qblk < cum + nb) {
         b = s;
-        tile = blockIdx.x - cum;
+        tile = qblk - cum;
         valid = 1;
         break;
       }
@@ -493,7 +496,7 @@ static int launch_p5(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
   auto kern = fa_paged512_kernel<T>;
   static std::atomic<bool> attr[kMaxContexts];
   if (int s = smem_attr_once(kern, kP5SmemBytes, attr)) return s;
-  const dim3 grid(grid_x, p.Hk, 2);
+  const dim3 grid(2 * grid_x, p.Hk);
   prof_begin(FA_PROF_PAGED, st);
   kern<<<grid, kP5Threads, kP5SmemBytes, st>>>(tq, tk, tv, to, p);
   prof_end(FA_PROF_PAGED, st);
