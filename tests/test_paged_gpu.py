@@ -149,3 +149,22 @@ def test_seq_len_past_block_table_is_clamped_and_reported(cuda_dev):
                                            np.zeros_like(pkl), causal=False)
     assert_close(out, ref_out, what="out")
     assert_close(lse, ref_lse, what="lse")
+
+
+def test_many_sequences_cross_the_item_scan(cuda_dev):
+    """70 ragged sequences: the persistent kernel finds an item's sequence with a
+    warp-wide scan 32 sequences at a time, so this crosses two chunk boundaries (and
+    holds empty query chunks and single-token ones)."""
+    rng = np.random.default_rng(70)
+    q_lens = [int(x) for x in rng.integers(0, 40, size=70)]
+    q_lens[5], q_lens[40] = 0, 1
+    kv_lens = [ql + int(x) for ql, x in zip(q_lens, rng.integers(0, 90, size=70))]
+    kv_lens = [max(1, n) for n in kv_lens]
+    q, kc, vc, bt, sl, qsl, pkl = _varlen_case(71, q_lens, kv_lens, 8, 2, 128, 16, torch.float16)
+    out, lse = _run(cuda_dev, q, kc, vc, bt, sl, qsl, pkl, True, 16)
+    ref_out, ref_lse, bound = R.paged_prefill_ref(q.float().numpy(), kc.float().numpy(),
+                                                  vc.float().numpy(), bt, sl, qsl, pkl,
+                                                  causal=True,
+                                                  unit_roundoff=unit_roundoff(torch.float16))
+    assert_out_close(out, ref_out, torch.float16, bound, what="out")
+    assert_close(lse, ref_lse, what="lse")

@@ -116,3 +116,41 @@ def test_varlen_equal_lengths_match_dense(cuda_dev):
     torch.cuda.synchronize()
     diff = (packed.reshape(b, s_, h, d).float() - dense.float()).abs().max().item()
     assert diff <= 2 ** -6, diff
+
+
+@pytest.mark.parametrize("deterministic", [False, True])
+def test_varlen_many_short_sequences(cuda_dev, deterministic):
+    """70 packed sequences of 1-60 tokens (prefix keys too): the forward's item scan over
+    sequences crosses two 32-sequence chunks and the backward grids span 70 batch
+    entries, most of them shorter than one tile."""
+    rng = np.random.default_rng(72)
+    q_lens = [int(x) for x in rng.integers(1, 61, size=70)]
+    k_lens = [ql + int(x) for ql, x in zip(q_lens, rng.integers(0, 30, size=70))]
+    case = (q_lens, k_lens, 4, 2, 64, True, (-1, -1), 0.0, torch.float16)
+    q, k, v, do, cq, ck = _inputs(case, seed=73)
+    qd, kd, vd = (x.to(cuda_dev).requires_grad_(True) for x in (q, k, v))
+    out, lse, _ = fa.tilelang_flash_attn_varlen_func(qd, kd, vd, cq.to(cuda_dev), ck.to(cuda_dev),
+                                                     max(q_lens), max(k_lens), causal=True,
+                                                     deterministic=deterministic,
+                                                     return_attn_probs=True)
+    out.backward(do.to(cuda_dev))
+    torch.cuda.synchronize()
+    o_all, lse = out.detach().float().cpu(), lse.detach().cpu().numpy()
+    got = [x.grad.float().cpu().numpy() for x in (qd, kd, vd)]
+    dt = torch.float16
+    for s in range(0, 70, 3):  # every third sequence: both chunks of the scan and the tail
+        qa, qb, ka, kb = int(cq[s]), int(cq[s + 1]), int(ck[s]), int(ck[s + 1])
+        args = (_seq(q, qa, qb), _seq(k, ka, kb), _seq(v, ka, kb), True)
+        ro, rl = R.attention_ref(*args)
+        bound = R.attention_out_bound(*args, unit_roundoff(dt))
+        assert_out_close(o_all[qa:qb].numpy(), _unseq(ro), dt, _unseq(bound), what="out seq %d" % s)
+        assert_close(lse[:, qa:qb], rl[0], what="lse seq %d" % s)
+        bargs = args[:3] + (_seq(do, qa, qb), True)
+        exact = R.attention_bwd_ref(*bargs)
+        faithful, bounds = R.attention_bwd_ref(*bargs, o=_seq(o_all, qa, qb),
+                                               unit_roundoff=unit_roundoff(dt))
+        rows = (slice(qa, qb), slice(ka, kb), slice(ka, kb))
+        for g_, r_, want, want_f, bnd, w in zip(got, rows, exact, faithful, bounds,
+                                                ("dq", "dk", "dv")):
+            assert_grad_close(g_[r_], _unseq(want), dt, "%s seq %d" % (w, s),
+                              bound=_unseq(bnd), want_faithful=_unseq(want_f))
