@@ -154,3 +154,24 @@ def test_varlen_many_short_sequences(cuda_dev, deterministic):
                                                 ("dq", "dk", "dv")):
             assert_grad_close(g_[r_], _unseq(want), dt, "%s seq %d" % (w, s),
                               bound=_unseq(bnd), want_faithful=_unseq(want_f))
+
+
+def test_empty_inputs_give_the_fully_masked_result(cuda_dev):
+    """No key at all (dense Skv = 0, varlen total_k = 0) gives the library's fully masked
+    rows -- out 0, lse -inf, zero gradients -- and no rows gives empty results, instead of
+    handing the C ABI the null data pointers of empty tensors."""
+    mk = lambda *s: torch.randn(*s, device=cuda_dev, dtype=torch.float16).requires_grad_(True)
+    q, k, v = mk(2, 5, 2, 64), mk(2, 0, 2, 64), mk(2, 0, 2, 64)
+    out, lse, _ = fa.tilelang_flash_attn_func(q, k, v, causal=True, return_attn_probs=True)
+    out.sum().backward()
+    assert not out.any() and torch.isneginf(lse).all() and not q.grad.any()
+    q0 = mk(2, 0, 2, 64)
+    out0 = fa.tilelang_flash_attn_func(q0, mk(2, 7, 2, 64), mk(2, 7, 2, 64))
+    assert out0.shape == (2, 0, 2, 64)
+    cq = torch.tensor([0, 3, 5], dtype=torch.int32, device=cuda_dev)
+    ck = torch.zeros(3, dtype=torch.int32, device=cuda_dev)
+    qv, kv_, vv = mk(5, 2, 64), mk(0, 2, 64), mk(0, 2, 64)
+    out, lse, _ = fa.tilelang_flash_attn_varlen_func(qv, kv_, vv, cq, ck, 3, 0, causal=True,
+                                                     return_attn_probs=True)
+    out.sum().backward()
+    assert not out.any() and torch.isneginf(lse).all() and not qv.grad.any()

@@ -250,6 +250,11 @@ def dense_forward(q, k, v, softmax_scale, causal, window_size=(-1, -1), softcap=
     q, k, v = _bshd(q), _bshd(k), _bshd(v)
     out = torch.empty((b, sq, h, d), dtype=q.dtype, device=q.device)
     lse = torch.empty((b, h, sq), dtype=torch.float32, device=q.device)
+    if out.numel() == 0 or skv == 0:
+        # nothing to compute, or no key at all: the library's fully masked rows (out 0,
+        # lse -inf); empty tensors have no data pointer to hand the C ABI
+        load()
+        return out.zero_(), lse.fill_(float("-inf"))
     a = FwdArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr(),
                 _strides3(q), _strides3(k), _strides3(v), _strides3(out),
                 b, sq, skv, h, hk, d, _dtype_code(q.dtype), 1 if causal else 0,
@@ -271,6 +276,9 @@ def dense_backward(q, k, v, out, dout, lse, softmax_scale, causal, deterministic
     dq = torch.empty((b, sq, h, d), dtype=q.dtype, device=q.device)
     dk = torch.empty((b, skv, hk, d), dtype=q.dtype, device=q.device)
     dv = torch.empty((b, skv, hk, d), dtype=q.dtype, device=q.device)
+    if dq.numel() == 0 or dk.numel() == 0:
+        load()  # nothing attends: every gradient is zero
+        return dq.zero_(), dk.zero_(), dv.zero_()
     a = BwdArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dout.data_ptr(),
                 lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
                 _strides3(q), _strides3(k), _strides3(v), _strides3(out), _strides3(dout),
@@ -318,6 +326,9 @@ def varlen_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen
     tk, hk = k.shape[0], k.shape[1]
     out = torch.empty((tq, h, d), dtype=q.dtype, device=q.device)
     lse = torch.empty((h, tq), dtype=torch.float32, device=q.device)
+    if out.numel() == 0 or tk == 0:
+        load()  # no rows, or no key in any sequence: out 0, lse -inf
+        return out.zero_(), lse.fill_(float("-inf"))
     st2 = lambda t: (_i64 * 2)(t.stride(0), t.stride(1))
     a = VarlenFwdArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr(),
                       cq.data_ptr(), ck.data_ptr(), st2(q), st2(k), st2(v), st2(out),
@@ -340,6 +351,9 @@ def varlen_backward(q, k, v, out, dout, lse, cu_seqlens_q, cu_seqlens_k, max_seq
     batch = cu_seqlens_q.numel() - 1
     cq, ck = _cu(cu_seqlens_q, q.device, batch + 1), _cu(cu_seqlens_k, q.device, batch + 1)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    if dq.numel() == 0 or dk.numel() == 0:
+        load()  # nothing attends: every gradient is zero
+        return dq.zero_(), dk.zero_(), dv.zero_()
     st2 = lambda t: (_i64 * 2)(t.stride(0), t.stride(1))
     tq, h, d = q.shape
     a = VarlenBwdArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dout.data_ptr(),
