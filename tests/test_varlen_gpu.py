@@ -21,6 +21,8 @@ CASES = [
     ([10, 64, 40], [0, 64, 40], 2, 2, 128, True, (-1, -1), 0.0, torch.bfloat16),  # no keys at all
     ([400, 130], [400, 200], 4, 2, 128, True, (64, -1), 5.0, torch.bfloat16),  # window + softcap
     ([257, 3], [257, 3], 2, 1, 64, False, (-1, -1), 0.0, torch.float16),
+    ([333, 150], [400, 150], 4, 2, 256, True, (100, 20), 3.0, torch.bfloat16),  # D = 256 EXT
+    ([190, 70, 260], [190, 300, 260], 8, 2, 64, False, (-1, 40), 1.5, torch.float16),
 ]
 
 
