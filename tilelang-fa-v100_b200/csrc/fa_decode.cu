@@ -25,9 +25,29 @@ namespace fa {
 
 constexpr int kDecChunk = 16;  // tokens per pipeline chunk
 
+// Kv heads per CTA and ring stages, per head dim (64 / 128 / 256 / 512) and cache type.
+// A CTA streams its split of the caches through its ring once, so each CTA ramps its
+// pipeline up and down.  HBM stays busy when several CTAs share an SM and overlap those
+// ramps.  So the 16-bit tables use small CTAs (one or two kv heads, 48 KB rings) and the
+// kernel promises the compiler several blocks per SM (DecCfg::MINB), which caps
+// registers.  Measured against one CTA per SM with 192 KB rings, same process, same
+// outputs:
+//   configs[4] (32 / 8 heads, D = 128)   0.938 -> 0.720 ms (5.05 -> 6.58 TB/s);
+//   D = 64, 16 / 16 heads                 1.185 -> 0.714 ms;
+//   D = 256, 32 / 8 heads                 0.927 -> 0.711 ms; D = 256, 8 / 1 heads even.
+// D = 512 and fp8 caches are bound by their compute (the MMAs, the fp8 conversions),
+// not the stream, and keep larger CTAs.
+constexpr int kDecMaxG16[4] = {2, 2, 1, 1};
+constexpr int kDecStages16[4] = {6, 3, 3, 6};
+constexpr int kDecMaxG8[4] = {2, 8, 4, 1};  // fp8 caches (head_dim 128 and up)
+constexpr int kDecStages8[4] = {6, 6, 6, 8};
+constexpr int dec_dim_index(int D) { return D == 64 ? 0 : D == 128 ? 1 : D == 256 ? 2 : 3; }
+constexpr int dec_maxg(int D, bool kv8) {
+  return kv8 ? kDecMaxG8[dec_dim_index(D)] : kDecMaxG16[dec_dim_index(D)];
+}
+
 // KV8: the caches hold fp8 e4m3 (one byte per element, 128 elements per 128-byte box
-// row) instead of the query's 16-bit type (64 per box row); half the bytes per chunk,
-// so twice the stages keep as many bytes in flight.
+// row) instead of the query's 16-bit type (64 per box row).
 template <int D, bool KV8 = false>
 struct DecCfg {
   static constexpr int ELEM = KV8 ? 1 : 2;                // cache bytes per element
@@ -36,14 +56,15 @@ struct DecCfg {
   // compute warps per kv head: one up to D = 128, then one per 128 output columns
   static constexpr int WPH = D > 128 ? D / 128 : 1;
   static constexpr int DW = D / WPH;                      // output columns per compute warp
-  // kv heads per CTA.  D = 512: one, so the CTA's 160 threads may hold the 128 registers
-  // of Q fragments next to the 64 of their O columns (each warp forms the whole S).
-  static constexpr int MAXG = D > 256 ? 1 : (D > 128 ? 4 : 8);
+  static constexpr int MAXG = dec_maxg(D, KV8);        // kv heads per CTA
   static constexpr int NTHREADS = 32 + 32 * MAXG * WPH;   // producer warp + compute warps
+  // Blocks per SM promised to the compiler: a register cap of 224 per thread whatever the
+  // CTA size, so small CTAs (one or two kv heads) still fit several to an SM.
+  static constexpr int MINB = 65536 / (224 * NTHREADS) > 1 ? 65536 / (224 * NTHREADS) : 1;
   static constexpr int HEAD_BYTES = kDecChunk * D * ELEM; // one kv head, one chunk, K or V
   static constexpr int STAGE_BYTES_MAX = 2 * MAXG * HEAD_BYTES;
-  // D = 512 runs one CTA per SM (registers), so its ring is deeper.
-  static constexpr int STAGES = D == 512 ? (KV8 ? 8 : 6) : (KV8 ? 6 : ((D == 64) ? 6 : 3));
+  static constexpr int STAGES =
+      KV8 ? kDecStages8[dec_dim_index(D)] : kDecStages16[dec_dim_index(D)];
   static_assert(STAGES <= 8, "decode ring: DecSmemCtl holds 8 stages");
   // Above D = 128 the WPH warps of a kv head each form the partial S over their own
   // D / WPH dims and exchange it through shared memory (double buffered per chunk):
@@ -138,7 +159,7 @@ struct DecSmemCtl {
 };
 
 template <typename T, int D, bool KV8>
-__global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, 1)
+__global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, DecCfg<D, KV8>::MINB)
     fa_decode_split_kernel(const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v, const DecParams p) {
   using Cfg = DecCfg<D, KV8>;
@@ -622,9 +643,7 @@ int launch_decode(const fa_decode_args_t* a, void* ws, size_t ws_bytes, int* err
   p.H = a->num_heads;
   p.Hkv = a->num_kv_heads;
   p.G = G;
-  p.HG = dec_group(a->num_kv_heads, D > 256   ? DecCfg<512>::MAXG
-                                     : D > 128 ? DecCfg<256>::MAXG
-                                               : DecCfg<128>::MAXG);
+  p.HG = dec_group(a->num_kv_heads, dec_maxg(D, kv8));
   p.page_size = ps;
   p.num_pages = a->num_pages;
   p.max_blocks = a->max_blocks;
