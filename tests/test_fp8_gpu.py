@@ -66,6 +66,28 @@ def test_decode_fp8_cache_vs_oracle(cuda_dev, case):
     assert_close(lse.cpu().numpy(), ref_lse, what="lse")
 
 
+@pytest.mark.parametrize("q_scale", [3.0e5, 1.0e-6])
+@pytest.mark.parametrize("d", [128, 256])
+def test_decode_fp8_bf16_query_outside_f16_range(cuda_dev, q_scale, d):
+    """Over fp8 caches a bf16 query enters f16 MMAs after a power-of-two scaling chosen
+    per kv-head group.  Groups far above the f16 maximum (3e5) or below its normal range
+    (1e-6), next to unscaled groups, give the oracle's result."""
+    lens, h, hkv, page = [100, 1, 515, 2000], 32, 8, 16
+    q, kraw, vraw, bt, sl = _fp8_case(5 + d, lens, h, hkv, d, page, torch.bfloat16)
+    group = torch.arange(h) // (h // hkv)
+    q = (q.float() * torch.where(group % 2 == 0, q_scale, 1.0)[None, :, None]).to(torch.bfloat16)
+    t = lambda x: torch.as_tensor(x).to(cuda_dev)
+    lse = torch.empty(q.shape[0], q.shape[1], dtype=torch.float32, device=cuda_dev)
+    out = _ext.decode(t(q), _as_fp8(kraw, cuda_dev), _as_fp8(vraw, cuda_dev), t(bt), t(sl), page,
+                      hkv, d ** -0.5, lse=lse, k_scale=K_SCALE, v_scale=V_SCALE)
+    torch.cuda.synchronize()
+    kd, vd = R.dequantize_e4m3(kraw, K_SCALE), R.dequantize_e4m3(vraw, V_SCALE)
+    ref_out, ref_lse, bound = R.decode_ref(q.float().numpy(), kd, vd, bt, sl,
+                                           unit_roundoff=unit_roundoff(torch.bfloat16))
+    assert_out_close(out.float().cpu().numpy(), ref_out, torch.bfloat16, bound, what="out")
+    assert_close(lse.cpu().numpy(), ref_lse, what="lse")
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_kv_cache_write_fp8_is_bit_exact(cuda_dev, dtype):
     rng = np.random.default_rng(7)

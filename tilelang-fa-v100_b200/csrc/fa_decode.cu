@@ -20,6 +20,7 @@
 #include <cmath>
 #include <cstdio>
 #include <mutex>
+#include <type_traits>
 
 namespace fa {
 
@@ -35,7 +36,7 @@ constexpr int kDecChunk = 16;  // tokens per pipeline chunk
 //   configs[4] (32 / 8 heads, D = 128)   0.938 -> 0.720 ms (5.05 -> 6.58 TB/s);
 //   D = 64, 16 / 16 heads                 1.185 -> 0.714 ms;
 //   D = 256, 32 / 8 heads                 0.927 -> 0.711 ms; D = 256, 8 / 1 heads even.
-// D = 512 and fp8 caches are bound by their compute (the MMAs, the fp8 conversions),
+// D = 512 and fp8 caches are bound by their compute chains (MMAs, fp8 conversions),
 // not the stream, and keep larger CTAs.
 constexpr int kDecMaxG16[4] = {2, 2, 1, 1};
 constexpr int kDecStages16[4] = {6, 3, 3, 6};
@@ -137,19 +138,13 @@ __device__ __forceinline__ uint32_t prmt(uint32_t x, uint32_t sel) {
   asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(x), "r"(sel));
   return r;
 }
-// Two e4m3 values (the first in the low byte) as a 16-bit pair of the MMA's input type.
-// Every e4m3 value is exact in f16 and in bf16, so the conversion loses nothing.
-template <typename T>
-__device__ __forceinline__ uint32_t e4m3x2_to(uint32_t v) {
+// Two e4m3 values (the first in the low byte) as an f16x2 pair: one cvt, exact (every
+// e4m3 value is an f16 normal or zero).
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t v) {
   uint32_t h;
   const uint16_t v16 = static_cast<uint16_t>(v);
   asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(v16));
-  if constexpr (Pack2<T>::kBf16) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
-    return Pack2<T>::pack(f.x, f.y);
-  } else {
-    return h;
-  }
+  return h;
 }
 
 struct DecSmemCtl {
@@ -164,7 +159,10 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, DecCfg<D, KV8>::MINB
                            const __grid_constant__ CUtensorMap tm_v, const DecParams p) {
   using Cfg = DecCfg<D, KV8>;
   constexpr int ST = Cfg::STAGES;
-  constexpr bool kBf16 = Pack2<T>::kBf16;
+  // fp8 caches run the MMAs in f16 whatever the query type: the cache bytes convert
+  // with one exact cvt, and P keeps 11 bits.  (A bf16 query converts once, below.)
+  using MT = std::conditional_t<KV8, __half, T>;
+  constexpr bool kBf16 = Pack2<MT>::kBf16;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -256,6 +254,29 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, DecCfg<D, KV8>::MINB
   constexpr int KS = Cfg::KS;
   const int ks0 = Cfg::WPH > 1 ? part * KS : 0;
   uint32_t qa[KS][4];
+  // A bf16 query over fp8 caches enters the f16 MMAs scaled by 2^qk, qk chosen so that
+  // the largest |q| of the kv head's group lies in [2^14, 2^15): every element down to
+  // 2^-28 of that maximum is an f16 normal and converts exactly (bf16 has 8 significant
+  // bits, f16 11), smaller ones round as f16 subnormals, and S carries the factor 2^qk,
+  // which the softmax scales divide out (power-of-two scalings are exact).  The warps of
+  // a kv head read the same group, so they agree on qk.
+  float q_up = 1.f, q_down = 1.f;
+  if constexpr (KV8 && Pack2<T>::kBf16) {
+    const uint32_t* qw = reinterpret_cast<const uint32_t*>(
+        reinterpret_cast<const T*>(p.q) + ((int64_t)b * p.H + hk * G) * D);
+    float amax = 0.f;
+    for (int i = lane; i < G * D / 2; i += 32) {
+      const float2 f = Pack2<T>::unpack(qw[i]);
+      amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    const int eb = (__float_as_int(amax) >> 23) & 0xFF;  // biased exponent of the maximum
+    const int qk = max(-100, min(100, 141 - eb));        // 14 - (eb - 127)
+    q_up = __int_as_float((127 + qk) << 23);
+    q_down = __int_as_float((127 - qk) << 23);
+  }
   {
     const T* qb = reinterpret_cast<const T*>(p.q) + ((int64_t)b * p.H + hk * G) * D;
 #pragma unroll
@@ -269,7 +290,13 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, DecCfg<D, KV8>::MINB
       const int k8 = KV8 ? k0 + 2 : k0 + 8;
       auto ld2 = [&](int row, int col) -> uint32_t {
         if (row >= G) return 0u;
-        return *reinterpret_cast<const uint32_t*>(qb + (int64_t)row * D + col);
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(qb + (int64_t)row * D + col);
+        if constexpr (KV8 && Pack2<T>::kBf16) {
+          const float2 f = Pack2<T>::unpack(w);
+          return Pack2<__half>::pack(f.x * q_up, f.y * q_up);
+        } else {
+          return w;
+        }
       };
       qa[i][0] = ld2(g, k0);
       qa[i][1] = ld2(g + 8, k0);
@@ -282,7 +309,7 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, DecCfg<D, KV8>::MINB
 #pragma unroll
   for (int i = 0; i < DW / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  const float c2 = p.scale_log2;
+  const float c2 = p.scale_log2 * q_down;  // S carries the query's 2^qk
 
   // Partial-S exchange slots of this kv head: [2 chunk parities][WPH warps][32 lanes][8].
   float* const xch = reinterpret_cast<float*>(base_ptr + ST * stage_bytes + 256) +
@@ -316,8 +343,8 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, DecCfg<D, KV8>::MINB
         uint32_t c[8];
 #pragma unroll
         for (int x = 0; x < 4; ++x) {
-          c[2 * x] = e4m3x2_to<T>(w[x] & 0xFFFFu);
-          c[2 * x + 1] = e4m3x2_to<T>(w[x] >> 16);
+          c[2 * x] = e4m3x2_to_f16x2(w[x] & 0xFFFFu);
+          c[2 * x + 1] = e4m3x2_to_f16x2(w[x] >> 16);
         }
         mma16816<kBf16>(sc[0], qa[i], c[0], c[1]);
         mma16816<kBf16>(sc[1], qa[i], c[2], c[3]);
@@ -393,10 +420,10 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, DecCfg<D, KV8>::MINB
     l0 = l0 * f0 + rs0;  // partial (per-thread) row sums, reduced across the quad at the end
     l1 = l1 * f1 + rs1;
     uint32_t pa[4];
-    pa[0] = Pack2<T>::pack(pr[0][0], pr[0][1]);
-    pa[1] = Pack2<T>::pack(pr[0][2], pr[0][3]);
-    pa[2] = Pack2<T>::pack(pr[1][0], pr[1][1]);
-    pa[3] = Pack2<T>::pack(pr[1][2], pr[1][3]);
+    pa[0] = Pack2<MT>::pack(pr[0][0], pr[0][1]);
+    pa[1] = Pack2<MT>::pack(pr[0][2], pr[0][3]);
+    pa[2] = Pack2<MT>::pack(pr[1][0], pr[1][1]);
+    pa[3] = Pack2<MT>::pack(pr[1][2], pr[1][3]);
 #pragma unroll
     for (int dn = 0; dn < DW / 8; ++dn) {
       o[dn][0] *= f0;
@@ -423,10 +450,10 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, DecCfg<D, KV8>::MINB
 #pragma unroll
         for (int gp = 0; gp < 2; ++gp) {
           const uint32_t lo = w[2 * gp], hi = w[2 * gp + 1];  // tokens 0-7 / 8-15
-          mma16816<kBf16>(o[2 * (dpl + gp)], pa, e4m3x2_to<T>(prmt(lo, 0x0020)),
-                          e4m3x2_to<T>(prmt(hi, 0x0020)));
-          mma16816<kBf16>(o[2 * (dpl + gp) + 1], pa, e4m3x2_to<T>(prmt(lo, 0x0031)),
-                          e4m3x2_to<T>(prmt(hi, 0x0031)));
+          mma16816<kBf16>(o[2 * (dpl + gp)], pa, e4m3x2_to_f16x2(prmt(lo, 0x0020)),
+                          e4m3x2_to_f16x2(prmt(hi, 0x0020)));
+          mma16816<kBf16>(o[2 * (dpl + gp) + 1], pa, e4m3x2_to_f16x2(prmt(lo, 0x0031)),
+                          e4m3x2_to_f16x2(prmt(hi, 0x0031)));
         }
       } else {
         // matrices: (tok 0-7, d 16dp..+7), (tok 8-15, same), (tok 0-7, d +8..+15), (tok 8-15, +8..)
@@ -451,8 +478,8 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, DecCfg<D, KV8>::MINB
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
   const float inv0 = l0 > 0.f ? p.v_scale / l0 : 0.f;
   const float inv1 = l1 > 0.f ? p.v_scale / l1 : 0.f;
-  const float lse0 = l0 > 0.f ? m0 * p.scale + logf(l0) : -INFINITY;
-  const float lse1 = l1 > 0.f ? m1 * p.scale + logf(l1) : -INFINITY;
+  const float lse0 = l0 > 0.f ? m0 * (p.scale * q_down) + logf(l0) : -INFINITY;
+  const float lse1 = l1 > 0.f ? m1 * (p.scale * q_down) + logf(l1) : -INFINITY;
   const bool direct = p.num_splits == 1;
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
