@@ -36,11 +36,13 @@ constexpr int kDecChunk = 16;  // tokens per pipeline chunk
 //   configs[4] (32 / 8 heads, D = 128)   0.938 -> 0.720 ms (5.05 -> 6.58 TB/s);
 //   D = 64, 16 / 16 heads                 1.185 -> 0.714 ms;
 //   D = 256, 32 / 8 heads                 0.927 -> 0.711 ms; D = 256, 8 / 1 heads even.
-// D = 512 and fp8 caches are bound by their compute chains (MMAs, fp8 conversions),
-// not the stream, and keep larger CTAs.
+// fp8 caches at D = 128 gain the same way once their MMAs run in f16 (8 -> 2 kv heads
+// per CTA: 0.732 -> 0.505 ms at configs[4]); at D = 256 two heads per CTA lose (0.69 ->
+// 0.83 ms: its 160-register warps cap the CTAs per SM), and D = 512 is bound by its
+// compute chains (MMAs, conversions), not the stream: it keeps larger CTAs.
 constexpr int kDecMaxG16[4] = {2, 2, 1, 1};
 constexpr int kDecStages16[4] = {6, 3, 3, 6};
-constexpr int kDecMaxG8[4] = {2, 8, 4, 1};  // fp8 caches (head_dim 128 and up)
+constexpr int kDecMaxG8[4] = {2, 2, 4, 1};  // fp8 caches (head_dim 128 and up)
 constexpr int kDecStages8[4] = {6, 6, 6, 8};
 constexpr int dec_dim_index(int D) { return D == 64 ? 0 : D == 128 ? 1 : D == 256 ? 2 : 3; }
 constexpr int dec_maxg(int D, bool kv8) {
