@@ -13,7 +13,9 @@ Two bars, both written here:
   bar, so no bf16 kernel meets the north-star bar on every element.  Measured on the
   dense test cases the kernels stay below 0.9 of the bound in both dtypes.
 """
+import collections
 import glob
+import hashlib
 import os
 
 import numpy as np
@@ -109,3 +111,31 @@ def max_abs(x, ref):
 
 def unit_roundoff(dtype):
     return 2.0 ** -8 if is_bf16(dtype) else 2.0 ** -11
+
+
+_BWD_REFS = collections.OrderedDict()
+
+
+def bwd_refs(args, o, unit_roundoff, **kw):
+    """The oracle's exact gradients, its rounding-faithful gradients and their bounds for
+    attention_bwd_ref(*args, **kw) with the kernel's output ``o``.
+
+    The backward tests run each case in both backward modes on the same inputs, and the
+    forward (hence ``o``) does not depend on the mode, so the last two results are kept,
+    keyed by a digest of every array and option: the CPU oracle, not the GPU, dominates
+    the long cases."""
+    from oracle import attention_ref as R
+    h = hashlib.sha1(repr((sorted(kw.items()), unit_roundoff,
+                           [a if np.isscalar(a) or isinstance(a, bool) else a.shape
+                            for a in args])).encode())
+    for a in list(args) + [o]:
+        if isinstance(a, np.ndarray):
+            h.update(np.ascontiguousarray(a).tobytes())
+    key = h.hexdigest()
+    if key not in _BWD_REFS:
+        exact = R.attention_bwd_ref(*args, **kw)
+        faithful, bounds = R.attention_bwd_ref(*args, o=o, unit_roundoff=unit_roundoff, **kw)
+        _BWD_REFS[key] = (exact, faithful, bounds)
+        while len(_BWD_REFS) > 2:
+            _BWD_REFS.popitem(last=False)
+    return _BWD_REFS[key]

@@ -5,8 +5,8 @@ import pytest
 import torch
 
 import tilelang_fa_v100 as fa
-from helpers import (assert_close, assert_grad_close, assert_out_close, golden, golden_names,
-                     max_abs, unit_roundoff)
+from helpers import (assert_close, assert_grad_close, assert_out_close, bwd_refs, golden,
+                     golden_names, max_abs, unit_roundoff)
 from oracle import attention_ref as R
 from slice_ref import slice_ref
 
@@ -154,9 +154,7 @@ def test_backward_vs_oracle(cuda_dev, case, deterministic):
     out.backward(do.to(cuda_dev))
     torch.cuda.synchronize()
     args = (_to_bhsd(q), _to_bhsd(k), _to_bhsd(v), _to_bhsd(do), causal)
-    exact = R.attention_bwd_ref(*args)
-    faithful, bounds = R.attention_bwd_ref(*args, o=_to_bhsd(out.detach()),
-                                           unit_roundoff=unit_roundoff(dt))
+    exact, faithful, bounds = bwd_refs(args, _to_bhsd(out.detach()), unit_roundoff(dt))
     for got, want, want_f, bnd, w in zip((qd.grad, kd.grad, vd.grad), exact, faithful, bounds,
                                          ("dq", "dk", "dv")):
         assert_grad_close(_to_bhsd(got), want, dt, w, bound=bnd, want_faithful=want_f)

@@ -8,7 +8,7 @@ import pytest
 import torch
 
 import tilelang_fa_v100 as fa
-from helpers import assert_close, assert_grad_close, assert_out_close, unit_roundoff
+from helpers import assert_close, assert_grad_close, assert_out_close, bwd_refs, unit_roundoff
 from oracle import attention_ref as R
 
 pytestmark = pytest.mark.gpu
@@ -77,9 +77,7 @@ def test_softcap_backward_vs_oracle(cuda_dev, case, deterministic):
     torch.cuda.synchronize()
     args = (_to_bhsd(q), _to_bhsd(k), _to_bhsd(v), _to_bhsd(do), causal)
     kw = dict(scale=_scale(case), window=window, softcap=cap)
-    exact = R.attention_bwd_ref(*args, **kw)
-    faithful, bounds = R.attention_bwd_ref(*args, o=_to_bhsd(out), unit_roundoff=unit_roundoff(dt),
-                                           **kw)
+    exact, faithful, bounds = bwd_refs(args, _to_bhsd(out), unit_roundoff(dt), **kw)
     for got, want, want_f, bnd, w in zip((qd.grad, kd.grad, vd.grad), exact, faithful, bounds,
                                          ("dq", "dk", "dv")):
         assert_grad_close(_to_bhsd(got), want, dt, w, bound=bnd, want_faithful=want_f)

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 import tilelang_fa_v100 as fa
-from helpers import assert_close, assert_grad_close, assert_out_close, unit_roundoff
+from helpers import assert_close, assert_grad_close, assert_out_close, bwd_refs, unit_roundoff
 from oracle import attention_ref as R
 
 pytestmark = pytest.mark.gpu
@@ -95,9 +95,7 @@ def test_varlen_backward_vs_oracle(cuda_dev, case, deterministic):
             continue
         args = (_seq(q, qa, qb), _seq(k, ka, kb), _seq(v, ka, kb), _seq(do, qa, qb), causal)
         kw = dict(window=window, softcap=cap)
-        exact = R.attention_bwd_ref(*args, **kw)
-        faithful, bounds = R.attention_bwd_ref(*args, o=_seq(o_all, qa, qb),
-                                               unit_roundoff=unit_roundoff(dt), **kw)
+        exact, faithful, bounds = bwd_refs(args, _seq(o_all, qa, qb), unit_roundoff(dt), **kw)
         for g_, r_, want, want_f, bnd, w in zip(got, rows, exact, faithful, bounds,
                                                 ("dq", "dk", "dv")):
             assert_grad_close(g_[r_], _unseq(want), dt, "%s seq %d" % (w, s),
@@ -148,9 +146,7 @@ def test_varlen_many_short_sequences(cuda_dev, deterministic):
         assert_out_close(o_all[qa:qb].numpy(), _unseq(ro), dt, _unseq(bound), what="out seq %d" % s)
         assert_close(lse[:, qa:qb], rl[0], what="lse seq %d" % s)
         bargs = args[:3] + (_seq(do, qa, qb), True)
-        exact = R.attention_bwd_ref(*bargs)
-        faithful, bounds = R.attention_bwd_ref(*bargs, o=_seq(o_all, qa, qb),
-                                               unit_roundoff=unit_roundoff(dt))
+        exact, faithful, bounds = bwd_refs(bargs, _seq(o_all, qa, qb), unit_roundoff(dt))
         rows = (slice(qa, qb), slice(ka, kb), slice(ka, kb))
         for g_, r_, want, want_f, bnd, w in zip(got, rows, exact, faithful, bounds,
                                                 ("dq", "dk", "dv")):
