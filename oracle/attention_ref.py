@@ -106,7 +106,7 @@ def _expand_kv(x, hq):
 def _scores(q, k, scale, softcap):
     """scale q k^T, softcapped to c tanh(. / c) when softcap = c > 0; also returns the
     factor d(capped)/d(scaled) = 1 - tanh^2 (1 without softcap)."""
-    s = np.einsum("bhqd,bhkd->bhqk", q, k) * scale
+    s = (q @ k.swapaxes(-1, -2)) * scale
     if softcap is None or softcap <= 0:
         return s, 1.0
     t = np.tanh(s / softcap)
@@ -125,7 +125,7 @@ def attention_ref(q, k, v, causal, scale=None, return_p=False, window=(-1, -1), 
     if vis is not None:
         s = np.where(vis, s, NEG_INF)
     p, lse = _softmax_lse(s)
-    out = np.einsum("bhqk,bhkd->bhqd", p, v)
+    out = p @ v
     if return_p:
         return out.astype(np.float32), lse.astype(np.float32), p
     return out.astype(np.float32), lse.astype(np.float32)
@@ -164,13 +164,13 @@ def attention_bwd_ref(q, k, v, do, causal, scale=None, o=None, unit_roundoff=Non
         s = np.where(vis, s, NEG_INF)
     p, _ = _softmax_lse(s)
     if o is None:
-        o = np.einsum("bhqk,bhkd->bhqd", p, ve)
+        o = p @ ve
     dsum = np.sum(do64 * np.asarray(o, np.float64), axis=-1, keepdims=True)  # row-dot D
-    dp = np.einsum("bhqd,bhkd->bhqk", do64, ve)            # dO V^T
+    dp = do64 @ ve.swapaxes(-1, -2)  # dO V^T
     ds = p * (dp - dsum) * dcap
-    dq = np.einsum("bhqk,bhkd->bhqd", ds, ke) * scale
-    dke = np.einsum("bhqk,bhqd->bhkd", ds, q64) * scale
-    dve = np.einsum("bhqk,bhqd->bhkd", p, do64)
+    dq = (ds @ ke) * scale
+    dke = (ds.swapaxes(-1, -2) @ q64) * scale
+    dve = p.swapaxes(-1, -2) @ do64
     g = hq // hkv
     b, _, n, _ = dke.shape
     dk = dke.reshape(b, hkv, g, n, d).sum(axis=2)
@@ -180,10 +180,10 @@ def attention_bwd_ref(q, k, v, do, causal, scale=None, o=None, unit_roundoff=Non
         return grads
     u = float(unit_roundoff)
     ads = np.abs(ds) * scale
-    bq = u * (np.einsum("bhqk,bhkd->bhqd", ads, np.abs(ke)) + np.abs(dq))
-    bk = np.einsum("bhqk,bhqd->bhkd", ads, np.abs(q64)).reshape(b, hkv, g, n, d).sum(axis=2)
+    bq = u * (ads @ np.abs(ke) + np.abs(dq))
+    bk = (ads.swapaxes(-1, -2) @ np.abs(q64)).reshape(b, hkv, g, n, d).sum(axis=2)
     bk = u * (bk + np.abs(dk))
-    bv = np.einsum("bhqk,bhqd->bhkd", p, np.abs(do64)).reshape(b, hkv, g, n, d).sum(axis=2)
+    bv = (p.swapaxes(-1, -2) @ np.abs(do64)).reshape(b, hkv, g, n, d).sum(axis=2)
     bv = u * (bv + np.abs(dv))
     return grads, (bq, bk, bv)
 
@@ -196,8 +196,8 @@ def attention_out_bound(q, k, v, causal, unit_roundoff, scale=None, window=(-1, 
     _, _, p = attention_ref(q, k, v, causal, scale=scale, return_p=True, window=window,
                             softcap=softcap)
     ve = _expand_kv(np.asarray(v, np.float64), np.asarray(q).shape[1])
-    out = np.einsum("bhqk,bhkd->bhqd", p, ve)
-    return float(unit_roundoff) * (np.einsum("bhqk,bhkd->bhqd", p, np.abs(ve)) + np.abs(out))
+    out = p @ ve
+    return float(unit_roundoff) * (p @ np.abs(ve) + np.abs(out))
 
 
 # Unit roundoff of the 16-bit input types (round to nearest: |fl(x) - x| <= u |x|).
@@ -235,7 +235,7 @@ def paged_prefill_ref(q, k_cache, v_cache, block_table, seq_lens, query_start_lo
         kb = np.repeat(kb, h // hkv, axis=0)
         vb = np.repeat(vb, h // hkv, axis=0)
         qb = q[q0:q1].transpose(1, 0, 2)                      # [H, ql, D]
-        s = np.einsum("hqd,hkd->hqk", qb, kb) * scale
+        s = (qb @ kb.swapaxes(-1, -2)) * scale
         i = np.arange(q1 - q0)[:, None]
         j = np.arange(length)[None, :]
         vis = np.ones((q1 - q0, length), bool)
@@ -247,10 +247,10 @@ def paged_prefill_ref(q, k_cache, v_cache, block_table, seq_lens, query_start_lo
                 vis &= j < i + sliding_window_k
         s = np.where(vis[None], s, NEG_INF)
         p, l_ = _softmax_lse(s)
-        out[q0:q1] = np.einsum("hqk,hkd->hqd", p, vb).transpose(1, 0, 2)
+        out[q0:q1] = (p @ vb).transpose(1, 0, 2)
         lse[:, q0:q1] = l_
         if unit_roundoff is not None:
-            bound[q0:q1] = np.einsum("hqk,hkd->hqd", p, np.abs(vb)).transpose(1, 0, 2)
+            bound[q0:q1] = (p @ np.abs(vb)).transpose(1, 0, 2)
     if unit_roundoff is not None:
         bound = float(unit_roundoff) * (bound + np.abs(out))
         return out.astype(np.float32), lse.astype(np.float32), bound
