@@ -222,9 +222,10 @@ typedef struct {
   float softmax_scale;
   /* KV-cache element type: 0 = the query dtype, FA_DTYPE_E4M3 = fp8 (e4m3) caches
    * holding key / k_scale and value / v_scale (head_dim 128, 256 or 512); the kernel folds
-   * k_scale into the scores and v_scale into the output.  No counterpart in the
-   * reference (fp16 caches only); the layout of vLLM's fp8 KV cache with per-tensor
-   * scales. */
+   * k_scale into the scores and v_scale into the output.  Over fp8 caches the products
+   * run in f16 for either query dtype (a bf16 query group enters them scaled by a power
+   * of two, exact), so P is rounded to f16.  No counterpart in the reference (fp16
+   * caches only); the layout of vLLM's fp8 KV cache with per-tensor scales. */
   int32_t kv_dtype;
   float k_scale, v_scale;
 } fa_decode_args_t;
