@@ -261,7 +261,9 @@ __global__ void __launch_bounds__(DecCfg<D, KV8>::NTHREADS, DecCfg<D, KV8>::MINB
   // 2^-28 of that maximum is an f16 normal and converts exactly (bf16 has 8 significant
   // bits, f16 11), smaller ones round as f16 subnormals, and S carries the factor 2^qk,
   // which the softmax scales divide out (power-of-two scalings are exact).  The warps of
-  // a kv head read the same group, so they agree on qk.
+  // a kv head read the same group, so they agree on qk.  qk is clamped to [-100, 100] to
+  // keep the softmax scales times 2^-qk normal floats; only a group whose largest |q| is
+  // below 2^-86 stays under 2^14 after scaling (its elements are exact down to 2^-14).
   float q_up = 1.f, q_down = 1.f;
   if constexpr (KV8 && Pack2<T>::kBf16) {
     const uint32_t* qw = reinterpret_cast<const uint32_t*>(
