@@ -121,9 +121,10 @@ def bwd_refs(args, o, unit_roundoff, **kw):
     attention_bwd_ref(*args, **kw) with the kernel's output ``o``.
 
     The backward tests run each case in both backward modes on the same inputs, and the
-    forward (hence ``o``) does not depend on the mode, so the last two results are kept,
-    keyed by a digest of every array and option: the CPU oracle, not the GPU, dominates
-    the long cases."""
+    forward (hence ``o``) does not depend on the mode, so recent results are kept (up to
+    1 GiB, oldest dropped first; the varlen tests make one entry per sequence), keyed by
+    a digest of every array and option: the CPU oracle, not the GPU, dominates the long
+    cases."""
     from oracle import attention_ref as R
     h = hashlib.sha1(repr((sorted(kw.items()), unit_roundoff,
                            [a if np.isscalar(a) or isinstance(a, bool) else a.shape
@@ -136,6 +137,7 @@ def bwd_refs(args, o, unit_roundoff, **kw):
         exact = R.attention_bwd_ref(*args, **kw)
         faithful, bounds = R.attention_bwd_ref(*args, o=o, unit_roundoff=unit_roundoff, **kw)
         _BWD_REFS[key] = (exact, faithful, bounds)
-        while len(_BWD_REFS) > 2:
+        size = lambda e: sum(a.nbytes for part in e for a in part)
+        while len(_BWD_REFS) > 1 and sum(size(e) for e in _BWD_REFS.values()) > 2 ** 30:
             _BWD_REFS.popitem(last=False)
     return _BWD_REFS[key]
